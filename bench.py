@@ -1,0 +1,338 @@
+#!/usr/bin/env python
+"""Batch-1 int8 decode throughput of the Qwen3.5-0.8B hybrid decoder on B200.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference]
+
+Workload (config 0 of the build): random-init Qwen3.5-0.8B (seed 1234), a
+16-token prompt (default_rng(0)) prefilled one token at a time (untimed), then
+64 greedy decode steps (timed), repeated as "episodes" until K decode steps
+have been timed.  A step is one decode_step: embed, 24 layers, tied head,
+argmax.  Algorithmic bytes of a step attending T positions:
+B(T) = 758,248,704 + 24,576 * T (int8 weights + row scales + fp32 small
+tensors, plus fp32 K/V reads of the 6 attention layers).
+
+Under torchrun each rank decodes its own sequence on its own GPU (independent
+replicas; no collective on the data path) and the throughput is summed.
+
+--impl reference times the reference's own CPU decoder (the HLS C++ qwen_top
+compiled from the reference sources into oracle/_ref, single thread) on a
+bounded sample of the same workload; without that build it times the oracle
+port (numpy restatement of golden/model.py) instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "batch-1 decode tokens/s (int8, ~0.76 GB/token) and achieved HBM GB/s vs peak"
+UNIT = "tokens/s"
+B_WEIGHTS = 758_248_704
+KV_PER_POS = 24_576
+STATE_RW = 41_287_680
+PROMPT_LEN, EPISODE = 16, 64
+VOCAB = 248320
+
+
+def bytes_per_step(T):
+    return B_WEIGHTS + KV_PER_POS * T
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return 6650.0, "fallback 6.65 TB/s"
+
+
+def prompt_ids():
+    return np.random.default_rng(0).integers(0, VOCAB, PROMPT_LEN).astype(np.int32)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id=None):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.path = os.path.join("/tmp", f"qwen_b200_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+               "-lms", "200"]
+        if self.gpu_id is not None:
+            cmd += ["-i", str(self.gpu_id)]
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(cmd, stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows
+                                                         if r[3].replace(".", "").isdigit())}
+
+
+def blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return int(max(n)) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline_port(blob_path, n_steps):
+    """The oracle port (numpy restatement of golden/model.py) on this host's cores:
+    16-token prefill untimed, then n_steps greedy decode steps timed."""
+    from oracle import golden_port as P
+    from qwen_fpga_b200 import synth
+    cfg = synth.model_config()
+    dec = P.PortDecoder(synth.Blob(blob_path).fake_quant(), cfg)
+    st = P.PortState.zeros(cfg)
+    lg = None
+    for t in prompt_ids():
+        lg = dec.step(int(t), st)
+    t0 = time.perf_counter()
+    for _ in range(n_steps):
+        lg = dec.step(int(np.argmax(lg)), st)
+    dt = time.perf_counter() - t0
+    return {"value": n_steps / dt, "unit": UNIT, "cores": blas_threads(), "kind": "port",
+            "sample": f"oracle port (numpy golden restatement), config0 prompt prefill untimed + "
+                      f"{n_steps} greedy decode steps timed"}
+
+
+def cpu_reference_hls(blob_path, n_steps):
+    """The reference's HLS C++ decoder (oracle/_ref), single thread, same sample shape."""
+    from oracle import native
+    ref = native.HlsRef(blob_path)
+    am = 0
+    for t in prompt_ids():
+        am, _ = ref.step(int(t))
+    t0 = time.perf_counter()
+    for _ in range(n_steps):
+        am, _ = ref.step(am)
+    dt = time.perf_counter() - t0
+    ref.close()
+    return {"value": n_steps / dt, "unit": UNIT, "cores": 1, "kind": "reference",
+            "sample": f"reference HLS C++ qwen_top (hls/src/qwen_synth.hpp, g++ -O2, 1 thread), "
+                      f"config0 prompt prefill untimed + {n_steps} greedy decode steps timed"}
+
+
+def load_traffic():
+    p = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return None
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return 0
+    from qwen_fpga_b200 import synth
+    blob_path = synth.ensure_blob(1234)
+    from oracle import native
+    n = max(1, min(args.steps, 32))
+    if native.have_ref():
+        cb = cpu_reference_hls(blob_path, n)
+    else:
+        cb = cpu_baseline_port(blob_path, n)
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT,
+            "n_gpus": args.gpus, "steps": n, "warmup": 0, "ms_per_step": 1e3 / cb["value"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (int8 weights dequantised on the fly)", "data": "synthetic",
+            "config": {"workload": "config0 (random-init Qwen3.5-0.8B, 16-token prompt, greedy)",
+                       "batch": 1},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64 * 64, help="timed decode steps (multiple of 64)")
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--e2e-episodes", type=int, default=8)
+    ap.add_argument("--cpu-steps", type=int, default=24)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from qwen_fpga_b200 import api, synth
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(minutes=10))
+    if rank == 0:
+        blob_path = synth.ensure_blob(1234)
+    if world > 1:
+        dist.barrier()
+    blob_path = synth.ensure_blob(1234)
+
+    episodes = max(1, args.steps // EPISODE)
+    K = episodes * EPISODE
+    dec = api.Decoder(blob_path, device=local, max_ctx=PROMPT_LEN + EPISODE + 64)
+    prompt = prompt_ids()
+
+    # warm-up: W untimed steps
+    dec.reset()
+    dec.generate(prompt[:1], max(args.warmup, 3))
+
+    # timed: K decode steps in episodes of (16-token prefill untimed, 64 decode timed)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    dev_sec = 0.0
+    ids0 = None
+    with ClockSampler(local if world == 1 else local) as clk:
+        for e in range(episodes):
+            dec.reset()
+            ids, sec = dec.generate(prompt, EPISODE)
+            dev_sec += sec
+            if ids0 is None:
+                ids0 = ids
+            elif ids != ids0:
+                raise RuntimeError("episodes produced different tokens")
+    torch.cuda.synchronize()
+    if world > 1:
+        t = torch.tensor([dev_sec], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_sec = float(t.item())
+        dist.barrier()
+    ms_per_step = dev_sec / K * 1e3
+    value = world * K / dev_sec
+
+    # end to end through the C ABI: host token in, host argmax out, every step
+    e2e_sec = 0.0
+    e2e_steps = 0
+    for e in range(max(1, args.e2e_episodes)):
+        dec.reset()
+        am = 0
+        for t in prompt:
+            am, _ = dec.decode_step(int(t), want_logits=False)
+        t0 = time.perf_counter()
+        for _ in range(EPISODE):
+            am, _ = dec.decode_step(am, want_logits=False)
+        e2e_sec += time.perf_counter() - t0
+        e2e_steps += EPISODE
+    # with the fp32 logits returned to host memory each step (what golden decode_step returns)
+    dec.reset()
+    am = 0
+    for t in prompt:
+        am, _ = dec.decode_step(int(t), want_logits=False)
+    t0 = time.perf_counter()
+    for _ in range(EPISODE):
+        am, lg = dec.decode_step(am, want_logits=True)
+    lg_sec = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_sec, lg_sec], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_sec, lg_sec = (float(v) for v in t.tolist())
+    dec.close()
+
+    clocks = clk.summary()
+    if rank != 0:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+
+    peak, peak_src = peaks()
+    t_mean = PROMPT_LEN + 1 + (EPISODE - 1) / 2.0
+    bstep = bytes_per_step(t_mean)
+    achieved = bstep / (ms_per_step * 1e-3) / 1e9
+    traffic = load_traffic()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 weights x fp32 activations -> int32 digit accumulators",
+        "data": "synthetic (random-init Qwen3.5-0.8B, seed 1234)",
+        "config": {"workload": "config0: 16-token prompt prefill (untimed) + 64 greedy decode "
+                               "steps (timed), repeated", "model": "Qwen3.5-0.8B (random init)",
+                   "batch": 1, "global_batch": world, "episodes": episodes,
+                   "T_ctx": f"{PROMPT_LEN + 1}..{PROMPT_LEN + EPISODE}",
+                   "l2": "no flush: 758 MB of weights per step > 126 MB L2",
+                   "parallelism": "1 GPU" if world == 1 else f"{world} independent replicas"},
+        "e2e": {"value": world * e2e_steps / e2e_sec, "unit": UNIT, "h2d_bytes_per_step": 44,
+                "d2h_bytes_per_step": 20,
+                "with_logits": {"value": world * EPISODE / lg_sec, "unit": UNIT,
+                                "d2h_bytes_per_step": 20 + 4 * VOCAB}},
+        "gpu_launches": K * (24 * 5 + 2),
+        "roofline": {"bound": "hbm", "kernel": "whole decode step (graph of 122 kernels)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_src,
+                     "algorithmic_bytes_per_step": bstep,
+                     "state_bytes_per_step": STATE_RW,
+                     "traffic": traffic.get("bytes_per_step") if traffic else None},
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu:
+        try:
+            line["cpu_baseline"] = cpu_baseline_port(blob_path, args.cpu_steps)
+        except Exception as exc:  # the CPU leg never hides the GPU number
+            line["cpu_baseline"] = {"value": None, "error": str(exc)}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,115 @@
+/* qwen_b200.h -- C ABI of libqwenb200.so, the B200 (sm_100a) int8 batch-1
+ * decode step of the Qwen3.5-0.8B hybrid text decoder.
+ *
+ * Every entry point returns an int status (0 = QWEN_OK); a context keeps the
+ * message of its last failure (qwen_last_error).  Plain pointers and sizes
+ * only.  A context is thread-compatible: use one context per host thread, or
+ * lock around it.
+ *
+ * The reference interfaces each call replaces are cited as file:line inside
+ * allthingssecurity/qwen_fpga.
+ */
+#ifndef QWEN_B200_H
+#define QWEN_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QWEN_OK 0
+#define QWEN_ERR_ARG 1       /* bad argument (null, size, alignment, range) */
+#define QWEN_ERR_IO 2        /* blob / index file unreadable or inconsistent */
+#define QWEN_ERR_CUDA 3      /* a CUDA runtime call failed */
+#define QWEN_ERR_DEVICE 4    /* a kernel reported a bounded wait that ran out */
+#define QWEN_ERR_STATE 5     /* context too long, or call out of order */
+
+typedef struct qwen_ctx qwen_ctx;
+typedef struct CUstream_st* qwen_stream_t; /* same handle as cudaStream_t */
+
+/* Load a packed int8 blob (scripts/pack_weights.py:28-101 layout) and its
+ * index (either the flat weights.idx of scripts/emit_weight_index.py:1-22 or
+ * the *.manifest.json of pack_weights.py:93-101) onto the GPU and create one
+ * batch-1 decode state with room for max_ctx cached positions per attention
+ * layer.  Replaces the blob mmap + DecodeState set-up of
+ * hls/tb/run_hls.cpp:27-52 and golden/model.py:97-107.  n_gpus must be 1;
+ * device_ids may be NULL (device 0).  max_batch must be 1. */
+int qwen_create(const char* blob_path, const char* index_path, int n_gpus,
+                const int* device_ids, int max_ctx, int max_batch, qwen_ctx** out);
+
+/* Free every device and host resource of the context. */
+int qwen_destroy(qwen_ctx* ctx);
+
+/* Zero the recurrent state, empty the KV cache, pos = 0
+ * (hls/src/state.hpp:24-34, golden/model.py:97-107).  seq must be 0. */
+int qwen_reset(qwen_ctx* ctx, int seq);
+
+/* Load / read back the decode state (golden/model.py:86-95 DecodeState):
+ *   conv [18][6144][4]   rec [18][16][128][128]
+ *   kc, vc [6][T][2][256] (K after QK-norm and RoPE, V raw)   pos
+ * Host pointers.  Import requires T <= max_ctx - 1.  Export writes T and pos
+ * through the int pointers; kc/vc may be NULL to skip the cache, and must then
+ * hold max_ctx * 6 * 512 floats each when given. */
+int qwen_state_import(qwen_ctx* ctx, int seq, const float* conv, const float* rec,
+                      const float* kc, const float* vc, int T, int pos);
+int qwen_state_export(qwen_ctx* ctx, int seq, float* conv, float* rec, float* kc,
+                      float* vc, int* T, int* pos);
+
+/* ACT_INT8 switch of golden/model.py:34-45: on = every projection input is
+ * quantised per vector to int8 (int8 x int8 -> int32 GEMVs); off = fp32
+ * activations (W8A32).  The tied head always takes fp32 activations. */
+int qwen_set_act_int8(qwen_ctx* ctx, int on);
+
+/* One decode step for each of `batch` (must be 1) tokens: embed, 24 layers,
+ * final norm, tied head, argmax (first index on ties).  Mirrors
+ * golden/model.py:243-267 decode_step and hls/src/qwen_synth.hpp:39-92
+ * qwen_top.  tok and argmax_out are host pointers; logits_out (nullable) may be
+ * a host or device pointer of vocab (248320) floats. */
+int qwen_decode_step(qwen_ctx* ctx, const int* tok, int batch, float* logits_out,
+                     int* argmax_out);
+
+/* Prefill n_prompt tokens one at a time, then n_new greedy steps; out_ids gets
+ * the n_new generated ids (golden/model.py:270-280, run_prompt.py:80-98).
+ * decode_seconds (nullable) receives the device time of the n_new decode
+ * steps only, as run_prompt.py times them. */
+int qwen_generate(qwen_ctx* ctx, const int* prompt, int n_prompt, int n_new, int* out_ids,
+                  double* decode_seconds);
+
+/* Standalone int8-weight GEMV on device pointers, y[N] = s[o] * W[o,:] . x
+ * with fp32 x -- the operator of hls/src/gemv.hpp:28-42 (gemv_i8).  K must be
+ * a multiple of 32 in [32, 3584]; w 32-byte aligned.  x is mapped to a
+ * 23-bit signed fixed-point image (step 2^-22 of its largest power-of-two
+ * bound), split into three int8 digits, and each digit is dotted with the row
+ * exactly in int32; the digits are recombined exactly in int64 and scaled once
+ * in fp64, so the only error is x's fixed-point rounding (about fp32 round-off
+ * of the largest |x|). */
+int qwen_gemv_i8_f32(float* y, const int8_t* w, const float* s, const float* x, int N,
+                     int K, qwen_stream_t stream);
+
+/* Standalone int8 x int8 GEMV on device pointers: acc[o] = sum_i w[o,i]*xq[i]
+ * exactly in int32 (rtl/gemv_i8.sv:13-76, scripts/export_gemv_tv.py:49) and
+ * y[o] = acc[o] * sx * sw[o] in fp32, left to right (rtl/dequant.sv:12-29,
+ * export_gemv_tv.py:50).  acc and y are each nullable (not both).  Same K /
+ * alignment rules as above. */
+int qwen_gemv_i8_i8(int32_t* acc, float* y, const int8_t* w, const float* sw,
+                    const int8_t* xq, float sx, int N, int K, qwen_stream_t stream);
+
+/* One gated delta-rule step of a 16-head DeltaNet layer on device pointers,
+ * S [16][128][128] updated in place, out [16][128]:
+ *   S *= exp(g); kv = k^T S; d = (v - kv) * beta; S += k (x) d; out = q^T S
+ * hls/src/deltanet.hpp:118-127 delta_rule_layer, golden/model.py:174-178. */
+int qwen_delta_rule_layer(const float* q, const float* k, const float* v, const float* g,
+                          const float* beta, float* S, float* out, qwen_stream_t stream);
+
+/* Message of the context's last failure ("" when none).  ctx may be NULL for
+ * the last failure of a call that had no context. */
+const char* qwen_last_error(qwen_ctx* ctx);
+
+/* Library version string. */
+const char* qwen_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QWEN_B200_H */

@@ -1,0 +1,256 @@
+"""ctypes binding of libqwenb200.so -- the Python face of the C ABI in
+include/qwen_b200.h.
+
+It mirrors the reference's decode interface so callers of
+``golden/model.py`` can switch with a one-line change:
+
+    golden                                       this package
+    -------------------------------------------  -----------------------------------------
+    DecodeState.new(cfg)       (model.py:97)     Decoder(blob).state()  /  dec.reset()
+    decode_step(W, cfg, tok, st) (model.py:243)  decode_step(dec, cfg, tok, st)
+    generate(W, cfg, ids, n)   (model.py:270)    generate(dec, cfg, ids, n)
+    model.ACT_INT8 = True      (model.py:34)     dec.set_act_int8(True)
+
+There is no CPU fallback: if the library is missing or no CUDA device is
+present the calls raise.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libqwenb200.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "qwen_b200.h")
+VOCAB = 248320
+
+QWEN_OK, QWEN_ERR_ARG, QWEN_ERR_IO, QWEN_ERR_CUDA, QWEN_ERR_DEVICE, QWEN_ERR_STATE = range(6)
+
+_fp = C.POINTER(C.c_float)
+_ip = C.POINTER(C.c_int)
+_i8p = C.POINTER(C.c_int8)
+_i32p = C.POINTER(C.c_int32)
+_vp = C.c_void_p
+
+_lib = None
+
+
+class QwenError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"qwen error {code}: {msg}")
+        self.code = code
+
+
+def header_symbols() -> list[str]:
+    """Function names declared in include/qwen_b200.h."""
+    txt = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(qwen_\w+)\s*\(", txt, re.M)))
+
+
+def load() -> C.CDLL:
+    """Load the in-tree library (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise FileNotFoundError(f"{LIB_PATH} missing: run `python -m qwen_fpga_b200.build`")
+    L = C.CDLL(LIB_PATH)
+    L.qwen_version.restype = C.c_char_p
+    L.qwen_last_error.restype = C.c_char_p
+    L.qwen_last_error.argtypes = [_vp]
+    L.qwen_create.argtypes = [C.c_char_p, C.c_char_p, C.c_int, _ip, C.c_int, C.c_int,
+                              C.POINTER(_vp)]
+    L.qwen_destroy.argtypes = [_vp]
+    L.qwen_reset.argtypes = [_vp, C.c_int]
+    L.qwen_state_import.argtypes = [_vp, C.c_int, _fp, _fp, _fp, _fp, C.c_int, C.c_int]
+    L.qwen_state_export.argtypes = [_vp, C.c_int, _fp, _fp, _fp, _fp, _ip, _ip]
+    L.qwen_set_act_int8.argtypes = [_vp, C.c_int]
+    L.qwen_decode_step.argtypes = [_vp, _ip, C.c_int, _vp, _ip]
+    L.qwen_generate.argtypes = [_vp, _ip, C.c_int, C.c_int, _ip, C.POINTER(C.c_double)]
+    L.qwen_gemv_i8_f32.argtypes = [_vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]
+    L.qwen_gemv_i8_i8.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_float, C.c_int, C.c_int, _vp]
+    L.qwen_delta_rule_layer.argtypes = [_vp] * 7 + [_vp]
+    _lib = L
+    return L
+
+
+def _check(rc, ctx=None):
+    if rc != QWEN_OK:
+        msg = load().qwen_last_error(ctx).decode(errors="replace")
+        raise QwenError(rc, msg)
+
+
+def _fptr(a):
+    return a.ctypes.data_as(_fp) if a is not None else None
+
+
+class DecodeStateView:
+    """Host copy of the decode state, field for field the golden DecodeState
+    (golden/model.py:86-95): conv [18,6144,4], rec [18,16,128,128], kc/vc lists
+    of [T,2,256] per attention layer, pos."""
+
+    def __init__(self, conv, rec, kc, vc, pos):
+        self.conv, self.rec, self.kc, self.vc, self.pos = conv, rec, kc, vc, pos
+
+
+class Decoder:
+    """One GPU context: weights resident in HBM + one batch-1 decode state."""
+
+    def __init__(self, blob_path: str, index_path: str | None = None, device: int = 0,
+                 max_ctx: int = 4096, act_int8: bool = False):
+        L = load()
+        if index_path is None:
+            index_path = os.path.splitext(blob_path)[0] + ".idx"
+        self.max_ctx = max_ctx
+        dev = (C.c_int * 1)(device)
+        h = _vp()
+        rc = L.qwen_create(blob_path.encode(), index_path.encode(), 1, dev, max_ctx, 1,
+                           C.byref(h))
+        _check(rc)
+        self.h = h
+        self.act_int8 = False
+        if act_int8:
+            self.set_act_int8(True)
+
+    def close(self):
+        if getattr(self, "h", None):
+            load().qwen_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_act_int8(self, on: bool):
+        _check(load().qwen_set_act_int8(self.h, 1 if on else 0), self.h)
+        self.act_int8 = bool(on)
+
+    def reset(self):
+        _check(load().qwen_reset(self.h, 0), self.h)
+
+    def decode_step(self, tok: int, want_logits: bool = True):
+        """Returns (argmax, logits or None)."""
+        t = (C.c_int * 1)(int(tok))
+        am = (C.c_int * 1)()
+        lg = np.empty(VOCAB, np.float32) if want_logits else None
+        rc = load().qwen_decode_step(self.h, t, 1, lg.ctypes.data if lg is not None else None, am)
+        _check(rc, self.h)
+        return int(am[0]), lg
+
+    def generate(self, prompt, n_new: int):
+        """Prefill + greedy decode; returns (ids, decode seconds)."""
+        p = np.ascontiguousarray(np.asarray(prompt, np.int32))
+        out = np.empty(max(n_new, 1), np.int32)
+        sec = C.c_double()
+        rc = load().qwen_generate(self.h, p.ctypes.data_as(_ip), len(p), int(n_new),
+                                  out.ctypes.data_as(_ip), C.byref(sec))
+        _check(rc, self.h)
+        return [int(v) for v in out[:n_new]], sec.value
+
+    def import_state(self, st):
+        """st: golden DecodeState or anything with conv/rec/kc/vc/pos (kc/vc per layer [T,2,256])."""
+        conv = np.ascontiguousarray(st.conv, np.float32)
+        rec = np.ascontiguousarray(st.rec, np.float32)
+        T = int(st.kc[0].shape[0]) if len(st.kc) else 0
+        if T:
+            kc = np.ascontiguousarray(np.stack([np.asarray(k, np.float32) for k in st.kc]))
+            vc = np.ascontiguousarray(np.stack([np.asarray(v, np.float32) for v in st.vc]))
+        else:
+            kc = vc = None
+        rc = load().qwen_state_import(self.h, 0, _fptr(conv), _fptr(rec), _fptr(kc), _fptr(vc),
+                                      T, int(st.pos))
+        _check(rc, self.h)
+
+    def export_state(self) -> DecodeStateView:
+        T = C.c_int()
+        pos = C.c_int()
+        L = load()
+        _check(L.qwen_state_export(self.h, 0, None, None, None, None, C.byref(T), C.byref(pos)),
+               self.h)
+        conv = np.empty((18, 6144, 4), np.float32)
+        rec = np.empty((18, 16, 128, 128), np.float32)
+        kc = np.empty((6, T.value, 2, 256), np.float32)
+        vc = np.empty((6, T.value, 2, 256), np.float32)
+        rc = L.qwen_state_export(self.h, 0, _fptr(conv), _fptr(rec),
+                                 _fptr(kc) if T.value else None, _fptr(vc) if T.value else None,
+                                 C.byref(T), C.byref(pos))
+        _check(rc, self.h)
+        return DecodeStateView(conv, rec, list(kc), list(vc), pos.value)
+
+
+# ---------------------------------------------------------------- golden-shaped façade
+
+def decode_step(dec: Decoder, cfg, tok: int, st=None):
+    """Drop-in for golden/model.py:243 decode_step: returns fp32 logits [vocab].
+
+    The state lives on the GPU inside ``dec``; ``st`` is accepted for signature
+    compatibility and, if it carries a ``pos`` attribute, advanced like the
+    golden's ``st.pos += 1``."""
+    _, lg = dec.decode_step(tok, want_logits=True)
+    if st is not None and hasattr(st, "pos"):
+        st.pos += 1
+    return lg
+
+
+def generate(dec: Decoder, cfg, prompt_ids, n_new=16, greedy=True):
+    """Drop-in for golden/model.py:270 generate (greedy only): returns (ids, None)."""
+    ids, _ = dec.generate(prompt_ids, n_new)
+    return ids, None
+
+
+# ---------------------------------------------------------------- operators on torch tensors
+
+def _ptr(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream(stream):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def gemv_i8_f32(w, s, x, y=None, stream=None):
+    """y = s * (w @ x) for torch CUDA tensors w int8 [N,K], s fp32 [N], x fp32 [K]."""
+    import torch
+    N, K = w.shape
+    y = y if y is not None else torch.empty(N, dtype=torch.float32, device=w.device)
+    rc = load().qwen_gemv_i8_f32(_ptr(y), _ptr(w), _ptr(s), _ptr(x), N, K, _stream(stream))
+    _check(rc)
+    return y
+
+
+def gemv_i8_i8(w, sw, xq, sx, acc=None, y=None, stream=None, want_acc=True, want_y=True):
+    """acc = w @ xq (int32, exact), y = acc * sx * sw for torch CUDA tensors."""
+    import torch
+    N, K = w.shape
+    if want_acc and acc is None:
+        acc = torch.empty(N, dtype=torch.int32, device=w.device)
+    if want_y and y is None:
+        y = torch.empty(N, dtype=torch.float32, device=w.device)
+    rc = load().qwen_gemv_i8_i8(_ptr(acc if want_acc else None), _ptr(y if want_y else None),
+                                _ptr(w), _ptr(sw), _ptr(xq), float(sx), N, K, _stream(stream))
+    _check(rc)
+    return acc, y
+
+
+def delta_rule_layer(q, k, v, g, beta, S, out=None, stream=None):
+    """In-place gated delta rule of one 16-head layer on torch CUDA fp32 tensors."""
+    import torch
+    out = out if out is not None else torch.empty((16, 128), dtype=torch.float32, device=S.device)
+    rc = load().qwen_delta_rule_layer(_ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(S),
+                                      _ptr(out), _stream(stream))
+    _check(rc)
+    return out

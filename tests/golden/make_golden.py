@@ -1,0 +1,228 @@
+"""Generate the committed golden fixtures by running the UNMODIFIED reference.
+
+Runs in the build container only (it imports ``golden/model.py`` and
+``golden/quant.py`` of allthingssecurity/qwen_fpga from REF, default the
+read-only reference checkout).  The GPU box never runs this; it only reads
+the ``.npz`` files written here.
+
+    python tests/golden/make_golden.py [--ref PATH]
+
+Fixtures (all small; logits are stored as fixed-index samples + top-k):
+
+* ``config0.npz``  -- W8A32 random-init model (seed 1234), 16-token prompt
+  (``default_rng(0)``), 64 greedy steps: argmax of all 80 calls, logits
+  samples at steps 0, 15 and 79, plus the blob's sha256.
+* ``config2.npz``  -- ACT_INT8 (W8A8) warm start: rec N(0,0.1), 4096 cached
+  positions N(0,1), first token ``default_rng(0).integers(vocab)``; 6 greedy steps.
+* ``config3.npz``  -- W8A32 warm start with 32768 cached positions; 2 steps.
+* ``deltanet_trace.npz`` -- delta-rule inputs/outputs of linear layer 0 on a
+  warm state (5 prompt tokens, then the 6th traced), the capture pattern of
+  scripts/export_testvectors.py:31-40; full q,k,v,g,beta,o and S for heads 0 and 9.
+* ``ref_layout.json`` -- offsets/sizes of the reference's packed manifest
+  (artifacts/qwen35_int8.manifest.json) and its flat index (artifacts/weights.idx).
+* ``gemv_i8.npz`` -- int32 accumulator digests of the int8 GEMV microbench
+  shapes, computed with the reference's own quantiser and int32 product
+  (scripts/export_gemv_tv.py:25-50).
+* ``w8a8_gemv.npz`` -- a real model activation (embedding row 6511 under the
+  layer-3 input norm) quantised with export_gemv_tv.q_i8_vec and multiplied
+  with layer 3's k_proj, exactly as export_gemv_tv.py:37-50 does.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+import time
+import zlib
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+from qwen_fpga_b200 import synth  # noqa: E402
+from oracle.golden_port import warm_state  # noqa: E402
+
+VOCAB = 248320
+SAMPLE_IDX = np.sort(np.random.default_rng(7).choice(VOCAB, 4096, replace=False))
+GEMV_SHAPES = [(6144, 1024), (2048, 1024), (7168, 1024), (1024, 3584), (1024, 2048),
+               (4096, 1024), (248320, 1024)]
+
+
+def logit_digest(lg: np.ndarray, k=16) -> dict:
+    top = np.argsort(-lg, kind="stable")[:k]
+    return {"sample": lg[SAMPLE_IDX].astype(np.float32), "top_idx": top.astype(np.int64),
+            "top_val": lg[top].astype(np.float32), "sum": np.float64(lg.astype(np.float64).sum()),
+            "absmax": np.float32(np.abs(lg).max())}
+
+
+def put(out: dict, prefix: str, d: dict):
+    for k, v in d.items():
+        out[f"{prefix}_{k}"] = v
+
+
+def gemv_inputs(N, K, seed=0):
+    """Config-1 inputs: w int8 U[-127,127], sw U[1e-3,1e-2], x int8 U[-127,127], sx U[1e-3,1e-2]."""
+    rng = np.random.default_rng(seed)
+    w = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    sw = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    x = rng.integers(-127, 128, K, dtype=np.int8)
+    sx = np.float32(rng.uniform(1e-3, 1e-2))
+    return w, sw, x, sx
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--only", default="")
+    args = ap.parse_args()
+    sys.path.insert(0, os.path.join(args.ref, "golden"))
+    sys.path.insert(0, os.path.join(args.ref, "scripts"))
+    import model as G  # the reference golden, unmodified
+    from quant import quantize_weights
+
+    cfg = synth.model_config()
+    only = set(args.only.split(",")) if args.only else None
+    blob_path = synth.ensure_blob(1234)
+    blob = synth.Blob(blob_path)
+
+    # The golden's own quantiser must agree with the packed int8 + scales.
+    raw = np.random.default_rng(1234)
+    first = blob.manifest["tensors"][0]
+    shp0 = tuple(first["shape"])
+    assert np.array_equal(raw.standard_normal(shp0, np.float32) * 0.02, blob.fp32(first["name"]))
+
+    W = blob.fake_quant()
+
+    def golden_state_from(pst):
+        st = G.DecodeState.new(cfg)
+        st.conv[...] = pst.conv
+        st.rec[...] = pst.rec
+        st.kc = [k.copy() for k in pst.kc]
+        st.vc = [v.copy() for v in pst.vc]
+        st.pos = pst.pos
+        return st
+
+    if only is None or "layout" in only:
+        # the reference's own packed layout and flat index, for the packer test
+        import json as _json
+        man = _json.load(open(os.path.join(args.ref, "artifacts", "qwen35_int8.manifest.json")))
+        idx = open(os.path.join(args.ref, "artifacts", "weights.idx")).read().splitlines()
+        lay = {"total_bytes": man["total_bytes"], "config": man["config"],
+               "tensors": [[t["name"], t["offset"], t["nbytes"], t.get("scale_offset", 0),
+                            t["dtype"]] for t in man["tensors"]],
+               "idx_lines": idx}
+        with open(os.path.join(HERE, "ref_layout.json"), "w") as f:
+            _json.dump(lay, f)
+        print("layout: ok")
+
+    if only is None or "config0" in only:
+        t0 = time.time()
+        G.ACT_INT8 = False
+        prompt = np.random.default_rng(0).integers(0, VOCAB, 16)
+        st = G.DecodeState.new(cfg)
+        out = {"prompt": prompt.astype(np.int64), "blob_sha256": np.array(blob.digest())}
+        argmax, gen = [], []
+        logits = None
+        for i, t in enumerate(prompt):
+            logits = G.decode_step(W, cfg, int(t), st)
+            argmax.append(int(np.argmax(logits)))
+            if i in (0, 15):
+                put(out, f"step{i}", logit_digest(logits))
+        for j in range(64):
+            nxt = int(np.argmax(logits))
+            gen.append(nxt)
+            logits = G.decode_step(W, cfg, nxt, st)
+            argmax.append(int(np.argmax(logits)))
+        put(out, "step79", logit_digest(logits))
+        out["argmax"] = np.array(argmax, np.int64)
+        out["generated"] = np.array(gen, np.int64)
+        np.savez_compressed(os.path.join(HERE, "config0.npz"), **out)
+        print(f"config0: {time.time() - t0:.1f}s  gen[:8]={gen[:8]}")
+
+    if only is None or "trace" in only:
+        G.ACT_INT8 = False
+        prompt = np.random.default_rng(0).integers(0, VOCAB, 16)
+        st = G.DecodeState.new(cfg)
+        for t in prompt[:5]:
+            G.decode_step(W, cfg, int(t), st)
+        G.TRACE = {"layer": 0}
+        G.decode_step(W, cfg, int(prompt[5]), st)
+        tr = G.TRACE
+        G.TRACE = None
+        heads = np.array([0, 9])
+        assert np.abs(tr["S_in"]).max() > 1e-3
+        np.savez_compressed(os.path.join(HERE, "deltanet_trace.npz"),
+                            heads=heads, q=tr["q"], k=tr["k"], v=tr["v"], g=tr["g"],
+                            beta=tr["beta"], o_core=tr["o_core"],
+                            S_in=tr["S_in"][heads], S_out=tr["S_out"][heads])
+        print("trace: ok")
+
+    if only is None or "config2" in only:
+        t0 = time.time()
+        G.ACT_INT8 = True
+        pst = warm_state(cfg, 4096, seed=2)
+        st = golden_state_from(pst)
+        tok = int(np.random.default_rng(0).integers(0, VOCAB))
+        out = {"first_token": np.int64(tok), "T0": np.int64(4096)}
+        argmax = []
+        for j in range(6):
+            logits = G.decode_step(W, cfg, tok, st)
+            tok = int(np.argmax(logits))
+            argmax.append(tok)
+            if j in (0, 5):
+                put(out, f"step{j}", logit_digest(logits))
+        out["argmax"] = np.array(argmax, np.int64)
+        np.savez_compressed(os.path.join(HERE, "config2.npz"), **out)
+        G.ACT_INT8 = False
+        print(f"config2: {time.time() - t0:.1f}s argmax={argmax}")
+
+    if only is None or "config3" in only:
+        t0 = time.time()
+        G.ACT_INT8 = False
+        pst = warm_state(cfg, 32768, seed=3)
+        st = golden_state_from(pst)
+        del pst
+        tok = int(np.random.default_rng(0).integers(0, VOCAB))
+        out = {"first_token": np.int64(tok), "T0": np.int64(32768)}
+        argmax = []
+        for j in range(2):
+            logits = G.decode_step(W, cfg, tok, st)
+            tok = int(np.argmax(logits))
+            argmax.append(tok)
+            put(out, f"step{j}", logit_digest(logits))
+        out["argmax"] = np.array(argmax, np.int64)
+        np.savez_compressed(os.path.join(HERE, "config3.npz"), **out)
+        print(f"config3: {time.time() - t0:.1f}s argmax={argmax}")
+
+    if only is None or "gemv" in only:
+        import export_gemv_tv as TV   # reference quantiser q_i8_vec
+        out = {}
+        for (N, K) in GEMV_SHAPES:
+            w, sw, x, sx = gemv_inputs(N, K)
+            acc = (w.astype(np.int32) @ x.astype(np.int32)).astype(np.int32)
+            y = acc.astype(np.float32) * sx * sw
+            key = f"{N}x{K}"
+            out[key + "_crc"] = np.int64(zlib.crc32(acc.tobytes()))
+            out[key + "_sum"] = np.int64(acc.astype(np.int64).sum())
+            out[key + "_head"] = acc[:32].copy()
+            out[key + "_yhead"] = y[:32].copy()
+        np.savez_compressed(os.path.join(HERE, "gemv_i8.npz"), **out)
+        # a model activation through the reference's own quantiser
+        import model as GM
+        Wf = W
+        h = Wf["embed_tokens.weight"][6511].astype(np.float32)
+        hn = GM.rmsnorm(h, Wf["layers.3.input_layernorm.weight"], cfg["rms_norm_eps"])
+        x_i8, sx = TV.q_i8_vec(hn)
+        wq, ws = blob.int8("layers.3.self_attn.k_proj.weight")
+        acc = (wq.astype(np.int32) @ x_i8.astype(np.int32)).astype(np.int32)
+        np.savez_compressed(os.path.join(HERE, "w8a8_gemv.npz"), hn=hn, x_i8=x_i8,
+                            sx=np.float32(sx), acc=acc,
+                            y=acc.astype(np.float32) * np.float32(sx) * ws)
+        print("gemv: ok")
+
+
+if __name__ == "__main__":
+    main()
