@@ -12,6 +12,8 @@ Fixtures (all small; logits are stored as fixed-index samples + top-k):
 * ``config0.npz``  -- W8A32 random-init model (seed 1234), 16-token prompt
   (``default_rng(0)``), 64 greedy steps: argmax of all 80 calls, logits
   samples at steps 0, 15 and 79, plus the blob's sha256.
+* ``config0_w8a8.npz`` -- the config-0 run with ACT_INT8 (W8A8) from a cold
+  state, plus the golden's own logit movement under a 1e-7 perturbation.
 * ``config2.npz``  -- ACT_INT8 (W8A8) warm start: rec N(0,0.1), 4096 cached
   positions N(0,1), first token ``default_rng(0).integers(vocab)``; 6 greedy steps.
 * ``config3.npz``  -- W8A32 warm start with 32768 cached positions; 2 steps.
@@ -141,6 +143,69 @@ def main():
         out["generated"] = np.array(gen, np.int64)
         np.savez_compressed(os.path.join(HERE, "config0.npz"), **out)
         print(f"config0: {time.time() - t0:.1f}s  gen[:8]={gen[:8]}")
+
+    if only is None or "config0w8" in only:
+        # ACT_INT8 (W8A8) from a cold state on the config-0 prompt.  The same run
+        # with layer 0's in_proj_qkv (fake-quant fp32) perturbed by ~1e-7 relative
+        # gives the golden's own logit sensitivity to one-ulp arithmetic differences.
+        t0 = time.time()
+        prompt = np.random.default_rng(0).integers(0, VOCAB, 16)
+        out = {"prompt": prompt.astype(np.int64)}
+        runs = {}
+        for tag, pert in (("ref", 0.0), ("pert", 1e-7)):
+            Wp = W
+            if pert:
+                Wp = dict(W)
+                w0 = W["layers.0.linear_attn.in_proj_qkv.weight"]
+                noise = np.random.default_rng(1).standard_normal(w0.shape).astype(np.float32)
+                Wp["layers.0.linear_attn.in_proj_qkv.weight"] = w0 * (1 + np.float32(pert) * noise)
+            G.ACT_INT8 = True
+            st = G.DecodeState.new(cfg)
+            argmax, gen, digests = [], [], {}
+            logits = None
+            for i, t in enumerate(prompt):
+                logits = G.decode_step(Wp, cfg, int(t), st)
+                argmax.append(int(np.argmax(logits)))
+                if i in (0, 15):
+                    digests[i] = logits.copy()
+            for j in range(64):
+                nxt = int(np.argmax(logits))
+                gen.append(nxt)
+                logits = G.decode_step(Wp, cfg, nxt, st)
+                argmax.append(int(np.argmax(logits)))
+            digests[79] = logits.copy()
+            runs[tag] = (argmax, gen, digests)
+        G.ACT_INT8 = False
+        argmax, gen, dg = runs["ref"]
+        for i, lg in dg.items():
+            put(out, f"step{i}", logit_digest(lg))
+            d = np.abs(runs["pert"][2][i] - lg).max() / np.abs(lg).max()
+            out[f"step{i}_sens"] = np.float64(d)
+        out["argmax"] = np.array(argmax, np.int64)
+        out["generated"] = np.array(gen, np.int64)
+        out["pert_same_tokens"] = np.bool_(runs["pert"][1] == gen)
+        np.savez_compressed(os.path.join(HERE, "config0_w8a8.npz"), **out)
+        print(f"config0w8: {time.time() - t0:.1f}s sens="
+              f"{[float(out[f'step{i}_sens']) for i in (0, 15, 79)]} same={runs['pert'][1] == gen}")
+
+    if only is None or "config2sens" in only:
+        # the warm W8A8 start is chaotic: record the golden's own step-0 logit
+        # movement when the warm DeltaNet state is perturbed by 1e-7 / 3e-7 relative
+        fx2 = np.load(os.path.join(HERE, "config2.npz"))
+        out = {k: fx2[k] for k in fx2.files}
+        G.ACT_INT8 = True
+        for pert in (1e-7, 3e-7):
+            pst = warm_state(cfg, 4096, seed=2)
+            rng = np.random.default_rng(99)
+            pst.rec *= (1 + pert * rng.standard_normal(pst.rec.shape)).astype(np.float32)
+            st = golden_state_from(pst)
+            lg = G.decode_step(W, cfg, int(fx2["first_token"]), st)
+            ref = fx2["step0_sample"]
+            d = np.abs(lg[SAMPLE_IDX] - ref).max() / float(fx2["step0_absmax"])
+            out[f"step0_sens_{pert:.0e}"] = np.float64(d)
+            print(f"config2 sensitivity at {pert:.0e}: {d:.3e}")
+        G.ACT_INT8 = False
+        np.savez_compressed(os.path.join(HERE, "config2.npz"), **out)
 
     if only is None or "trace" in only:
         G.ACT_INT8 = False
