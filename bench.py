@@ -168,6 +168,18 @@ def load_traffic():
     return None
 
 
+def run_profile(args):
+    """Target for ncu: build the context, then exactly args.profile decode steps."""
+    from qwen_fpga_b200 import api, synth
+    dec = api.Decoder(synth.ensure_blob(1234), max_ctx=PROMPT_LEN + args.profile + 8)
+    dec.set_engine(args.engine)
+    for t in prompt_ids()[:args.profile]:
+        dec.decode_step(int(t), want_logits=False)
+    dec.close()
+    print("profile ok")
+    return 0
+
+
 def run_reference(args, rank):
     if rank != 0:
         return 0
@@ -201,7 +213,13 @@ def main():
     ap.add_argument("--e2e-episodes", type=int, default=8)
     ap.add_argument("--cpu-steps", type=int, default=24)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--engine", type=int, default=1,
+                    help="1 = persistent weight-streaming kernel, 0 = graph of phase kernels")
+    ap.add_argument("--profile", type=int, default=0,
+                    help="run N decode steps of the config-0 prompt (no timing, no JSON) for ncu")
     args = ap.parse_args()
+    if args.profile:
+        return run_profile(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -227,6 +245,11 @@ def main():
     episodes = max(1, args.steps // EPISODE)
     K = episodes * EPISODE
     dec = api.Decoder(blob_path, device=local, max_ctx=PROMPT_LEN + EPISODE + 64)
+    dec.set_engine(args.engine)
+    engine = dec.engine
+    launches_per_step = 1 if engine == 1 else 24 * 5 + 2
+    kernel_name = ("k_decode_persistent (one cooperative launch per step)" if engine == 1
+                   else "whole decode step (CUDA graph of 122 kernels)")
     prompt = prompt_ids()
 
     # warm-up: W untimed steps
@@ -313,8 +336,9 @@ def main():
                 "d2h_bytes_per_step": 20,
                 "with_logits": {"value": world * EPISODE / lg_sec, "unit": UNIT,
                                 "d2h_bytes_per_step": 20 + 4 * VOCAB}},
-        "gpu_launches": K * (24 * 5 + 2),
-        "roofline": {"bound": "hbm", "kernel": "whole decode step (graph of 122 kernels)",
+        "gpu_launches": K * launches_per_step,
+        "engine": "persistent" if engine == 1 else "graph",
+        "roofline": {"bound": "hbm", "kernel": kernel_name,
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_src,
                      "algorithmic_bytes_per_step": bstep,

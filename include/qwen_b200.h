@@ -61,6 +61,24 @@ int qwen_state_export(qwen_ctx* ctx, int seq, float* conv, float* rec, float* kc
  * activations (W8A32).  The tied head always takes fp32 activations. */
 int qwen_set_act_int8(qwen_ctx* ctx, int on);
 
+/* Select the decode engine of the context (no counterpart in the reference,
+ * which has one sequencer): 1 = one persistent cooperative kernel per step
+ * that streams the weights through a shared-memory ring (default), 0 = a CUDA
+ * graph of per-phase kernels.  Both compute the same arithmetic.  The
+ * environment variable QWEN_B200_ENGINE=0 selects 0 at qwen_create.
+ * qwen_get_engine returns the current engine (-1 for a NULL context). */
+int qwen_set_engine(qwen_ctx* ctx, int engine);
+int qwen_get_engine(qwen_ctx* ctx);
+
+/* Per-phase tracing of the persistent engine (no counterpart in the reference,
+ * which times steps with perf_counter at run_prompt.py:80-98): when on, every
+ * step records, per CTA and per phase, %globaltimer stamps [entry, inputs
+ * ready, first weight chunk landed, exit] (ns).  qwen_trace_read copies the
+ * last step's record, n_ctas * n_phases * 4 words, to host memory. */
+int qwen_trace_enable(qwen_ctx* ctx, int on);
+int qwen_trace_read(qwen_ctx* ctx, unsigned long long* out, int max_words, int* n_ctas,
+                    int* n_phases);
+
 /* One decode step for each of `batch` (must be 1) tokens: embed, 24 layers,
  * final norm, tied head, argmax (first index on ties).  Mirrors
  * golden/model.py:243-267 decode_step and hls/src/qwen_synth.hpp:39-92

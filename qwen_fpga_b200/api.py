@@ -69,6 +69,10 @@ def load() -> C.CDLL:
     L.qwen_state_import.argtypes = [_vp, C.c_int, _fp, _fp, _fp, _fp, C.c_int, C.c_int]
     L.qwen_state_export.argtypes = [_vp, C.c_int, _fp, _fp, _fp, _fp, _ip, _ip]
     L.qwen_set_act_int8.argtypes = [_vp, C.c_int]
+    L.qwen_set_engine.argtypes = [_vp, C.c_int]
+    L.qwen_get_engine.argtypes = [_vp]
+    L.qwen_trace_enable.argtypes = [_vp, C.c_int]
+    L.qwen_trace_read.argtypes = [_vp, C.POINTER(C.c_ulonglong), C.c_int, _ip, _ip]
     L.qwen_decode_step.argtypes = [_vp, _ip, C.c_int, _vp, _ip]
     L.qwen_generate.argtypes = [_vp, _ip, C.c_int, C.c_int, _ip, C.POINTER(C.c_double)]
     L.qwen_gemv_i8_f32.argtypes = [_vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]
@@ -136,6 +140,29 @@ class Decoder:
     def set_act_int8(self, on: bool):
         _check(load().qwen_set_act_int8(self.h, 1 if on else 0), self.h)
         self.act_int8 = bool(on)
+
+    def set_engine(self, engine: int):
+        """1 = persistent weight-streaming kernel (default), 0 = graph of phase kernels."""
+        _check(load().qwen_set_engine(self.h, int(engine)), self.h)
+
+    @property
+    def engine(self) -> int:
+        return int(load().qwen_get_engine(self.h))
+
+    def trace_enable(self, on: bool = True):
+        _check(load().qwen_trace_enable(self.h, 1 if on else 0), self.h)
+
+    def trace_read(self):
+        """Last step's per-CTA, per-phase stamps [entry, ready, first chunk, exit] (ns),
+        shape [n_ctas, n_phases, 4]."""
+        n = 160 * 121 * 4 + 4096
+        buf = np.zeros(n, np.uint64)
+        nc, npz = C.c_int(), C.c_int()
+        _check(load().qwen_trace_read(self.h, buf.ctypes.data_as(C.POINTER(C.c_ulonglong)), n,
+                                      C.byref(nc), C.byref(npz)), self.h)
+        m = nc.value * npz.value * 4
+        self.trace_chunks = buf[m:m + 448 * 4].reshape(448, 4)
+        return buf[:m].reshape(nc.value, npz.value, 4)
 
     def reset(self):
         _check(load().qwen_reset(self.h, 0), self.h)

@@ -98,7 +98,7 @@ struct StepDyn {
   int n_prompt;   // tokens taken from `prompt` before switching to greedy feedback
   int act_int8;   // ACT_INT8 switch
   int want_logits;
-  int pad;
+  int seq;        // launch sequence number (tags of the persistent kernel)
 };
 
 // ---- device decode state + scratch of one sequence
@@ -153,15 +153,18 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // Block-wide sum / max; `red` is >= 32 floats of shared scratch.  All threads
-// of the block must call; returns the result to every thread.
+// of the block must call; returns the result to every thread.  The sum adds
+// the per-warp partials in warp order, the same order as the persistent
+// kernel, so both engines round identically.
 __device__ __forceinline__ float block_sum(float v, float* red) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
   v = warp_sum(v);
   __syncthreads();
   if (lane == 0) red[wid] = v;
   __syncthreads();
-  float t = (lane < nw) ? red[lane] : 0.0f;
-  return warp_sum(t);
+  float t = 0.0f;
+  for (int w = 0; w < nw; ++w) t += red[w];
+  return t;
 }
 __device__ __forceinline__ float block_max(float v, float* red) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;

@@ -1,0 +1,1203 @@
+// Persistent weight-streaming decode step of libqwenb200: the whole token
+// (embed, 24 layers, tied head, argmax) in ONE cooperative launch with one
+// CTA per SM.
+//
+// Weight streamer.  Every CTA owns a ring of NSLOT shared-memory slots (16 KB
+// of weight rows + the rows' fp32 scales).  A static per-CTA schedule lists
+// the weight chunks (contiguous rows of one matrix) the CTA consumes during
+// the token, in consumption order.  Each slot is refilled with cp.async.bulk
+// (L2 evict-first, completion on the slot's mbarrier) by whichever of the
+// eight warps finishes reading it last (a per-slot shared-memory counter), so
+// the HBM stream runs ahead of the compute by the ring's depth wherever the
+// compute is waiting -- the decoupled weight-stationary streaming the
+// reference's HBM engine is built around (docs/hbm_bandwidth.md), on 148 SMs.
+// Warps never synchronise with each other per chunk.
+//
+// No grid barriers.  Activations crossing CTAs are 64-bit words {fp32 value,
+// 32-bit tag} written with relaxed gpu-scope stores; tag = step_seq*128 +
+// phase + 1 is unique per (token, phase).  A consumer polls exactly the words
+// it needs (all of a thread's loads issued before any is checked) until every
+// tag matches.  The split-KV attention merge and the head argmax use
+// last-arriver counters.  Every wait is bounded by %globaltimer; on expiry the
+// CTA records ERR_WAIT, raises a global abort flag that every other wait also
+// watches, drains its in-flight bulk copies and returns.
+//
+// Phase program per layer l (p = 5l + sub): IN (projections of the normed
+// residual), MIX (DeltaNet delta rule, or split-KV attention), OUT (out/o
+// projection + residual), GATEUP (silu(gate)*up), DOWN (down projection +
+// residual); phase 120 is the tied head.  Arithmetic (and its rounding order)
+// is that of decode.cu, so both engines agree bit for bit; the contract is
+// golden/model.py:243-267.
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "persist.cuh"
+
+namespace qb {
+
+constexpr int NCW = 8;                  // warps per CTA
+constexpr int PT = NCW * 32;            // threads per CTA
+constexpr int NTHREADS = PT;
+constexpr int SLOTW = 16384;            // weight bytes per ring slot
+constexpr int SLOT = SLOTW + 256;       // + row scales of the chunk (two arrays for gate/up)
+constexpr int NSLOT = 11;               // ring depth
+constexpr int MAXCH = 448;              // chunk-list capacity per CTA
+constexpr int NPHASE = NLAYER * 5 + 1;  // 121
+constexpr int PH_HEAD = NLAYER * 5;
+constexpr int MAXP = KMAX / 2 / PT;     // tagged pairs per thread in a full-vector wait (7)
+constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s bound on any wait
+
+// ---- shared memory layout (dynamic, offsets from the aligned base)
+constexpr int OFF_RING = 0;
+constexpr int OFF_DIG = OFF_RING + NSLOT * SLOT;          // int8 [3][KMAX]
+constexpr int OFF_XF = OFF_DIG + 3 * KMAX;                // float [KMAX]
+constexpr int OFF_HS = OFF_XF + 4 * KMAX;                 // float [HID]
+constexpr int OFF_LAY = OFF_HS + 4 * HID;                 // LayerW [NLAYER]
+constexpr int OFF_CH = OFF_LAY + ((int)sizeof(LayerW) * NLAYER + 15) / 16 * 16;  // Chunk [MAXCH]
+constexpr int OFF_BAR = OFF_CH + 8 * MAXCH;               // u64 full[NSLOT]
+constexpr int OFF_MISC = OFF_BAR + 8 * NSLOT;             // small scalars
+constexpr int SMEM_BYTES = OFF_MISC + 1024;
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+static_assert(OFF_DIG % 16 == 0 && OFF_XF % 16 == 0 && OFF_HS % 16 == 0 && SLOT % 16 == 0, "alignment");
+static_assert(OFF_BAR % 8 == 0 && OFF_MISC % 8 == 0, "alignment");
+static_assert(MAXP * 2 * PT == KMAX, "pair split");
+
+struct Misc {
+  float red[32];
+  double scale;
+  int ndig;
+  int abort;
+  int tok;
+  int last;
+  int slot_cnt[NSLOT];     // warps done with the slot's current chunk
+  int slot_last[NSLOT];    // last chunk issued into the slot (-1: none)
+  int pos, T, conv_base, act_int8, want_logits, seq, step;
+  unsigned long long wbest[NCW];
+  float inv_h[LH];
+  float gate_g, gate_beta;
+};
+static_assert(sizeof(Misc) <= 1024, "misc");
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ unsigned smem_u32(const void* p) {
+  return (unsigned)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// all warps of the CTA (named barrier 1)
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ int consumer_and(int v) {
+  int r;
+  asm volatile("{ .reg .pred p, q; setp.ne.s32 p, %1, 0; bar.red.and.pred q, 1, 256, p; selp.s32 %0, 1, 0, q; }"
+               : "=r"(r) : "r"(v) : "memory");
+  return r;
+}
+__device__ __forceinline__ void ld_tv2(const unsigned long long* p, unsigned long long& a,
+                                       unsigned long long& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0,%1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tv(const unsigned long long* p) {
+  unsigned long long a;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
+  return a;
+}
+__device__ __forceinline__ void st_tv(unsigned long long* p, float v, unsigned tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" :: "l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ int ld_flag(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool tag_ok(unsigned long long w, unsigned tag) {
+  return (unsigned)(w >> 32) == tag;
+}
+__device__ __forceinline__ float tv_val(unsigned long long w) { return __uint_as_float((unsigned)w); }
+__device__ __forceinline__ void mbar_init(unsigned bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(unsigned bar, unsigned parity) {
+  unsigned ok;
+  asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void mbar_arrive(unsigned bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(unsigned dst, const void* src, unsigned bytes, unsigned bar,
+                                         unsigned long long pol) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+               :: "r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(pol) : "memory");
+}
+__device__ __forceinline__ void mbar_expect(unsigned bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ int redux_add(int v) {
+  return (int)__reduce_add_sync(0xffffffffu, (unsigned)v);
+}
+
+// ---------------------------------------------------------------- kernel context
+struct PCtx {
+  const PersistArgs* A;
+  unsigned char* sm;
+  Misc* ms;
+  LayerW* lay;
+  const Chunk* ch;
+  int nch;          // chunks of this CTA
+  int cur;          // next chunk index to consume (per consumer warp; all warps agree)
+  unsigned long long pol;
+};
+
+__device__ __forceinline__ unsigned full_bar(const PCtx& c, int slot) { return smem_u32(c.sm + OFF_BAR + 8 * slot); }
+
+__device__ __forceinline__ unsigned tag_of(const PCtx& c, int phase) {
+  return (unsigned)c.ms->seq * 128u + (unsigned)phase + 1u;
+}
+
+__device__ __forceinline__ void trace_mark(const PCtx& c, int p, int k) {
+  if (c.A->trace && threadIdx.x == 0)
+    c.A->trace[((size_t)blockIdx.x * NPHASE + p) * TRACE_STAMPS + k] = gtime();
+}
+// per-chunk stamps of CTA 0 (after the per-phase block): [chunk][4]
+__device__ __forceinline__ void trace_chunk(const PCtx& c, int i, int k) {
+  if (c.A->trace && blockIdx.x == 0 && threadIdx.x == 0)
+    c.A->trace[(size_t)gridDim.x * NPHASE * TRACE_STAMPS + (size_t)i * 4 + k] = gtime();
+}
+
+__device__ void raise_abort(const PCtx& c) {
+  atomicCAS(c.A->err, 0, ERR_WAIT);
+  atomicExch(c.A->abort_flag, 1);
+  *(volatile int*)&c.ms->abort = 1;
+}
+__device__ __forceinline__ bool aborted(const PCtx& c) {
+  return *(volatile int*)&c.ms->abort || ld_flag(c.A->abort_flag);
+}
+
+// Sources of chunk k: weight rows (src, and src2 for the up rows of a
+// gate/up pair) and the row-scale arrays (sc, sc2; null for fp32 rows).
+__device__ __forceinline__ void chunk_src(const PCtx& c, const Chunk& k, const char*& src,
+                                          const char*& src2, unsigned& bytes, const float*& sc,
+                                          const float*& sc2) {
+  const int p = k.phase;
+  const int row0 = (int)k.row0, n = k.nrows;
+  src2 = nullptr;
+  sc = sc2 = nullptr;
+  if (p == PH_HEAD) {
+    src = (const char*)c.A->emb_q + (size_t)row0 * HID;
+    bytes = n * HID;
+    sc = c.A->emb_s;
+    return;
+  }
+  const LayerW& L = c.lay[p / 5];
+  const int sub = p % 5;
+  if (sub == 0) {
+    if (L.linear) {
+      if (k.seg == 0) { src = (const char*)L.qkv_q + (size_t)row0 * HID; bytes = n * HID; sc = L.qkv_s; }
+      else if (k.seg == 1) { src = (const char*)L.z_q + (size_t)row0 * HID; bytes = n * HID; sc = L.z_s; }
+      else if (k.seg == 2) { src = (const char*)(L.b_w + (size_t)row0 * HID); bytes = n * HID * 4; }
+      else { src = (const char*)(L.a_w + (size_t)row0 * HID); bytes = n * HID * 4; }
+    } else {
+      if (k.seg == 0) { src = (const char*)L.q_q + (size_t)row0 * HID; sc = L.q_s; }
+      else if (k.seg == 1) { src = (const char*)L.k_q + (size_t)row0 * HID; sc = L.k_s; }
+      else { src = (const char*)L.v_q + (size_t)row0 * HID; sc = L.v_s; }
+      bytes = n * HID;
+    }
+  } else if (sub == 2) {
+    src = (const char*)(L.linear ? L.out_q : L.o_q) + (size_t)row0 * VDIM;
+    bytes = n * VDIM;
+    sc = L.linear ? L.out_s : L.o_s;
+  } else if (sub == 3) {
+    src = (const char*)L.gate_q + (size_t)row0 * HID;
+    src2 = (const char*)L.up_q + (size_t)row0 * HID;
+    bytes = n * HID;
+    sc = L.gate_s;
+    sc2 = L.up_s;
+  } else {
+    src = (const char*)L.down_q + (size_t)row0 * FFN;
+    bytes = n * FFN;
+    sc = L.down_s;
+  }
+}
+
+// Scales of rows [row0, row0+n) are copied from the 16-byte aligned start
+// row0 & ~3; row o's scale sits at tail[o - (row0 & ~3)] (second array at +32).
+__device__ __forceinline__ unsigned scale_bytes(int row0, int n) {
+  const int a = row0 & ~3, b = (row0 + n + 3) & ~3;
+  return (unsigned)(b - a) * 4u;
+}
+
+// Issue the bulk copies of chunk i into its slot (one lane).
+__device__ __forceinline__ void issue_chunk(const PCtx& c, int i) {
+  const int slot = i % NSLOT;
+  const Chunk k = c.ch[i];
+  const char* src;
+  const char* src2;
+  unsigned bytes;
+  const float* sc;
+  const float* sc2;
+  chunk_src(c, k, src, src2, bytes, sc, sc2);
+  const unsigned bar = full_bar(c, slot);
+  const unsigned dst = smem_u32(c.sm + OFF_RING + slot * SLOT);
+  const unsigned sb = sc ? scale_bytes((int)k.row0, k.nrows) : 0u;
+  const unsigned total = (src2 ? 2 * bytes : bytes) + (sc ? sb : 0u) + (sc2 ? sb : 0u);
+  mbar_expect(bar, total);
+  bulk_g2s(dst, src, bytes, bar, c.pol);
+  if (src2) bulk_g2s(dst + bytes, src2, bytes, bar, c.pol);
+  const int a = (int)k.row0 & ~3;
+  if (sc) bulk_g2s(dst + SLOTW, sc + a, sb, bar, c.pol);
+  if (sc2) bulk_g2s(dst + SLOTW + 128, sc2 + a, sb, bar, c.pol);
+}
+
+// Lane 0 of a warp that has finished reading chunk i: count it; the last of
+// the eight warps refills the slot with chunk i + NSLOT.
+__device__ __forceinline__ void release_slot(PCtx& c, int i) {
+  const int s = i % NSLOT;
+  if (atomicAdd(&c.ms->slot_cnt[s], 1) == NCW - 1) {
+    c.ms->slot_cnt[s] = 0;
+    const int nx = i + NSLOT;
+    if (nx < c.nch && !*(volatile int*)&c.ms->abort) {
+      issue_chunk(c, nx);
+      c.ms->slot_last[s] = nx;
+    }
+  }
+}
+
+// Consumer warp: wait for chunk i's bytes.  Same result in every lane.
+__device__ __forceinline__ bool wait_full(PCtx& c, int i) {
+  const unsigned bar = full_bar(c, i % NSLOT);
+  const unsigned parity = (unsigned)((i / NSLOT) & 1);
+  int good = 1;
+  if (!mbar_try(bar, parity)) {
+    const unsigned long long t0 = gtime();
+    int it = 0;
+    while (!mbar_try(bar, parity)) {
+      if (((++it) & 63) == 0) {
+        if (aborted(c)) { good = 0; break; }
+        if (gtime() - t0 > WAIT_NS) { raise_abort(c); good = 0; break; }
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, good) != 0;
+}
+
+// Poll tagged words src[0..n) (n even, n <= KMAX) until all carry `tag`; values
+// into dst (smem).  Each thread issues all its pending loads before checking
+// any.  Collective over the consumer threads.  false on abort.
+__device__ bool wait_tagged(PCtx& c, const unsigned long long* src, int n, unsigned tag,
+                                         float* dst) {
+  const unsigned long long t0 = gtime();
+  const int npair = n >> 1;
+  unsigned pend = 0;
+#pragma unroll
+  for (int j = 0; j < MAXP; ++j)
+    if ((int)threadIdx.x + PT * j < npair) pend |= 1u << j;
+  int it = 0;
+  for (;;) {
+    unsigned long long a[MAXP], b[MAXP];
+#pragma unroll
+    for (int j = 0; j < MAXP; ++j)
+      if (pend >> j & 1) ld_tv2(src + 2 * (threadIdx.x + PT * j), a[j], b[j]);
+#pragma unroll
+    for (int j = 0; j < MAXP; ++j) {
+      if ((pend >> j & 1) && tag_ok(a[j], tag) && tag_ok(b[j], tag)) {
+        const int q = threadIdx.x + PT * j;
+        dst[2 * q] = tv_val(a[j]);
+        dst[2 * q + 1] = tv_val(b[j]);
+        pend &= ~(1u << j);
+      }
+    }
+    if (consumer_and(pend == 0)) return true;
+    if (((++it) & 15) == 0) {
+      int bad = 0;
+      if (threadIdx.x == 0) {
+        if (aborted(c)) bad = 1;
+        else if (gtime() - t0 > WAIT_NS) { raise_abort(c); bad = 1; }
+      }
+      if (!consumer_and(!bad)) return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------- prologues
+
+// 2^e as a float for -126 <= e <= 127.
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
+
+// Digit image of xf[0..K) into the linear digit planes (W8A32), or the golden
+// _qa int8 quantiser (ACT_INT8).  Same values as encode_x in common.cuh.
+__device__ void encode_lin(PCtx& c, int K, bool act_int8) {
+  float* xf = (float*)(c.sm + OFF_XF);
+  int8_t* dg = (int8_t*)(c.sm + OFF_DIG);
+  Misc* ms = c.ms;
+  float m = 0.0f;
+  for (int i = threadIdx.x; i < K; i += PT) m = fmaxf(m, fabsf(xf[i]));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) ms->red[threadIdx.x >> 5] = m;
+  consumer_sync();
+  float amax = 0.0f;
+#pragma unroll
+  for (int w = 0; w < NCW; ++w) amax = fmaxf(amax, ms->red[w]);
+  // every thread handles 4 consecutive elements -> one 32-bit word per plane
+  if (act_int8) {
+    const float s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+    for (int i4 = threadIdx.x; i4 < K / 4; i4 += PT) {
+      unsigned w0 = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = 4 * i4 + e;
+        int qi = 0;
+        if (amax > 0.0f) {
+          const float q = fminf(fmaxf(rintf(__fdiv_rn(xf[i], s)), -127.0f), 127.0f);
+          xf[i] = __fmul_rn(q, s);
+          qi = (int)q;
+        }
+        w0 |= ((unsigned)qi & 0xffu) << (8 * e);
+      }
+      reinterpret_cast<unsigned*>(dg)[i4] = w0;
+    }
+    if (threadIdx.x == 0) { ms->scale = (double)s; ms->ndig = 1; }
+  } else {
+    const int ex = amax > 0.0f ? (int)((__float_as_uint(amax) >> 23) & 0xff) - 126 : 0;
+    const int sh = 22 - ex;               // amax in [2^(ex-1), 2^ex) for normal amax
+    const bool fast = (__float_as_uint(amax) >> 23) != 0 && sh >= -126 && sh <= 127;
+    const float p2 = fast ? pow2f(sh) : 0.0f;
+    int exs = 0;
+    if (!fast && amax > 0.0f) frexpf(amax, &exs);
+    const int shs = fast ? sh : 22 - exs;
+    for (int i4 = threadIdx.x; i4 < K / 4; i4 += PT) {
+      unsigned w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float v = xf[4 * i4 + e];
+        int X = 0;
+        if (amax > 0.0f) X = fast ? __float2int_rn(v * p2) : (int)rintf(ldexpf(v, shs));
+        const int a0 = (X << 24) >> 24;
+        const int X1 = (X - a0) >> 8;
+        const int a1 = (X1 << 24) >> 24;
+        const int a2 = (X1 - a1) >> 8;
+        w0 |= ((unsigned)a0 & 0xffu) << (8 * e);
+        w1 |= ((unsigned)a1 & 0xffu) << (8 * e);
+        w2 |= ((unsigned)a2 & 0xffu) << (8 * e);
+      }
+      reinterpret_cast<unsigned*>(dg)[i4] = w0;
+      reinterpret_cast<unsigned*>(dg + KMAX)[i4] = w1;
+      reinterpret_cast<unsigned*>(dg + 2 * KMAX)[i4] = w2;
+    }
+    if (threadIdx.x == 0) { ms->scale = ldexp(1.0, -shs); ms->ndig = 3; }
+  }
+  consumer_sync();
+}
+
+// Gains of a (1+w) RMSNorm over HID for this thread's elements i = tid + 256 j,
+// loaded before the inputs are waited for.
+struct Gain4 { float v[HID / PT]; };
+__device__ __forceinline__ Gain4 load_gain(const float* w) {
+  Gain4 g;
+#pragma unroll
+  for (int j = 0; j < HID / PT; ++j) g.v[j] = __ldg(w + threadIdx.x + PT * j);
+  return g;
+}
+
+// xf = rmsnorm(h) * (1 + w) over HID (golden/model.py:63-75); h is in hs.
+__device__ void norm_into_xf(PCtx& c, const Gain4& w) {
+  float* xf = (float*)(c.sm + OFF_XF);
+  float* hs = (float*)(c.sm + OFF_HS);
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < HID; i += PT) ss = fmaf(hs[i], hs[i], ss);
+  ss = warp_sum(ss);
+  consumer_sync();
+  if ((threadIdx.x & 31) == 0) c.ms->red[threadIdx.x >> 5] = ss;
+  consumer_sync();
+  float tot = 0.0f;
+#pragma unroll
+  for (int q = 0; q < NCW; ++q) tot += c.ms->red[q];
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)HID), EPS)));
+#pragma unroll
+  for (int j = 0; j < HID / PT; ++j) {
+    const int i = threadIdx.x + PT * j;
+    xf[i] = __fmul_rn(__fmul_rn(hs[i], inv), __fadd_rn(1.0f, w.v[j]));
+  }
+  consumer_sync();
+}
+
+// Prologue of GEMV phase p: wait for the inputs, build xf, encode.  false on abort.
+__device__ bool prologue(PCtx& c, int p) {
+  float* xf = (float*)(c.sm + OFF_XF);
+  float* hs = (float*)(c.sm + OFF_HS);
+  const PersistArgs& A = *c.A;
+  Misc* ms = c.ms;
+  const bool i8 = ms->act_int8 != 0;
+  if (p == PH_HEAD) {
+    const Gain4 g = load_gain(A.final_norm);
+    if (!wait_tagged(c, A.tv_h, HID, tag_of(c, PH_HEAD - 1), hs)) return false;
+    norm_into_xf(c, g);
+    encode_lin(c, HID, false);
+    return true;
+  }
+  const int l = p / 5, sub = p % 5;
+  const LayerW& L = c.lay[l];
+  if (sub == 0) {
+    const Gain4 g = load_gain(L.in_norm);
+    if (l == 0) {
+      // residual stream starts at the dequantised embedding row (golden/model.py:246)
+      const int tok = ms->tok;
+      const float sc = __ldg(A.emb_s + tok);
+      const int8_t* row = A.emb_q + (size_t)tok * HID;
+      for (int i = threadIdx.x; i < HID; i += PT) hs[i] = __fmul_rn((float)row[i], sc);
+      consumer_sync();
+    } else if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) {
+      return false;
+    }
+    norm_into_xf(c, g);
+    encode_lin(c, HID, i8);
+  } else if (sub == 2) {
+    if (L.linear) {
+      // gated RMSNorm of the delta-rule output (golden/model.py:183-189):
+      // o from MIX(l) into xf, z from IN(l) parked in the digit region
+      float* zb = (float*)(c.sm + OFF_DIG);
+      const float gw = __ldg(L.gnorm_w + (threadIdx.x % LV));   // element i = tid + 256 j
+      if (!wait_tagged(c, A.tv_o, VDIM, tag_of(c, p - 1), xf)) return false;
+      if (!wait_tagged(c, A.tv_z, VDIM, tag_of(c, p - 2), zb)) return false;
+      const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+      for (int h = wid; h < LH; h += NCW) {
+        float ss = 0.0f;
+        for (int i = lane; i < LV; i += 32) ss = fmaf(xf[h * LV + i], xf[h * LV + i], ss);
+        ss = warp_sum(ss);
+        if (lane == 0) ms->inv_h[h] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)LV), EPS)));
+      }
+      consumer_sync();
+      for (int i = threadIdx.x; i < VDIM; i += PT) {
+        const float v = __fmul_rn(__fmul_rn(xf[i], ms->inv_h[i / LV]), gw);
+        xf[i] = __fmul_rn(v, silu_f(zb[i]));
+      }
+      consumer_sync();
+      encode_lin(c, VDIM, i8);
+    } else {
+      // gated attention output, already o * sigmoid(gate) (written by the merge)
+      if (!wait_tagged(c, A.tv_attn, NH * HD, tag_of(c, p - 1), xf)) return false;
+      encode_lin(c, NH * HD, i8);
+    }
+  } else if (sub == 3) {
+    const Gain4 g = load_gain(L.post_norm);
+    if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) return false;
+    norm_into_xf(c, g);
+    encode_lin(c, HID, i8);
+  } else {  // sub == 4
+    if (!wait_tagged(c, A.tv_act, FFN, tag_of(c, p - 1), xf)) return false;
+    encode_lin(c, FFN, i8);
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------- GEMV chunks
+
+// Digits of this lane's 16-byte positions; held in registers only for K = 1024.
+template <int NC, int ND>
+struct Dig {
+  int4 d[ND][NC];
+};
+
+template <int NC, int ND>
+__device__ __forceinline__ void load_dig(const PCtx& c, Dig<NC, ND>& D) {
+  const int8_t* dg = (const int8_t*)(c.sm + OFF_DIG);
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int d = 0; d < ND; ++d)
+#pragma unroll
+    for (int q = 0; q < NC; ++q)
+      D.d[d][q] = *reinterpret_cast<const int4*>(dg + d * KMAX + 16 * (lane + 32 * q));
+}
+
+__device__ __forceinline__ void dp16(int& a, const int4 w, const int4 x) {
+  a = __dp4a(w.x, x.x, a);
+  a = __dp4a(w.y, x.y, a);
+  a = __dp4a(w.z, x.z, a);
+  a = __dp4a(w.w, x.w, a);
+}
+
+// Digit sums of one smem weight row (K = NC*512) in every lane (redux.sync);
+// digits from registers.
+template <int NC, int ND>
+__device__ __forceinline__ void row_dot_r(const int8_t* row, const Dig<NC, ND>& D, int (&acc)[3]) {
+  const int lane = threadIdx.x & 31;
+  acc[0] = acc[1] = acc[2] = 0;
+#pragma unroll
+  for (int q = 0; q < NC; ++q) {
+    const int4 w = *reinterpret_cast<const int4*>(row + 16 * (lane + 32 * q));
+#pragma unroll
+    for (int d = 0; d < ND; ++d) dp16(acc[d], w, D.d[d][q]);
+  }
+#pragma unroll
+  for (int d = 0; d < ND; ++d) acc[d] = redux_add(acc[d]);
+}
+// Same, digits read from the shared digit planes, K = nc*512 at run time.
+template <int ND>
+__device__ __forceinline__ void row_dot_s(const int8_t* row, const int8_t* dg, int nc, int (&acc)[3]) {
+  const int lane = threadIdx.x & 31;
+  acc[0] = acc[1] = acc[2] = 0;
+#pragma unroll 1
+  for (int q = 0; q < nc; ++q) {
+    const int off = 16 * (lane + 32 * q);
+    const int4 w = *reinterpret_cast<const int4*>(row + off);
+#pragma unroll
+    for (int d = 0; d < ND; ++d) dp16(acc[d], w, *reinterpret_cast<const int4*>(dg + d * KMAX + off));
+  }
+#pragma unroll
+  for (int d = 0; d < ND; ++d) acc[d] = redux_add(acc[d]);
+}
+
+// fp32 row (K = HID floats) against xf.
+__device__ __forceinline__ float row_dot_f32(const float* row, const float* xf) {
+  const int lane = threadIdx.x & 31;
+  float a = 0.0f;
+#pragma unroll
+  for (int q = 0; q < HID / 128; ++q) {
+    const float4 w = *reinterpret_cast<const float4*>(row + 4 * (lane + 32 * q));
+    const float4 x = *reinterpret_cast<const float4*>(xf + 4 * (lane + 32 * q));
+    a = fmaf(w.x, x.x, a);
+    a = fmaf(w.y, x.y, a);
+    a = fmaf(w.z, x.z, a);
+    a = fmaf(w.w, x.w, a);
+  }
+  return warp_sum(a);
+}
+
+// Consume every chunk of GEMV phase p (one consumer warp's share).  Per
+// chunk: wait for the bytes; the warp dots its rows (wid, wid + 8); lane q
+// reads row q's scales; the warp releases the slot; lane q runs row q's
+// epilogue.  No synchronisation with the other warps.  false on abort.
+template <bool REG>
+__device__ bool gemv_phase(PCtx& c, int p, int nc_rt) {
+  constexpr int ND = 3;
+  constexpr int NC = 2;                       // K = 1024 for the register-digit variant
+  const int nc = REG ? NC : nc_rt;            // 16-byte lane chunks per row
+  // rows a warp can get from one chunk: 16 KB / (K bytes) / 8 warps
+  constexpr int QMAX = REG ? 2 : 1;
+  const PersistArgs& A = *c.A;
+  Misc* ms = c.ms;
+  const float* hs = (const float*)(c.sm + OFF_HS);
+  const float* xf = (const float*)(c.sm + OFF_XF);
+  const int8_t* dg = (const int8_t*)(c.sm + OFF_DIG);
+  Dig<NC, ND> D;
+  if constexpr (REG) load_dig<NC, ND>(c, D);
+  const double xs = ms->scale;
+  const int nd = ms->ndig;
+  const unsigned tag = tag_of(c, p);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const bool head = (p == PH_HEAD);
+  const int l = head ? 0 : p / 5, sub = head ? -1 : p % 5;
+  const LayerW& L = c.lay[l];
+  const bool want = ms->want_logits != 0;
+  unsigned long long best = 0ull;
+  const int first_i = c.cur;
+  while (c.cur < c.nch && c.ch[c.cur].phase == p) {
+    const int i = c.cur;
+    const Chunk k = c.ch[i];
+    trace_chunk(c, i, 0);
+    if (!wait_full(c, i)) return false;
+    trace_chunk(c, i, 1);
+    if (i == first_i) trace_mark(c, p, 2);
+    const int8_t* buf = (const int8_t*)(c.sm + OFF_RING + (i % NSLOT) * SLOT);
+    const float* tail = (const float*)(buf + SLOTW);
+    const int row0 = (int)k.row0, n = k.nrows, a0 = row0 & ~3;
+    const bool pair = (sub == 3);
+    const bool f32 = (sub == 0 && L.linear && k.seg >= 2);
+    int acc[QMAX][3], acc2[QMAX][3];
+    float fv[QMAX];
+    float sc = 0.f, sc2 = 0.f;
+#pragma unroll
+    for (int q = 0; q < QMAX; ++q) {
+      const int r = wid + q * NCW;
+      fv[q] = 0.f;
+      if (r >= n) continue;
+      if (f32) {
+        fv[q] = row_dot_f32((const float*)buf + r * HID, xf);
+      } else {
+        if constexpr (REG) row_dot_r<NC, ND>(buf + r * (NC * 512), D, acc[q]);
+        else row_dot_s<ND>(buf + r * (nc * 512), dg, nc, acc[q]);
+        if (lane == q) sc = tail[row0 + r - a0];
+        if (pair) {
+          if constexpr (REG) row_dot_r<NC, ND>(buf + (n + r) * (NC * 512), D, acc2[q]);
+          else row_dot_s<ND>(buf + (n + r) * (nc * 512), dg, nc, acc2[q]);
+          if (lane == q) sc2 = tail[32 + row0 + r - a0];
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) release_slot(c, i);
+    c.cur = i + 1;
+    trace_chunk(c, i, 2);
+    // epilogue: lane q handles row q of this warp
+#pragma unroll
+    for (int q = 0; q < QMAX; ++q) {
+      const int r = wid + q * NCW;
+      if (lane != q || r >= n) continue;
+      const int o = row0 + r;
+      if (head) {
+        const float y = finish_row(acc[q][0], acc[q][1], acc[q][2], 3, xs, sc);
+        if (want) A.logits[o] = y;
+        best = umax64(best, am_pack(y, o));
+      } else if (pair) {
+        const float g = finish_row(acc[q][0], acc[q][1], acc[q][2], nd, xs, sc);
+        const float u = finish_row(acc2[q][0], acc2[q][1], acc2[q][2], nd, xs, sc2);
+        st_tv(A.tv_act + o, __fmul_rn(silu_f(g), u), tag);
+      } else if (f32) {
+        st_tv(A.tv_ab + (k.seg == 2 ? 0 : LH) + o, fv[q], tag);
+      } else {
+        const float y = finish_row(acc[q][0], acc[q][1], acc[q][2], nd, xs, sc);
+        if (sub == 0) {
+          unsigned long long* out;
+          if (L.linear) out = (k.seg == 0) ? A.tv_qkv : A.tv_z;
+          else out = (k.seg == 0) ? A.tv_qg : (k.seg == 1 ? A.tv_kvn : A.tv_kvn + KVPROJ);
+          st_tv(out + o, y, tag);
+        } else {
+          // sub 2 / 4: row-parallel projection + residual (h = r + y)
+          st_tv(A.tv_h + o, __fadd_rn(hs[o], y), tag);
+        }
+      }
+    }
+    trace_chunk(c, i, 3);
+  }
+  if (head) {
+    // block argmax, then the last CTA reduces every block's maximum
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) best = umax64(best, __shfl_xor_sync(0xffffffffu, best, o));
+    if (lane == 0) ms->wbest[wid] = best;
+    consumer_sync();
+    if (threadIdx.x == 0) {
+      unsigned long long b = 0ull;
+      for (int w = 0; w < NCW; ++w) b = umax64(b, ms->wbest[w]);
+      A.am_part[blockIdx.x] = b;
+      __threadfence();
+      ms->last = (atomicAdd(A.head_cnt, 1) == (int)gridDim.x - 1);
+    }
+    consumer_sync();
+    if (ms->last) {
+      __threadfence();
+      unsigned long long b = 0ull;
+      for (int q = threadIdx.x; q < (int)gridDim.x; q += PT) b = umax64(b, __ldcg(A.am_part + q));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) b = umax64(b, __shfl_xor_sync(0xffffffffu, b, o));
+      if (lane == 0) ms->wbest[wid] = b;
+      consumer_sync();
+      if (threadIdx.x == 0) {
+        for (int w = 0; w < NCW; ++w) b = umax64(b, ms->wbest[w]);
+        const int step = ms->step;
+        if (step < A.max_steps) A.ids[step] = am_index(b);
+        else atomicCAS(A.err, 0, ERR_CTX);
+        *A.head_cnt = 0;
+        A.io[0] = step + 1;
+        A.dyn->pos = ms->pos + 1;
+        A.dyn->T = ms->T + 1;
+        A.dyn->conv_base = ms->conv_base + 1;
+        A.dyn->seq = ms->seq + 1;
+      }
+    }
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------- DeltaNet item
+
+// (head h, value slice j) of linear layer l: conv+SiLU of the head's q/k and the
+// slice's v channels, gates, l2norm, delta rule on S[h][:, slice], raw o out.
+// golden/model.py:149-178.  Uses the digit region of smem as scratch.
+__device__ bool delta_item(PCtx& c, int p, int item) {
+  const PersistArgs& A = *c.A;
+  Misc* ms = c.ms;
+  const LayerW& L = c.lay[p / 5];
+  const int h = item / NDSLICE, j = item % NDSLICE;
+  const int t = threadIdx.x;
+  const int lin = L.lin_idx;
+  const int base = ms->conv_base;
+  float* qs = (float*)(c.sm + OFF_DIG);
+  float* ks = qs + LK;
+  float* vs = ks + LK;
+  float (*part)[DSLICE + 1] = reinterpret_cast<float (*)[DSLICE + 1]>(vs + 32);
+  float* cs = A.conv + (size_t)lin * CONVD * CONVK;
+  float* Sh = A.rec + ((size_t)lin * LH + h) * LK * LV;
+  const int v0 = j * DSLICE;
+  const int vi = t & 15, kg = t >> 4;
+  // prefetch state slice, conv history and taps (previous launches wrote them)
+  float sv[8];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) sv[kk] = Sh[(size_t)(kg * 8 + kk) * LV + v0 + vi];
+  const int ch = (t < LK) ? (h * LK + t) : (KDIM + h * LK + (t - LK));
+  const float* st = cs + (size_t)ch * CONVK;
+  const float s1 = st[(base + 1) & 3], s2 = st[(base + 2) & 3], s3 = st[(base + 3) & 3];
+  const float4 w4 = *reinterpret_cast<const float4*>(L.conv_w + (size_t)ch * CONVK);
+  const int vch = 2 * KDIM + h * LV + v0 + (t & 15);
+  float vs1 = 0.f, vs2 = 0.f, vs3 = 0.f;
+  float4 vw4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (t < DSLICE) {
+    const float* vst = cs + (size_t)vch * CONVK;
+    vs1 = vst[(base + 1) & 3]; vs2 = vst[(base + 2) & 3]; vs3 = vst[(base + 3) & 3];
+    vw4 = *reinterpret_cast<const float4*>(L.conv_w + (size_t)vch * CONVK);
+  }
+  const float alog = __ldg(L.A_log + h), dtb = __ldg(L.dt_bias + h);
+  // wait for this token's projections: every thread its q/k channel; the
+  // first 16 threads their v channel; thread 16 the b/a gate inputs.  All of a
+  // thread's polls are issued before any is checked.
+  const unsigned tin = tag_of(c, p - 1);
+  const unsigned long long t0 = gtime();
+  float nv = 0.f, nvv = 0.f, bb = 0.f, aa = 0.f;
+  bool have = false, havev = (t >= DSLICE), haveb = (t != DSLICE);
+  int it = 0;
+  for (;;) {
+    unsigned long long w = 0, wv = 0, wb = 0, wa = 0;
+    if (!have) w = ld_tv(A.tv_qkv + ch);
+    if (!havev) wv = ld_tv(A.tv_qkv + vch);
+    if (!haveb) { wb = ld_tv(A.tv_ab + h); wa = ld_tv(A.tv_ab + LH + h); }
+    if (!have && tag_ok(w, tin)) { nv = tv_val(w); have = true; }
+    if (!havev && tag_ok(wv, tin)) { nvv = tv_val(wv); havev = true; }
+    if (!haveb && tag_ok(wb, tin) && tag_ok(wa, tin)) { bb = tv_val(wb); aa = tv_val(wa); haveb = true; }
+    if (consumer_and(have && havev && haveb)) break;
+    if (((++it) & 15) == 0) {
+      int bad = 0;
+      if (t == 0) {
+        if (aborted(c)) bad = 1;
+        else if (gtime() - t0 > WAIT_NS) { raise_abort(c); bad = 1; }
+      }
+      if (!consumer_and(!bad)) return false;
+    }
+  }
+  auto conv = [](float a1, float a2, float a3, float nw, float4 w) {
+    float acc = __fmul_rn(a1, w.x);
+    acc = __fadd_rn(acc, __fmul_rn(a2, w.y));
+    acc = __fadd_rn(acc, __fmul_rn(a3, w.z));
+    acc = __fadd_rn(acc, __fmul_rn(nw, w.w));
+    return silu_f(acc);
+  };
+  const float x = conv(s1, s2, s3, nv, w4);
+  if (j == 0) cs[(size_t)ch * CONVK + (base & 3)] = nv;   // dead oldest column <- newest
+  if (t < DSLICE) {
+    vs[t] = conv(vs1, vs2, vs3, nvv, vw4);
+    cs[(size_t)vch * CONVK + (base & 3)] = nvv;
+  }
+  if (t == DSLICE) {
+    ms->gate_beta = sigmoid_f(bb);
+    ms->gate_g = __fmul_rn(-expf(alog), softplus_f(__fadd_rn(aa, dtb)));
+  }
+  float ss = warp_sum(x * x);
+  if ((t & 31) == 0) ms->red[t >> 5] = ss;
+  consumer_sync();
+  {
+    const int g0 = (t < LK) ? 0 : 4;
+    const float tot = ((ms->red[g0] + ms->red[g0 + 1]) + ms->red[g0 + 2]) + ms->red[g0 + 3];
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(tot, EPS)));
+    if (t < LK) qs[t] = __fmul_rn(__fmul_rn(x, inv), 0.08838834764831845f);
+    else ks[t - LK] = __fmul_rn(x, inv);
+  }
+  consumer_sync();
+  // delta rule on the prefetched slice (same arithmetic as delta_slice in decode.cu)
+  const float gexp = expf(ms->gate_g);
+  float pkv = 0.0f;
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    sv[kk] = __fmul_rn(sv[kk], gexp);
+    pkv = fmaf(sv[kk], ks[kg * 8 + kk], pkv);
+  }
+  part[kg][vi] = pkv;
+  consumer_sync();
+  float kvv = 0.0f;
+#pragma unroll
+  for (int g = 0; g < 16; ++g) kvv += part[g][vi];
+  const float delta = __fmul_rn(__fsub_rn(vs[vi], kvv), ms->gate_beta);
+  consumer_sync();
+  float po = 0.0f;
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const int k = kg * 8 + kk;
+    const float s2v = __fadd_rn(sv[kk], __fmul_rn(ks[k], delta));
+    Sh[(size_t)k * LV + v0 + vi] = s2v;
+    po = fmaf(s2v, qs[k], po);
+  }
+  part[kg][vi] = po;
+  consumer_sync();
+  if (t < DSLICE) {
+    float o = 0.0f;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) o += part[g][t];
+    st_tv(A.tv_o + h * LV + v0 + t, o, tag_of(c, p));
+  }
+  consumer_sync();
+  return true;
+}
+
+// ---------------------------------------------------------------- attention item
+
+// QK rmsnorm (1+w) + partial RoPE of one 256-vector held by one warp as
+// elements lane + 32 q; gains w[] and this lane's cos/sin preloaded.
+__device__ __forceinline__ void warp_norm_rope_v(const float* v_in, const float (&w)[8], float co,
+                                                 float si, float* dst) {
+  const int lane = threadIdx.x & 31;
+  float v[8];
+  float ss = 0.0f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) { v[q] = v_in[lane + 32 * q]; ss = fmaf(v[q], v[q], ss); }
+  ss = warp_sum(ss);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)HD), EPS)));
+#pragma unroll
+  for (int q = 0; q < 8; ++q) v[q] = __fmul_rn(__fmul_rn(v[q], inv), __fadd_rn(1.0f, w[q]));
+  const float a = v[0], b = v[1];
+  v[0] = __fadd_rn(__fmul_rn(a, co), __fmul_rn(-b, si));
+  v[1] = __fadd_rn(__fmul_rn(b, co), __fmul_rn(a, si));
+#pragma unroll
+  for (int q = 0; q < 8; ++q) dst[lane + 32 * q] = v[q];
+}
+
+// Split-KV item (kv group g, chunk cc) of attention layer l; the last item of a
+// group merges the partials and writes o * sigmoid(gate) (golden/model.py:194-229).
+__device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
+  const PersistArgs& A = *c.A;
+  Misc* ms = c.ms;
+  const LayerW& L = c.lay[p / 5];
+  const int T = ms->T, pos = ms->pos, Tn = T + 1;
+  const int fi = L.full_idx;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int t0 = cc * cl, t1 = min(Tn, t0 + cl), n = t1 - t0;
+  float* qn = (float*)(c.sm + OFF_DIG);    // [4][256] normed + roped queries
+  float* kn = qn + 4 * HD;                  // [256] new key
+  float* vn = kn + HD;                      // [256] new value
+  float* raw = vn + HD;                     // [6][256] projections as read (q x4, k, v)
+  float* sc = raw;                          // [4][ATT_MAXLEN] scores, after raw is consumed
+  const unsigned tin = tag_of(c, p - 1);
+  // prefetch this warp's norm gains and RoPE cos/sin before waiting
+  float nw[8];
+  const float* wsrc = (wid < 4) ? L.qn_w : L.kn_w;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) nw[q] = __ldg(wsrc + lane + 32 * q);
+  const float* rope = A.rope + (size_t)pos * ROT;
+  const float rco = __ldg(rope + lane), rsi = __ldg(rope + 32 + lane);
+  // wait for q (4 heads), k, v of this group (tagged, from IN); element e of
+  // [0, 1536): e < 1024 -> q of head 4g + e/256; then k; then v
+  {
+    const unsigned long long tw = gtime();
+    constexpr int NP = 6 * HD / 2 / PT;   // 3 pairs per thread
+    unsigned pend = (1u << NP) - 1;
+    int it = 0;
+    for (;;) {
+      unsigned long long a[NP], b[NP];
+#pragma unroll
+      for (int jj = 0; jj < NP; ++jj) {
+        if (!(pend >> jj & 1)) continue;
+        const int e = 2 * ((int)threadIdx.x + PT * jj);
+        const unsigned long long* src;
+        if (e < 4 * HD) src = A.tv_qg + (size_t)(4 * g + e / HD) * 2 * HD + (e % HD);
+        else if (e < 5 * HD) src = A.tv_kvn + g * HD + (e - 4 * HD);
+        else src = A.tv_kvn + KVPROJ + g * HD + (e - 5 * HD);
+        ld_tv2(src, a[jj], b[jj]);
+      }
+#pragma unroll
+      for (int jj = 0; jj < NP; ++jj) {
+        if ((pend >> jj & 1) && tag_ok(a[jj], tin) && tag_ok(b[jj], tin)) {
+          const int e = 2 * ((int)threadIdx.x + PT * jj);
+          raw[e] = tv_val(a[jj]);
+          raw[e + 1] = tv_val(b[jj]);
+          pend &= ~(1u << jj);
+        }
+      }
+      if (consumer_and(pend == 0)) break;
+      if (((++it) & 15) == 0) {
+        int bad = 0;
+        if (threadIdx.x == 0) {
+          if (aborted(c)) bad = 1;
+          else if (gtime() - tw > WAIT_NS) { raise_abort(c); bad = 1; }
+        }
+        if (!consumer_and(!bad)) return false;
+      }
+    }
+  }
+  if (wid < 4) warp_norm_rope_v(raw + wid * HD, nw, rco, rsi, qn + wid * HD);
+  else if (wid == 4) warp_norm_rope_v(raw + 4 * HD, nw, rco, rsi, kn);
+  else if (wid == 5) for (int d = lane; d < HD; d += 32) vn[d] = raw[5 * HD + d];
+  consumer_sync();
+  float* kc = A.kcache + (size_t)fi * A.max_ctx * KVPROJ;
+  float* vc = A.vcache + (size_t)fi * A.max_ctx * KVPROJ;
+  if (cc == 0) {   // roped K and raw V of this token into slot T (golden/model.py:216-217)
+    kc[(size_t)T * KVPROJ + g * HD + threadIdx.x] = kn[threadIdx.x];
+    vc[(size_t)T * KVPROJ + g * HD + threadIdx.x] = vn[threadIdx.x];
+  }
+  for (int i = wid; i < n; i += NCW) {
+    const int tt = t0 + i;
+    float4 k0, k1;
+    if (tt < T) {
+      const float* kp = kc + (size_t)tt * KVPROJ + g * HD;
+      k0 = *reinterpret_cast<const float4*>(kp + 4 * lane);
+      k1 = *reinterpret_cast<const float4*>(kp + 128 + 4 * lane);
+    } else {
+      k0 = *reinterpret_cast<const float4*>(kn + 4 * lane);
+      k1 = *reinterpret_cast<const float4*>(kn + 128 + 4 * lane);
+    }
+#pragma unroll
+    for (int hq = 0; hq < 4; ++hq) {
+      const float4 q0 = *reinterpret_cast<const float4*>(qn + hq * HD + 4 * lane);
+      const float4 q1 = *reinterpret_cast<const float4*>(qn + hq * HD + 128 + 4 * lane);
+      float d = q0.x * k0.x + q0.y * k0.y + q0.z * k0.z + q0.w * k0.w;
+      d += q1.x * k1.x + q1.y * k1.y + q1.z * k1.z + q1.w * k1.w;
+      d = warp_sum(d);
+      if (lane == 0) sc[hq * ATT_MAXLEN + i] = d * 0.0625f;   // 256^-0.5, exact
+    }
+  }
+  consumer_sync();
+  float* mh = ms->red;       // [4] maxima, [4..8) sums
+  if (wid < 4) {
+    float m = -INFINITY;
+    for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[wid * ATT_MAXLEN + i]);
+    m = warp_max(m);
+    float lsum = 0.0f;
+    for (int i = lane; i < n; i += 32) {
+      const float pe = expf(sc[wid * ATT_MAXLEN + i] - m);
+      sc[wid * ATT_MAXLEN + i] = pe;
+      lsum += pe;
+    }
+    lsum = warp_sum(lsum);
+    if (lane == 0) { mh[wid] = m; mh[4 + wid] = lsum; }
+  }
+  consumer_sync();
+  const int d = threadIdx.x;
+  float o[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int i = 0; i < n; ++i) {
+    const int tt = t0 + i;
+    const float v = (tt < T) ? vc[(size_t)tt * KVPROJ + g * HD + d] : vn[d];
+#pragma unroll
+    for (int hq = 0; hq < 4; ++hq) o[hq] = fmaf(sc[hq * ATT_MAXLEN + i], v, o[hq]);
+  }
+  float* part = A.att_part + ((size_t)(g * ATT_MAXCH + cc) * 4) * (2 + HD);
+#pragma unroll
+  for (int hq = 0; hq < 4; ++hq) {
+    part[hq * (2 + HD) + 2 + d] = o[hq];
+    if (d == 0) { part[hq * (2 + HD)] = mh[hq]; part[hq * (2 + HD) + 1] = mh[4 + hq]; }
+  }
+  __threadfence();
+  consumer_sync();
+  int* cnt = A.att_cnt + (L.full_idx * NKV + g);
+  if (threadIdx.x == 0) ms->last = (atomicAdd(cnt, 1) == nch - 1);
+  consumer_sync();
+  if (!ms->last) return true;
+  __threadfence();
+  if (threadIdx.x == 0) *cnt = 0;
+  // gates of the 4 heads (tagged, from IN): all four polls issued together
+  const unsigned long long tg0 = gtime();
+  float gv[4];
+  {
+    unsigned pend = 0xf;
+    int it = 0;
+    unsigned long long w[4];
+    while (pend) {
+#pragma unroll
+      for (int hq = 0; hq < 4; ++hq)
+        if (pend >> hq & 1) w[hq] = ld_tv(A.tv_qg + (size_t)(4 * g + hq) * 2 * HD + HD + d);
+#pragma unroll
+      for (int hq = 0; hq < 4; ++hq)
+        if ((pend >> hq & 1) && tag_ok(w[hq], tin)) { gv[hq] = tv_val(w[hq]); pend &= ~(1u << hq); }
+      if (pend && ((++it) & 63) == 0) {
+        if (aborted(c)) break;
+        if (gtime() - tg0 > WAIT_NS) { raise_abort(c); break; }
+      }
+    }
+  }
+  const unsigned tout = tag_of(c, p);
+  for (int hq = 0; hq < 4; ++hq) {
+    const float* pb = A.att_part + ((size_t)(g * ATT_MAXCH) * 4 + hq) * (2 + HD);
+    const size_t stride = 4 * (2 + HD);
+    float M = -INFINITY;
+    for (int q = 0; q < nch; ++q) M = fmaxf(M, __ldcg(pb + q * stride));
+    float Ls = 0.0f, O = 0.0f;
+    for (int q = 0; q < nch; ++q) {
+      const float f = expf(__ldcg(pb + q * stride) - M);
+      Ls = fmaf(__ldcg(pb + q * stride + 1), f, Ls);
+      O = fmaf(__ldcg(pb + q * stride + 2 + d), f, O);
+    }
+    st_tv(A.tv_attn + (4 * g + hq) * HD + d, __fmul_rn(__fdiv_rn(O, Ls), sigmoid_f(gv[hq])), tout);
+  }
+  consumer_sync();
+  return true;
+}
+
+// ---------------------------------------------------------------- the kernel
+
+__global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* sm = smem_raw;
+  PCtx c;
+  c.A = &A;
+  c.sm = sm;
+  c.ms = (Misc*)(sm + OFF_MISC);
+  c.lay = (LayerW*)(sm + OFF_LAY);
+  Chunk* chs = (Chunk*)(sm + OFF_CH);
+  c.ch = chs;
+  c.nch = A.nchunks[blockIdx.x];
+  c.cur = 0;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(c.pol));
+  Misc* ms = c.ms;
+  // stage the layer table, this CTA's chunk list and the step scalars
+  for (int i = threadIdx.x; i < (int)(sizeof(LayerW) * NLAYER / 4); i += NTHREADS)
+    ((int*)c.lay)[i] = ((const int*)A.layers)[i];
+  for (int i = threadIdx.x; i < c.nch; i += NTHREADS) chs[i] = A.chunks[(size_t)blockIdx.x * MAXCH + i];
+  if (threadIdx.x == 0) {
+    ms->abort = 0;
+    ms->pos = A.dyn->pos;
+    ms->T = A.dyn->T;
+    ms->conv_base = A.dyn->conv_base;
+    ms->act_int8 = A.dyn->act_int8;
+    ms->want_logits = A.dyn->want_logits;
+    ms->seq = A.dyn->seq;
+    const int step = A.io[0], np = A.io[1];
+    ms->step = step;
+    int tok = (step < np) ? A.io[2 + step] : A.ids[step > 0 ? step - 1 : 0];
+    if (tok < 0 || tok >= VOCAB) { atomicCAS(A.err, 0, ERR_TOKEN); tok = 0; }
+    ms->tok = tok;
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(full_bar(c, s), 1);
+      ms->slot_cnt[s] = 0;
+      ms->slot_last[s] = -1;
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (ms->T >= A.max_ctx || ms->pos >= A.max_rope) {
+    if (threadIdx.x == 0) atomicCAS(A.err, 0, ERR_CTX);
+    return;
+  }
+  if (threadIdx.x == 0)
+    for (int i = 0; i < NSLOT && i < c.nch; ++i) {
+      issue_chunk(c, i);
+      ms->slot_last[i] = i;
+    }
+  {
+    bool ok = true;
+    for (int p = 0; p < NPHASE && ok; ++p) {
+      if (*(volatile int*)&ms->abort) { ok = false; break; }
+      const int sub = p % 5;
+      trace_mark(c, p, 0);
+      if (p != PH_HEAD && sub == 1) {
+        const LayerW& L = c.lay[p / 5];
+        if (L.linear) {
+          if ((int)blockIdx.x < LH * NDSLICE) ok = delta_item(c, p, blockIdx.x);
+        } else {
+          const int Tn = ms->T + 1;
+          int nch = (Tn + ATT_MINLEN - 1) / ATT_MINLEN;
+          nch = nch < 1 ? 1 : (nch > ATT_MAXCH ? ATT_MAXCH : nch);
+          const int cl = (Tn + nch - 1) / nch;
+          if (cl > ATT_MAXLEN) { if (threadIdx.x == 0) raise_abort(c); ok = false; break; }
+          for (int it = blockIdx.x; it < NKV * nch && ok; it += gridDim.x)
+            ok = attn_item(c, p, it % NKV, it / NKV, nch, cl);
+        }
+        trace_mark(c, p, 3);
+        continue;
+      }
+      if (!prologue(c, p)) { ok = false; break; }
+      trace_mark(c, p, 1);
+      const int K = (p == PH_HEAD) ? HID : (sub == 2 ? VDIM : (sub == 4 ? FFN : HID));
+      ok = (K == HID) ? gemv_phase<true>(c, p, 2) : gemv_phase<false>(c, p, K / 512);
+      // the warps leave a GEMV phase independently; line them up again
+      consumer_sync();
+      trace_mark(c, p, 3);
+    }
+    if (!ok && threadIdx.x == 0) *(volatile int*)&ms->abort = 1;
+  }
+  // drain: every bulk copy that was issued must land before the CTA exits
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned long long t0 = gtime();
+    for (int s = 0; s < NSLOT; ++s) {
+      const int last = ms->slot_last[s];
+      if (last < 0) continue;
+      const unsigned bar = full_bar(c, s);
+      while (!mbar_try(bar, (unsigned)((last / NSLOT) & 1)))
+        if (gtime() - t0 > WAIT_NS) break;
+    }
+  }
+  __syncthreads();
+}
+
+static_assert(OFF_DIG + (4 * HD + 2 * HD + 4 * ATT_MAXLEN) * 4 <= OFF_HS,
+              "attention scratch must fit in the digit/xf region");
+
+// ---------------------------------------------------------------- host side
+
+int persist_smem_bytes() { return SMEM_BYTES; }
+int persist_num_phases() { return NPHASE; }
+int persist_max_chunks() { return MAXCH; }
+
+// Build the per-CTA chunk lists: for every GEMV phase, its rows are split
+// into G contiguous byte-balanced ranges, each cut into <= SLOT-byte chunks
+// that never straddle a segment.
+bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks, std::vector<int>& counts,
+                    std::string& err) {
+  (void)M;
+  chunks.assign((size_t)G * MAXCH, Chunk{});
+  counts.assign(G, 0);
+  struct Seg { int rows; int rowbytes; int unit_rows; };
+  for (int p = 0; p < NPHASE; ++p) {
+    std::vector<Seg> segs;
+    const int sub = p % 5;
+    if (p == PH_HEAD) segs = {{VOCAB, HID, 1}};
+    else if (sub == 1) continue;
+    else if (sub == 0) {
+      const bool linear = (p / 5) % 4 != 3;
+      if (linear) segs = {{CONVD, HID, 1}, {VDIM, HID, 1}, {LH, HID * 4, 1}, {LH, HID * 4, 1}};
+      else segs = {{QPROJ, HID, 1}, {KVPROJ, HID, 1}, {KVPROJ, HID, 1}};
+    } else if (sub == 2) segs = {{HID, VDIM, 1}};
+    else if (sub == 3) segs = {{FFN, 2 * HID, 1}};   // a unit = one (gate, up) row pair
+    else segs = {{HID, FFN, 1}};
+    long long total = 0;
+    for (auto& s : segs) total += (long long)s.rows * s.rowbytes;
+    // walk the rows, assigning each to the CTA whose byte window holds its start
+    long long off = 0;
+    for (int si = 0; si < (int)segs.size(); ++si) {
+      const Seg& s = segs[si];
+      const int per_chunk = SLOTW / s.rowbytes;
+      int r = 0;
+      while (r < s.rows) {
+        const int cta = (int)std::min<long long>(G - 1, (off * G) / total);
+        // rows of this segment that start inside cta's window
+        const long long win_end = ((long long)(cta + 1) * total + G - 1) / G;
+        int n = 0;
+        while (r + n < s.rows && n < per_chunk && off + (long long)n * s.rowbytes < win_end) ++n;
+        if (n == 0) n = 1;
+        int& cnt = counts[cta];
+        if (cnt >= MAXCH) { err = "chunk list overflow"; return false; }
+        Chunk& k = chunks[(size_t)cta * MAXCH + cnt++];
+        k.phase = (unsigned short)p;
+        k.seg = (unsigned char)si;
+        k.nrows = (unsigned char)n;
+        k.row0 = (unsigned)r;
+        r += n;
+        off += (long long)n * s.rowbytes;
+      }
+    }
+  }
+  // the chunk order inside a CTA must follow the phase order (it does: phases are walked in order)
+  return true;
+}
+
+cudaError_t launch_persistent(const PersistArgs& args, int G, cudaStream_t st) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(k_decode_persistent,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  void* kargs[] = {(void*)&args};
+  return cudaLaunchCooperativeKernel((const void*)k_decode_persistent, dim3(G), dim3(NTHREADS), kargs,
+                                     SMEM_BYTES, st);
+}
+
+int persist_max_blocks_per_sm() {
+  int n = 0;
+  cudaFuncSetAttribute(k_decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_decode_persistent, NTHREADS, SMEM_BYTES);
+  return n;
+}
+
+}  // namespace qb

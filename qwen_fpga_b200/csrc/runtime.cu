@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <map>
@@ -19,6 +20,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "gemv.cuh"
+#include "persist.cuh"
 
 using namespace qb;
 
@@ -191,7 +193,12 @@ struct qwen_ctx {
   int* h_ids = nullptr;       // pinned
   int* h_err = nullptr;       // pinned
   int pos = 0, T = 0, conv_base = 0;
+  unsigned seq = 1;           // launch sequence number (tag base of the persistent kernel)
   int act_int8 = 0;
+  int engine = 1;             // 1 = persistent weight-streaming kernel, 0 = graph of phase kernels
+  PersistArgs P{};
+  unsigned long long* tv_base = nullptr;
+  size_t tv_words = 0;
   cudaGraphExec_t graph = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
 };
@@ -355,6 +362,27 @@ void fill_dyn(qwen_ctx* c, int want_logits) {
   d->conv_base = c->conv_base;
   d->act_int8 = c->act_int8;
   d->want_logits = want_logits;
+  d->seq = (int)c->seq;
+}
+
+// Keep launch tags unique: before the sequence number would wrap, clear the
+// tagged activation words and restart it.
+int ensure_seq_room(qwen_ctx* c, int launches) {
+  if (c->seq + (unsigned)launches < (1u << 24)) return QWEN_OK;
+  QCUDA(c, cudaMemsetAsync(c->tv_base, 0, c->tv_words * 8, c->st));
+  c->seq = 1;
+  return QWEN_OK;
+}
+
+// One decode step on the context stream with the selected engine.
+int launch_step(qwen_ctx* c) {
+  if (c->engine == 1) {
+    cudaError_t e = launch_persistent(c->P, c->sm_count, c->st);
+    if (e != cudaSuccess) return fail(c, QWEN_ERR_CUDA, "persistent launch: %s", cudaGetErrorString(e));
+  } else {
+    QCUDA(c, cudaGraphLaunch(c->graph, c->st));
+  }
+  return QWEN_OK;
 }
 
 // Inspect the device error word (already copied into h_err together with the
@@ -363,6 +391,9 @@ int check_device(qwen_ctx* c) {
   if (*c->h_err != 0) {
     const int code = *c->h_err;
     QCUDA(c, cudaMemset(c->S.err, 0, sizeof(int)));
+    QCUDA(c, cudaMemset(c->P.abort_flag, 0, sizeof(int)));
+    QCUDA(c, cudaMemset(c->P.head_cnt, 0, sizeof(int)));
+    QCUDA(c, cudaMemset(c->P.att_cnt, 0, NFULL * NKV * sizeof(int)));
     if (code == ERR_TOKEN) return fail(c, QWEN_ERR_ARG, "token id outside [0, %d)", VOCAB);
     if (code == ERR_CTX) return fail(c, QWEN_ERR_STATE, "context or step capacity exceeded on device");
     return fail(c, QWEN_ERR_DEVICE, "device reported error %d", code);
@@ -493,6 +524,55 @@ int qwen_create(const char* blob_path, const char* index_path, int n_gpus, const
   if (head_grid_size(c->sm_count) > AM_PARTS) { fail(c, QWEN_ERR_STATE, "too many SMs"); return bail(QWEN_ERR_STATE); }
   if ((rc = build_graph(c))) return bail(rc);
   {
+    // persistent engine: tagged activation words, counters, per-CTA schedule
+    const size_t words = HID + CONVD + VDIM + 2 * LH + VDIM + QPROJ + 2 * KVPROJ + NH * HD + FFN;
+    if ((rc = dalloc(c, &c->tv_base, words * 8))) return bail(rc);
+    c->tv_words = words;
+    PersistArgs& P = c->P;
+    unsigned long long* w = c->tv_base;
+    P.tv_h = w; w += HID;
+    P.tv_qkv = w; w += CONVD;
+    P.tv_z = w; w += VDIM;
+    P.tv_ab = w; w += 2 * LH;
+    P.tv_o = w; w += VDIM;
+    P.tv_qg = w; w += QPROJ;
+    P.tv_kvn = w; w += 2 * KVPROJ;
+    P.tv_attn = w; w += NH * HD;
+    P.tv_act = w; w += FFN;
+    std::vector<Chunk> chunks;
+    std::vector<int> counts;
+    std::string serr;
+    if (!build_schedule(c->Mh, c->sm_count, chunks, counts, serr)) {
+      fail(c, QWEN_ERR_STATE, "schedule: %s", serr.c_str());
+      return bail(QWEN_ERR_STATE);
+    }
+    Chunk* dch = nullptr;
+    int* dcnt = nullptr;
+    if ((rc = dalloc(c, &dch, chunks.size() * sizeof(Chunk))) ||
+        (rc = dalloc(c, &dcnt, counts.size() * sizeof(int))) ||
+        (rc = dalloc(c, &P.att_cnt, NFULL * NKV * sizeof(int))) ||
+        (rc = dalloc(c, &P.head_cnt, 64)) || (rc = dalloc(c, &P.abort_flag, 64)))
+      return bail(rc);
+    cudaMemcpy(dch, chunks.data(), chunks.size() * sizeof(Chunk), cudaMemcpyHostToDevice);
+    cudaMemcpy(dcnt, counts.data(), counts.size() * sizeof(int), cudaMemcpyHostToDevice);
+    P.chunks = dch;
+    P.nchunks = dcnt;
+    P.layers = &c->Md->L[0];
+    P.emb_q = c->Mh.emb_q;
+    P.emb_s = c->Mh.emb_s;
+    P.final_norm = c->Mh.final_norm;
+    P.conv = S.conv; P.rec = S.rec; P.kcache = S.kcache; P.vcache = S.vcache;
+    P.att_part = S.att_part;
+    P.am_part = S.am_part;
+    P.rope = S.rope;
+    P.logits = S.logits;
+    P.io = S.io; P.ids = S.ids; P.err = S.err; P.dyn = S.dyn;
+    P.max_ctx = S.max_ctx; P.max_rope = S.max_rope; P.max_steps = S.max_steps;
+    const char* env = getenv("QWEN_B200_ENGINE");
+    c->engine = (env && env[0] == '0') ? 0 : 1;
+    if (c->engine == 1 && persist_max_blocks_per_sm() < 1) c->engine = 0;
+  }
+  {
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) { fail(c, QWEN_ERR_CUDA, "create: %s", cudaGetErrorString(e)); return bail(QWEN_ERR_CUDA); }
   }
@@ -515,6 +595,46 @@ int qwen_set_act_int8(qwen_ctx* c, int on) {
   int rc;
   if ((rc = check_ctx(c))) return rc;
   c->act_int8 = on ? 1 : 0;
+  return QWEN_OK;
+}
+
+int qwen_set_engine(qwen_ctx* c, int engine) {
+  int rc;
+  if ((rc = check_ctx(c))) return rc;
+  if (engine != 0 && engine != 1) return fail(c, QWEN_ERR_ARG, "engine must be 0 or 1");
+  if (engine == 1 && persist_max_blocks_per_sm() < 1)
+    return fail(c, QWEN_ERR_STATE, "persistent kernel does not fit on this device");
+  c->engine = engine;
+  return QWEN_OK;
+}
+
+int qwen_get_engine(qwen_ctx* c) { return c ? c->engine : -1; }
+
+int qwen_trace_enable(qwen_ctx* c, int on) {
+  int rc;
+  if ((rc = check_ctx(c))) return rc;
+  if (on && !c->P.trace) {
+    const size_t words = (size_t)c->sm_count * persist_num_phases() * TRACE_STAMPS +
+                         (size_t)persist_max_chunks() * 4;
+    if ((rc = dalloc(c, &c->P.trace, words * 8))) return rc;
+  } else if (!on) {
+    c->P.trace = nullptr;   // the buffer stays allocated until qwen_destroy
+  }
+  return QWEN_OK;
+}
+
+int qwen_trace_read(qwen_ctx* c, unsigned long long* out, int max_words, int* n_ctas,
+                    int* n_phases) {
+  int rc;
+  if ((rc = check_ctx(c))) return rc;
+  if (!c->P.trace) return fail(c, QWEN_ERR_STATE, "tracing is off");
+  const size_t words = (size_t)c->sm_count * persist_num_phases() * TRACE_STAMPS +
+                       (size_t)persist_max_chunks() * 4;
+  if (!out || (size_t)max_words < words) return fail(c, QWEN_ERR_ARG, "need %zu words", words);
+  QCUDA(c, cudaStreamSynchronize(c->st));
+  QCUDA(c, cudaMemcpy(out, c->P.trace, words * 8, cudaMemcpyDeviceToHost));
+  if (n_ctas) *n_ctas = c->sm_count;
+  if (n_phases) *n_phases = persist_num_phases();
   return QWEN_OK;
 }
 
@@ -577,17 +697,19 @@ int qwen_decode_step(qwen_ctx* c, const int* tok, int batch, float* logits_out, 
   if (tok[0] < 0 || tok[0] >= VOCAB) return fail(c, QWEN_ERR_ARG, "token %d outside [0, %d)", tok[0], VOCAB);
   if (c->T + 1 > c->max_ctx || c->pos + 1 >= c->max_rope)
     return fail(c, QWEN_ERR_STATE, "context full (T=%d, max_ctx=%d)", c->T, c->max_ctx);
+  if ((rc = ensure_seq_room(c, 1))) return rc;
   fill_dyn(c, logits_out ? 1 : 0);
   int* io = ctl_io(c);
   io[0] = 0;
   io[1] = 1;
   io[2] = tok[0];
   if ((rc = push_ctl(c, 1))) return rc;
-  QCUDA(c, cudaGraphLaunch(c->graph, c->st));
+  if ((rc = launch_step(c))) return rc;
   QCUDA(c, cudaMemcpyAsync(c->h_err, c->S.err, 16 + sizeof(int), cudaMemcpyDeviceToHost, c->st));
   if (logits_out)
     QCUDA(c, cudaMemcpyAsync(logits_out, c->S.logits, (size_t)VOCAB * 4, cudaMemcpyDefault, c->st));
   QCUDA(c, cudaStreamSynchronize(c->st));
+  c->seq += 1;
   if ((rc = check_device(c))) return rc;
   c->pos += 1;
   c->T += 1;
@@ -608,6 +730,7 @@ int qwen_generate(qwen_ctx* c, const int* prompt, int n_prompt, int n_new, int* 
     return fail(c, QWEN_ERR_STATE, "context would overflow (T=%d + %d > %d)", c->T, total, c->max_ctx);
   for (int i = 0; i < n_prompt; ++i)
     if (prompt[i] < 0 || prompt[i] >= VOCAB) return fail(c, QWEN_ERR_ARG, "prompt token %d out of range", i);
+  if ((rc = ensure_seq_room(c, total))) return rc;
   fill_dyn(c, 0);
   int* io = ctl_io(c);
   io[0] = 0;
@@ -616,11 +739,12 @@ int qwen_generate(qwen_ctx* c, const int* prompt, int n_prompt, int n_new, int* 
   if ((rc = push_ctl(c, n_prompt))) return rc;
   for (int s = 0; s < total; ++s) {
     if (s == n_prompt) QCUDA(c, cudaEventRecord(c->ev0, c->st));
-    QCUDA(c, cudaGraphLaunch(c->graph, c->st));
+    if ((rc = launch_step(c))) return rc;
   }
   QCUDA(c, cudaEventRecord(c->ev1, c->st));
   QCUDA(c, cudaMemcpyAsync(c->h_err, c->S.err, 16 + sizeof(int) * total, cudaMemcpyDeviceToHost, c->st));
   QCUDA(c, cudaStreamSynchronize(c->st));
+  c->seq += total;
   if ((rc = check_device(c))) return rc;
   c->pos += total;
   c->T += total;

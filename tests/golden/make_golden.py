@@ -184,7 +184,29 @@ def main():
         out["argmax"] = np.array(argmax, np.int64)
         out["generated"] = np.array(gen, np.int64)
         out["pert_same_tokens"] = np.bool_(runs["pert"][1] == gen)
+        # teacher-forced self-agreement of the golden under small weight noise:
+        # feed the reference token stream to a perturbed golden and count equal argmaxes
+        feed = prompt.tolist() + gen
+        spread = []
+        for pert in (1e-7, 1e-6, 3e-6):
+            for seed in (1, 2, 3):
+                Wp = dict(W)
+                for name in ("layers.0.linear_attn.in_proj_qkv.weight",
+                             "layers.5.mlp.down_proj.weight", "layers.11.self_attn.o_proj.weight"):
+                    w0 = W[name]
+                    noise = np.random.default_rng(seed).standard_normal(w0.shape).astype(np.float32)
+                    Wp[name] = w0 * (1 + np.float32(pert) * noise)
+                G.ACT_INT8 = True
+                st = G.DecodeState.new(cfg)
+                agree = 0
+                for i, t in enumerate(feed):
+                    lg = G.decode_step(Wp, cfg, int(t), st)
+                    agree += int(int(np.argmax(lg)) == argmax[i])
+                spread.append(agree)
+        G.ACT_INT8 = False
+        out["self_agreement"] = np.array(spread, np.int64)
         np.savez_compressed(os.path.join(HERE, "config0_w8a8.npz"), **out)
+        print("config0w8 self-agreement spread", spread)
         print(f"config0w8: {time.time() - t0:.1f}s sens="
               f"{[float(out[f'step{i}_sens']) for i in (0, 15, 79)]} same={runs['pert'][1] == gen}")
 
