@@ -37,7 +37,7 @@
 
 namespace qb {
 
-constexpr int NCW = 8;                  // warps per CTA
+constexpr int NCW = 16;                 // warps per CTA
 constexpr int PT = NCW * 32;            // threads per CTA
 constexpr int NTHREADS = PT;
 constexpr int SLOTW = 16384;            // weight bytes per ring slot
@@ -46,7 +46,7 @@ constexpr int NSLOT = 11;               // ring depth
 constexpr int MAXCH = 448;              // chunk-list capacity per CTA
 constexpr int NPHASE = NLAYER * 5 + 1;  // 121
 constexpr int PH_HEAD = NLAYER * 5;
-constexpr int MAXP = KMAX / 2 / PT;     // tagged pairs per thread in a full-vector wait (7)
+constexpr int MAXP = (KMAX / 2 + PT - 1) / PT;  // tagged pairs per thread in a full-vector wait (4)
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s bound on any wait
 
 // ---- shared memory layout (dynamic, offsets from the aligned base)
@@ -56,13 +56,13 @@ constexpr int OFF_XF = OFF_DIG + 3 * KMAX;                // float [KMAX]
 constexpr int OFF_HS = OFF_XF + 4 * KMAX;                 // float [HID]
 constexpr int OFF_LAY = OFF_HS + 4 * HID;                 // LayerW [NLAYER]
 constexpr int OFF_CH = OFF_LAY + ((int)sizeof(LayerW) * NLAYER + 15) / 16 * 16;  // Chunk [MAXCH]
-constexpr int OFF_BAR = OFF_CH + 8 * MAXCH;               // u64 full[NSLOT]
-constexpr int OFF_MISC = OFF_BAR + 8 * NSLOT;             // small scalars
+constexpr int OFF_BAR = OFF_CH + 8 * MAXCH;               // u64 full[NSLOT], empty[NSLOT]
+constexpr int OFF_MISC = OFF_BAR + 16 * NSLOT;            // small scalars
 constexpr int SMEM_BYTES = OFF_MISC + 1024;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 static_assert(OFF_DIG % 16 == 0 && OFF_XF % 16 == 0 && OFF_HS % 16 == 0 && SLOT % 16 == 0, "alignment");
 static_assert(OFF_BAR % 8 == 0 && OFF_MISC % 8 == 0, "alignment");
-static_assert(MAXP * 2 * PT == KMAX, "pair split");
+static_assert(MAXP * 2 * PT >= KMAX, "pair split");
 
 struct Misc {
   float red[32];
@@ -71,7 +71,6 @@ struct Misc {
   int abort;
   int tok;
   int last;
-  int slot_cnt[NSLOT];     // warps done with the slot's current chunk
   int slot_last[NSLOT];    // last chunk issued into the slot (-1: none)
   int pos, T, conv_base, act_int8, want_logits, seq, step;
   unsigned long long wbest[NCW];
@@ -90,10 +89,10 @@ __device__ __forceinline__ unsigned long long gtime() {
   return t;
 }
 // all warps of the CTA (named barrier 1)
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
 __device__ __forceinline__ int consumer_and(int v) {
   int r;
-  asm volatile("{ .reg .pred p, q; setp.ne.s32 p, %1, 0; bar.red.and.pred q, 1, 256, p; selp.s32 %0, 1, 0, q; }"
+  asm volatile("{ .reg .pred p, q; setp.ne.s32 p, %1, 0; bar.red.and.pred q, 1, 512, p; selp.s32 %0, 1, 0, q; }"
                : "=r"(r) : "r"(v) : "memory");
   return r;
 }
@@ -156,6 +155,9 @@ struct PCtx {
 };
 
 __device__ __forceinline__ unsigned full_bar(const PCtx& c, int slot) { return smem_u32(c.sm + OFF_BAR + 8 * slot); }
+__device__ __forceinline__ unsigned empty_bar(const PCtx& c, int slot) {
+  return smem_u32(c.sm + OFF_BAR + 8 * (NSLOT + slot));
+}
 
 __device__ __forceinline__ unsigned tag_of(const PCtx& c, int phase) {
   return (unsigned)c.ms->seq * 128u + (unsigned)phase + 1u;
@@ -165,10 +167,11 @@ __device__ __forceinline__ void trace_mark(const PCtx& c, int p, int k) {
   if (c.A->trace && threadIdx.x == 0)
     c.A->trace[((size_t)blockIdx.x * NPHASE + p) * TRACE_STAMPS + k] = gtime();
 }
-// per-chunk stamps of CTA 0 (after the per-phase block): [chunk][4]
+// per-chunk stamps of CTA 0, warp 0 (after the per-phase block): [chunk][4]
+// SM clock cycles (clock64), finer than the global timer
 __device__ __forceinline__ void trace_chunk(const PCtx& c, int i, int k) {
   if (c.A->trace && blockIdx.x == 0 && threadIdx.x == 0)
-    c.A->trace[(size_t)gridDim.x * NPHASE * TRACE_STAMPS + (size_t)i * 4 + k] = gtime();
+    c.A->trace[(size_t)gridDim.x * NPHASE * TRACE_STAMPS + (size_t)i * 4 + k] = clock64();
 }
 
 __device__ void raise_abort(const PCtx& c) {
@@ -255,18 +258,35 @@ __device__ __forceinline__ void issue_chunk(const PCtx& c, int i) {
   if (sc2) bulk_g2s(dst + SLOTW + 128, sc2 + a, sb, bar, c.pol);
 }
 
-// Lane 0 of a warp that has finished reading chunk i: count it; the last of
-// the eight warps refills the slot with chunk i + NSLOT.
+// Warp done reading chunk i: arrive on the slot's `empty` barrier (lane 0,
+// non-blocking).  The slot's refill with chunk i + NSLOT is issued by warp
+// i % NCW once all NCW warps have arrived; that warp waits for the stragglers,
+// the others never wait here.
 __device__ __forceinline__ void release_slot(PCtx& c, int i) {
   const int s = i % NSLOT;
-  if (atomicAdd(&c.ms->slot_cnt[s], 1) == NCW - 1) {
-    c.ms->slot_cnt[s] = 0;
-    const int nx = i + NSLOT;
-    if (nx < c.nch && !*(volatile int*)&c.ms->abort) {
+  const int lane = threadIdx.x & 31;
+  if (lane == 0) mbar_arrive(empty_bar(c, s));
+  if ((int)(threadIdx.x >> 5) != i % NCW) return;
+  const int nx = i + NSLOT;
+  if (nx >= c.nch) return;
+  if (lane == 0) {
+    const unsigned bar = empty_bar(c, s);
+    const unsigned parity = (unsigned)((i / NSLOT) & 1);
+    const unsigned long long t0 = gtime();
+    int it = 0;
+    bool good = true;
+    while (!mbar_try(bar, parity)) {
+      if (((++it) & 63) == 0) {
+        if (aborted(c)) { good = false; break; }
+        if (gtime() - t0 > WAIT_NS) { raise_abort(c); good = false; break; }
+      }
+    }
+    if (good && !*(volatile int*)&c.ms->abort) {
       issue_chunk(c, nx);
       c.ms->slot_last[s] = nx;
     }
   }
+  __syncwarp();
 }
 
 // Consumer warp: wait for chunk i's bytes.  Same result in every lane.
@@ -326,6 +346,14 @@ __device__ bool wait_tagged(PCtx& c, const unsigned long long* src, int n, unsig
 }
 
 // ---------------------------------------------------------------- prologues
+
+// Recombine the digit sums in fp32: (a2 * 65536 + a1 * 256 + a0) * (x_scale * s_w).
+// Two fp32 roundings instead of the graph engine's single fp64 one (|rel| < 2e-7).
+__device__ __forceinline__ float finish_f32(int a0, int a1, int a2, int ndig, float xs_sw) {
+  float y = (float)a0;
+  if (ndig == 3) y = fmaf((float)a2, 65536.0f, fmaf((float)a1, 256.0f, y));
+  return y * xs_sw;
+}
 
 // 2^e as a float for -126 <= e <= 127.
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
@@ -395,74 +423,167 @@ __device__ void encode_lin(PCtx& c, int K, bool act_int8) {
   consumer_sync();
 }
 
-// Gains of a (1+w) RMSNorm over HID for this thread's elements i = tid + 256 j,
-// loaded before the inputs are waited for.
-struct Gain4 { float v[HID / PT]; };
-__device__ __forceinline__ Gain4 load_gain(const float* w) {
-  Gain4 g;
+
+// ---------------------------------------------------------------- per-warp K=1024 input
+
+// Sum of squares of hs[0..HID) in numpy's pairwise order (blocks of 128 summed
+// with 8 strided accumulators, then a binary tree of blocks) -- the order of
+// np.mean(x**2) in golden/model.py:74, so the norm is bit-exact when its input
+// is.  One warp; the result in every lane.
+__device__ __forceinline__ float pairwise_sumsq_1024(const float* hs) {
+  const int lane = threadIdx.x & 31;
+  float r[2];
 #pragma unroll
-  for (int j = 0; j < HID / PT; ++j) g.v[j] = __ldg(w + threadIdx.x + PT * j);
-  return g;
+  for (int u = 0; u < 2; ++u) {
+    const int ch = lane + 32 * u;            // chain: block ch / 8, accumulator ch % 8
+    const float* a = hs + 128 * (ch >> 3) + (ch & 7);
+    float acc = __fmul_rn(a[0], a[0]);
+#pragma unroll
+    for (int i = 1; i < 16; ++i) acc = __fadd_rn(acc, __fmul_rn(a[8 * i], a[8 * i]));
+    // ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)) within the block
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+    // ((B0 + B1) + (B2 + B3)) over the four blocks of this half
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 16));
+    r[u] = acc;
+  }
+  return __fadd_rn(r[0], r[1]);
 }
 
-// xf = rmsnorm(h) * (1 + w) over HID (golden/model.py:63-75); h is in hs.
-__device__ void norm_into_xf(PCtx& c, const Gain4& w) {
-  float* xf = (float*)(c.sm + OFF_XF);
-  float* hs = (float*)(c.sm + OFF_HS);
-  float ss = 0.0f;
-  for (int i = threadIdx.x; i < HID; i += PT) ss = fmaf(hs[i], hs[i], ss);
-  ss = warp_sum(ss);
-  consumer_sync();
-  if ((threadIdx.x & 31) == 0) c.ms->red[threadIdx.x >> 5] = ss;
-  consumer_sync();
-  float tot = 0.0f;
+// CTA-level encode of a normed HID input (every thread two elements, 2t and
+// 2t+1): the sum of squares in numpy's pairwise order by warps 0-1 (the order
+// of np.mean(x**2), golden/model.py:74), then 1/rms, x = h * inv * (1 + w), the
+// digit image (the shift from an upper bound of max|x|) or, under ACT_INT8,
+// the golden quantiser with the exact max|x| (golden/model.py:37-45).  Digits
+// land in the shared planes; returns inv and (ACT_INT8) s_x.  Two barriers
+// (three under ACT_INT8).
+__device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2 g2, bool act_int8,
+                                                float& inv_out, float& sx_out) {
+  Misc* ms = c.ms;
+  int8_t* dg = (int8_t*)(c.sm + OFF_DIG);
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  const float2 h2 = *reinterpret_cast<const float2*>(hs + 2 * t);
+  const float w0 = __fadd_rn(1.0f, g2.x), w1 = __fadd_rn(1.0f, g2.y);
+  if (wid < 2) {
+    const int ch = lane + 32 * wid;          // chain: block ch / 8, accumulator ch % 8
+    const float* a = hs + 128 * (ch >> 3) + (ch & 7);
+    float acc = __fmul_rn(a[0], a[0]);
 #pragma unroll
-  for (int q = 0; q < NCW; ++q) tot += c.ms->red[q];
+    for (int i = 1; i < 16; ++i) acc = __fadd_rn(acc, __fmul_rn(a[8 * i], a[8 * i]));
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));   // (r0+r1), ...
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));   // ((r0+r1)+(r2+r3)), ...
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));   // block sums
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 8));   // (B0+B1), ...
+    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 16));  // ((B0+B1)+(B2+B3))
+    if (lane == 0) ms->red[wid] = acc;
+  }
+  const float mb = warp_max(fmaxf(fabsf(h2.x * w0), fabsf(h2.y * w1)));
+  if (lane == 0) ms->red[2 + wid] = mb;
+  consumer_sync();
+  const float tot = __fadd_rn(ms->red[0], ms->red[1]);
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)HID), EPS)));
+  inv_out = inv;
+  const float x0 = __fmul_rn(__fmul_rn(h2.x, inv), w0);
+  const float x1 = __fmul_rn(__fmul_rn(h2.y, inv), w1);
+  if (act_int8) {
+    const float m = warp_max(fmaxf(fabsf(x0), fabsf(x1)));
+    if (lane == 0) ms->red[18 + wid] = m;
+    consumer_sync();
+    float amax = 0.0f;
 #pragma unroll
-  for (int j = 0; j < HID / PT; ++j) {
-    const int i = threadIdx.x + PT * j;
-    xf[i] = __fmul_rn(__fmul_rn(hs[i], inv), __fadd_rn(1.0f, w.v[j]));
+    for (int w = 0; w < NCW; ++w) amax = fmaxf(amax, ms->red[18 + w]);
+    const float s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+    int q0 = 0, q1 = 0;
+    if (amax > 0.0f) {
+      q0 = (int)fminf(fmaxf(rintf(__fdiv_rn(x0, s)), -127.0f), 127.0f);
+      q1 = (int)fminf(fmaxf(rintf(__fdiv_rn(x1, s)), -127.0f), 127.0f);
+    }
+    reinterpret_cast<unsigned short*>(dg)[t] = (unsigned short)(((unsigned)q0 & 0xffu) | (((unsigned)q1 & 0xffu) << 8));
+    if (t == 0) { ms->scale = (double)s; ms->ndig = 1; }
+    sx_out = s;
+  } else {
+    float mbound = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) mbound = fmaxf(mbound, ms->red[2 + w]);
+    // max|x| <= inv * max|h (1 + w)| up to two roundings: the shift keeps |X| <= 2^22 + 1
+    const float amax = mbound * inv;
+    const int ex = amax > 0.0f ? (int)((__float_as_uint(amax) >> 23) & 0xff) - 126 : 0;
+    int sh = 22 - ex;
+    const bool fast = (__float_as_uint(amax) >> 23) != 0 && sh >= -126 && sh <= 127;
+    if (!fast && amax > 0.0f) { int exs = 0; frexpf(amax, &exs); sh = 22 - exs; }
+    int X[2] = {0, 0};
+    if (amax > 0.0f) {
+      if (fast) { const float p2 = pow2f(sh); X[0] = __float2int_rn(x0 * p2); X[1] = __float2int_rn(x1 * p2); }
+      else { X[0] = (int)rintf(ldexpf(x0, sh)); X[1] = (int)rintf(ldexpf(x1, sh)); }
+    }
+    unsigned w_[3] = {0u, 0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int a0 = (X[e] << 24) >> 24;
+      const int X1 = (X[e] - a0) >> 8;
+      const int a1 = (X1 << 24) >> 24;
+      const int a2 = (X1 - a1) >> 8;
+      w_[0] |= ((unsigned)a0 & 0xffu) << (8 * e);
+      w_[1] |= ((unsigned)a1 & 0xffu) << (8 * e);
+      w_[2] |= ((unsigned)a2 & 0xffu) << (8 * e);
+    }
+#pragma unroll
+    for (int d = 0; d < 3; ++d) reinterpret_cast<unsigned short*>(dg + d * KMAX)[t] = (unsigned short)w_[d];
+    if (t == 0) { ms->scale = ldexp(1.0, -sh); ms->ndig = 3; }
+    sx_out = 0.0f;
   }
   consumer_sync();
 }
 
-// Prologue of GEMV phase p: wait for the inputs, build xf, encode.  false on abort.
+// fp32 row (HID floats, smem) dotted with x on this lane's positions, x rebuilt
+// from hs, 1/rms and the gains exactly as cta_encode_1024 formed it (and
+// fake-quantised with s_x under ACT_INT8, golden/model.py:37-45); warp sum.
+__device__ __forceinline__ float row_dot_f32_lane(const float* row, const float* hs, const float* gw,
+                                                  float inv, bool act_int8, float sx) {
+  const int lane = threadIdx.x & 31;
+  float a = 0.0f;
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+#pragma unroll
+    for (int e4 = 0; e4 < 4; ++e4) {
+      const int pos = 16 * (lane + 32 * q) + 4 * e4;
+      const float4 w = *reinterpret_cast<const float4*>(row + pos);
+      const float4 h4 = *reinterpret_cast<const float4*>(hs + pos);
+      const float4 g4 = __ldg(reinterpret_cast<const float4*>(gw + pos));
+      float x[4] = {__fmul_rn(__fmul_rn(h4.x, inv), __fadd_rn(1.0f, g4.x)),
+                    __fmul_rn(__fmul_rn(h4.y, inv), __fadd_rn(1.0f, g4.y)),
+                    __fmul_rn(__fmul_rn(h4.z, inv), __fadd_rn(1.0f, g4.z)),
+                    __fmul_rn(__fmul_rn(h4.w, inv), __fadd_rn(1.0f, g4.w))};
+      if (act_int8) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          x[e] = __fmul_rn(fminf(fmaxf(rintf(__fdiv_rn(x[e], sx)), -127.0f), 127.0f), sx);
+      }
+      a = fmaf(w.x, x[0], a);
+      a = fmaf(w.y, x[1], a);
+      a = fmaf(w.z, x[2], a);
+      a = fmaf(w.w, x[3], a);
+    }
+  return warp_sum(a);
+}
+
+// Prologue of the OUT (sub 2) and DOWN (sub 4) phases: wait for the inputs,
+// build xf, encode into the shared digit planes.  false on abort.
 __device__ bool prologue(PCtx& c, int p) {
   float* xf = (float*)(c.sm + OFF_XF);
-  float* hs = (float*)(c.sm + OFF_HS);
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
   const bool i8 = ms->act_int8 != 0;
-  if (p == PH_HEAD) {
-    const Gain4 g = load_gain(A.final_norm);
-    if (!wait_tagged(c, A.tv_h, HID, tag_of(c, PH_HEAD - 1), hs)) return false;
-    norm_into_xf(c, g);
-    encode_lin(c, HID, false);
-    return true;
-  }
   const int l = p / 5, sub = p % 5;
   const LayerW& L = c.lay[l];
-  if (sub == 0) {
-    const Gain4 g = load_gain(L.in_norm);
-    if (l == 0) {
-      // residual stream starts at the dequantised embedding row (golden/model.py:246)
-      const int tok = ms->tok;
-      const float sc = __ldg(A.emb_s + tok);
-      const int8_t* row = A.emb_q + (size_t)tok * HID;
-      for (int i = threadIdx.x; i < HID; i += PT) hs[i] = __fmul_rn((float)row[i], sc);
-      consumer_sync();
-    } else if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) {
-      return false;
-    }
-    norm_into_xf(c, g);
-    encode_lin(c, HID, i8);
-  } else if (sub == 2) {
+  if (sub == 2) {
     if (L.linear) {
       // gated RMSNorm of the delta-rule output (golden/model.py:183-189):
       // o from MIX(l) into xf, z from IN(l) parked in the digit region
       float* zb = (float*)(c.sm + OFF_DIG);
-      const float gw = __ldg(L.gnorm_w + (threadIdx.x % LV));   // element i = tid + 256 j
+      const float gw = __ldg(L.gnorm_w + (threadIdx.x % LV));   // element i = tid + 512 j
       if (!wait_tagged(c, A.tv_o, VDIM, tag_of(c, p - 1), xf)) return false;
       if (!wait_tagged(c, A.tv_z, VDIM, tag_of(c, p - 2), zb)) return false;
       const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -484,11 +605,6 @@ __device__ bool prologue(PCtx& c, int p) {
       if (!wait_tagged(c, A.tv_attn, NH * HD, tag_of(c, p - 1), xf)) return false;
       encode_lin(c, NH * HD, i8);
     }
-  } else if (sub == 3) {
-    const Gain4 g = load_gain(L.post_norm);
-    if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) return false;
-    norm_into_xf(c, g);
-    encode_lin(c, HID, i8);
   } else {  // sub == 4
     if (!wait_tagged(c, A.tv_act, FFN, tag_of(c, p - 1), xf)) return false;
     encode_lin(c, FFN, i8);
@@ -569,34 +685,85 @@ __device__ __forceinline__ float row_dot_f32(const float* row, const float* xf) 
   return warp_sum(a);
 }
 
-// Consume every chunk of GEMV phase p (one consumer warp's share).  Per
-// chunk: wait for the bytes; the warp dots its rows (wid, wid + 8); lane q
-// reads row q's scales; the warp releases the slot; lane q runs row q's
-// epilogue.  No synchronisation with the other warps.  false on abort.
-template <bool REG>
-__device__ bool gemv_phase(PCtx& c, int p, int nc_rt) {
-  constexpr int ND = 3;
-  constexpr int NC = 2;                       // K = 1024 for the register-digit variant
-  const int nc = REG ? NC : nc_rt;            // 16-byte lane chunks per row
-  // rows a warp can get from one chunk: 16 KB / (K bytes) / 8 warps
-  constexpr int QMAX = REG ? 2 : 1;
+// Block argmax of the head, then the last CTA reduces every block's maximum,
+// records the step's argmax and advances the step scalars for the next launch.
+__device__ void head_finish(PCtx& c, unsigned long long best) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
-  const float* hs = (const float*)(c.sm + OFF_HS);
-  const float* xf = (const float*)(c.sm + OFF_XF);
-  const int8_t* dg = (const int8_t*)(c.sm + OFF_DIG);
-  Dig<NC, ND> D;
-  if constexpr (REG) load_dig<NC, ND>(c, D);
-  const double xs = ms->scale;
-  const int nd = ms->ndig;
-  const unsigned tag = tag_of(c, p);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) best = umax64(best, __shfl_xor_sync(0xffffffffu, best, o));
+  if (lane == 0) ms->wbest[wid] = best;
+  consumer_sync();
+  if (threadIdx.x == 0) {
+    unsigned long long b = 0ull;
+    for (int w = 0; w < NCW; ++w) b = umax64(b, ms->wbest[w]);
+    A.am_part[blockIdx.x] = b;
+    __threadfence();
+    ms->last = (atomicAdd(A.head_cnt, 1) == (int)gridDim.x - 1);
+  }
+  consumer_sync();
+  if (ms->last) {
+    __threadfence();
+    unsigned long long b = 0ull;
+    for (int q = threadIdx.x; q < (int)gridDim.x; q += PT) b = umax64(b, __ldcg(A.am_part + q));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) b = umax64(b, __shfl_xor_sync(0xffffffffu, b, o));
+    if (lane == 0) ms->wbest[wid] = b;
+    consumer_sync();
+    if (threadIdx.x == 0) {
+      for (int w = 0; w < NCW; ++w) b = umax64(b, ms->wbest[w]);
+      const int step = ms->step;
+      if (step < A.max_steps) A.ids[step] = am_index(b);
+      else atomicCAS(A.err, 0, ERR_CTX);
+      *A.head_cnt = 0;
+      A.io[0] = step + 1;
+      A.dyn->pos = ms->pos + 1;
+      A.dyn->T = ms->T + 1;
+      A.dyn->conv_base = ms->conv_base + 1;
+      A.dyn->seq = ms->seq + 1;
+    }
+  }
+}
+
+// GEMV phases whose input is a normed HID vector -- IN (both layer kinds),
+// GATEUP, HEAD.  Inputs polled into hs once per CTA; then every warp encodes
+// its own register digits (no further CTA synchronisation) and consumes the
+// chunks.  Chunk k's row r goes to warp (rows before k + r) mod 16, so small
+// consecutive chunks are worked on by different warps at the same time.
+__device__ bool phase_1024(PCtx& c, int p) {
+  const PersistArgs& A = *c.A;
+  Misc* ms = c.ms;
+  float* hs = (float*)(c.sm + OFF_HS);
   const bool head = (p == PH_HEAD);
   const int l = head ? 0 : p / 5, sub = head ? -1 : p % 5;
   const LayerW& L = c.lay[l];
+  const float* gw = head ? A.final_norm : (sub == 0 ? L.in_norm : L.post_norm);
+  const float2 g2 = __ldg(reinterpret_cast<const float2*>(gw) + threadIdx.x);
+  if (!head && sub == 0 && l == 0) {
+    // residual stream starts at the dequantised embedding row (golden/model.py:246)
+    const int tok = ms->tok;
+    const float sc = __ldg(A.emb_s + tok);
+    const int8_t* row = A.emb_q + (size_t)tok * HID;
+    for (int i = threadIdx.x; i < HID; i += PT) hs[i] = __fmul_rn((float)row[i], sc);
+    consumer_sync();
+  } else if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) {
+    return false;
+  }
+  float inv, sx;
+  const bool i8 = (!head) && ms->act_int8 != 0;
+  cta_encode_1024(c, hs, g2, i8, inv, sx);
+  Dig<2, 3> D;
+  load_dig<2, 3>(c, D);
+  const int nd = ms->ndig;
+  const double xs = ms->scale;
+  trace_mark(c, p, 1);
+  const unsigned tag = tag_of(c, p);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const bool want = ms->want_logits != 0;
   unsigned long long best = 0ull;
   const int first_i = c.cur;
+  int rows_off = 0;
   while (c.cur < c.nch && c.ch[c.cur].phase == p) {
     const int i = c.cur;
     const Chunk k = c.ch[i];
@@ -608,98 +775,98 @@ __device__ bool gemv_phase(PCtx& c, int p, int nc_rt) {
     const float* tail = (const float*)(buf + SLOTW);
     const int row0 = (int)k.row0, n = k.nrows, a0 = row0 & ~3;
     const bool pair = (sub == 3);
-    const bool f32 = (sub == 0 && L.linear && k.seg >= 2);
-    int acc[QMAX][3], acc2[QMAX][3];
-    float fv[QMAX];
-    float sc = 0.f, sc2 = 0.f;
-#pragma unroll
-    for (int q = 0; q < QMAX; ++q) {
-      const int r = wid + q * NCW;
-      fv[q] = 0.f;
-      if (r >= n) continue;
+    const bool f32 = (sub == 0) && L.linear && k.seg >= 2;
+    const int r = (wid - rows_off) & (NCW - 1);
+    rows_off += n;
+    int acc[3] = {0, 0, 0}, acc2[3] = {0, 0, 0};
+    float fv = 0.0f, sc = 0.0f, sc2 = 0.0f;
+    const bool mine = r < n;
+    if (mine) {
       if (f32) {
-        fv[q] = row_dot_f32((const float*)buf + r * HID, xf);
+        fv = row_dot_f32_lane((const float*)buf + r * HID, hs, gw, inv, i8, sx);
       } else {
-        if constexpr (REG) row_dot_r<NC, ND>(buf + r * (NC * 512), D, acc[q]);
-        else row_dot_s<ND>(buf + r * (nc * 512), dg, nc, acc[q]);
-        if (lane == q) sc = tail[row0 + r - a0];
+        row_dot_r<2, 3>(buf + r * HID, D, acc);
+        if (lane == 0) sc = tail[row0 + r - a0];
         if (pair) {
-          if constexpr (REG) row_dot_r<NC, ND>(buf + (n + r) * (NC * 512), D, acc2[q]);
-          else row_dot_s<ND>(buf + (n + r) * (nc * 512), dg, nc, acc2[q]);
-          if (lane == q) sc2 = tail[32 + row0 + r - a0];
+          row_dot_r<2, 3>(buf + (n + r) * HID, D, acc2);
+          if (lane == 0) sc2 = tail[32 + row0 + r - a0];
         }
       }
     }
     __syncwarp();
-    if (lane == 0) release_slot(c, i);
-    c.cur = i + 1;
     trace_chunk(c, i, 2);
-    // epilogue: lane q handles row q of this warp
-#pragma unroll
-    for (int q = 0; q < QMAX; ++q) {
-      const int r = wid + q * NCW;
-      if (lane != q || r >= n) continue;
+    release_slot(c, i);
+    c.cur = i + 1;
+    trace_chunk(c, i, 3);
+    if (mine && lane == 0) {
       const int o = row0 + r;
+      const float xsf = (float)xs;
       if (head) {
-        const float y = finish_row(acc[q][0], acc[q][1], acc[q][2], 3, xs, sc);
+        const float y = finish_f32(acc[0], acc[1], acc[2], 3, xsf * sc);
         if (want) A.logits[o] = y;
         best = umax64(best, am_pack(y, o));
       } else if (pair) {
-        const float g = finish_row(acc[q][0], acc[q][1], acc[q][2], nd, xs, sc);
-        const float u = finish_row(acc2[q][0], acc2[q][1], acc2[q][2], nd, xs, sc2);
+        const float g = finish_f32(acc[0], acc[1], acc[2], nd, xsf * sc);
+        const float u = finish_f32(acc2[0], acc2[1], acc2[2], nd, xsf * sc2);
         st_tv(A.tv_act + o, __fmul_rn(silu_f(g), u), tag);
       } else if (f32) {
-        st_tv(A.tv_ab + (k.seg == 2 ? 0 : LH) + o, fv[q], tag);
+        st_tv(A.tv_ab + (k.seg == 2 ? 0 : LH) + o, fv, tag);
       } else {
-        const float y = finish_row(acc[q][0], acc[q][1], acc[q][2], nd, xs, sc);
-        if (sub == 0) {
-          unsigned long long* out;
-          if (L.linear) out = (k.seg == 0) ? A.tv_qkv : A.tv_z;
-          else out = (k.seg == 0) ? A.tv_qg : (k.seg == 1 ? A.tv_kvn : A.tv_kvn + KVPROJ);
-          st_tv(out + o, y, tag);
-        } else {
-          // sub 2 / 4: row-parallel projection + residual (h = r + y)
-          st_tv(A.tv_h + o, __fadd_rn(hs[o], y), tag);
-        }
+        const float y = finish_f32(acc[0], acc[1], acc[2], nd, xsf * sc);
+        unsigned long long* out;
+        if (L.linear) out = (k.seg == 0) ? A.tv_qkv : A.tv_z;
+        else out = (k.seg == 0) ? A.tv_qg : (k.seg == 1 ? A.tv_kvn : A.tv_kvn + KVPROJ);
+        st_tv(out + o, y, tag);
       }
+    }
+  }
+  if (head) head_finish(c, best);
+  return true;
+}
+
+// GEMV phases with K = 2048 / 3584 (OUT: out_proj / o_proj, DOWN): digits in
+// the shared planes (written by the CTA prologue), row-parallel projection
+// with the residual add, h = r + y (golden/model.py:259,263).
+__device__ bool phase_wide(PCtx& c, int p, int nc) {
+  const PersistArgs& A = *c.A;
+  Misc* ms = c.ms;
+  const float* hs = (const float*)(c.sm + OFF_HS);
+  const int8_t* dg = (const int8_t*)(c.sm + OFF_DIG);
+  const double xs = ms->scale;
+  const int nd = ms->ndig;
+  const unsigned tag = tag_of(c, p);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int first_i = c.cur;
+  int rows_off = 0;
+  while (c.cur < c.nch && c.ch[c.cur].phase == p) {
+    const int i = c.cur;
+    const Chunk k = c.ch[i];
+    trace_chunk(c, i, 0);
+    if (!wait_full(c, i)) return false;
+    trace_chunk(c, i, 1);
+    if (i == first_i) trace_mark(c, p, 2);
+    const int8_t* buf = (const int8_t*)(c.sm + OFF_RING + (i % NSLOT) * SLOT);
+    const float* tail = (const float*)(buf + SLOTW);
+    const int row0 = (int)k.row0, n = k.nrows, a0 = row0 & ~3;
+    const int r = (wid - rows_off) & (NCW - 1);
+    rows_off += n;
+    int acc[3] = {0, 0, 0};
+    float sc = 0.0f;
+    const bool mine = r < n;
+    if (mine) {
+      row_dot_s<3>(buf + r * (nc * 512), dg, nc, acc);
+      if (lane == 0) sc = tail[row0 + r - a0];
+    }
+    __syncwarp();
+    release_slot(c, i);
+    c.cur = i + 1;
+    trace_chunk(c, i, 2);
+    if (mine && lane == 0) {
+      const int o = row0 + r;
+      const float y = finish_f32(acc[0], acc[1], acc[2], nd, (float)xs * sc);
+      st_tv(A.tv_h + o, __fadd_rn(hs[o], y), tag);
     }
     trace_chunk(c, i, 3);
-  }
-  if (head) {
-    // block argmax, then the last CTA reduces every block's maximum
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) best = umax64(best, __shfl_xor_sync(0xffffffffu, best, o));
-    if (lane == 0) ms->wbest[wid] = best;
-    consumer_sync();
-    if (threadIdx.x == 0) {
-      unsigned long long b = 0ull;
-      for (int w = 0; w < NCW; ++w) b = umax64(b, ms->wbest[w]);
-      A.am_part[blockIdx.x] = b;
-      __threadfence();
-      ms->last = (atomicAdd(A.head_cnt, 1) == (int)gridDim.x - 1);
-    }
-    consumer_sync();
-    if (ms->last) {
-      __threadfence();
-      unsigned long long b = 0ull;
-      for (int q = threadIdx.x; q < (int)gridDim.x; q += PT) b = umax64(b, __ldcg(A.am_part + q));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) b = umax64(b, __shfl_xor_sync(0xffffffffu, b, o));
-      if (lane == 0) ms->wbest[wid] = b;
-      consumer_sync();
-      if (threadIdx.x == 0) {
-        for (int w = 0; w < NCW; ++w) b = umax64(b, ms->wbest[w]);
-        const int step = ms->step;
-        if (step < A.max_steps) A.ids[step] = am_index(b);
-        else atomicCAS(A.err, 0, ERR_CTX);
-        *A.head_cnt = 0;
-        A.io[0] = step + 1;
-        A.dyn->pos = ms->pos + 1;
-        A.dyn->T = ms->T + 1;
-        A.dyn->conv_base = ms->conv_base + 1;
-        A.dyn->seq = ms->seq + 1;
-      }
-    }
   }
   return true;
 }
@@ -708,7 +875,10 @@ __device__ bool gemv_phase(PCtx& c, int p, int nc_rt) {
 
 // (head h, value slice j) of linear layer l: conv+SiLU of the head's q/k and the
 // slice's v channels, gates, l2norm, delta rule on S[h][:, slice], raw o out.
-// golden/model.py:149-178.  Uses the digit region of smem as scratch.
+// golden/model.py:149-178.  512 threads: 0..127 q channels, 128..255 k channels,
+// 256..271 the slice's v channels, 272 the b/a gate inputs; the delta rule maps
+// thread t to column t & 15 and rows 4*(t >> 4) .. +3.  Uses the digit region
+// of smem as scratch.
 __device__ bool delta_item(PCtx& c, int p, int item) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
@@ -720,45 +890,44 @@ __device__ bool delta_item(PCtx& c, int p, int item) {
   float* qs = (float*)(c.sm + OFF_DIG);
   float* ks = qs + LK;
   float* vs = ks + LK;
-  float (*part)[DSLICE + 1] = reinterpret_cast<float (*)[DSLICE + 1]>(vs + 32);
+  float* wsq = vs + 32;                                           // [16] per-warp sums
+  float (*part)[DSLICE + 1] = reinterpret_cast<float (*)[DSLICE + 1]>(wsq + 16);  // [32][17]
   float* cs = A.conv + (size_t)lin * CONVD * CONVK;
   float* Sh = A.rec + ((size_t)lin * LH + h) * LK * LV;
   const int v0 = j * DSLICE;
-  const int vi = t & 15, kg = t >> 4;
-  // prefetch state slice, conv history and taps (previous launches wrote them)
-  float sv[8];
+  const int vi = t & 15, kg = t >> 4;                              // 32 groups of 4 rows
+  constexpr int KPG = LK / 32;
+  // prefetch the state slice, conv history and taps (previous launches wrote them)
+  float sv[KPG];
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk) sv[kk] = Sh[(size_t)(kg * 8 + kk) * LV + v0 + vi];
-  const int ch = (t < LK) ? (h * LK + t) : (KDIM + h * LK + (t - LK));
-  const float* st = cs + (size_t)ch * CONVK;
-  const float s1 = st[(base + 1) & 3], s2 = st[(base + 2) & 3], s3 = st[(base + 3) & 3];
-  const float4 w4 = *reinterpret_cast<const float4*>(L.conv_w + (size_t)ch * CONVK);
-  const int vch = 2 * KDIM + h * LV + v0 + (t & 15);
-  float vs1 = 0.f, vs2 = 0.f, vs3 = 0.f;
-  float4 vw4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (t < DSLICE) {
-    const float* vst = cs + (size_t)vch * CONVK;
-    vs1 = vst[(base + 1) & 3]; vs2 = vst[(base + 2) & 3]; vs3 = vst[(base + 3) & 3];
-    vw4 = *reinterpret_cast<const float4*>(L.conv_w + (size_t)vch * CONVK);
+  for (int kk = 0; kk < KPG; ++kk) sv[kk] = Sh[(size_t)(kg * KPG + kk) * LV + v0 + vi];
+  const int role = (t < 2 * LK) ? 0 : (t < 2 * LK + DSLICE ? 1 : (t == 2 * LK + DSLICE ? 2 : 3));
+  int ch = 0;
+  if (role == 0) ch = (t < LK) ? (h * LK + t) : (KDIM + h * LK + (t - LK));
+  else if (role == 1) ch = 2 * KDIM + h * LV + v0 + (t - 2 * LK);
+  float s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (role <= 1) {
+    const float* st = cs + (size_t)ch * CONVK;
+    s1 = st[(base + 1) & 3]; s2 = st[(base + 2) & 3]; s3 = st[(base + 3) & 3];
+    w4 = *reinterpret_cast<const float4*>(L.conv_w + (size_t)ch * CONVK);
   }
   const float alog = __ldg(L.A_log + h), dtb = __ldg(L.dt_bias + h);
-  // wait for this token's projections: every thread its q/k channel; the
-  // first 16 threads their v channel; thread 16 the b/a gate inputs.  All of a
-  // thread's polls are issued before any is checked.
+  // wait for this token's projections (tagged, from IN)
   const unsigned tin = tag_of(c, p - 1);
   const unsigned long long t0 = gtime();
-  float nv = 0.f, nvv = 0.f, bb = 0.f, aa = 0.f;
-  bool have = false, havev = (t >= DSLICE), haveb = (t != DSLICE);
+  float nv = 0.f, bb = 0.f, aa = 0.f;
+  bool have = (role == 3);
   int it = 0;
   for (;;) {
-    unsigned long long w = 0, wv = 0, wb = 0, wa = 0;
-    if (!have) w = ld_tv(A.tv_qkv + ch);
-    if (!havev) wv = ld_tv(A.tv_qkv + vch);
-    if (!haveb) { wb = ld_tv(A.tv_ab + h); wa = ld_tv(A.tv_ab + LH + h); }
-    if (!have && tag_ok(w, tin)) { nv = tv_val(w); have = true; }
-    if (!havev && tag_ok(wv, tin)) { nvv = tv_val(wv); havev = true; }
-    if (!haveb && tag_ok(wb, tin) && tag_ok(wa, tin)) { bb = tv_val(wb); aa = tv_val(wa); haveb = true; }
-    if (consumer_and(have && havev && haveb)) break;
+    unsigned long long w = 0, w2 = 0;
+    if (!have) {
+      if (role <= 1) w = ld_tv(A.tv_qkv + ch);
+      else { w = ld_tv(A.tv_ab + h); w2 = ld_tv(A.tv_ab + LH + h); }
+      if (role <= 1 && tag_ok(w, tin)) { nv = tv_val(w); have = true; }
+      if (role == 2 && tag_ok(w, tin) && tag_ok(w2, tin)) { bb = tv_val(w); aa = tv_val(w2); have = true; }
+    }
+    if (consumer_and(have)) break;
     if (((++it) & 15) == 0) {
       int bad = 0;
       if (t == 0) {
@@ -768,29 +937,27 @@ __device__ bool delta_item(PCtx& c, int p, int item) {
       if (!consumer_and(!bad)) return false;
     }
   }
-  auto conv = [](float a1, float a2, float a3, float nw, float4 w) {
-    float acc = __fmul_rn(a1, w.x);
-    acc = __fadd_rn(acc, __fmul_rn(a2, w.y));
-    acc = __fadd_rn(acc, __fmul_rn(a3, w.z));
-    acc = __fadd_rn(acc, __fmul_rn(nw, w.w));
-    return silu_f(acc);
-  };
-  const float x = conv(s1, s2, s3, nv, w4);
-  if (j == 0) cs[(size_t)ch * CONVK + (base & 3)] = nv;   // dead oldest column <- newest
-  if (t < DSLICE) {
-    vs[t] = conv(vs1, vs2, vs3, nvv, vw4);
-    cs[(size_t)vch * CONVK + (base & 3)] = nvv;
-  }
-  if (t == DSLICE) {
+  float x = 0.0f;
+  if (role <= 1) {
+    float acc = __fmul_rn(s1, w4.x);
+    acc = __fadd_rn(acc, __fmul_rn(s2, w4.y));
+    acc = __fadd_rn(acc, __fmul_rn(s3, w4.z));
+    acc = __fadd_rn(acc, __fmul_rn(nv, w4.w));
+    x = silu_f(acc);
+    // the dead oldest column takes the newest value (q/k channels: slice 0 only)
+    if (role == 1 || j == 0) cs[(size_t)ch * CONVK + (base & 3)] = nv;
+    if (role == 1) vs[t - 2 * LK] = x;
+  } else if (role == 2) {
     ms->gate_beta = sigmoid_f(bb);
     ms->gate_g = __fmul_rn(-expf(alog), softplus_f(__fadd_rn(aa, dtb)));
   }
-  float ss = warp_sum(x * x);
-  if ((t & 31) == 0) ms->red[t >> 5] = ss;
+  // l2norm of q (warps 0-3) and k (warps 4-7)
+  const float ss = warp_sum(role == 0 ? x * x : 0.0f);
+  if ((t & 31) == 0) wsq[t >> 5] = ss;
   consumer_sync();
-  {
+  if (role == 0) {
     const int g0 = (t < LK) ? 0 : 4;
-    const float tot = ((ms->red[g0] + ms->red[g0 + 1]) + ms->red[g0 + 2]) + ms->red[g0 + 3];
+    const float tot = ((wsq[g0] + wsq[g0 + 1]) + wsq[g0 + 2]) + wsq[g0 + 3];
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(tot, EPS)));
     if (t < LK) qs[t] = __fmul_rn(__fmul_rn(x, inv), 0.08838834764831845f);
     else ks[t - LK] = __fmul_rn(x, inv);
@@ -800,21 +967,21 @@ __device__ bool delta_item(PCtx& c, int p, int item) {
   const float gexp = expf(ms->gate_g);
   float pkv = 0.0f;
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
+  for (int kk = 0; kk < KPG; ++kk) {
     sv[kk] = __fmul_rn(sv[kk], gexp);
-    pkv = fmaf(sv[kk], ks[kg * 8 + kk], pkv);
+    pkv = fmaf(sv[kk], ks[kg * KPG + kk], pkv);
   }
   part[kg][vi] = pkv;
   consumer_sync();
   float kvv = 0.0f;
 #pragma unroll
-  for (int g = 0; g < 16; ++g) kvv += part[g][vi];
+  for (int g = 0; g < 32; ++g) kvv += part[g][vi];
   const float delta = __fmul_rn(__fsub_rn(vs[vi], kvv), ms->gate_beta);
   consumer_sync();
   float po = 0.0f;
 #pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    const int k = kg * 8 + kk;
+  for (int kk = 0; kk < KPG; ++kk) {
+    const int k = kg * KPG + kk;
     const float s2v = __fadd_rn(sv[kk], __fmul_rn(ks[k], delta));
     Sh[(size_t)k * LV + v0 + vi] = s2v;
     po = fmaf(s2v, qs[k], po);
@@ -824,7 +991,7 @@ __device__ bool delta_item(PCtx& c, int p, int item) {
   if (t < DSLICE) {
     float o = 0.0f;
 #pragma unroll
-    for (int g = 0; g < 16; ++g) o += part[g][t];
+    for (int g = 0; g < 32; ++g) o += part[g][t];
     st_tv(A.tv_o + h * LV + v0 + t, o, tag_of(c, p));
   }
   consumer_sync();
@@ -880,8 +1047,11 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
   // [0, 1536): e < 1024 -> q of head 4g + e/256; then k; then v
   {
     const unsigned long long tw = gtime();
-    constexpr int NP = 6 * HD / 2 / PT;   // 3 pairs per thread
-    unsigned pend = (1u << NP) - 1;
+    constexpr int NP = (6 * HD / 2 + PT - 1) / PT;   // pairs per thread (2)
+    unsigned pend = 0;
+#pragma unroll
+    for (int jj = 0; jj < NP; ++jj)
+      if ((int)threadIdx.x + PT * jj < 6 * HD / 2) pend |= 1u << jj;
     int it = 0;
     for (;;) {
       unsigned long long a[NP], b[NP];
@@ -921,7 +1091,7 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
   consumer_sync();
   float* kc = A.kcache + (size_t)fi * A.max_ctx * KVPROJ;
   float* vc = A.vcache + (size_t)fi * A.max_ctx * KVPROJ;
-  if (cc == 0) {   // roped K and raw V of this token into slot T (golden/model.py:216-217)
+  if (cc == 0 && threadIdx.x < HD) {   // roped K and raw V into slot T (golden/model.py:216-217)
     kc[(size_t)T * KVPROJ + g * HD + threadIdx.x] = kn[threadIdx.x];
     vc[(size_t)T * KVPROJ + g * HD + threadIdx.x] = vn[threadIdx.x];
   }
@@ -962,19 +1132,21 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
     if (lane == 0) { mh[wid] = m; mh[4 + wid] = lsum; }
   }
   consumer_sync();
-  const int d = threadIdx.x;
-  float o[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int i = 0; i < n; ++i) {
-    const int tt = t0 + i;
-    const float v = (tt < T) ? vc[(size_t)tt * KVPROJ + g * HD + d] : vn[d];
-#pragma unroll
-    for (int hq = 0; hq < 4; ++hq) o[hq] = fmaf(sc[hq * ATT_MAXLEN + i], v, o[hq]);
-  }
+  const int d = threadIdx.x;          // threads 0..255: one head dimension each
   float* part = A.att_part + ((size_t)(g * ATT_MAXCH + cc) * 4) * (2 + HD);
+  if (d < HD) {
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int i = 0; i < n; ++i) {
+      const int tt = t0 + i;
+      const float v = (tt < T) ? vc[(size_t)tt * KVPROJ + g * HD + d] : vn[d];
 #pragma unroll
-  for (int hq = 0; hq < 4; ++hq) {
-    part[hq * (2 + HD) + 2 + d] = o[hq];
-    if (d == 0) { part[hq * (2 + HD)] = mh[hq]; part[hq * (2 + HD) + 1] = mh[4 + hq]; }
+      for (int hq = 0; hq < 4; ++hq) o[hq] = fmaf(sc[hq * ATT_MAXLEN + i], v, o[hq]);
+    }
+#pragma unroll
+    for (int hq = 0; hq < 4; ++hq) {
+      part[hq * (2 + HD) + 2 + d] = o[hq];
+      if (d == 0) { part[hq * (2 + HD)] = mh[hq]; part[hq * (2 + HD) + 1] = mh[4 + hq]; }
+    }
   }
   __threadfence();
   consumer_sync();
@@ -984,9 +1156,10 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
   if (!ms->last) return true;
   __threadfence();
   if (threadIdx.x == 0) *cnt = 0;
+  if (d >= HD) { consumer_sync(); return true; }
   // gates of the 4 heads (tagged, from IN): all four polls issued together
   const unsigned long long tg0 = gtime();
-  float gv[4];
+  float gv[4] = {0.f, 0.f, 0.f, 0.f};
   {
     unsigned pend = 0xf;
     int it = 0;
@@ -1057,7 +1230,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
     ms->tok = tok;
     for (int s = 0; s < NSLOT; ++s) {
       mbar_init(full_bar(c, s), 1);
-      ms->slot_cnt[s] = 0;
+      mbar_init(empty_bar(c, s), NCW);
       ms->slot_last[s] = -1;
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1094,10 +1267,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
         trace_mark(c, p, 3);
         continue;
       }
-      if (!prologue(c, p)) { ok = false; break; }
-      trace_mark(c, p, 1);
-      const int K = (p == PH_HEAD) ? HID : (sub == 2 ? VDIM : (sub == 4 ? FFN : HID));
-      ok = (K == HID) ? gemv_phase<true>(c, p, 2) : gemv_phase<false>(c, p, K / 512);
+      if (p == PH_HEAD || sub == 0 || sub == 3) {
+        ok = phase_1024(c, p);
+      } else {
+        if (!prologue(c, p)) { ok = false; break; }
+        trace_mark(c, p, 1);
+        ok = phase_wide(c, p, (sub == 2 ? VDIM : FFN) / 512);
+      }
       // the warps leave a GEMV phase independently; line them up again
       consumer_sync();
       trace_mark(c, p, 3);
