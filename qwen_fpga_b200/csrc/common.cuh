@@ -134,6 +134,7 @@ struct StateW {
 constexpr int ERR_TOKEN = 1;   // token id outside the vocabulary
 constexpr int ERR_CTX = 2;     // KV cache / RoPE table / step log full
 constexpr int ERR_WAIT = 3;    // a bounded device wait ran out
+constexpr int ERR_CHECK = 4;   // a device-side bounds check failed (site in err[1], value in err[2])
 
 // ---- small helpers
 __device__ __forceinline__ float warp_sum(float v) {

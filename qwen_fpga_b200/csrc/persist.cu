@@ -25,7 +25,12 @@
 // Phase program per layer l (p = 5l + sub): IN (projections of the normed
 // residual), MIX (DeltaNet delta rule, or split-KV attention), OUT (out/o
 // projection + residual), GATEUP (silu(gate)*up), DOWN (down projection +
-// residual); phase 120 is the tied head.  Arithmetic (and its rounding order)
+// residual); phase 120 is the tied head, on the 5th-generation tensor cores
+// (tcgen05.mma kind::i8, accumulators in tensor memory) over a copy of the
+// embedding re-tiled at load time into the canonical K-major layout.
+//
+// A phase's chunks are a precomputed index range of the CTA's list (counted
+// loops; the schedule stores where every phase starts).  Arithmetic (and its rounding order)
 // is that of decode.cu, so both engines agree bit for bit; the contract is
 // golden/model.py:243-267.
 #include <cstdio>
@@ -44,7 +49,7 @@ constexpr int SLOTW = 16384;            // weight bytes per ring slot
 constexpr int SLOT = SLOTW + 256;       // + row scales of the chunk (two arrays for gate/up)
 constexpr int NSLOT = 11;               // ring depth
 constexpr int MAXCH = 448;              // chunk-list capacity per CTA
-constexpr int NPHASE = NLAYER * 5 + 1;  // 121
+constexpr int NPHASE = PERSIST_NPHASE;  // 121
 constexpr int PH_HEAD = NLAYER * 5;
 constexpr int MAXP = (KMAX / 2 + PT - 1) / PT;  // tagged pairs per thread in a full-vector wait (4)
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s bound on any wait
@@ -56,8 +61,15 @@ constexpr int OFF_XF = OFF_DIG + 3 * KMAX;                // float [KMAX]
 constexpr int OFF_HS = OFF_XF + 4 * KMAX;                 // float [HID]
 constexpr int OFF_LAY = OFF_HS + 4 * HID;                 // LayerW [NLAYER]
 constexpr int OFF_CH = OFF_LAY + ((int)sizeof(LayerW) * NLAYER + 15) / 16 * 16;  // Chunk [MAXCH]
-constexpr int OFF_BAR = OFF_CH + 8 * MAXCH;               // u64 full[NSLOT], empty[NSLOT]
-constexpr int OFF_MISC = OFF_BAR + 16 * NSLOT;            // small scalars
+constexpr int OFF_BAR = OFF_CH + 8 * MAXCH;               // u64 mbarriers, see bar_* below
+constexpr int NBAR = 3 * NSLOT + 5;                       // full, empty, mma per slot; acc_full[2], acc_empty[2], fin
+constexpr int OFF_MISC = OFF_BAR + 8 * NBAR;              // small scalars
+// head phase: the x digits as the tensor-core B operand (16 rows x HID, canonical
+// K-major layout: rows 0-2 the digit planes, 3-15 zero; 8-row groups BT_SBO
+// bytes apart), over the digit planes and xf, which the head does not use
+constexpr int BT_SBO = (HID / 16) * 128;
+constexpr int OFF_BT = OFF_DIG;
+static_assert(OFF_BT % 128 == 0 && OFF_BT + 2 * BT_SBO <= OFF_HS, "head B tile");
 constexpr int SMEM_BYTES = OFF_MISC + 1024;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 static_assert(OFF_DIG % 16 == 0 && OFF_XF % 16 == 0 && OFF_HS % 16 == 0 && SLOT % 16 == 0, "alignment");
@@ -65,19 +77,24 @@ static_assert(OFF_BAR % 8 == 0 && OFF_MISC % 8 == 0, "alignment");
 static_assert(MAXP * 2 * PT >= KMAX, "pair split");
 
 struct Misc {
-  float red[32];
+  unsigned tmem;           // tensor memory base (head accumulators), written by tcgen05.alloc
+  unsigned pad_[3];
+  float red[48];
+  int pend_min;
   double scale;
   int ndig;
   int abort;
   int tok;
   int last;
   int slot_last[NSLOT];    // last chunk issued into the slot (-1: none)
+  unsigned short pf[NPHASE + 1];  // this CTA's chunk range of each phase (phase_first)
   int pos, T, conv_base, act_int8, want_logits, seq, step;
   unsigned long long wbest[NCW];
   float inv_h[LH];
   float gate_g, gate_beta;
 };
 static_assert(sizeof(Misc) <= 1024, "misc");
+static_assert(OFF_MISC % 16 == 0, "tcgen05.alloc destination alignment");
 
 // ---------------------------------------------------------------- PTX helpers
 __device__ __forceinline__ unsigned smem_u32(const void* p) {
@@ -88,11 +105,23 @@ __device__ __forceinline__ unsigned long long gtime() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// all warps of the CTA (named barrier 1)
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 512;" ::: "memory"); }
+// Named barrier 1 over all 512 threads.  The non-.aligned forms: a warp may
+// reach them with its lanes not yet reconverged (lane-0 work just before).
+__device__ __forceinline__ void consumer_sync() {
+  __syncwarp();
+  asm volatile("barrier.sync 1, 512;" ::: "memory");
+}
+__device__ __forceinline__ int consumer_or(int v) {
+  int r;
+  __syncwarp();
+  asm volatile("{ .reg .pred p, q; setp.ne.s32 p, %1, 0; barrier.red.or.pred q, 1, 512, p; selp.s32 %0, 1, 0, q; }"
+               : "=r"(r) : "r"(v) : "memory");
+  return r;
+}
 __device__ __forceinline__ int consumer_and(int v) {
   int r;
-  asm volatile("{ .reg .pred p, q; setp.ne.s32 p, %1, 0; bar.red.and.pred q, 1, 512, p; selp.s32 %0, 1, 0, q; }"
+  __syncwarp();
+  asm volatile("{ .reg .pred p, q; setp.ne.s32 p, %1, 0; barrier.red.and.pred q, 1, 512, p; selp.s32 %0, 1, 0, q; }"
                : "=r"(r) : "r"(v) : "memory");
   return r;
 }
@@ -150,7 +179,6 @@ struct PCtx {
   LayerW* lay;
   const Chunk* ch;
   int nch;          // chunks of this CTA
-  int cur;          // next chunk index to consume (per consumer warp; all warps agree)
   unsigned long long pol;
 };
 
@@ -158,6 +186,47 @@ __device__ __forceinline__ unsigned full_bar(const PCtx& c, int slot) { return s
 __device__ __forceinline__ unsigned empty_bar(const PCtx& c, int slot) {
   return smem_u32(c.sm + OFF_BAR + 8 * (NSLOT + slot));
 }
+
+// tcgen05 completion of the MMAs that read slot s (head phase)
+__device__ __forceinline__ unsigned mma_bar(const PCtx& c, int slot) {
+  return smem_u32(c.sm + OFF_BAR + 8 * (2 * NSLOT + slot));
+}
+// head accumulator buffer b: MMAs done (acc_full) / epilogue done reading it (acc_empty)
+__device__ __forceinline__ unsigned accf_bar(const PCtx& c, int b) { return smem_u32(c.sm + OFF_BAR + 8 * (3 * NSLOT + b)); }
+__device__ __forceinline__ unsigned acce_bar(const PCtx& c, int b) { return smem_u32(c.sm + OFF_BAR + 8 * (3 * NSLOT + 2 + b)); }
+__device__ __forceinline__ unsigned fin_bar(const PCtx& c) { return smem_u32(c.sm + OFF_BAR + 8 * (3 * NSLOT + 4)); }
+
+// ---------------------------------------------------------------- tcgen05 (5th-gen tensor cores)
+
+// Shared-memory matrix descriptor, canonical K-major layout without swizzle:
+// start address, leading byte offset (between the two 16-byte core-matrix
+// columns of one MMA's K = 32), stride byte offset (between 8-row groups),
+// descriptor version 1.
+__device__ __forceinline__ unsigned long long umma_desc(unsigned addr, unsigned lbo, unsigned sbo) {
+  return (unsigned long long)((addr >> 4) & 0x3fffu) | (unsigned long long)((lbo >> 4) & 0x3fffu) << 16 |
+         (unsigned long long)((sbo >> 4) & 0x3fffu) << 32 | 1ull << 46;
+}
+// Instruction descriptor of kind::i8: s32 accumulators, signed int8 A and B,
+// both K-major, N columns, M rows.
+__host__ __device__ constexpr unsigned umma_idesc_i8(int M, int N) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((unsigned)(N >> 3) << 17) | ((unsigned)(M >> 4) << 24);
+}
+// D[tmem] (+)= A[M x 32] * B[N x 32]^T, one int8 K-step; issued by one thread.
+__device__ __forceinline__ void umma_i8(unsigned tmem, unsigned long long a, unsigned long long b,
+                                        unsigned idesc, unsigned accumulate) {
+  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+               "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+               :: "r"(tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate) : "memory");
+}
+// Arrive (once) on an mbarrier when every tcgen05 op this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit(unsigned bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               :: "r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// generic-proxy shared-memory writes -> visible to the tensor core (async proxy)
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 __device__ __forceinline__ unsigned tag_of(const PCtx& c, int phase) {
   return (unsigned)c.ms->seq * 128u + (unsigned)phase + 1u;
@@ -174,8 +243,26 @@ __device__ __forceinline__ void trace_chunk(const PCtx& c, int i, int k) {
     c.A->trace[(size_t)gridDim.x * NPHASE * TRACE_STAMPS + (size_t)i * 4 + k] = clock64();
 }
 
-__device__ void raise_abort(const PCtx& c) {
-  atomicCAS(c.A->err, 0, ERR_WAIT);
+// A device-side bounds check failed: record the site and the offending value,
+// stop every CTA (the access itself is skipped by the caller).
+__device__ __forceinline__ void check_fail(const PCtx& c, int site, int value) {
+  if (atomicCAS(c.A->err, 0, ERR_CHECK) == 0) {
+    c.A->err[1] = site;
+    c.A->err[2] = value;
+  }
+  atomicExch(c.A->abort_flag, 1);
+  *(volatile int*)&c.ms->abort = 1;
+}
+
+// A bounded wait ran out (or the schedule is unusable): record ERR_WAIT with
+// the site, a site-specific value and the CTA (err[1..3], first one wins), and
+// stop every CTA.
+__device__ void raise_abort(const PCtx& c, int site = 0, int value = 0) {
+  if (atomicCAS(c.A->err, 0, ERR_WAIT) == 0) {
+    c.A->err[1] = site;
+    c.A->err[2] = value;
+    c.A->err[3] = (int)blockIdx.x;
+  }
   atomicExch(c.A->abort_flag, 1);
   *(volatile int*)&c.ms->abort = 1;
 }
@@ -192,10 +279,10 @@ __device__ __forceinline__ void chunk_src(const PCtx& c, const Chunk& k, const c
   const int row0 = (int)k.row0, n = k.nrows;
   src2 = nullptr;
   sc = sc2 = nullptr;
-  if (p == PH_HEAD) {
-    src = (const char*)c.A->emb_q + (size_t)row0 * HID;
-    bytes = n * HID;
-    sc = c.A->emb_s;
+  if (p == PH_HEAD) {   // one K-slab of a head tile; scales are read by the epilogue
+    if (row0 >= HEAD_TILES || n >= HEAD_NSLAB) { src = nullptr; bytes = 0; return; }
+    src = (const char*)c.A->head_tiles + ((size_t)row0 * HEAD_NSLAB + n) * SLOTW;
+    bytes = SLOTW;
     return;
   }
   const LayerW& L = c.lay[p / 5];
@@ -246,6 +333,7 @@ __device__ __forceinline__ void issue_chunk(const PCtx& c, int i) {
   const float* sc;
   const float* sc2;
   chunk_src(c, k, src, src2, bytes, sc, sc2);
+  if (!src) { check_fail(c, 5, (int)k.row0); return; }
   const unsigned bar = full_bar(c, slot);
   const unsigned dst = smem_u32(c.sm + OFF_RING + slot * SLOT);
   const unsigned sb = sc ? scale_bytes((int)k.row0, k.nrows) : 0u;
@@ -278,7 +366,7 @@ __device__ __forceinline__ void release_slot(PCtx& c, int i) {
     while (!mbar_try(bar, parity)) {
       if (((++it) & 63) == 0) {
         if (aborted(c)) { good = false; break; }
-        if (gtime() - t0 > WAIT_NS) { raise_abort(c); good = false; break; }
+        if (gtime() - t0 > WAIT_NS) { raise_abort(c, 10, i); good = false; break; }
       }
     }
     if (good && !*(volatile int*)&c.ms->abort) {
@@ -289,10 +377,23 @@ __device__ __forceinline__ void release_slot(PCtx& c, int i) {
   __syncwarp();
 }
 
-// Consumer warp: wait for chunk i's bytes.  Same result in every lane.
-__device__ __forceinline__ bool wait_full(PCtx& c, int i) {
-  const unsigned bar = full_bar(c, i % NSLOT);
-  const unsigned parity = (unsigned)((i / NSLOT) & 1);
+// One thread: bounded wait for phase `parity` of an mbarrier.  false on abort
+// or time-out (which raises the abort).
+__device__ bool wait_bar1(const PCtx& c, unsigned bar, unsigned parity, int site, int value) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = gtime();
+  int it = 0;
+  while (!mbar_try(bar, parity)) {
+    if (((++it) & 63) == 0) {
+      if (aborted(c)) return false;
+      if (gtime() - t0 > WAIT_NS) { raise_abort(c, site, value); return false; }
+    }
+  }
+  return true;
+}
+
+// Whole warp: bounded wait on an mbarrier phase.  Same result in every lane.
+__device__ __forceinline__ bool wait_bar_warp(PCtx& c, unsigned bar, unsigned parity, int site, int value) {
   int good = 1;
   if (!mbar_try(bar, parity)) {
     const unsigned long long t0 = gtime();
@@ -300,11 +401,15 @@ __device__ __forceinline__ bool wait_full(PCtx& c, int i) {
     while (!mbar_try(bar, parity)) {
       if (((++it) & 63) == 0) {
         if (aborted(c)) { good = 0; break; }
-        if (gtime() - t0 > WAIT_NS) { raise_abort(c); good = 0; break; }
+        if (gtime() - t0 > WAIT_NS) { raise_abort(c, site, value); good = 0; break; }
       }
     }
   }
   return __all_sync(0xffffffffu, good) != 0;
+}
+// Consumer warp: wait for chunk i's bytes.  Same result in every lane.
+__device__ __forceinline__ bool wait_full(PCtx& c, int i) {
+  return wait_bar_warp(c, full_bar(c, i % NSLOT), (unsigned)((i / NSLOT) & 1), 11, i);
 }
 
 // Poll tagged words src[0..n) (n even, n <= KMAX) until all carry `tag`; values
@@ -338,7 +443,7 @@ __device__ bool wait_tagged(PCtx& c, const unsigned long long* src, int n, unsig
       int bad = 0;
       if (threadIdx.x == 0) {
         if (aborted(c)) bad = 1;
-        else if (gtime() - t0 > WAIT_NS) { raise_abort(c); bad = 1; }
+        else if (gtime() - t0 > WAIT_NS) { raise_abort(c, 12, (int)(tag & 127u)); bad = 1; }
       }
       if (!consumer_and(!bad)) return false;
     }
@@ -457,10 +562,11 @@ __device__ __forceinline__ float pairwise_sumsq_1024(const float* hs) {
 // of np.mean(x**2), golden/model.py:74), then 1/rms, x = h * inv * (1 + w), the
 // digit image (the shift from an upper bound of max|x|) or, under ACT_INT8,
 // the golden quantiser with the exact max|x| (golden/model.py:37-45).  Digits
-// land in the shared planes; returns inv and (ACT_INT8) s_x.  Two barriers
-// (three under ACT_INT8).
+// land in the shared planes, or (canon, W8A32 only) in the rows 0-2 of the
+// tensor-core B tile at OFF_BT with rows 3-7 zeroed; returns inv and
+// (ACT_INT8) s_x.  Two barriers (three under ACT_INT8).
 __device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2 g2, bool act_int8,
-                                                float& inv_out, float& sx_out) {
+                                                float& inv_out, float& sx_out, bool canon = false) {
   Misc* ms = c.ms;
   int8_t* dg = (int8_t*)(c.sm + OFF_DIG);
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
@@ -529,8 +635,20 @@ __device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2
       w_[1] |= ((unsigned)a1 & 0xffu) << (8 * e);
       w_[2] |= ((unsigned)a2 & 0xffu) << (8 * e);
     }
+    if (canon) {
+      // elements 2t, 2t+1 sit in core-matrix column (2t)/16 of the 8 x HID tile
+      unsigned char* bt = c.sm + OFF_BT + ((2 * t) >> 4) * 128 + ((2 * t) & 15);
 #pragma unroll
-    for (int d = 0; d < 3; ++d) reinterpret_cast<unsigned short*>(dg + d * KMAX)[t] = (unsigned short)w_[d];
+      for (int d = 0; d < 3; ++d) *reinterpret_cast<unsigned short*>(bt + 16 * d) = (unsigned short)w_[d];
+#pragma unroll
+      for (int d = 3; d < 8; ++d) *reinterpret_cast<unsigned short*>(bt + 16 * d) = 0;
+#pragma unroll
+      for (int d = 0; d < 8; ++d) *reinterpret_cast<unsigned short*>(bt + BT_SBO + 16 * d) = 0;
+      fence_async_smem();
+    } else {
+#pragma unroll
+      for (int d = 0; d < 3; ++d) reinterpret_cast<unsigned short*>(dg + d * KMAX)[t] = (unsigned short)w_[d];
+    }
     if (t == 0) { ms->scale = ldexp(1.0, -sh); ms->ndig = 3; }
     sx_out = 0.0f;
   }
@@ -726,21 +844,139 @@ __device__ void head_finish(PCtx& c, unsigned long long best) {
   }
 }
 
-// GEMV phases whose input is a normed HID vector -- IN (both layer kinds),
-// GATEUP, HEAD.  Inputs polled into hs once per CTA; then every warp encodes
-// its own register digits (no further CTA synchronisation) and consumes the
-// chunks.  Chunk k's row r goes to warp (rows before k + r) mod 16, so small
-// consecutive chunks are worked on by different warps at the same time.
-__device__ bool phase_1024(PCtx& c, int p) {
+// Head refiller (one thread): as soon as the MMAs that read head chunk q have
+// completed, its slot takes chunk q + NSLOT.  Runs beside the MMA issuer, so
+// the issuer never waits on an MMA completion.  1 = ok.
+__device__ int head_refill(PCtx& c, int h0, int h1) {
+  for (int q = h0; q + NSLOT < h1; ++q) {
+    const int s = q % NSLOT;
+    if (!wait_bar1(c, mma_bar(c, s), (unsigned)(((q - h0) / NSLOT) & 1), 15, q - h0)) return 0;
+    issue_chunk(c, q + NSLOT);
+    c.ms->slot_last[s] = q + NSLOT;
+  }
+  return 1;
+}
+
+// MMA issuer of the head (one thread).  Local tile t accumulates in TMEM
+// columns 16 (t & 1) .. +15: per K-slab four K = 32 steps, M = 128 weight rows
+// (A, the ring slot) against N = 16 digit rows (B; only columns 0-2 of the
+// accumulator are read).  A tile's buffer is reused once the epilogue released
+// the tile two before it.  All MMAs have completed when this returns.  1 = ok.
+__device__ int head_mma(PCtx& c, int h0, int h1, unsigned tmem) {
+  constexpr unsigned IDESC = umma_idesc_i8(HEAD_TM, 16);
+  constexpr unsigned SBO_A = (HEAD_KS / 16) * 128;
+  const unsigned bt = smem_u32(c.sm + OFF_BT);
+  const unsigned s_lo = smem_u32(c.sm), s_hi = s_lo + SMEM_BYTES;
+  int good = 1;
+  bool any = false;
+  // the accumulators: lane 0, two 16-column buffers inside the 512 columns
+  if ((tmem >> 16) != 0u || (tmem & 0xffffu) > 512u - 32u) { check_fail(c, 2, (int)tmem); return 0; }
+  if (bt < s_lo || bt + 2u * BT_SBO > s_hi) { check_fail(c, 4, (int)bt); return 0; }
+  for (int i = h0; i < h1; ++i) {
+    const int li = i - h0, t = li / HEAD_NSLAB, j = li % HEAD_NSLAB, b = t & 1;
+    if (j == 0 && t >= 2) {
+      if (!wait_bar1(c, acce_bar(c, b), (unsigned)(((t - 2) >> 1) & 1), 13, t)) { good = 0; break; }
+      tc_fence_after();
+    }
+    if (!wait_bar1(c, full_bar(c, i % NSLOT), (unsigned)((i / NSLOT) & 1), 14, li)) { good = 0; break; }
+    const unsigned a = smem_u32(c.sm + OFF_RING + (i % NSLOT) * SLOT);
+    if (a < s_lo || a + (unsigned)SLOTW > s_hi || (a & 127u)) { check_fail(c, 3, (int)a); good = 0; break; }
+#pragma unroll
+    for (int s = 0; s < HEAD_KS / 32; ++s)
+      umma_i8(tmem + 16u * b, umma_desc(a + 256u * s, 128u, SBO_A),
+              umma_desc(bt + (unsigned)((HEAD_KS / 16) * j + 2 * s) * 128u, 128u, (unsigned)BT_SBO), IDESC,
+              (unsigned)(j | s));
+    any = true;
+    umma_commit(mma_bar(c, i % NSLOT));
+    if (j == HEAD_NSLAB - 1) umma_commit(accf_bar(c, b));
+  }
+  if (any) {
+    umma_commit(fin_bar(c));
+    if (!wait_bar1(c, fin_bar(c), 0u, 16, h1 - h0)) good = 0;
+  }
+  return good;
+}
+
+// Tied head on the tensor cores, logits = emb_q x (golden/model.py:266): the
+// CTA's head tiles stream through the ring as 16 KB K-slabs; warp NCW-1 lane 0
+// issues the MMAs (head_mma), warp NCW-2 lane 0 refills the slots they have
+// finished with (head_refill), warps 0-3 are the epilogue: thread = TMEM lane =
+// tile row, the three exact digit sums recombined and scaled as in the CUDA-core
+// phases, logits stored, argmax kept.  The input is encoded once into the B tile.
+__device__ bool phase_head(PCtx& c, int p, int h0, int h1) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
   float* hs = (float*)(c.sm + OFF_HS);
-  const bool head = (p == PH_HEAD);
-  const int l = head ? 0 : p / 5, sub = head ? -1 : p % 5;
+  const float2 g2 = __ldg(reinterpret_cast<const float2*>(A.final_norm) + threadIdx.x);
+  if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) return false;
+  float inv, sx;
+  cta_encode_1024(c, hs, g2, false, inv, sx, true);
+  trace_mark(c, p, 1);
+  const float xsf = (float)ms->scale;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int ntiles = (h1 - h0) / HEAD_NSLAB;
+  const unsigned tmem = ms->tmem;
+  const bool want = ms->want_logits != 0;
+  unsigned long long best = 0ull;
+  int good = 1;
+  if (h1 != c.nch || h0 >= h1 || (h1 - h0) % HEAD_NSLAB != 0 || c.ch[h0].phase != PH_HEAD) {
+    if (threadIdx.x == 0) check_fail(c, 1, h1 - h0);
+    good = 0;
+  }
+  if (!good) {
+  } else if (wid == NCW - 1) {
+    if (lane == 0) good = head_mma(c, h0, h1, tmem);
+    __syncwarp();
+  } else if (wid == NCW - 2) {
+    if (lane == 0) good = head_refill(c, h0, h1);
+    __syncwarp();
+  } else if (wid < 4) {
+    for (int t = 0; t < ntiles; ++t) {
+      const int b = t & 1;
+      const int o = (int)c.ch[h0 + t * HEAD_NSLAB].row0 * HEAD_TM + 32 * wid + lane;
+      if (__any_sync(0xffffffffu, o < 0 || o >= VOCAB)) {
+        if (lane == 0) check_fail(c, 6, o);
+        good = 0;
+        break;
+      }
+      const float sw = __ldg(A.emb_s + o);
+      if (!wait_bar_warp(c, accf_bar(c, b), (unsigned)((t >> 1) & 1), 17, t)) { good = 0; break; }
+      if (t == 0) trace_mark(c, p, 2);
+      tc_fence_after();
+      // this warp's 32 TMEM lanes (rows), columns 0-2 (the three digit sums)
+      const unsigned ta = tmem + ((unsigned)(32 * wid) << 16) + 16u * b;
+      unsigned r0, r1, r2;
+      asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];"
+                   : "=r"(r0), "=r"(r1) : "r"(ta) : "memory");
+      asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r2) : "r"(ta + 2u) : "memory");
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acce_bar(c, b));
+      const float y = finish_f32((int)r0, (int)r1, (int)r2, 3, xsf * sw);
+      if (want) A.logits[o] = y;
+      best = umax64(best, am_pack(y, o));
+    }
+  }
+  if (!consumer_and(good)) return false;
+  head_finish(c, best);
+  return true;
+}
+
+// GEMV phases whose input is a normed HID vector -- IN (both layer kinds),
+// GATEUP.  Inputs polled into hs once per CTA; then every warp encodes
+// its own register digits (no further CTA synchronisation) and consumes the
+// chunks.  Chunk k's row r goes to warp (rows before k + r) mod 16, so small
+// consecutive chunks are worked on by different warps at the same time.
+__device__ bool phase_1024(PCtx& c, int p, int i0, int i1) {
+  const PersistArgs& A = *c.A;
+  Misc* ms = c.ms;
+  float* hs = (float*)(c.sm + OFF_HS);
+  const int l = p / 5, sub = p % 5;
   const LayerW& L = c.lay[l];
-  const float* gw = head ? A.final_norm : (sub == 0 ? L.in_norm : L.post_norm);
+  const float* gw = sub == 0 ? L.in_norm : L.post_norm;
   const float2 g2 = __ldg(reinterpret_cast<const float2*>(gw) + threadIdx.x);
-  if (!head && sub == 0 && l == 0) {
+  if (sub == 0 && l == 0) {
     // residual stream starts at the dequantised embedding row (golden/model.py:246)
     const int tok = ms->tok;
     const float sc = __ldg(A.emb_s + tok);
@@ -751,7 +987,7 @@ __device__ bool phase_1024(PCtx& c, int p) {
     return false;
   }
   float inv, sx;
-  const bool i8 = (!head) && ms->act_int8 != 0;
+  const bool i8 = ms->act_int8 != 0;
   cta_encode_1024(c, hs, g2, i8, inv, sx);
   Dig<2, 3> D;
   load_dig<2, 3>(c, D);
@@ -760,17 +996,13 @@ __device__ bool phase_1024(PCtx& c, int p) {
   trace_mark(c, p, 1);
   const unsigned tag = tag_of(c, p);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const bool want = ms->want_logits != 0;
-  unsigned long long best = 0ull;
-  const int first_i = c.cur;
   int rows_off = 0;
-  while (c.cur < c.nch && c.ch[c.cur].phase == p) {
-    const int i = c.cur;
+  for (int i = i0; i < i1; ++i) {
     const Chunk k = c.ch[i];
     trace_chunk(c, i, 0);
     if (!wait_full(c, i)) return false;
     trace_chunk(c, i, 1);
-    if (i == first_i) trace_mark(c, p, 2);
+    if (i == i0) trace_mark(c, p, 2);
     const int8_t* buf = (const int8_t*)(c.sm + OFF_RING + (i % NSLOT) * SLOT);
     const float* tail = (const float*)(buf + SLOTW);
     const int row0 = (int)k.row0, n = k.nrows, a0 = row0 & ~3;
@@ -796,16 +1028,11 @@ __device__ bool phase_1024(PCtx& c, int p) {
     __syncwarp();
     trace_chunk(c, i, 2);
     release_slot(c, i);
-    c.cur = i + 1;
     trace_chunk(c, i, 3);
     if (mine && lane == 0) {
       const int o = row0 + r;
       const float xsf = (float)xs;
-      if (head) {
-        const float y = finish_f32(acc[0], acc[1], acc[2], 3, xsf * sc);
-        if (want) A.logits[o] = y;
-        best = umax64(best, am_pack(y, o));
-      } else if (pair) {
+      if (pair) {
         const float g = finish_f32(acc[0], acc[1], acc[2], nd, xsf * sc);
         const float u = finish_f32(acc2[0], acc2[1], acc2[2], nd, xsf * sc2);
         st_tv(A.tv_act + o, __fmul_rn(silu_f(g), u), tag);
@@ -820,14 +1047,13 @@ __device__ bool phase_1024(PCtx& c, int p) {
       }
     }
   }
-  if (head) head_finish(c, best);
   return true;
 }
 
 // GEMV phases with K = 2048 / 3584 (OUT: out_proj / o_proj, DOWN): digits in
 // the shared planes (written by the CTA prologue), row-parallel projection
 // with the residual add, h = r + y (golden/model.py:259,263).
-__device__ bool phase_wide(PCtx& c, int p, int nc) {
+__device__ bool phase_wide(PCtx& c, int p, int nc, int i0, int i1) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
   const float* hs = (const float*)(c.sm + OFF_HS);
@@ -836,15 +1062,13 @@ __device__ bool phase_wide(PCtx& c, int p, int nc) {
   const int nd = ms->ndig;
   const unsigned tag = tag_of(c, p);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int first_i = c.cur;
   int rows_off = 0;
-  while (c.cur < c.nch && c.ch[c.cur].phase == p) {
-    const int i = c.cur;
+  for (int i = i0; i < i1; ++i) {
     const Chunk k = c.ch[i];
     trace_chunk(c, i, 0);
     if (!wait_full(c, i)) return false;
     trace_chunk(c, i, 1);
-    if (i == first_i) trace_mark(c, p, 2);
+    if (i == i0) trace_mark(c, p, 2);
     const int8_t* buf = (const int8_t*)(c.sm + OFF_RING + (i % NSLOT) * SLOT);
     const float* tail = (const float*)(buf + SLOTW);
     const int row0 = (int)k.row0, n = k.nrows, a0 = row0 & ~3;
@@ -859,7 +1083,6 @@ __device__ bool phase_wide(PCtx& c, int p, int nc) {
     }
     __syncwarp();
     release_slot(c, i);
-    c.cur = i + 1;
     trace_chunk(c, i, 2);
     if (mine && lane == 0) {
       const int o = row0 + r;
@@ -919,6 +1142,7 @@ __device__ bool delta_item(PCtx& c, int p, int item) {
   float nv = 0.f, bb = 0.f, aa = 0.f;
   bool have = (role == 3);
   int it = 0;
+  if (t == 0) ms->pend_min = 0x7fffffff;
   for (;;) {
     unsigned long long w = 0, w2 = 0;
     if (!have) {
@@ -929,12 +1153,22 @@ __device__ bool delta_item(PCtx& c, int p, int item) {
     }
     if (consumer_and(have)) break;
     if (((++it) & 15) == 0) {
-      int bad = 0;
+      int st = 0;   // 1: aborted elsewhere, 2: this wait ran out
       if (t == 0) {
-        if (aborted(c)) bad = 1;
-        else if (gtime() - t0 > WAIT_NS) { raise_abort(c); bad = 1; }
+        if (aborted(c)) st = 1;
+        else if (gtime() - t0 > WAIT_NS) st = 2;
       }
-      if (!consumer_and(!bad)) return false;
+      if (!consumer_and(st == 0)) {
+        if (!consumer_and(!(t == 0 && st == 2))) {
+          // report what is missing: q/k, v, gate words, and the lowest missing channel
+          if (!have && role <= 1) atomicMin(&ms->pend_min, ch);
+          const int pq = consumer_or(!have && role == 0), pv = consumer_or(!have && role == 1);
+          const int pg = consumer_or(!have && role == 2);
+          const int lo = (pq | pv) ? (ms->pend_min & 0x7ffff) : 0;   // a channel < CONVD
+          if (t == 0) raise_abort(c, 18, p | pq << 8 | pv << 9 | pg << 10 | lo << 12);
+        }
+        return false;
+      }
     }
   }
   float x = 0.0f;
@@ -1079,7 +1313,7 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
         int bad = 0;
         if (threadIdx.x == 0) {
           if (aborted(c)) bad = 1;
-          else if (gtime() - tw > WAIT_NS) { raise_abort(c); bad = 1; }
+          else if (gtime() - tw > WAIT_NS) { raise_abort(c, 19, p); bad = 1; }
         }
         if (!consumer_and(!bad)) return false;
       }
@@ -1173,7 +1407,7 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
         if ((pend >> hq & 1) && tag_ok(w[hq], tin)) { gv[hq] = tv_val(w[hq]); pend &= ~(1u << hq); }
       if (pend && ((++it) & 63) == 0) {
         if (aborted(c)) break;
-        if (gtime() - tg0 > WAIT_NS) { raise_abort(c); break; }
+        if (gtime() - tg0 > WAIT_NS) { raise_abort(c, 20, p); break; }
       }
     }
   }
@@ -1207,14 +1441,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
   c.lay = (LayerW*)(sm + OFF_LAY);
   Chunk* chs = (Chunk*)(sm + OFF_CH);
   c.ch = chs;
-  c.nch = A.nchunks[blockIdx.x];
-  c.cur = 0;
+  c.nch = A.phase_first[(size_t)blockIdx.x * (NPHASE + 1) + NPHASE];
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(c.pol));
+  const unsigned long long t_entry = gtime();
   Misc* ms = c.ms;
   // stage the layer table, this CTA's chunk list and the step scalars
   for (int i = threadIdx.x; i < (int)(sizeof(LayerW) * NLAYER / 4); i += NTHREADS)
     ((int*)c.lay)[i] = ((const int*)A.layers)[i];
   for (int i = threadIdx.x; i < c.nch; i += NTHREADS) chs[i] = A.chunks[(size_t)blockIdx.x * MAXCH + i];
+  for (int i = threadIdx.x; i <= NPHASE; i += NTHREADS) ms->pf[i] = A.phase_first[(size_t)blockIdx.x * (NPHASE + 1) + i];
   if (threadIdx.x == 0) {
     ms->abort = 0;
     ms->pos = A.dyn->pos;
@@ -1231,14 +1466,34 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
     for (int s = 0; s < NSLOT; ++s) {
       mbar_init(full_bar(c, s), 1);
       mbar_init(empty_bar(c, s), NCW);
+      mbar_init(mma_bar(c, s), 1);
       ms->slot_last[s] = -1;
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf_bar(c, b), 1);
+      mbar_init(acce_bar(c, b), 4);
+    }
+    mbar_init(fin_bar(c), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
   if (ms->T >= A.max_ctx || ms->pos >= A.max_rope) {
     if (threadIdx.x == 0) atomicCAS(A.err, 0, ERR_CTX);
     return;
+  }
+  // 32 TMEM columns: the head's two 128 x 16 int32 accumulators.  One CTA per
+  // SM (the launch holds the whole register file), so the allocation is free.
+  if ((threadIdx.x >> 5) == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 32;"
+                 :: "r"(smem_u32(&ms->tmem)) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (A.trace && threadIdx.x == 0) {   // kernel entry and TMEM ready, in the unused stamps of phase 1
+    A.trace[((size_t)blockIdx.x * NPHASE + 1) * TRACE_STAMPS + 1] = t_entry;
+    A.trace[((size_t)blockIdx.x * NPHASE + 1) * TRACE_STAMPS + 2] = gtime();
   }
   if (threadIdx.x == 0)
     for (int i = 0; i < NSLOT && i < c.nch; ++i) {
@@ -1248,7 +1503,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
   {
     bool ok = true;
     for (int p = 0; p < NPHASE && ok; ++p) {
-      if (*(volatile int*)&ms->abort) { ok = false; break; }
       const int sub = p % 5;
       trace_mark(c, p, 0);
       if (p != PH_HEAD && sub == 1) {
@@ -1260,27 +1514,34 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
           int nch = (Tn + ATT_MINLEN - 1) / ATT_MINLEN;
           nch = nch < 1 ? 1 : (nch > ATT_MAXCH ? ATT_MAXCH : nch);
           const int cl = (Tn + nch - 1) / nch;
-          if (cl > ATT_MAXLEN) { if (threadIdx.x == 0) raise_abort(c); ok = false; break; }
+          if (cl > ATT_MAXLEN) { if (threadIdx.x == 0) raise_abort(c, 21, p); ok = false; break; }
           for (int it = blockIdx.x; it < NKV * nch && ok; it += gridDim.x)
             ok = attn_item(c, p, it % NKV, it / NKV, nch, cl);
         }
         trace_mark(c, p, 3);
         continue;
       }
-      if (p == PH_HEAD || sub == 0 || sub == 3) {
-        ok = phase_1024(c, p);
+      // this phase's chunks, [i0, i1) of the CTA's list (counted loops only)
+      const int i0 = ms->pf[p], i1 = ms->pf[p + 1];
+      if (p == PH_HEAD) {
+        ok = phase_head(c, p, i0, i1);
+      } else if (sub == 0 || sub == 3) {
+        ok = phase_1024(c, p, i0, i1);
       } else {
         if (!prologue(c, p)) { ok = false; break; }
         trace_mark(c, p, 1);
-        ok = phase_wide(c, p, (sub == 2 ? VDIM : FFN) / 512);
+        ok = phase_wide(c, p, (sub == 2 ? VDIM : FFN) / 512, i0, i1);
       }
-      // the warps leave a GEMV phase independently; line them up again
-      consumer_sync();
+      // the warps leave a GEMV phase independently; line them up again (and
+      // make a failure in any warp the whole CTA's)
+      ok = consumer_and(ok) != 0;
       trace_mark(c, p, 3);
     }
     if (!ok && threadIdx.x == 0) *(volatile int*)&ms->abort = 1;
   }
   // drain: every bulk copy that was issued must land before the CTA exits
+  // (the head's MMAs have all completed: head_mma waits for them)
+  tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) {
     const unsigned long long t0 = gtime();
@@ -1293,6 +1554,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
     }
   }
   __syncthreads();
+  if ((threadIdx.x >> 5) == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 32;" :: "r"(ms->tmem) : "memory");
+  }
 }
 
 static_assert(OFF_DIG + (4 * HD + 2 * HD + 4 * ATT_MAXLEN) * 4 <= OFF_HS,
@@ -1307,29 +1572,50 @@ int persist_max_chunks() { return MAXCH; }
 // Build the per-CTA chunk lists: for every GEMV phase, its rows are split
 // into G contiguous byte-balanced ranges, each cut into <= SLOT-byte chunks
 // that never straddle a segment.
-bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks, std::vector<int>& counts,
-                    std::string& err) {
+bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
+                    std::vector<unsigned short>& phase_first, std::string& err) {
   (void)M;
   chunks.assign((size_t)G * MAXCH, Chunk{});
-  counts.assign(G, 0);
+  phase_first.assign((size_t)G * (NPHASE + 1), 0);
+  std::vector<int> counts(G, 0);
   struct Seg { int rows; int rowbytes; int unit_rows; };
   for (int p = 0; p < NPHASE; ++p) {
-    std::vector<Seg> segs;
+    // every CTA's chunks of phase p start where its list stands now
+    for (int b = 0; b < G; ++b) phase_first[(size_t)b * (NPHASE + 1) + p] = (unsigned short)counts[b];
+    Seg segs[4];
+    int nseg = 0;
+    auto add = [&](int rows, int rowbytes) { segs[nseg++] = Seg{rows, rowbytes, 1}; };
     const int sub = p % 5;
-    if (p == PH_HEAD) segs = {{VOCAB, HID, 1}};
-    else if (sub == 1) continue;
+    if (p == PH_HEAD) {
+      // whole tiles per CTA (a tile's K-slabs accumulate in one CTA's TMEM)
+      for (int b = 0; b < G; ++b) {
+        const int t0 = (int)((long long)HEAD_TILES * b / G), t1 = (int)((long long)HEAD_TILES * (b + 1) / G);
+        for (int t = t0; t < t1; ++t)
+          for (int j = 0; j < HEAD_NSLAB; ++j) {
+            int& cnt = counts[b];
+            if (cnt >= MAXCH) { err = "chunk list overflow"; return false; }
+            Chunk& k = chunks[(size_t)b * MAXCH + cnt++];
+            k.phase = (unsigned short)p;
+            k.seg = 0;
+            k.nrows = (unsigned char)j;
+            k.row0 = (unsigned)t;
+          }
+      }
+      continue;
+    }
+    if (sub == 1) continue;
     else if (sub == 0) {
       const bool linear = (p / 5) % 4 != 3;
-      if (linear) segs = {{CONVD, HID, 1}, {VDIM, HID, 1}, {LH, HID * 4, 1}, {LH, HID * 4, 1}};
-      else segs = {{QPROJ, HID, 1}, {KVPROJ, HID, 1}, {KVPROJ, HID, 1}};
-    } else if (sub == 2) segs = {{HID, VDIM, 1}};
-    else if (sub == 3) segs = {{FFN, 2 * HID, 1}};   // a unit = one (gate, up) row pair
-    else segs = {{HID, FFN, 1}};
+      if (linear) { add(CONVD, HID); add(VDIM, HID); add(LH, HID * 4); add(LH, HID * 4); }
+      else { add(QPROJ, HID); add(KVPROJ, HID); add(KVPROJ, HID); }
+    } else if (sub == 2) add(HID, VDIM);
+    else if (sub == 3) add(FFN, 2 * HID);   // a unit = one (gate, up) row pair
+    else add(HID, FFN);
     long long total = 0;
-    for (auto& s : segs) total += (long long)s.rows * s.rowbytes;
+    for (int si = 0; si < nseg; ++si) total += (long long)segs[si].rows * segs[si].rowbytes;
     // walk the rows, assigning each to the CTA whose byte window holds its start
     long long off = 0;
-    for (int si = 0; si < (int)segs.size(); ++si) {
+    for (int si = 0; si < nseg; ++si) {
       const Seg& s = segs[si];
       const int per_chunk = SLOTW / s.rowbytes;
       int r = 0;
@@ -1352,8 +1638,29 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks, std::vec
       }
     }
   }
-  // the chunk order inside a CTA must follow the phase order (it does: phases are walked in order)
+  for (int b = 0; b < G; ++b) phase_first[(size_t)b * (NPHASE + 1) + NPHASE] = (unsigned short)counts[b];
   return true;
+}
+
+// One 16-byte core-matrix row per thread: tile t, slab j, row m, K-group g.
+__global__ void k_repack_head(const int4* __restrict__ emb, int4* __restrict__ tiles) {
+  const size_t id = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  constexpr int G16 = HEAD_KS / 16;
+  if (id >= (size_t)VOCAB * (HID / 16)) return;
+  const int g = (int)(id % G16);
+  const int m = (int)((id / G16) % HEAD_TM);
+  const int j = (int)((id / (G16 * HEAD_TM)) % HEAD_NSLAB);
+  const size_t t = id / ((size_t)G16 * HEAD_TM * HEAD_NSLAB);
+  const int4 v = emb[((t * HEAD_TM + m) * HID + (size_t)j * HEAD_KS) / 16 + g];
+  tiles[((t * HEAD_NSLAB + j) * (HEAD_TM * HEAD_KS) + ((m >> 3) * G16 + g) * 128 + (m & 7) * 16) / 16] = v;
+}
+
+cudaError_t repack_head_tiles(const int8_t* emb_q, int8_t* tiles, cudaStream_t st) {
+  if (((uintptr_t)emb_q & 15) || ((uintptr_t)tiles & 15)) return cudaErrorMisalignedAddress;
+  const size_t n = (size_t)VOCAB * (HID / 16);
+  k_repack_head<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(reinterpret_cast<const int4*>(emb_q),
+                                                          reinterpret_cast<int4*>(tiles));
+  return cudaGetLastError();
 }
 
 cudaError_t launch_persistent(const PersistArgs& args, int G, cudaStream_t st) {

@@ -10,7 +10,8 @@
 namespace qb {
 
 // One weight chunk of a CTA's schedule: nrows rows (or (gate, up) row pairs)
-// of segment `seg` of phase `phase`, starting at row0.
+// of segment `seg` of phase `phase`, starting at row0.  Head chunks are one
+// K-slab of a head tile instead: row0 = tile index, nrows = slab index.
 struct Chunk {
   unsigned short phase;
   unsigned char seg;
@@ -19,12 +20,17 @@ struct Chunk {
 };
 static_assert(sizeof(Chunk) == 8, "Chunk layout");
 
+// Phases of one decode step: 5 per layer (IN, MIX, OUT, GATEUP, DOWN) + the head.
+constexpr int PERSIST_NPHASE = NLAYER * 5 + 1;
+
 // Everything the persistent kernel reads; tv_* are tagged {value, tag} words.
 struct PersistArgs {
   const LayerW* layers;        // [NLAYER] (device copy of ModelW::L)
   const int8_t* emb_q; const float* emb_s; const float* final_norm;
+  const int8_t* head_tiles;    // embed_tokens.weight re-tiled for the tensor cores (repack_head_tiles)
   const Chunk* chunks;         // [G][MAXCH]
-  const int* nchunks;          // [G]
+  const unsigned short* phase_first;  // [G][PERSIST_NPHASE + 1]: a phase's chunks are
+                                      // [first[p], first[p + 1]) of the CTA's list
   unsigned long long *tv_h, *tv_qkv, *tv_z, *tv_ab, *tv_o, *tv_qg, *tv_kvn, *tv_attn, *tv_act;
   float* conv; float* rec; float* kcache; float* vcache;
   float* att_part; int* att_cnt;   // att_cnt: [NFULL][NKV]
@@ -42,12 +48,25 @@ struct PersistArgs {
 // (prologue done), first weight chunk landed, phase exit.
 constexpr int TRACE_STAMPS = 4;
 
+// Head tiles: embed_tokens.weight [VOCAB, HID] int8 as HEAD_TILES tiles of
+// HEAD_TM rows, each cut into HEAD_NSLAB K-slabs of HEAD_KS bytes.  Slab
+// (t, j) is one contiguous 16 KB block at (t * HEAD_NSLAB + j) * 16384 in the
+// tcgen05 canonical K-major no-swizzle layout: element (m, k) of the slab at
+// ((m / 8) * (HEAD_KS / 16) + k / 16) * 128 + (m % 8) * 16 + k % 16.
+constexpr int HEAD_TM = 128;
+constexpr int HEAD_KS = 128;
+constexpr int HEAD_NSLAB = HID / HEAD_KS;
+constexpr int HEAD_TILES = VOCAB / HEAD_TM;
+static_assert(VOCAB % HEAD_TM == 0 && HID % HEAD_KS == 0, "head tiling");
+constexpr size_t HEAD_TILE_BYTES = (size_t)VOCAB * HID;
+cudaError_t repack_head_tiles(const int8_t* emb_q, int8_t* tiles, cudaStream_t st);
+
 int persist_smem_bytes();
 int persist_num_phases();
 int persist_max_chunks();
 int persist_max_blocks_per_sm();
-bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks, std::vector<int>& counts,
-                    std::string& err);
+bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
+                    std::vector<unsigned short>& phase_first, std::string& err);
 cudaError_t launch_persistent(const PersistArgs& args, int G, cudaStream_t st);
 
 }  // namespace qb

@@ -390,12 +390,17 @@ int launch_step(qwen_ctx* c) {
 int check_device(qwen_ctx* c) {
   if (*c->h_err != 0) {
     const int code = *c->h_err;
-    QCUDA(c, cudaMemset(c->S.err, 0, sizeof(int)));
+    QCUDA(c, cudaMemset(c->S.err, 0, 4 * sizeof(int)));
     QCUDA(c, cudaMemset(c->P.abort_flag, 0, sizeof(int)));
     QCUDA(c, cudaMemset(c->P.head_cnt, 0, sizeof(int)));
     QCUDA(c, cudaMemset(c->P.att_cnt, 0, NFULL * NKV * sizeof(int)));
     if (code == ERR_TOKEN) return fail(c, QWEN_ERR_ARG, "token id outside [0, %d)", VOCAB);
     if (code == ERR_CTX) return fail(c, QWEN_ERR_STATE, "context or step capacity exceeded on device");
+    if (code == ERR_WAIT)
+      return fail(c, QWEN_ERR_DEVICE, "device wait ran out (site %d, value %d, block %d)", c->h_err[1],
+                  c->h_err[2], c->h_err[3]);
+    if (code == ERR_CHECK)
+      return fail(c, QWEN_ERR_DEVICE, "device bounds check failed (site %d, value %d)", c->h_err[1], c->h_err[2]);
     return fail(c, QWEN_ERR_DEVICE, "device reported error %d", code);
   }
   return QWEN_OK;
@@ -540,26 +545,38 @@ int qwen_create(const char* blob_path, const char* index_path, int n_gpus, const
     P.tv_attn = w; w += NH * HD;
     P.tv_act = w; w += FFN;
     std::vector<Chunk> chunks;
-    std::vector<int> counts;
+    std::vector<unsigned short> first;
     std::string serr;
-    if (!build_schedule(c->Mh, c->sm_count, chunks, counts, serr)) {
+    if (!build_schedule(c->Mh, c->sm_count, chunks, first, serr)) {
       fail(c, QWEN_ERR_STATE, "schedule: %s", serr.c_str());
       return bail(QWEN_ERR_STATE);
     }
     Chunk* dch = nullptr;
-    int* dcnt = nullptr;
+    unsigned short* dfirst = nullptr;
     if ((rc = dalloc(c, &dch, chunks.size() * sizeof(Chunk))) ||
-        (rc = dalloc(c, &dcnt, counts.size() * sizeof(int))) ||
+        (rc = dalloc(c, &dfirst, first.size() * sizeof(unsigned short))) ||
         (rc = dalloc(c, &P.att_cnt, NFULL * NKV * sizeof(int))) ||
         (rc = dalloc(c, &P.head_cnt, 64)) || (rc = dalloc(c, &P.abort_flag, 64)))
       return bail(rc);
-    cudaMemcpy(dch, chunks.data(), chunks.size() * sizeof(Chunk), cudaMemcpyHostToDevice);
-    cudaMemcpy(dcnt, counts.data(), counts.size() * sizeof(int), cudaMemcpyHostToDevice);
+    if (cudaMemcpy(dch, chunks.data(), chunks.size() * sizeof(Chunk), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dfirst, first.data(), first.size() * sizeof(unsigned short), cudaMemcpyHostToDevice) != cudaSuccess) {
+      fail(c, QWEN_ERR_CUDA, "schedule upload failed");
+      return bail(QWEN_ERR_CUDA);
+    }
     P.chunks = dch;
-    P.nchunks = dcnt;
+    P.phase_first = dfirst;
     P.layers = &c->Md->L[0];
     P.emb_q = c->Mh.emb_q;
     P.emb_s = c->Mh.emb_s;
+    {
+      // the head's weights re-tiled once for the tensor cores (a second copy:
+      // the row-major table still serves the embedding lookup and engine 0)
+      int8_t* tiles = nullptr;
+      if ((rc = dalloc(c, &tiles, HEAD_TILE_BYTES))) return bail(rc);
+      cudaError_t e = repack_head_tiles(c->Mh.emb_q, tiles, c->st);
+      if (e != cudaSuccess) { fail(c, QWEN_ERR_CUDA, "head repack: %s", cudaGetErrorString(e)); return bail(QWEN_ERR_CUDA); }
+      P.head_tiles = tiles;
+    }
     P.final_norm = c->Mh.final_norm;
     P.conv = S.conv; P.rec = S.rec; P.kcache = S.kcache; P.vcache = S.vcache;
     P.att_part = S.att_part;
