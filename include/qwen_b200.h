@@ -49,8 +49,9 @@ int qwen_reset(qwen_ctx* ctx, int seq);
  *   conv [18][6144][4]   rec [18][16][128][128]
  *   kc, vc [6][T][2][256] (K after QK-norm and RoPE, V raw)   pos
  * Host pointers.  Import requires T <= max_ctx - 1.  Export writes T and pos
- * through the int pointers; kc/vc may be NULL to skip the cache, and must then
- * hold max_ctx * 6 * 512 floats each when given. */
+ * through the int pointers; kc/vc may be NULL to skip the cache (a call with
+ * both NULL reads T), and when given must each hold 6 * T * 512 floats for the
+ * current T. */
 int qwen_state_import(qwen_ctx* ctx, int seq, const float* conv, const float* rec,
                       const float* kc, const float* vc, int T, int pos);
 int qwen_state_export(qwen_ctx* ctx, int seq, float* conv, float* rec, float* kc,
