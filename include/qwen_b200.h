@@ -114,6 +114,27 @@ int qwen_gemv_i8_f32(float* y, const int8_t* w, const float* s, const float* x, 
 int qwen_gemv_i8_i8(int32_t* acc, float* y, const int8_t* w, const float* sw,
                     const int8_t* xq, float sx, int N, int K, qwen_stream_t stream);
 
+/* Allocation-free GEMV + argmax on device pointers (no counterpart in the
+ * reference): y = s .* (W x) exactly as qwen_gemv_i8_f32 computes it, and
+ * *argmax = the first index of the largest y (the tied-head argmax of
+ * golden/model.py:266-267).  For callers that may not allocate device memory
+ * while they run, such as a serving loop that has fixed its memory after
+ * warm-up or a caller with no qwen_ctx: the call uses no cudaMalloc and no
+ * library allocator.  Its per-block maxima and an arrival counter sit in a
+ * fixed 8 KiB static device array.
+ *   - N must be in [1, 1048576] (the array holds 1024 blocks of 1024 rows);
+ *     larger N is rejected with QWEN_ERR_ARG.  K, w alignment as for
+ *     qwen_gemv_i8_f32.  y may be NULL; argmax (one int) may not.
+ *   - The first call on each device resolves the array's address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - The arrival counter must be zero when a call starts: it is zero when the
+ *     library loads and every call leaves it zero.
+ *   - Calls on the same device share the array: two calls whose kernels run at
+ *     the same time (different streams, overlapping launches) race and return
+ *     wrong argmax values.  Order them (one stream, or events). */
+int qwen_gemv_i8_f32_argmax_noalloc(float* y, int* argmax, const int8_t* w, const float* s,
+                                    const float* x, int N, int K, qwen_stream_t stream);
+
 /* One gated delta-rule step of a 16-head DeltaNet layer on device pointers,
  * S [16][128][128] updated in place, out [16][128]:
  *   S *= exp(g); kv = k^T S; d = (v - kv) * beta; S += k (x) d; out = q^T S

@@ -78,6 +78,7 @@ def load() -> C.CDLL:
     L.qwen_gemv_i8_f32.argtypes = [_vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]
     L.qwen_gemv_i8_i8.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_float, C.c_int, C.c_int, _vp]
     L.qwen_delta_rule_layer.argtypes = [_vp] * 7 + [_vp]
+    L.qwen_gemv_i8_f32_argmax_noalloc.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]
     _lib = L
     return L
 
@@ -271,6 +272,17 @@ def gemv_i8_i8(w, sw, xq, sx, acc=None, y=None, stream=None, want_acc=True, want
                                 _ptr(w), _ptr(sw), _ptr(xq), float(sx), N, K, _stream(stream))
     _check(rc)
     return acc, y
+
+
+def gemv_i8_f32_argmax_noalloc(w, s, x, argmax, y=None, stream=None):
+    """y = s * (w @ x) (when y is given) and argmax[0] = first index of its maximum,
+    through the allocation-free entry point; argmax is a caller-owned int32 CUDA
+    tensor of one element, y an optional fp32 [N] CUDA tensor."""
+    N, K = w.shape
+    rc = load().qwen_gemv_i8_f32_argmax_noalloc(_ptr(y), _ptr(argmax), _ptr(w), _ptr(s), _ptr(x), N, K,
+                                                _stream(stream))
+    _check(rc)
+    return y, argmax
 
 
 def delta_rule_layer(q, k, v, g, beta, S, out=None, stream=None):

@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "decode.cuh"
 #include "gemv.cuh"
+#include "noalloc.cuh"
 #include "persist.cuh"
 
 using namespace qb;
@@ -810,6 +811,19 @@ int qwen_gemv_i8_i8(int32_t* acc, float* y, const int8_t* w, const float* sw, co
   cudaError_t e = enqueue_gemv(y, acc, w, sw, nullptr, xq, sx, N, K, sm_count_current(),
                                reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(nullptr, QWEN_ERR_CUDA, "gemv_i8_i8 launch: %s", cudaGetErrorString(e));
+  return QWEN_OK;
+}
+
+int qwen_gemv_i8_f32_argmax_noalloc(float* y, int* argmax, const int8_t* w, const float* s,
+                                    const float* x, int N, int K, qwen_stream_t stream) {
+  if (!argmax || !w || !s || !x) return fail(nullptr, QWEN_ERR_ARG, "null pointer");
+  if (N > NA_MAX_ROWS)
+    return fail(nullptr, QWEN_ERR_ARG, "N = %d exceeds the %d rows the static argmax scratch covers", N,
+                NA_MAX_ROWS);
+  int rc;
+  if ((rc = gemv_args_ok(w, N, K))) return rc;
+  cudaError_t e = enqueue_gemv_argmax_noalloc(y, argmax, w, s, x, N, K, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(nullptr, QWEN_ERR_CUDA, "gemv_i8_f32_argmax_noalloc: %s", cudaGetErrorString(e));
   return QWEN_OK;
 }
 
