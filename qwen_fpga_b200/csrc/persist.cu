@@ -54,6 +54,14 @@ constexpr int PH_HEAD = NLAYER * 5;
 constexpr int MAXP = (KMAX / 2 + PT - 1) / PT;  // tagged pairs per thread in a full-vector wait (4)
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s bound on any wait
 
+// IN and GATEUP on the tensor cores (tiles) or on the CUDA cores (row chunks).
+// A tile phase gives one CTA a whole 128 KB tile; with one tile per CTA the
+// single-thread MMA issue (four MMAs + a commit per 16 KB slab, ~700 cycles)
+// makes it no faster than the row chunks spread over every CTA, so the
+// layers use row chunks and only the head (13-14 tiles per CTA) uses tiles.
+constexpr bool kLayerTiles = false;
+
+
 // ---- shared memory layout (dynamic, offsets from the aligned base)
 constexpr int OFF_RING = 0;
 constexpr int OFF_DIG = OFF_RING + NSLOT * SLOT;          // int8 [3][KMAX]
@@ -64,7 +72,7 @@ constexpr int OFF_CH = OFF_LAY + ((int)sizeof(LayerW) * NLAYER + 15) / 16 * 16; 
 constexpr int OFF_BAR = OFF_CH + 8 * MAXCH;               // u64 mbarriers, see bar_* below
 constexpr int NBAR = 3 * NSLOT + 5;                       // full, empty, mma per slot; acc_full[2], acc_empty[2], fin
 constexpr int OFF_MISC = OFF_BAR + 8 * NBAR;              // small scalars
-// head phase: the x digits as the tensor-core B operand (16 rows x HID, canonical
+// tensor-core phases: the x digits as the B operand (16 rows x HID, canonical
 // K-major layout: rows 0-2 the digit planes, 3-15 zero; 8-row groups BT_SBO
 // bytes apart), over the digit planes and xf, which the head does not use
 constexpr int BT_SBO = (HID / 16) * 128;
@@ -77,10 +85,14 @@ static_assert(OFF_BAR % 8 == 0 && OFF_MISC % 8 == 0, "alignment");
 static_assert(MAXP * 2 * PT >= KMAX, "pair split");
 
 struct Misc {
-  unsigned tmem;           // tensor memory base (head accumulators), written by tcgen05.alloc
+  unsigned tmem;           // tensor memory base (accumulators), written by tcgen05.alloc
   unsigned pad_[3];
   float red[48];
   int pend_min;
+  int ntile;               // tensor-core tiles this CTA has issued so far in the step
+  unsigned mpar;           // refiller: per-slot parity of the next MMA-completion phase
+  int mma_any;             // the issuer has issued at least one MMA this launch
+  unsigned hs_tag;         // tag of the residual stream held in hs (0: none)
   double scale;
   int ndig;
   int abort;
@@ -279,9 +291,14 @@ __device__ __forceinline__ void chunk_src(const PCtx& c, const Chunk& k, const c
   const int row0 = (int)k.row0, n = k.nrows;
   src2 = nullptr;
   sc = sc2 = nullptr;
-  if (p == PH_HEAD) {   // one K-slab of a head tile; scales are read by the epilogue
-    if (row0 >= HEAD_TILES || n >= HEAD_NSLAB) { src = nullptr; bytes = 0; return; }
-    src = (const char*)c.A->head_tiles + ((size_t)row0 * HEAD_NSLAB + n) * SLOTW;
+  if (k.seg & CHUNK_MMA) {   // one K-slab of a tensor-core tile; row scales are read by the epilogue
+    const int8_t* base = nullptr;
+    int nt = 0;
+    if (p == PH_HEAD) { base = c.A->head_tiles; nt = HEAD_TILES; }
+    else if (p % 5 == 0) { base = c.lay[p / 5].in_tiles; nt = c.lay[p / 5].linear ? IN_TILES_LIN : IN_TILES_FULL; }
+    else if (p % 5 == 3) { base = c.lay[p / 5].gu_tiles; nt = GU_TILES; }
+    if (!base || row0 >= nt || n >= HEAD_NSLAB) { src = nullptr; bytes = 0; return; }
+    src = (const char*)base + ((size_t)row0 * HEAD_NSLAB + n) * SLOTW;
     bytes = SLOTW;
     return;
   }
@@ -392,7 +409,9 @@ __device__ bool wait_bar1(const PCtx& c, unsigned bar, unsigned parity, int site
   return true;
 }
 
-// Whole warp: bounded wait on an mbarrier phase.  Same result in every lane.
+// Whole warp: bounded wait on an mbarrier phase (every lane polls: when the
+// phase has completed, as it usually has, that is one probe per lane).  Same
+// result in every lane.
 __device__ __forceinline__ bool wait_bar_warp(PCtx& c, unsigned bar, unsigned parity, int site, int value) {
   int good = 1;
   if (!mbar_try(bar, parity)) {
@@ -562,8 +581,8 @@ __device__ __forceinline__ float pairwise_sumsq_1024(const float* hs) {
 // of np.mean(x**2), golden/model.py:74), then 1/rms, x = h * inv * (1 + w), the
 // digit image (the shift from an upper bound of max|x|) or, under ACT_INT8,
 // the golden quantiser with the exact max|x| (golden/model.py:37-45).  Digits
-// land in the shared planes, or (canon, W8A32 only) in the rows 0-2 of the
-// tensor-core B tile at OFF_BT with rows 3-7 zeroed; returns inv and
+// land in the shared planes, or (canon) in rows 0-2 (ACT_INT8: row 0) of the
+// tensor-core B tile at OFF_BT with the other rows zeroed; returns inv and
 // (ACT_INT8) s_x.  Two barriers (three under ACT_INT8).
 __device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2 g2, bool act_int8,
                                                 float& inv_out, float& sx_out, bool canon = false) {
@@ -606,7 +625,19 @@ __device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2
       q0 = (int)fminf(fmaxf(rintf(__fdiv_rn(x0, s)), -127.0f), 127.0f);
       q1 = (int)fminf(fmaxf(rintf(__fdiv_rn(x1, s)), -127.0f), 127.0f);
     }
-    reinterpret_cast<unsigned short*>(dg)[t] = (unsigned short)(((unsigned)q0 & 0xffu) | (((unsigned)q1 & 0xffu) << 8));
+    const unsigned short qq = (unsigned short)(((unsigned)q0 & 0xffu) | (((unsigned)q1 & 0xffu) << 8));
+    if (canon) {
+      // B tile: row 0 = the int8 activations, rows 1-15 zero
+      unsigned char* bt = c.sm + OFF_BT + ((2 * t) >> 4) * 128 + ((2 * t) & 15);
+      *reinterpret_cast<unsigned short*>(bt) = qq;
+#pragma unroll
+      for (int d = 1; d < 8; ++d) *reinterpret_cast<unsigned short*>(bt + 16 * d) = 0;
+#pragma unroll
+      for (int d = 0; d < 8; ++d) *reinterpret_cast<unsigned short*>(bt + BT_SBO + 16 * d) = 0;
+      fence_async_smem();
+    } else {
+      reinterpret_cast<unsigned short*>(dg)[t] = qq;
+    }
     if (t == 0) { ms->scale = (double)s; ms->ndig = 1; }
     sx_out = s;
   } else {
@@ -687,15 +718,76 @@ __device__ __forceinline__ float row_dot_f32_lane(const float* row, const float*
   return warp_sum(a);
 }
 
-// Prologue of the OUT (sub 2) and DOWN (sub 4) phases: wait for the inputs,
-// build xf, encode into the shared digit planes.  false on abort.
-__device__ bool prologue(PCtx& c, int p) {
+// Tagged words src[lo, hi) (any alignment, hi - lo <= HID) into dst[lo, hi)
+// once they carry `tag`.  Collective over the CTA.  false on abort.
+__device__ bool wait_tagged_range(PCtx& c, const unsigned long long* src, int lo, int hi, unsigned tag,
+                                  float* dst) {
+  const unsigned long long t0 = gtime();
+  constexpr int MW = (HID + PT - 1) / PT;
+  unsigned pend = 0;
+#pragma unroll
+  for (int j = 0; j < MW; ++j)
+    if (lo + (int)threadIdx.x + PT * j < hi) pend |= 1u << j;
+  int it = 0;
+  for (;;) {
+    unsigned long long w[MW];
+#pragma unroll
+    for (int j = 0; j < MW; ++j)
+      if (pend >> j & 1) w[j] = ld_tv(src + lo + threadIdx.x + PT * j);
+#pragma unroll
+    for (int j = 0; j < MW; ++j)
+      if ((pend >> j & 1) && tag_ok(w[j], tag)) {
+        dst[lo + threadIdx.x + PT * j] = tv_val(w[j]);
+        pend &= ~(1u << j);
+      }
+    if (consumer_and(pend == 0)) return true;
+    if (((++it) & 15) == 0) {
+      int bad = 0;
+      if (threadIdx.x == 0) {
+        if (aborted(c)) bad = 1;
+        else if (gtime() - t0 > WAIT_NS) { raise_abort(c, 22, (int)(tag & 127u)); bad = 1; }
+      }
+      if (!consumer_and(!bad)) return false;
+    }
+  }
+}
+
+// The residual stream rows [row0 of chunk i0, end of chunk i1 - 1) that an OUT
+// or DOWN phase adds its projection to (golden/model.py:259,263): h after the
+// previous residual add (tagged), or for layer 0's OUT the dequantised
+// embedding row (golden/model.py:246).  Into hs.
+__device__ bool load_residual(PCtx& c, int p, int i0, int i1) {
+  const PersistArgs& A = *c.A;
+  float* hs = (float*)(c.sm + OFF_HS);
+  const int lo = (int)c.ch[i0].row0, hi = (int)c.ch[i1 - 1].row0 + c.ch[i1 - 1].nrows;
+  if (lo < 0 || hi > HID || lo >= hi) {
+    if (threadIdx.x == 0) check_fail(c, 7, hi - lo);
+    return false;
+  }
+  const unsigned need = tag_of(c, p == 2 ? -1 : (p % 5 == 4 ? p - 2 : p - 3));
+  if (c.ms->hs_tag == need) return true;   // the previous GEMV phase left it in hs
+  if (p == 2) {
+    const int tok = c.ms->tok;
+    const float sc = __ldg(A.emb_s + tok);
+    const int8_t* row = A.emb_q + (size_t)tok * HID;
+    for (int i = lo + (int)threadIdx.x; i < hi; i += PT) hs[i] = __fmul_rn((float)row[i], sc);
+    consumer_sync();
+    return true;
+  }
+  // DOWN: h from OUT (p - 2); OUT of layer l >= 1: h from DOWN of layer l - 1 (p - 3)
+  return wait_tagged_range(c, A.tv_h, lo, hi, need, hs);
+}
+
+// Prologue of the OUT (sub 2) and DOWN (sub 4) phases: the residual rows, the
+// inputs into xf, encoded into the shared digit planes.  false on abort.
+__device__ bool prologue(PCtx& c, int p, int i0, int i1) {
   float* xf = (float*)(c.sm + OFF_XF);
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
   const bool i8 = ms->act_int8 != 0;
   const int l = p / 5, sub = p % 5;
   const LayerW& L = c.lay[l];
+  if (!load_residual(c, p, i0, i1)) return false;
   if (sub == 2) {
     if (L.linear) {
       // gated RMSNorm of the delta-rule output (golden/model.py:183-189):
@@ -844,106 +936,195 @@ __device__ void head_finish(PCtx& c, unsigned long long best) {
   }
 }
 
-// Head refiller (one thread): as soon as the MMAs that read head chunk q have
-// completed, its slot takes chunk q + NSLOT.  Runs beside the MMA issuer, so
-// the issuer never waits on an MMA completion.  1 = ok.
-__device__ int head_refill(PCtx& c, int h0, int h1) {
-  for (int q = h0; q + NSLOT < h1; ++q) {
+// ---------------------------------------------------------------- tensor-core phases
+//
+// IN and GATEUP (K = HID) and the tied head run on tcgen05.mma kind::i8.  A
+// CTA's tiles of the phase (128 weight rows x HID) stream through the ring as
+// 16 KB K-slabs.  Roles:
+//   warp NCW-1 lane 0  issues, per slab, four K = 32 MMAs (M = 128 rows of A =
+//                      the slab, N = 16 rows of B = the x digit planes) into
+//                      a double-buffered TMEM accumulator (columns 16 (T & 1)
+//                      .. +15, T = the CTA's running tile count of the step);
+//   warp NCW-2 lane 0  releases each slab once its MMAs have completed and
+//                      refills its slot (same empty-barrier protocol as the
+//                      CUDA-core phases, NCW arrivals at once);
+//   warps 0-3          epilogue: thread = TMEM lane = tile row, the three exact
+//                      digit sums recombined and scaled exactly as the CUDA-core
+//                      phases do (finish_f32), outputs written as tagged words.
+
+enum TileKind { TK_IN = 0, TK_GATEUP = 1, TK_HEAD = 2 };
+
+__device__ __forceinline__ void mbar_arrive_cnt(unsigned bar, unsigned cnt) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(cnt) : "memory");
+}
+// warps 0-3 only (named barrier 2)
+__device__ __forceinline__ void epi_sync() {
+  __syncwarp();
+  asm volatile("barrier.sync 2, 128;" ::: "memory");
+}
+__device__ __forceinline__ int epi_and(int v) {
+  int r;
+  __syncwarp();
+  asm volatile("{ .reg .pred p, q; setp.ne.s32 p, %1, 0; barrier.red.and.pred q, 2, 128, p; selp.s32 %0, 1, 0, q; }"
+               : "=r"(r) : "r"(v) : "memory");
+  return r;
+}
+
+// Refiller (one thread) over the phase's slabs [i0, i1): wait for the MMAs of
+// slab q (per-slot commit parity in *mpar), release its slot on the empty
+// barrier and issue chunk q + NSLOT into it.  1 = ok.
+__device__ int tile_refill(PCtx& c, int i0, int i1, unsigned& mpar) {
+  for (int q = i0; q < i1; ++q) {
     const int s = q % NSLOT;
-    if (!wait_bar1(c, mma_bar(c, s), (unsigned)(((q - h0) / NSLOT) & 1), 15, q - h0)) return 0;
-    issue_chunk(c, q + NSLOT);
-    c.ms->slot_last[s] = q + NSLOT;
+    if (!wait_bar1(c, mma_bar(c, s), (mpar >> s) & 1u, 15, q)) return 0;
+    mpar ^= 1u << s;
+    const int nx = q + NSLOT;
+    if (nx < c.nch) {
+      // a layer slab completes its slot's empty phase like a CUDA-core chunk
+      // does, so the parity of the chunks after it stays (i / NSLOT) & 1; a
+      // head slab has no CUDA-core chunk after it and skips the round trip
+      if (c.ch[q].phase != PH_HEAD) {
+        mbar_arrive_cnt(empty_bar(c, s), NCW);
+        if (!wait_bar1(c, empty_bar(c, s), (unsigned)((q / NSLOT) & 1), 10, q)) return 0;
+      }
+      issue_chunk(c, nx);
+      c.ms->slot_last[s] = nx;
+    }
   }
   return 1;
 }
 
-// MMA issuer of the head (one thread).  Local tile t accumulates in TMEM
-// columns 16 (t & 1) .. +15: per K-slab four K = 32 steps, M = 128 weight rows
-// (A, the ring slot) against N = 16 digit rows (B; only columns 0-2 of the
-// accumulator are read).  A tile's buffer is reused once the epilogue released
-// the tile two before it.  All MMAs have completed when this returns.  1 = ok.
-__device__ int head_mma(PCtx& c, int h0, int h1, unsigned tmem) {
+// MMA issuer (one thread) over the phase's slabs [i0, i1); T0 = tiles this CTA
+// issued earlier in the step.  A tile's buffer is reused once the epilogue
+// released the tile two before it.  1 = ok.
+__device__ int tile_mma(PCtx& c, int i0, int i1, unsigned tmem, int T0) {
   constexpr unsigned IDESC = umma_idesc_i8(HEAD_TM, 16);
   constexpr unsigned SBO_A = (HEAD_KS / 16) * 128;
   const unsigned bt = smem_u32(c.sm + OFF_BT);
   const unsigned s_lo = smem_u32(c.sm), s_hi = s_lo + SMEM_BYTES;
-  int good = 1;
-  bool any = false;
   // the accumulators: lane 0, two 16-column buffers inside the 512 columns
   if ((tmem >> 16) != 0u || (tmem & 0xffffu) > 512u - 32u) { check_fail(c, 2, (int)tmem); return 0; }
   if (bt < s_lo || bt + 2u * BT_SBO > s_hi) { check_fail(c, 4, (int)bt); return 0; }
-  for (int i = h0; i < h1; ++i) {
-    const int li = i - h0, t = li / HEAD_NSLAB, j = li % HEAD_NSLAB, b = t & 1;
+  if (i1 > i0) c.ms->mma_any = 1;
+  // descriptors: slot 0 / B tile at slab 0; a K = 32 step adds 256 B to both
+  const unsigned long long da0 = umma_desc(smem_u32(c.sm + OFF_RING), 128u, SBO_A);
+  const unsigned long long db0 = umma_desc(bt, 128u, (unsigned)BT_SBO);
+  for (int i = i0; i < i1; ++i) {
+    const int li = i - i0, t = T0 + li / HEAD_NSLAB, j = li % HEAD_NSLAB, b = t & 1;
     if (j == 0 && t >= 2) {
-      if (!wait_bar1(c, acce_bar(c, b), (unsigned)(((t - 2) >> 1) & 1), 13, t)) { good = 0; break; }
+      if (!wait_bar1(c, acce_bar(c, b), (unsigned)(((t - 2) >> 1) & 1), 13, t)) return 0;
       tc_fence_after();
     }
-    if (!wait_bar1(c, full_bar(c, i % NSLOT), (unsigned)((i / NSLOT) & 1), 14, li)) { good = 0; break; }
+    if (!wait_bar1(c, full_bar(c, i % NSLOT), (unsigned)((i / NSLOT) & 1), 14, i)) return 0;
     const unsigned a = smem_u32(c.sm + OFF_RING + (i % NSLOT) * SLOT);
-    if (a < s_lo || a + (unsigned)SLOTW > s_hi || (a & 127u)) { check_fail(c, 3, (int)a); good = 0; break; }
-#pragma unroll
-    for (int s = 0; s < HEAD_KS / 32; ++s)
-      umma_i8(tmem + 16u * b, umma_desc(a + 256u * s, 128u, SBO_A),
-              umma_desc(bt + (unsigned)((HEAD_KS / 16) * j + 2 * s) * 128u, 128u, (unsigned)BT_SBO), IDESC,
-              (unsigned)(j | s));
-    any = true;
+    if (a < s_lo || a + (unsigned)SLOTW > s_hi || (a & 127u)) { check_fail(c, 3, (int)a); return 0; }
+    // start-address fields are addr >> 4 in the low 14 bits (no carry: smem < 256 KB)
+    const unsigned long long da = da0 + (unsigned long long)(((i % NSLOT) * SLOT) >> 4);
+    const unsigned long long db = db0 + (unsigned long long)((HEAD_KS / 16) * j * 8);
+    const unsigned dt = tmem + 16u * b;
+    umma_i8(dt, da, db, IDESC, (unsigned)j);
+    umma_i8(dt, da + 16, db + 16, IDESC, 1u);
+    umma_i8(dt, da + 32, db + 32, IDESC, 1u);
+    umma_i8(dt, da + 48, db + 48, IDESC, 1u);
     umma_commit(mma_bar(c, i % NSLOT));
     if (j == HEAD_NSLAB - 1) umma_commit(accf_bar(c, b));
   }
-  if (any) {
-    umma_commit(fin_bar(c));
-    if (!wait_bar1(c, fin_bar(c), 0u, 16, h1 - h0)) good = 0;
-  }
-  return good;
+  return 1;
 }
 
-// Tied head on the tensor cores, logits = emb_q x (golden/model.py:266): the
-// CTA's head tiles stream through the ring as 16 KB K-slabs; warp NCW-1 lane 0
-// issues the MMAs (head_mma), warp NCW-2 lane 0 refills the slots they have
-// finished with (head_refill), warps 0-3 are the epilogue: thread = TMEM lane =
-// tile row, the three exact digit sums recombined and scaled as in the CUDA-core
-// phases, logits stored, argmax kept.  The input is encoded once into the B tile.
-__device__ bool phase_head(PCtx& c, int p, int h0, int h1) {
+// Output row of the epilogue thread for tile `tix` of an IN phase: destination
+// word, index and row scale.
+__device__ __forceinline__ void in_row_target(const PersistArgs& A, const LayerW& L, int row,
+                                              unsigned long long*& out, int& idx, const float*& sc) {
+  if (L.linear) {
+    if (row < CONVD) { out = A.tv_qkv; idx = row; sc = L.qkv_s + row; }
+    else { out = A.tv_z; idx = row - CONVD; sc = L.z_s + idx; }
+  } else {
+    if (row < QPROJ) { out = A.tv_qg; idx = row; sc = L.q_s + row; }
+    else if (row < QPROJ + KVPROJ) { out = A.tv_kvn; idx = row - QPROJ; sc = L.k_s + idx; }
+    else { out = A.tv_kvn + KVPROJ; idx = row - QPROJ - KVPROJ; sc = L.v_s + idx; }
+  }
+}
+
+// A tensor-core phase of this CTA: chunks [i0, i1) are its tiles' slabs (head:
+// possibly none, the argmax merge still needs every CTA).  Input: the residual
+// stream h (the dequantised embedding row for layer 0's IN), normed with the
+// phase's gains, encoded once into the B tile.
+__device__ bool phase_tiles(PCtx& c, int p, int i0, int i1) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
   float* hs = (float*)(c.sm + OFF_HS);
-  const float2 g2 = __ldg(reinterpret_cast<const float2*>(A.final_norm) + threadIdx.x);
-  if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) return false;
+  const bool head = (p == PH_HEAD);
+  const int kind = (head || !kLayerTiles) ? TK_HEAD : (p % 5 == 0 ? TK_IN : TK_GATEUP);
+  const int l = head ? 0 : p / 5;
+  const LayerW& L = c.lay[l];
+  const float* gw = head ? A.final_norm : (kind == TK_IN ? L.in_norm : L.post_norm);
+  const float2 g2 = __ldg(reinterpret_cast<const float2*>(gw) + threadIdx.x);
+  if (kind == TK_IN && l == 0) {
+    // residual stream starts at the dequantised embedding row (golden/model.py:246)
+    const int tok = ms->tok;
+    const float sc = __ldg(A.emb_s + tok);
+    const int8_t* row = A.emb_q + (size_t)tok * HID;
+    for (int i = threadIdx.x; i < HID; i += PT) hs[i] = __fmul_rn((float)row[i], sc);
+    consumer_sync();
+  } else if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) {
+    return false;
+  }
   float inv, sx;
-  cta_encode_1024(c, hs, g2, false, inv, sx, true);
+  const bool i8 = (!head) && ms->act_int8 != 0;
+  cta_encode_1024(c, hs, g2, i8, inv, sx, true);
+  if (threadIdx.x == 0) ms->hs_tag = 0;   // the GATEUP epilogue reuses hs
   trace_mark(c, p, 1);
   const float xsf = (float)ms->scale;
+  const int nd = ms->ndig;
+  const unsigned tag = tag_of(c, p);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int ntiles = (h1 - h0) / HEAD_NSLAB;
+  const int ntiles = (i1 - i0) / HEAD_NSLAB;
+  const int T0 = ms->ntile;
   const unsigned tmem = ms->tmem;
   const bool want = ms->want_logits != 0;
   unsigned long long best = 0ull;
   int good = 1;
-  if (h1 != c.nch || h0 >= h1 || (h1 - h0) % HEAD_NSLAB != 0 || c.ch[h0].phase != PH_HEAD) {
-    if (threadIdx.x == 0) check_fail(c, 1, h1 - h0);
+  if ((i1 - i0) % HEAD_NSLAB != 0 || (ntiles > 0 && !(c.ch[i0].seg & CHUNK_MMA))) {
+    if (threadIdx.x == 0) check_fail(c, 1, i1 - i0);
     good = 0;
   }
-  if (!good) {
+  float* ups = (float*)(c.sm + OFF_HS);   // [2][64] up values of a GATEUP tile (hs is consumed)
+  if (!good || ntiles == 0) {
   } else if (wid == NCW - 1) {
-    if (lane == 0) good = head_mma(c, h0, h1, tmem);
+    if (lane == 0) good = tile_mma(c, i0, i1, tmem, T0);
     __syncwarp();
   } else if (wid == NCW - 2) {
-    if (lane == 0) good = head_refill(c, h0, h1);
+    if (lane == 0) {
+      unsigned mpar = ms->mpar;
+      good = tile_refill(c, i0, i1, mpar);
+      ms->mpar = mpar;
+    }
     __syncwarp();
   } else if (wid < 4) {
-    for (int t = 0; t < ntiles; ++t) {
-      const int b = t & 1;
-      const int o = (int)c.ch[h0 + t * HEAD_NSLAB].row0 * HEAD_TM + 32 * wid + lane;
-      if (__any_sync(0xffffffffu, o < 0 || o >= VOCAB)) {
+    for (int tl = 0; tl < ntiles; ++tl) {
+      const int T = T0 + tl, b = T & 1;
+      const int tix = (int)c.ch[i0 + tl * HEAD_NSLAB].row0;
+      const int m = 32 * wid + lane;                       // tile row = TMEM lane
+      unsigned long long* out = nullptr;
+      int o = 0;
+      const float* scp;
+      if (kind == TK_HEAD) { o = tix * HEAD_TM + m; scp = A.emb_s + o; }
+      else if (kind == TK_IN) in_row_target(A, L, tix * HEAD_TM + m, out, o, scp);
+      else { o = tix * (HEAD_TM / 2) + (m & 63); scp = (m < 64 ? L.gate_s : L.up_s) + o; }
+      const bool bad = (kind == TK_HEAD) ? (o >= VOCAB) : (kind == TK_GATEUP ? (o >= FFN) : false);
+      if (__any_sync(0xffffffffu, bad)) {
         if (lane == 0) check_fail(c, 6, o);
         good = 0;
-        break;
       }
-      const float sw = __ldg(A.emb_s + o);
-      if (!wait_bar_warp(c, accf_bar(c, b), (unsigned)((t >> 1) & 1), 17, t)) { good = 0; break; }
-      if (t == 0) trace_mark(c, p, 2);
+      const float sw = bad ? 0.0f : __ldg(scp);
+      if (good && !wait_bar_warp(c, accf_bar(c, b), (unsigned)((T >> 1) & 1), 17, T)) good = 0;
+      // GATEUP's warps meet at a barrier below: they must leave the loop together
+      if (kind == TK_GATEUP) good = epi_and(good);
+      if (!good) break;
+      if (tl == 0) trace_mark(c, p, 2);
       tc_fence_after();
-      // this warp's 32 TMEM lanes (rows), columns 0-2 (the three digit sums)
+      // this warp's 32 TMEM lanes (rows), columns 0-2 (the digit sums)
       const unsigned ta = tmem + ((unsigned)(32 * wid) << 16) + 16u * b;
       unsigned r0, r1, r2;
       asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];"
@@ -953,13 +1134,23 @@ __device__ bool phase_head(PCtx& c, int p, int h0, int h1) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar(c, b));
-      const float y = finish_f32((int)r0, (int)r1, (int)r2, 3, xsf * sw);
-      if (want) A.logits[o] = y;
-      best = umax64(best, am_pack(y, o));
+      const float y = finish_f32((int)r0, (int)r1, (int)r2, nd, xsf * sw);
+      if (kind == TK_HEAD) {
+        if (want) A.logits[o] = y;
+        best = umax64(best, am_pack(y, o));
+      } else if (kind == TK_IN) {
+        st_tv(out + o, y, tag);
+      } else {
+        // silu(gate) * up: the up half of the tile (warps 2-3) hands its values over
+        if (wid >= 2) ups[64 * b + (m & 63)] = y;
+        epi_sync();
+        if (wid < 2) st_tv(A.tv_act + o, __fmul_rn(silu_f(y), ups[64 * b + m]), tag);
+      }
     }
   }
   if (!consumer_and(good)) return false;
-  head_finish(c, best);
+  if (threadIdx.x == 0) ms->ntile = T0 + ntiles;
+  if (head) head_finish(c, best);
   return true;
 }
 
@@ -986,6 +1177,7 @@ __device__ bool phase_1024(PCtx& c, int p, int i0, int i1) {
   } else if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) {
     return false;
   }
+  if (threadIdx.x == 0) ms->hs_tag = tag_of(c, p - 1);   // layer 0: the embedding (tag of "phase -1")
   float inv, sx;
   const bool i8 = ms->act_int8 != 0;
   cta_encode_1024(c, hs, g2, i8, inv, sx);
@@ -1474,6 +1666,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
       mbar_init(acce_bar(c, b), 4);
     }
     mbar_init(fin_bar(c), 1);
+    ms->ntile = 0;
+    ms->mpar = 0;
+    ms->mma_any = 0;
+    ms->hs_tag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -1524,11 +1720,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
       // this phase's chunks, [i0, i1) of the CTA's list (counted loops only)
       const int i0 = ms->pf[p], i1 = ms->pf[p + 1];
       if (p == PH_HEAD) {
-        ok = phase_head(c, p, i0, i1);
+        ok = phase_tiles(c, p, i0, i1);          // every CTA joins the argmax merge
+      } else if (i0 == i1) {                     // no rows of this phase on this CTA
+        trace_mark(c, p, 3);
+        continue;
       } else if (sub == 0 || sub == 3) {
-        ok = phase_1024(c, p, i0, i1);
+        if constexpr (kLayerTiles)
+          ok = (c.ch[i0].seg & CHUNK_MMA) ? phase_tiles(c, p, i0, i1) : phase_1024(c, p, i0, i1);
+        else
+          ok = phase_1024(c, p, i0, i1);
       } else {
-        if (!prologue(c, p)) { ok = false; break; }
+        if (!prologue(c, p, i0, i1)) { ok = false; break; }
         trace_mark(c, p, 1);
         ok = phase_wide(c, p, (sub == 2 ? VDIM : FFN) / 512, i0, i1);
       }
@@ -1539,8 +1741,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
     }
     if (!ok && threadIdx.x == 0) *(volatile int*)&ms->abort = 1;
   }
+  // every MMA the CTA issued has completed before its shared memory and tensor
+  // memory are released (on an abort path nobody else waited for them)
+  if (threadIdx.x == (NCW - 1) * 32 && ms->mma_any) {
+    umma_commit(fin_bar(c));
+    const unsigned long long t0 = gtime();
+    while (!mbar_try(fin_bar(c), 0u))
+      if (gtime() - t0 > WAIT_NS) { atomicCAS(A.err, 0, ERR_WAIT); break; }
+  }
   // drain: every bulk copy that was issued must land before the CTA exits
-  // (the head's MMAs have all completed: head_mma waits for them)
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -1569,43 +1778,73 @@ int persist_smem_bytes() { return SMEM_BYTES; }
 int persist_num_phases() { return NPHASE; }
 int persist_max_chunks() { return MAXCH; }
 
-// Build the per-CTA chunk lists: for every GEMV phase, its rows are split
-// into G contiguous byte-balanced ranges, each cut into <= SLOT-byte chunks
-// that never straddle a segment.
+bool persist_layer_tiles() { return kLayerTiles; }
+
+// Build the per-CTA chunk lists.
+//   IN, GATEUP with kLayerTiles: tensor-core tiles (8 slabs each), dealt
+//     round-robin over the CTAs from a base that advances phase to phase; the
+//     fp32 in_proj_a/b rows of a DeltaNet IN go to the CTAs after that phase's
+//     tile CTAs (4 rows per chunk, CUDA cores).
+//   Otherwise, and OUT, DOWN: rows split into G contiguous byte-balanced
+//     ranges, each cut into <= SLOTW-byte chunks that never straddle a
+//     segment (CUDA cores).
+//   HEAD: contiguous, balanced ranges of the 1940 tiles.
 bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
                     std::vector<unsigned short>& phase_first, std::string& err) {
   (void)M;
+  if (G < IN_TILES_LIN + 8) { err = "the persistent schedule needs at least 72 CTAs"; return false; }
   chunks.assign((size_t)G * MAXCH, Chunk{});
   phase_first.assign((size_t)G * (NPHASE + 1), 0);
   std::vector<int> counts(G, 0);
-  struct Seg { int rows; int rowbytes; int unit_rows; };
+  auto push = [&](int b, int p, int seg, int n, int row0) -> bool {
+    int& cnt = counts[b];
+    if (cnt >= MAXCH) { err = "chunk list overflow"; return false; }
+    Chunk& k = chunks[(size_t)b * MAXCH + cnt++];
+    k.phase = (unsigned short)p;
+    k.seg = (unsigned char)seg;
+    k.nrows = (unsigned char)n;
+    k.row0 = (unsigned)row0;
+    return true;
+  };
+  struct Seg { int rows; int rowbytes; };
+  int rr = 0;   // round-robin base of the tensor-core tiles
   for (int p = 0; p < NPHASE; ++p) {
     // every CTA's chunks of phase p start where its list stands now
     for (int b = 0; b < G; ++b) phase_first[(size_t)b * (NPHASE + 1) + p] = (unsigned short)counts[b];
-    Seg segs[4];
-    int nseg = 0;
-    auto add = [&](int rows, int rowbytes) { segs[nseg++] = Seg{rows, rowbytes, 1}; };
     const int sub = p % 5;
     if (p == PH_HEAD) {
       // whole tiles per CTA (a tile's K-slabs accumulate in one CTA's TMEM)
       for (int b = 0; b < G; ++b) {
         const int t0 = (int)((long long)HEAD_TILES * b / G), t1 = (int)((long long)HEAD_TILES * (b + 1) / G);
         for (int t = t0; t < t1; ++t)
-          for (int j = 0; j < HEAD_NSLAB; ++j) {
-            int& cnt = counts[b];
-            if (cnt >= MAXCH) { err = "chunk list overflow"; return false; }
-            Chunk& k = chunks[(size_t)b * MAXCH + cnt++];
-            k.phase = (unsigned short)p;
-            k.seg = 0;
-            k.nrows = (unsigned char)j;
-            k.row0 = (unsigned)t;
-          }
+          for (int j = 0; j < HEAD_NSLAB; ++j)
+            if (!push(b, p, CHUNK_MMA, j, t)) return false;
       }
       continue;
     }
     if (sub == 1) continue;
-    else if (sub == 0) {
-      const bool linear = (p / 5) % 4 != 3;
+    const bool linear = (p / 5) % 4 != 3;
+    if (kLayerTiles && (sub == 0 || sub == 3)) {
+      const int nt = sub == 3 ? GU_TILES : (linear ? IN_TILES_LIN : IN_TILES_FULL);
+      for (int t = 0; t < nt; ++t)
+        for (int j = 0; j < HEAD_NSLAB; ++j)
+          if (!push((rr + t) % G, p, CHUNK_MMA, j, t)) return false;
+      rr = (rr + nt) % G;
+      if (sub == 0 && linear) {
+        // in_proj_b (seg 2) and in_proj_a (seg 3): fp32 rows, 4 per chunk
+        constexpr int per = SLOTW / (HID * 4);
+        int k = 0;
+        for (int seg = 2; seg <= 3; ++seg)
+          for (int r = 0; r < LH; r += per, ++k)
+            if (!push((rr + k) % G, p, seg, per, r)) return false;
+        rr = (rr + k) % G;
+      }
+      continue;
+    }
+    Seg segs[4];
+    int nseg = 0;
+    auto add = [&](int rows, int rowbytes) { segs[nseg++] = Seg{rows, rowbytes}; };
+    if (sub == 0) {
       if (linear) { add(CONVD, HID); add(VDIM, HID); add(LH, HID * 4); add(LH, HID * 4); }
       else { add(QPROJ, HID); add(KVPROJ, HID); add(KVPROJ, HID); }
     } else if (sub == 2) add(HID, VDIM);
@@ -1616,30 +1855,43 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
     // walk the rows, assigning each to the CTA whose byte window holds its start
     long long off = 0;
     for (int si = 0; si < nseg; ++si) {
-      const Seg& s = segs[si];
-      const int per_chunk = SLOTW / s.rowbytes;
+      const Seg& sg = segs[si];
+      const int per_chunk = SLOTW / sg.rowbytes;
       int r = 0;
-      while (r < s.rows) {
+      while (r < sg.rows) {
         const int cta = (int)std::min<long long>(G - 1, (off * G) / total);
         // rows of this segment that start inside cta's window
         const long long win_end = ((long long)(cta + 1) * total + G - 1) / G;
         int n = 0;
-        while (r + n < s.rows && n < per_chunk && off + (long long)n * s.rowbytes < win_end) ++n;
+        while (r + n < sg.rows && n < per_chunk && off + (long long)n * sg.rowbytes < win_end) ++n;
         if (n == 0) n = 1;
-        int& cnt = counts[cta];
-        if (cnt >= MAXCH) { err = "chunk list overflow"; return false; }
-        Chunk& k = chunks[(size_t)cta * MAXCH + cnt++];
-        k.phase = (unsigned short)p;
-        k.seg = (unsigned char)si;
-        k.nrows = (unsigned char)n;
-        k.row0 = (unsigned)r;
+        if (!push(cta, p, si, n, r)) return false;
         r += n;
-        off += (long long)n * s.rowbytes;
+        off += (long long)n * sg.rowbytes;
       }
     }
   }
   for (int b = 0; b < G; ++b) phase_first[(size_t)b * (NPHASE + 1) + NPHASE] = (unsigned short)counts[b];
   return true;
+}
+
+// Re-tile rows: thread = one 16-byte K-group of one row.
+__global__ void k_repack_rows(const int8_t* const* __restrict__ rowptr, int4* __restrict__ out, int nrows) {
+  const size_t id = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (id >= (size_t)nrows * (HID / 16)) return;
+  const int g = (int)(id % (HID / 16));        // 16-byte group along K
+  const size_t row = id / (HID / 16);
+  const size_t t = row / HEAD_TM;
+  const int m = (int)(row % HEAD_TM), j = g / (HEAD_KS / 16), kg = g % (HEAD_KS / 16);
+  const int4 v = reinterpret_cast<const int4*>(rowptr[row])[g];
+  out[((t * HEAD_NSLAB + j) * (HEAD_TM * HEAD_KS) + ((m >> 3) * (HEAD_KS / 16) + kg) * 128 + (m & 7) * 16) / 16] = v;
+}
+
+cudaError_t repack_rows_tiles(const int8_t* const* rowptr, int8_t* out, int nrows, cudaStream_t st) {
+  if (nrows % HEAD_TM || ((uintptr_t)out & 15)) return cudaErrorInvalidValue;
+  const size_t n = (size_t)nrows * (HID / 16);
+  k_repack_rows<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rowptr, reinterpret_cast<int4*>(out), nrows);
+  return cudaGetLastError();
 }
 
 // One 16-byte core-matrix row per thread: tile t, slab j, row m, K-group g.

@@ -10,8 +10,9 @@
 namespace qb {
 
 // One weight chunk of a CTA's schedule: nrows rows (or (gate, up) row pairs)
-// of segment `seg` of phase `phase`, starting at row0.  Head chunks are one
-// K-slab of a head tile instead: row0 = tile index, nrows = slab index.
+// of segment `seg` of phase `phase`, starting at row0.  A tensor-core chunk
+// (seg has CHUNK_MMA set) is one K-slab of a tile instead: row0 = tile index
+// within the phase, nrows = slab index.
 struct Chunk {
   unsigned short phase;
   unsigned char seg;
@@ -19,6 +20,7 @@ struct Chunk {
   unsigned row0;
 };
 static_assert(sizeof(Chunk) == 8, "Chunk layout");
+constexpr unsigned char CHUNK_MMA = 0x80;
 
 // Phases of one decode step: 5 per layer (IN, MIX, OUT, GATEUP, DOWN) + the head.
 constexpr int PERSIST_NPHASE = NLAYER * 5 + 1;
@@ -61,6 +63,20 @@ static_assert(VOCAB % HEAD_TM == 0 && HID % HEAD_KS == 0, "head tiling");
 constexpr size_t HEAD_TILE_BYTES = (size_t)VOCAB * HID;
 cudaError_t repack_head_tiles(const int8_t* emb_q, int8_t* tiles, cudaStream_t st);
 
+// Layer GEMVs with K = HID on the tensor cores, same tile format as the head:
+// IN of a DeltaNet layer = [qkv | z] rows (64 tiles), IN of an attention layer =
+// [q | k | v] rows (40 tiles), GATEUP = 56 tiles of (64 gate rows, 64 up rows).
+constexpr int IN_TILES_LIN = (CONVD + VDIM) / HEAD_TM;
+constexpr int IN_TILES_FULL = (QPROJ + 2 * KVPROJ) / HEAD_TM;
+constexpr int GU_TILES = FFN / (HEAD_TM / 2);
+constexpr size_t TILE_BYTES = (size_t)HEAD_TM * HID;
+static_assert((CONVD + VDIM) % HEAD_TM == 0 && (QPROJ + 2 * KVPROJ) % HEAD_TM == 0 &&
+              FFN % (HEAD_TM / 2) == 0, "layer tiling");
+// Re-tile nrows (a multiple of HEAD_TM) rows of HID int8 each: row r of the
+// output tile sequence is read from rowptr[r] (device pointers, device array).
+cudaError_t repack_rows_tiles(const int8_t* const* rowptr, int8_t* out, int nrows, cudaStream_t st);
+
+bool persist_layer_tiles();   // IN / GATEUP scheduled as tensor-core tiles
 int persist_smem_bytes();
 int persist_num_phases();
 int persist_max_chunks();

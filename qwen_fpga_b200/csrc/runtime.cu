@@ -578,6 +578,47 @@ int qwen_create(const char* blob_path, const char* index_path, int n_gpus, const
       if (e != cudaSuccess) { fail(c, QWEN_ERR_CUDA, "head repack: %s", cudaGetErrorString(e)); return bail(QWEN_ERR_CUDA); }
       P.head_tiles = tiles;
     }
+    if (persist_layer_tiles()) {
+      // IN and GATEUP weights of every layer re-tiled for the tensor cores
+      // (second copies; the row-major tensors still serve engine 0)
+      std::vector<const int8_t*> rows;
+      std::vector<size_t> in_off(NLAYER), gu_off(NLAYER);
+      for (int l = 0; l < NLAYER; ++l) {
+        const LayerW& L = c->Mh.L[l];
+        in_off[l] = rows.size();
+        if (L.linear) {
+          for (int r = 0; r < CONVD; ++r) rows.push_back(L.qkv_q + (size_t)r * HID);
+          for (int r = 0; r < VDIM; ++r) rows.push_back(L.z_q + (size_t)r * HID);
+        } else {
+          for (int r = 0; r < QPROJ; ++r) rows.push_back(L.q_q + (size_t)r * HID);
+          for (int r = 0; r < KVPROJ; ++r) rows.push_back(L.k_q + (size_t)r * HID);
+          for (int r = 0; r < KVPROJ; ++r) rows.push_back(L.v_q + (size_t)r * HID);
+        }
+        gu_off[l] = rows.size();
+        for (int u = 0; u < GU_TILES; ++u) {   // tile u: gate rows 64u.., then up rows 64u..
+          for (int m = 0; m < HEAD_TM / 2; ++m) rows.push_back(L.gate_q + (size_t)(u * (HEAD_TM / 2) + m) * HID);
+          for (int m = 0; m < HEAD_TM / 2; ++m) rows.push_back(L.up_q + (size_t)(u * (HEAD_TM / 2) + m) * HID);
+        }
+      }
+      int8_t* lt = nullptr;
+      const int8_t** drows = nullptr;
+      if ((rc = dalloc(c, &lt, rows.size() * (size_t)HID))) return bail(rc);
+      if (cudaMalloc((void**)&drows, rows.size() * sizeof(void*)) != cudaSuccess) {
+        fail(c, QWEN_ERR_CUDA, "layer tile row table");
+        return bail(QWEN_ERR_CUDA);
+      }
+      cudaError_t e = cudaMemcpy(drows, rows.data(), rows.size() * sizeof(void*), cudaMemcpyHostToDevice);
+      if (e == cudaSuccess) e = repack_rows_tiles(drows, lt, (int)rows.size(), c->st);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);
+      cudaFree(drows);
+      if (e != cudaSuccess) { fail(c, QWEN_ERR_CUDA, "layer repack: %s", cudaGetErrorString(e)); return bail(QWEN_ERR_CUDA); }
+      for (int l = 0; l < NLAYER; ++l) {
+        c->Mh.L[l].in_tiles = lt + in_off[l] * HID;
+        c->Mh.L[l].gu_tiles = lt + gu_off[l] * HID;
+      }
+      e = cudaMemcpy(c->Md, &c->Mh, sizeof(ModelW), cudaMemcpyHostToDevice);
+      if (e != cudaSuccess) { fail(c, QWEN_ERR_CUDA, "model table upload: %s", cudaGetErrorString(e)); return bail(QWEN_ERR_CUDA); }
+    }
     P.final_norm = c->Mh.final_norm;
     P.conv = S.conv; P.rec = S.rec; P.kcache = S.kcache; P.vcache = S.vcache;
     P.att_part = S.att_part;
