@@ -80,13 +80,13 @@ struct LayerW {
   const int8_t* gate_q; const float* gate_s; // [3584,1024]
   const int8_t* up_q;   const float* up_s;   // [3584,1024]
   const int8_t* down_q; const float* down_s; // [1024,3584]
-  // copies re-tiled for the tensor cores (persistent engine; null until built):
-  // in_tiles: the K = 1024 input projections ([qkv | z] or [q | k | v]) as
-  // 128-row tiles; gu_tiles: 56 tiles, tile u = gate rows 64u..64u+63 then up
-  // rows 64u..64u+63.  Each tile is 8 K-slabs of 16 KB in the canonical K-major
-  // no-swizzle layout (persist.cuh).
-  const int8_t* in_tiles;
-  const int8_t* gu_tiles;
+  // panel copies for the persistent engine (layout in persist.cuh; null until
+  // built): pin = the input projections [qkv | z] or [q | k | v]; pout =
+  // out_proj / o_proj; pgu = (gate, up) pair panels; pdown = down_proj
+  const int8_t* pin;
+  const int8_t* pout;
+  const int8_t* pgu;
+  const int8_t* pdown;
 };
 
 struct ModelW {

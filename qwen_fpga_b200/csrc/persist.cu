@@ -54,12 +54,6 @@ constexpr int PH_HEAD = NLAYER * 5;
 constexpr int MAXP = (KMAX / 2 + PT - 1) / PT;  // tagged pairs per thread in a full-vector wait (4)
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s bound on any wait
 
-// IN and GATEUP on the tensor cores (tiles) or on the CUDA cores (row chunks).
-// A tile phase gives one CTA a whole 128 KB tile; with one tile per CTA the
-// single-thread MMA issue (four MMAs + a commit per 16 KB slab, ~700 cycles)
-// makes it no faster than the row chunks spread over every CTA, so the
-// layers use row chunks and only the head (13-14 tiles per CTA) uses tiles.
-constexpr bool kLayerTiles = false;
 
 
 // ---- shared memory layout (dynamic, offsets from the aligned base)
@@ -291,14 +285,24 @@ __device__ __forceinline__ void chunk_src(const PCtx& c, const Chunk& k, const c
   const int row0 = (int)k.row0, n = k.nrows;
   src2 = nullptr;
   sc = sc2 = nullptr;
-  if (k.seg & CHUNK_MMA) {   // one K-slab of a tensor-core tile; row scales are read by the epilogue
+  if (k.seg & CHUNK_PANEL) {   // one K-slice of a panel; row scales are read at the end of the phase
+    const LayerW& L = c.lay[p / 5];
+    const int sub = p % 5;
     const int8_t* base = nullptr;
-    int nt = 0;
-    if (p == PH_HEAD) { base = c.A->head_tiles; nt = HEAD_TILES; }
-    else if (p % 5 == 0) { base = c.lay[p / 5].in_tiles; nt = c.lay[p / 5].linear ? IN_TILES_LIN : IN_TILES_FULL; }
-    else if (p % 5 == 3) { base = c.lay[p / 5].gu_tiles; nt = GU_TILES; }
-    if (!base || row0 >= nt || n >= HEAD_NSLAB) { src = nullptr; bytes = 0; return; }
-    src = (const char*)base + ((size_t)row0 * HEAD_NSLAB + n) * SLOTW;
+    int np = 0;
+    size_t pbytes = 0;
+    if (sub == 0) { base = L.pin; np = (L.linear ? CONVD + VDIM : QPROJ + 2 * KVPROJ) / PANEL; pbytes = (size_t)PANEL * HID; }
+    else if (sub == 2) { base = L.pout; np = HID / PANEL; pbytes = (size_t)PANEL * VDIM; }
+    else if (sub == 3) { base = L.pgu; np = FFN / PANEL; pbytes = (size_t)2 * PANEL * HID; }
+    else if (sub == 4) { base = L.pdown; np = HID / PANEL; pbytes = (size_t)PANEL * FFN; }
+    if (!base || row0 >= np || (size_t)(n + 1) * SLOTW > pbytes) { src = nullptr; bytes = 0; return; }
+    src = (const char*)base + (size_t)row0 * pbytes + (size_t)n * SLOTW;
+    bytes = SLOTW;
+    return;
+  }
+  if (k.seg & CHUNK_MMA) {   // one K-slab of a head tile; row scales are read by the epilogue
+    if (p != PH_HEAD || row0 >= HEAD_TILES || n >= HEAD_NSLAB) { src = nullptr; bytes = 0; return; }
+    src = (const char*)c.A->head_tiles + ((size_t)row0 * HEAD_NSLAB + n) * SLOTW;
     bytes = SLOTW;
     return;
   }
@@ -718,76 +722,38 @@ __device__ __forceinline__ float row_dot_f32_lane(const float* row, const float*
   return warp_sum(a);
 }
 
-// Tagged words src[lo, hi) (any alignment, hi - lo <= HID) into dst[lo, hi)
-// once they carry `tag`.  Collective over the CTA.  false on abort.
-__device__ bool wait_tagged_range(PCtx& c, const unsigned long long* src, int lo, int hi, unsigned tag,
-                                  float* dst) {
-  const unsigned long long t0 = gtime();
-  constexpr int MW = (HID + PT - 1) / PT;
-  unsigned pend = 0;
-#pragma unroll
-  for (int j = 0; j < MW; ++j)
-    if (lo + (int)threadIdx.x + PT * j < hi) pend |= 1u << j;
-  int it = 0;
-  for (;;) {
-    unsigned long long w[MW];
-#pragma unroll
-    for (int j = 0; j < MW; ++j)
-      if (pend >> j & 1) w[j] = ld_tv(src + lo + threadIdx.x + PT * j);
-#pragma unroll
-    for (int j = 0; j < MW; ++j)
-      if ((pend >> j & 1) && tag_ok(w[j], tag)) {
-        dst[lo + threadIdx.x + PT * j] = tv_val(w[j]);
-        pend &= ~(1u << j);
-      }
-    if (consumer_and(pend == 0)) return true;
-    if (((++it) & 15) == 0) {
-      int bad = 0;
-      if (threadIdx.x == 0) {
-        if (aborted(c)) bad = 1;
-        else if (gtime() - t0 > WAIT_NS) { raise_abort(c, 22, (int)(tag & 127u)); bad = 1; }
-      }
-      if (!consumer_and(!bad)) return false;
-    }
-  }
-}
-
-// The residual stream rows [row0 of chunk i0, end of chunk i1 - 1) that an OUT
-// or DOWN phase adds its projection to (golden/model.py:259,263): h after the
-// previous residual add (tagged), or for layer 0's OUT the dequantised
-// embedding row (golden/model.py:246).  Into hs.
-__device__ bool load_residual(PCtx& c, int p, int i0, int i1) {
+// The residual stream that an OUT or DOWN phase adds its projection to
+// (golden/model.py:259,263): h after the previous residual add (tagged), or for
+// layer 0's OUT the dequantised embedding row (golden/model.py:246).  Into hs,
+// unless hs holds it already.
+__device__ bool load_residual(PCtx& c, int p) {
   const PersistArgs& A = *c.A;
   float* hs = (float*)(c.sm + OFF_HS);
-  const int lo = (int)c.ch[i0].row0, hi = (int)c.ch[i1 - 1].row0 + c.ch[i1 - 1].nrows;
-  if (lo < 0 || hi > HID || lo >= hi) {
-    if (threadIdx.x == 0) check_fail(c, 7, hi - lo);
-    return false;
-  }
   const unsigned need = tag_of(c, p == 2 ? -1 : (p % 5 == 4 ? p - 2 : p - 3));
-  if (c.ms->hs_tag == need) return true;   // the previous GEMV phase left it in hs
+  if (c.ms->hs_tag == need) return true;   // the previous phase of this CTA left it in hs
   if (p == 2) {
     const int tok = c.ms->tok;
     const float sc = __ldg(A.emb_s + tok);
     const int8_t* row = A.emb_q + (size_t)tok * HID;
-    for (int i = lo + (int)threadIdx.x; i < hi; i += PT) hs[i] = __fmul_rn((float)row[i], sc);
+    for (int i = threadIdx.x; i < HID; i += PT) hs[i] = __fmul_rn((float)row[i], sc);
     consumer_sync();
-    return true;
+  } else if (!wait_tagged(c, A.tv_h, HID, need, hs)) {
+    return false;
   }
-  // DOWN: h from OUT (p - 2); OUT of layer l >= 1: h from DOWN of layer l - 1 (p - 3)
-  return wait_tagged_range(c, A.tv_h, lo, hi, need, hs);
+  if (threadIdx.x == 0) c.ms->hs_tag = need;
+  return true;
 }
 
 // Prologue of the OUT (sub 2) and DOWN (sub 4) phases: the residual rows, the
 // inputs into xf, encoded into the shared digit planes.  false on abort.
-__device__ bool prologue(PCtx& c, int p, int i0, int i1) {
+__device__ bool prologue(PCtx& c, int p) {
   float* xf = (float*)(c.sm + OFF_XF);
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
   const bool i8 = ms->act_int8 != 0;
   const int l = p / 5, sub = p % 5;
   const LayerW& L = c.lay[l];
-  if (!load_residual(c, p, i0, i1)) return false;
+  if (!load_residual(c, p)) return false;
   if (sub == 2) {
     if (L.linear) {
       // gated RMSNorm of the delta-rule output (golden/model.py:183-189):
@@ -936,38 +902,22 @@ __device__ void head_finish(PCtx& c, unsigned long long best) {
   }
 }
 
-// ---------------------------------------------------------------- tensor-core phases
+// ---------------------------------------------------------------- tensor-core head
 //
-// IN and GATEUP (K = HID) and the tied head run on tcgen05.mma kind::i8.  A
-// CTA's tiles of the phase (128 weight rows x HID) stream through the ring as
-// 16 KB K-slabs.  Roles:
+// The tied head (248320 x HID) runs on tcgen05.mma kind::i8.  A CTA's head
+// tiles (128 embedding rows x HID) stream through the ring as 16 KB K-slabs.
+// Roles:
 //   warp NCW-1 lane 0  issues, per slab, four K = 32 MMAs (M = 128 rows of A =
 //                      the slab, N = 16 rows of B = the x digit planes) into
 //                      a double-buffered TMEM accumulator (columns 16 (T & 1)
-//                      .. +15, T = the CTA's running tile count of the step);
-//   warp NCW-2 lane 0  releases each slab once its MMAs have completed and
-//                      refills its slot (same empty-barrier protocol as the
-//                      CUDA-core phases, NCW arrivals at once);
+//                      .. +15, T = the CTA's running tile count);
+//   warp NCW-2 lane 0  refills each slab's slot once its MMAs have completed;
 //   warps 0-3          epilogue: thread = TMEM lane = tile row, the three exact
 //                      digit sums recombined and scaled exactly as the CUDA-core
-//                      phases do (finish_f32), outputs written as tagged words.
-
-enum TileKind { TK_IN = 0, TK_GATEUP = 1, TK_HEAD = 2 };
+//                      GEMVs do (finish_f32), logits stored, argmax kept.
 
 __device__ __forceinline__ void mbar_arrive_cnt(unsigned bar, unsigned cnt) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(cnt) : "memory");
-}
-// warps 0-3 only (named barrier 2)
-__device__ __forceinline__ void epi_sync() {
-  __syncwarp();
-  asm volatile("barrier.sync 2, 128;" ::: "memory");
-}
-__device__ __forceinline__ int epi_and(int v) {
-  int r;
-  __syncwarp();
-  asm volatile("{ .reg .pred p, q; setp.ne.s32 p, %1, 0; barrier.red.and.pred q, 2, 128, p; selp.s32 %0, 1, 0, q; }"
-               : "=r"(r) : "r"(v) : "memory");
-  return r;
 }
 
 // Refiller (one thread) over the phase's slabs [i0, i1): wait for the MMAs of
@@ -980,13 +930,8 @@ __device__ int tile_refill(PCtx& c, int i0, int i1, unsigned& mpar) {
     mpar ^= 1u << s;
     const int nx = q + NSLOT;
     if (nx < c.nch) {
-      // a layer slab completes its slot's empty phase like a CUDA-core chunk
-      // does, so the parity of the chunks after it stays (i / NSLOT) & 1; a
-      // head slab has no CUDA-core chunk after it and skips the round trip
-      if (c.ch[q].phase != PH_HEAD) {
-        mbar_arrive_cnt(empty_bar(c, s), NCW);
-        if (!wait_bar1(c, empty_bar(c, s), (unsigned)((q / NSLOT) & 1), 10, q)) return 0;
-      }
+      // (the head is the last phase: no chunk after it waits on the slot's
+      // empty barrier, so the refill goes out as soon as the MMAs are done)
       issue_chunk(c, nx);
       c.ms->slot_last[s] = nx;
     }
@@ -1046,38 +991,20 @@ __device__ __forceinline__ void in_row_target(const PersistArgs& A, const LayerW
   }
 }
 
-// A tensor-core phase of this CTA: chunks [i0, i1) are its tiles' slabs (head:
-// possibly none, the argmax merge still needs every CTA).  Input: the residual
-// stream h (the dequantised embedding row for layer 0's IN), normed with the
-// phase's gains, encoded once into the B tile.
-__device__ bool phase_tiles(PCtx& c, int p, int i0, int i1) {
+// The tied head on the tensor cores: chunks [i0, i1) are this CTA's head tile
+// slabs (possibly none: the argmax merge still needs every CTA).  Input: the
+// residual stream after the last layer, final-normed, encoded once into the B
+// tile.
+__device__ bool phase_head(PCtx& c, int p, int i0, int i1) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
   float* hs = (float*)(c.sm + OFF_HS);
-  const bool head = (p == PH_HEAD);
-  const int kind = (head || !kLayerTiles) ? TK_HEAD : (p % 5 == 0 ? TK_IN : TK_GATEUP);
-  const int l = head ? 0 : p / 5;
-  const LayerW& L = c.lay[l];
-  const float* gw = head ? A.final_norm : (kind == TK_IN ? L.in_norm : L.post_norm);
-  const float2 g2 = __ldg(reinterpret_cast<const float2*>(gw) + threadIdx.x);
-  if (kind == TK_IN && l == 0) {
-    // residual stream starts at the dequantised embedding row (golden/model.py:246)
-    const int tok = ms->tok;
-    const float sc = __ldg(A.emb_s + tok);
-    const int8_t* row = A.emb_q + (size_t)tok * HID;
-    for (int i = threadIdx.x; i < HID; i += PT) hs[i] = __fmul_rn((float)row[i], sc);
-    consumer_sync();
-  } else if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) {
-    return false;
-  }
+  const float2 g2 = __ldg(reinterpret_cast<const float2*>(A.final_norm) + threadIdx.x);
+  if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) return false;
   float inv, sx;
-  const bool i8 = (!head) && ms->act_int8 != 0;
-  cta_encode_1024(c, hs, g2, i8, inv, sx, true);
-  if (threadIdx.x == 0) ms->hs_tag = 0;   // the GATEUP epilogue reuses hs
+  cta_encode_1024(c, hs, g2, false, inv, sx, true);
   trace_mark(c, p, 1);
   const float xsf = (float)ms->scale;
-  const int nd = ms->ndig;
-  const unsigned tag = tag_of(c, p);
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int ntiles = (i1 - i0) / HEAD_NSLAB;
   const int T0 = ms->ntile;
@@ -1089,7 +1016,6 @@ __device__ bool phase_tiles(PCtx& c, int p, int i0, int i1) {
     if (threadIdx.x == 0) check_fail(c, 1, i1 - i0);
     good = 0;
   }
-  float* ups = (float*)(c.sm + OFF_HS);   // [2][64] up values of a GATEUP tile (hs is consumed)
   if (!good || ntiles == 0) {
   } else if (wid == NCW - 1) {
     if (lane == 0) good = tile_mma(c, i0, i1, tmem, T0);
@@ -1104,24 +1030,14 @@ __device__ bool phase_tiles(PCtx& c, int p, int i0, int i1) {
   } else if (wid < 4) {
     for (int tl = 0; tl < ntiles; ++tl) {
       const int T = T0 + tl, b = T & 1;
-      const int tix = (int)c.ch[i0 + tl * HEAD_NSLAB].row0;
-      const int m = 32 * wid + lane;                       // tile row = TMEM lane
-      unsigned long long* out = nullptr;
-      int o = 0;
-      const float* scp;
-      if (kind == TK_HEAD) { o = tix * HEAD_TM + m; scp = A.emb_s + o; }
-      else if (kind == TK_IN) in_row_target(A, L, tix * HEAD_TM + m, out, o, scp);
-      else { o = tix * (HEAD_TM / 2) + (m & 63); scp = (m < 64 ? L.gate_s : L.up_s) + o; }
-      const bool bad = (kind == TK_HEAD) ? (o >= VOCAB) : (kind == TK_GATEUP ? (o >= FFN) : false);
-      if (__any_sync(0xffffffffu, bad)) {
+      const int o = (int)c.ch[i0 + tl * HEAD_NSLAB].row0 * HEAD_TM + 32 * wid + lane;   // TMEM lane = tile row
+      if (__any_sync(0xffffffffu, o >= VOCAB)) {
         if (lane == 0) check_fail(c, 6, o);
         good = 0;
+        break;
       }
-      const float sw = bad ? 0.0f : __ldg(scp);
-      if (good && !wait_bar_warp(c, accf_bar(c, b), (unsigned)((T >> 1) & 1), 17, T)) good = 0;
-      // GATEUP's warps meet at a barrier below: they must leave the loop together
-      if (kind == TK_GATEUP) good = epi_and(good);
-      if (!good) break;
+      const float sw = __ldg(A.emb_s + o);
+      if (!wait_bar_warp(c, accf_bar(c, b), (unsigned)((T >> 1) & 1), 17, T)) { good = 0; break; }
       if (tl == 0) trace_mark(c, p, 2);
       tc_fence_after();
       // this warp's 32 TMEM lanes (rows), columns 0-2 (the digit sums)
@@ -1134,23 +1050,249 @@ __device__ bool phase_tiles(PCtx& c, int p, int i0, int i1) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acce_bar(c, b));
-      const float y = finish_f32((int)r0, (int)r1, (int)r2, nd, xsf * sw);
-      if (kind == TK_HEAD) {
-        if (want) A.logits[o] = y;
-        best = umax64(best, am_pack(y, o));
-      } else if (kind == TK_IN) {
-        st_tv(out + o, y, tag);
-      } else {
-        // silu(gate) * up: the up half of the tile (warps 2-3) hands its values over
-        if (wid >= 2) ups[64 * b + (m & 63)] = y;
-        epi_sync();
-        if (wid < 2) st_tv(A.tv_act + o, __fmul_rn(silu_f(y), ups[64 * b + m]), tag);
-      }
+      const float y = finish_f32((int)r0, (int)r1, (int)r2, 3, xsf * sw);
+      if (want) A.logits[o] = y;
+      best = umax64(best, am_pack(y, o));
     }
   }
   if (!consumer_and(good)) return false;
-  if (threadIdx.x == 0) ms->ntile = T0 + ntiles;
-  if (head) head_finish(c, best);
+  if (threadIdx.x == 0) { ms->ntile = T0 + ntiles; ms->hs_tag = 0; }
+  head_finish(c, best);
+  return true;
+}
+
+// ---------------------------------------------------------------- panel GEMVs
+
+// Digit sums of the 32 rows of one plain panel chunk (lane = row), K offset k0
+// of the digit planes: per 16-byte K-group one conflict-free 16-byte load of
+// the lane's row and one broadcast load per digit plane.  Exact int32.
+template <int ND>
+__device__ __forceinline__ void panel_dot(const unsigned char* slot, const int8_t* dg, int k0, int (&sum)[3]) {
+  const int lane = threadIdx.x & 31;
+  const int4* w = reinterpret_cast<const int4*>(slot) + lane;
+  int a[ND][2];
+#pragma unroll
+  for (int d = 0; d < ND; ++d) a[d][0] = a[d][1] = 0;
+#pragma unroll 8
+  for (int g = 0; g < PANEL_KB / 16; ++g) {
+    const int4 wv = w[g * PANEL];
+#pragma unroll
+    for (int d = 0; d < ND; ++d) {
+      const int4 x = *reinterpret_cast<const int4*>(dg + d * KMAX + k0 + 16 * g);
+      int& acc = a[d][g & 1];
+      acc = __dp4a(wv.x, x.x, acc);
+      acc = __dp4a(wv.y, x.y, acc);
+      acc = __dp4a(wv.z, x.z, acc);
+      acc = __dp4a(wv.w, x.w, acc);
+    }
+  }
+  sum[0] = sum[1] = sum[2] = 0;
+#pragma unroll
+  for (int d = 0; d < ND; ++d) sum[d] = a[d][0] + a[d][1];
+}
+
+// Same for a pair chunk: 32 gate rows (first 8 KB) and the same 32 up rows.
+template <int ND>
+__device__ __forceinline__ void pair_dot(const unsigned char* slot, const int8_t* dg, int k0, int (&gs)[3],
+                                         int (&us)[3]) {
+  const int lane = threadIdx.x & 31;
+  const int4* wg = reinterpret_cast<const int4*>(slot) + lane;
+  const int4* wu = reinterpret_cast<const int4*>(slot + SLOTW / 2) + lane;
+  int ag[ND], au[ND];
+#pragma unroll
+  for (int d = 0; d < ND; ++d) ag[d] = au[d] = 0;
+#pragma unroll 8
+  for (int g = 0; g < PAIR_KB / 16; ++g) {
+    const int4 vg = wg[g * PANEL], vu = wu[g * PANEL];
+#pragma unroll
+    for (int d = 0; d < ND; ++d) {
+      const int4 x = *reinterpret_cast<const int4*>(dg + d * KMAX + k0 + 16 * g);
+      ag[d] = __dp4a(vg.x, x.x, ag[d]); au[d] = __dp4a(vu.x, x.x, au[d]);
+      ag[d] = __dp4a(vg.y, x.y, ag[d]); au[d] = __dp4a(vu.y, x.y, au[d]);
+      ag[d] = __dp4a(vg.z, x.z, ag[d]); au[d] = __dp4a(vu.z, x.z, au[d]);
+      ag[d] = __dp4a(vg.w, x.w, ag[d]); au[d] = __dp4a(vu.w, x.w, au[d]);
+    }
+  }
+  gs[0] = gs[1] = gs[2] = us[0] = us[1] = us[2] = 0;
+#pragma unroll
+  for (int d = 0; d < ND; ++d) { gs[d] = ag[d]; us[d] = au[d]; }
+}
+
+// A warp is done with panel chunk i (it alone read it): complete the slot's
+// empty phase for every warp at once and refill the slot itself.
+__device__ __forceinline__ void release_panel_chunk(PCtx& c, int i) {
+  const int s = i % NSLOT;
+  if ((threadIdx.x & 31) == 0) {
+    mbar_arrive_cnt(empty_bar(c, s), NCW);
+    const int nx = i + NSLOT;
+    if (nx < c.nch && wait_bar1(c, empty_bar(c, s), (unsigned)((i / NSLOT) & 1), 10, i) &&
+        !*(volatile int*)&c.ms->abort) {
+      issue_chunk(c, nx);
+      c.ms->slot_last[s] = nx;
+    }
+  }
+  __syncwarp();
+}
+
+// A GEMV phase over panels (IN, OUT, GATEUP, DOWN).  The input vector is
+// encoded once into the digit planes; chunk j of the phase goes to warp
+// j % NCW, which writes its rows' partial digit sums to shared memory; after a
+// CTA barrier, warp v % NCW adds the partials of the v-th panel in chunk order
+// (exact int32) and writes the panel's 32 outputs: the projection rows (IN),
+// silu(gate) * up (GATEUP, golden/model.py:236), or h + y (OUT, DOWN).
+__device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
+  const PersistArgs& A = *c.A;
+  Misc* ms = c.ms;
+  float* hs = (float*)(c.sm + OFF_HS);
+  const int l = p / 5, sub = p % 5;
+  const LayerW& L = c.lay[l];
+  const bool i8 = ms->act_int8 != 0;
+  const float* gw = sub == 0 ? L.in_norm : L.post_norm;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int nj = i1 - i0;
+  // the row scales of the panels this warp will finish, fetched before the
+  // input wait so that their latency hides behind it (lane = row)
+  constexpr int MPW = 2;
+  float scp_pre[MPW][2];
+  {
+    int v = 0;
+    for (int ja = 0; ja < nj; ++ja) {
+      const Chunk k = c.ch[i0 + ja];
+      if (!(k.seg & CHUNK_PANEL) || (ja > 0 && (c.ch[i0 + ja - 1].seg & CHUNK_PANEL) &&
+                                     c.ch[i0 + ja - 1].row0 == k.row0))
+        continue;
+      if (v % NCW == wid && v / NCW < MPW) {
+        const int r = (int)k.row0 * PANEL + lane;
+        const float* s0;
+        const float* s1 = nullptr;
+        if (sub == 0) {
+          if (L.linear) s0 = r < CONVD ? L.qkv_s + r : L.z_s + (r - CONVD);
+          else s0 = r < QPROJ ? L.q_s + r : (r < QPROJ + KVPROJ ? L.k_s + (r - QPROJ) : L.v_s + (r - QPROJ - KVPROJ));
+        } else if (sub == 3) { s0 = L.gate_s + r; s1 = L.up_s + r; }
+        else s0 = (sub == 2 ? (L.linear ? L.out_s : L.o_s) : L.down_s) + r;
+        scp_pre[v / NCW][0] = __ldg(s0);
+        scp_pre[v / NCW][1] = s1 ? __ldg(s1) : 0.0f;
+      }
+      ++v;
+    }
+  }
+  float inv = 0.0f, sx = 0.0f;
+  if (sub == 0 || sub == 3) {
+    const float2 g2 = __ldg(reinterpret_cast<const float2*>(gw) + threadIdx.x);
+    if (sub == 0 && l == 0) {
+      // residual stream starts at the dequantised embedding row (golden/model.py:246)
+      const int tok = ms->tok;
+      const float sc = __ldg(A.emb_s + tok);
+      const int8_t* row = A.emb_q + (size_t)tok * HID;
+      for (int i = threadIdx.x; i < HID; i += PT) hs[i] = __fmul_rn((float)row[i], sc);
+      consumer_sync();
+    } else if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) {
+      return false;
+    }
+    if (threadIdx.x == 0) ms->hs_tag = tag_of(c, p - 1);   // layer 0: the embedding (tag of "phase -1")
+    cta_encode_1024(c, hs, g2, i8, inv, sx);
+  } else if (!prologue(c, p)) {
+    return false;
+  }
+  trace_mark(c, p, 1);
+  const int8_t* dg = (const int8_t*)(c.sm + OFF_DIG);
+  int* part = (int*)(c.sm + OFF_XF);                     // [chunk][3 or 6][32] partial sums
+  const int nd = ms->ndig;
+  const float xsf = (float)ms->scale;
+  const unsigned tag = tag_of(c, p);
+  const bool pair = (sub == 3);
+  const int pw = pair ? 6 : 3;
+  int good = 1;
+  if (nj * pw * 32 * 4 > 4 * KMAX) {
+    if (threadIdx.x == 0) check_fail(c, 8, nj);
+    good = 0;
+  }
+  for (int j = wid; good && j < nj; j += NCW) {
+    const int i = i0 + j;
+    const Chunk k = c.ch[i];
+    const bool f32 = !(k.seg & CHUNK_PANEL);
+    if (f32 && !(sub == 0 && L.linear && k.seg >= 2)) { if (lane == 0) check_fail(c, 9, i); good = 0; break; }
+    if (!wait_full(c, i)) { good = 0; break; }
+    if (j == 0) trace_mark(c, p, 2);
+    const unsigned char* slot = c.sm + OFF_RING + (i % NSLOT) * SLOT;
+    int* pj = part + j * pw * 32;
+    if (f32) {
+      // in_proj_b / in_proj_a rows (fp32, golden/model.py:146-147), one warp
+      for (int r = 0; r < k.nrows; ++r) {
+        const float v = row_dot_f32_lane((const float*)slot + r * HID, hs, gw, inv, i8, sx);
+        if (lane == 0) st_tv(A.tv_ab + (k.seg == 2 ? 0 : LH) + (int)k.row0 + r, v, tag);
+      }
+    } else if (pair) {
+      int gs[3], us[3];
+      const int k0 = k.nrows * PAIR_KB;
+      if (nd == 3) pair_dot<3>(slot, dg, k0, gs, us);
+      else pair_dot<1>(slot, dg, k0, gs, us);
+#pragma unroll
+      for (int d = 0; d < 3; ++d) { pj[d * 32 + lane] = gs[d]; pj[(3 + d) * 32 + lane] = us[d]; }
+    } else {
+      int sm3[3];
+      const int k0 = k.nrows * PANEL_KB;
+      if (nd == 3) panel_dot<3>(slot, dg, k0, sm3);
+      else panel_dot<1>(slot, dg, k0, sm3);
+#pragma unroll
+      for (int d = 0; d < 3; ++d) pj[d * 32 + lane] = sm3[d];
+    }
+    // chunks beyond the ring's depth arrive only as slots free up: release now
+    if (nj > NSLOT) release_panel_chunk(c, i);
+  }
+  if (!consumer_and(good)) return false;
+  // panel v = the v-th run of consecutive chunks with the same panel index
+  int v = 0;
+  for (int ja = 0; ja < nj;) {
+    if (!(c.ch[i0 + ja].seg & CHUNK_PANEL)) { ++ja; continue; }   // fp32 rows: written above
+    const unsigned q = c.ch[i0 + ja].row0;
+    int jb = ja + 1;
+    while (jb < nj && (c.ch[i0 + jb].seg & CHUNK_PANEL) && c.ch[i0 + jb].row0 == q) ++jb;
+    if (v % NCW == wid) {
+      int t[6] = {0, 0, 0, 0, 0, 0};
+      for (int j = ja; j < jb; ++j)
+#pragma unroll
+        for (int e = 0; e < 6; ++e)
+          if (e < pw) t[e] += part[(j * pw + e) * 32 + lane];
+      const int r = (int)q * PANEL + lane;
+      // row scales: prefetched for this warp's first MPW panels
+      float sa = 0.0f, sb = 0.0f;
+      const int u = v / NCW;
+#pragma unroll
+      for (int e = 0; e < MPW; ++e)
+        if (e == u) { sa = scp_pre[e][0]; sb = scp_pre[e][1]; }
+      if (sub == 0) {
+        unsigned long long* out;
+        int o;
+        const float* scp;
+        if (L.linear) {
+          if (r < CONVD) { out = A.tv_qkv; o = r; scp = L.qkv_s + r; }
+          else { out = A.tv_z; o = r - CONVD; scp = L.z_s + o; }
+        } else {
+          if (r < QPROJ) { out = A.tv_qg; o = r; scp = L.q_s + r; }
+          else if (r < QPROJ + KVPROJ) { out = A.tv_kvn; o = r - QPROJ; scp = L.k_s + o; }
+          else { out = A.tv_kvn + KVPROJ; o = r - QPROJ - KVPROJ; scp = L.v_s + o; }
+        }
+        if (u >= MPW) sa = __ldg(scp);
+        st_tv(out + o, finish_f32(t[0], t[1], t[2], nd, xsf * sa), tag);
+      } else if (sub == 3) {
+        if (u >= MPW) { sa = __ldg(L.gate_s + r); sb = __ldg(L.up_s + r); }
+        const float g = finish_f32(t[0], t[1], t[2], nd, xsf * sa);
+        const float uu = finish_f32(t[3], t[4], t[5], nd, xsf * sb);
+        st_tv(A.tv_act + r, __fmul_rn(silu_f(g), uu), tag);
+      } else {
+        if (u >= MPW) sa = __ldg((sub == 2 ? (L.linear ? L.out_s : L.o_s) : L.down_s) + r);
+        const float y = finish_f32(t[0], t[1], t[2], nd, xsf * sa);
+        st_tv(A.tv_h + r, __fadd_rn(hs[r], y), tag);
+      }
+    }
+    ++v;
+    ja = jb;
+  }
+  // the outputs are out: now give the slots back and refill them (off the
+  // phase's critical path; the schedule keeps a phase within the ring's depth)
+  if (nj <= NSLOT)
+    for (int j = wid; j < nj; j += NCW) release_panel_chunk(c, i0 + j);
   return true;
 }
 
@@ -1720,19 +1862,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
       // this phase's chunks, [i0, i1) of the CTA's list (counted loops only)
       const int i0 = ms->pf[p], i1 = ms->pf[p + 1];
       if (p == PH_HEAD) {
-        ok = phase_tiles(c, p, i0, i1);          // every CTA joins the argmax merge
+        ok = phase_head(c, p, i0, i1);           // every CTA joins the argmax merge
       } else if (i0 == i1) {                     // no rows of this phase on this CTA
         trace_mark(c, p, 3);
         continue;
-      } else if (sub == 0 || sub == 3) {
-        if constexpr (kLayerTiles)
-          ok = (c.ch[i0].seg & CHUNK_MMA) ? phase_tiles(c, p, i0, i1) : phase_1024(c, p, i0, i1);
-        else
-          ok = phase_1024(c, p, i0, i1);
       } else {
-        if (!prologue(c, p, i0, i1)) { ok = false; break; }
-        trace_mark(c, p, 1);
-        ok = phase_wide(c, p, (sub == 2 ? VDIM : FFN) / 512, i0, i1);
+        ok = phase_panels(c, p, i0, i1);
       }
       // the warps leave a GEMV phase independently; line them up again (and
       // make a failure in any warp the whole CTA's)
@@ -1778,24 +1913,21 @@ int persist_smem_bytes() { return SMEM_BYTES; }
 int persist_num_phases() { return NPHASE; }
 int persist_max_chunks() { return MAXCH; }
 
-bool persist_layer_tiles() { return kLayerTiles; }
 
 // Build the per-CTA chunk lists.
-//   IN, GATEUP with kLayerTiles: tensor-core tiles (8 slabs each), dealt
-//     round-robin over the CTAs from a base that advances phase to phase; the
-//     fp32 in_proj_a/b rows of a DeltaNet IN go to the CTAs after that phase's
-//     tile CTAs (4 rows per chunk, CUDA cores).
-//   Otherwise, and OUT, DOWN: rows split into G contiguous byte-balanced
-//     ranges, each cut into <= SLOTW-byte chunks that never straddle a
-//     segment (CUDA cores).
+//   IN, OUT, GATEUP, DOWN: whole panels (32 rows; all of a panel's K-slices on
+//     one CTA), each given to the CTA with the fewest bytes so far in the step
+//     (ties: lowest index); the fp32 in_proj_a/b rows of a DeltaNet IN go, 4 rows
+//     per chunk, to the least-loaded CTAs too.
 //   HEAD: contiguous, balanced ranges of the 1940 tiles.
 bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
                     std::vector<unsigned short>& phase_first, std::string& err) {
   (void)M;
-  if (G < IN_TILES_LIN + 8) { err = "the persistent schedule needs at least 72 CTAs"; return false; }
+  if (G < 1) { err = "no CTAs"; return false; }
   chunks.assign((size_t)G * MAXCH, Chunk{});
   phase_first.assign((size_t)G * (NPHASE + 1), 0);
   std::vector<int> counts(G, 0);
+  std::vector<long long> load(G, 0);
   auto push = [&](int b, int p, int seg, int n, int row0) -> bool {
     int& cnt = counts[b];
     if (cnt >= MAXCH) { err = "chunk list overflow"; return false; }
@@ -1804,10 +1936,9 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
     k.seg = (unsigned char)seg;
     k.nrows = (unsigned char)n;
     k.row0 = (unsigned)row0;
+    load[b] += SLOTW;
     return true;
   };
-  struct Seg { int rows; int rowbytes; };
-  int rr = 0;   // round-robin base of the tensor-core tiles
   for (int p = 0; p < NPHASE; ++p) {
     // every CTA's chunks of phase p start where its list stands now
     for (int b = 0; b < G; ++b) phase_first[(size_t)b * (NPHASE + 1) + p] = (unsigned short)counts[b];
@@ -1824,74 +1955,39 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
     }
     if (sub == 1) continue;
     const bool linear = (p / 5) % 4 != 3;
-    if (kLayerTiles && (sub == 0 || sub == 3)) {
-      const int nt = sub == 3 ? GU_TILES : (linear ? IN_TILES_LIN : IN_TILES_FULL);
-      for (int t = 0; t < nt; ++t)
-        for (int j = 0; j < HEAD_NSLAB; ++j)
-          if (!push((rr + t) % G, p, CHUNK_MMA, j, t)) return false;
-      rr = (rr + nt) % G;
-      if (sub == 0 && linear) {
-        // in_proj_b (seg 2) and in_proj_a (seg 3): fp32 rows, 4 per chunk
-        constexpr int per = SLOTW / (HID * 4);
-        int k = 0;
-        for (int seg = 2; seg <= 3; ++seg)
-          for (int r = 0; r < LH; r += per, ++k)
-            if (!push((rr + k) % G, p, seg, per, r)) return false;
-        rr = (rr + k) % G;
-      }
-      continue;
+    int npan, nslice;
+    if (sub == 0) { npan = (linear ? CONVD + VDIM : QPROJ + 2 * KVPROJ) / PANEL; nslice = HID / PANEL_KB; }
+    else if (sub == 2) { npan = HID / PANEL; nslice = VDIM / PANEL_KB; }
+    else if (sub == 3) { npan = FFN / PANEL; nslice = HID / PAIR_KB; }
+    else { npan = HID / PANEL; nslice = FFN / PANEL_KB; }
+    std::vector<int> inph(G, 0);   // chunks of this phase per CTA: at most NSLOT (all resident at once)
+    auto least_fit = [&](int need) {
+      int best = -1;
+      for (int b = 0; b < G; ++b)
+        if (inph[b] + need <= NSLOT && (best < 0 || load[b] < load[best])) best = b;
+      return best;
+    };
+    for (int q = 0; q < npan; ++q) {
+      const int b = least_fit(nslice);
+      if (b < 0) { err = "phase does not fit the rings"; return false; }
+      inph[b] += nslice;
+      for (int j = 0; j < nslice; ++j)
+        if (!push(b, p, CHUNK_PANEL, j, q)) return false;
     }
-    Seg segs[4];
-    int nseg = 0;
-    auto add = [&](int rows, int rowbytes) { segs[nseg++] = Seg{rows, rowbytes}; };
-    if (sub == 0) {
-      if (linear) { add(CONVD, HID); add(VDIM, HID); add(LH, HID * 4); add(LH, HID * 4); }
-      else { add(QPROJ, HID); add(KVPROJ, HID); add(KVPROJ, HID); }
-    } else if (sub == 2) add(HID, VDIM);
-    else if (sub == 3) add(FFN, 2 * HID);   // a unit = one (gate, up) row pair
-    else add(HID, FFN);
-    long long total = 0;
-    for (int si = 0; si < nseg; ++si) total += (long long)segs[si].rows * segs[si].rowbytes;
-    // walk the rows, assigning each to the CTA whose byte window holds its start
-    long long off = 0;
-    for (int si = 0; si < nseg; ++si) {
-      const Seg& sg = segs[si];
-      const int per_chunk = SLOTW / sg.rowbytes;
-      int r = 0;
-      while (r < sg.rows) {
-        const int cta = (int)std::min<long long>(G - 1, (off * G) / total);
-        // rows of this segment that start inside cta's window
-        const long long win_end = ((long long)(cta + 1) * total + G - 1) / G;
-        int n = 0;
-        while (r + n < sg.rows && n < per_chunk && off + (long long)n * sg.rowbytes < win_end) ++n;
-        if (n == 0) n = 1;
-        if (!push(cta, p, si, n, r)) return false;
-        r += n;
-        off += (long long)n * sg.rowbytes;
-      }
+    if (sub == 0 && linear) {
+      // in_proj_b (seg 2) and in_proj_a (seg 3): fp32 rows, 4 per chunk
+      constexpr int per = SLOTW / (HID * 4);
+      for (int seg = 2; seg <= 3; ++seg)
+        for (int r = 0; r < LH; r += per) {
+          const int b = least_fit(1);
+          if (b < 0) { err = "phase does not fit the rings"; return false; }
+          inph[b] += 1;
+          if (!push(b, p, seg, per, r)) return false;
+        }
     }
   }
   for (int b = 0; b < G; ++b) phase_first[(size_t)b * (NPHASE + 1) + NPHASE] = (unsigned short)counts[b];
   return true;
-}
-
-// Re-tile rows: thread = one 16-byte K-group of one row.
-__global__ void k_repack_rows(const int8_t* const* __restrict__ rowptr, int4* __restrict__ out, int nrows) {
-  const size_t id = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (id >= (size_t)nrows * (HID / 16)) return;
-  const int g = (int)(id % (HID / 16));        // 16-byte group along K
-  const size_t row = id / (HID / 16);
-  const size_t t = row / HEAD_TM;
-  const int m = (int)(row % HEAD_TM), j = g / (HEAD_KS / 16), kg = g % (HEAD_KS / 16);
-  const int4 v = reinterpret_cast<const int4*>(rowptr[row])[g];
-  out[((t * HEAD_NSLAB + j) * (HEAD_TM * HEAD_KS) + ((m >> 3) * (HEAD_KS / 16) + kg) * 128 + (m & 7) * 16) / 16] = v;
-}
-
-cudaError_t repack_rows_tiles(const int8_t* const* rowptr, int8_t* out, int nrows, cudaStream_t st) {
-  if (nrows % HEAD_TM || ((uintptr_t)out & 15)) return cudaErrorInvalidValue;
-  const size_t n = (size_t)nrows * (HID / 16);
-  k_repack_rows<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rowptr, reinterpret_cast<int4*>(out), nrows);
-  return cudaGetLastError();
 }
 
 // One 16-byte core-matrix row per thread: tile t, slab j, row m, K-group g.
@@ -1912,6 +2008,40 @@ cudaError_t repack_head_tiles(const int8_t* emb_q, int8_t* tiles, cudaStream_t s
   const size_t n = (size_t)VOCAB * (HID / 16);
   k_repack_head<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(reinterpret_cast<const int4*>(emb_q),
                                                           reinterpret_cast<int4*>(tiles));
+  return cudaGetLastError();
+}
+
+// Re-lay rows as panels: thread = one 16-byte K-group of one row.
+__global__ void k_repack_panels(const int8_t* const* __restrict__ rowptr, int4* __restrict__ out, int nrows,
+                                int K, int pair) {
+  const size_t id = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int G16 = K / 16;
+  if (id >= (size_t)nrows * G16) return;
+  const int g = (int)(id % G16);
+  const size_t r = id / G16;
+  const int4 v = reinterpret_cast<const int4*>(rowptr[r])[g];
+  size_t dst;
+  if (!pair) {
+    const size_t q = r / PANEL;
+    const int m = (int)(r % PANEL);
+    dst = q * PANEL * K + ((size_t)g * PANEL + m) * 16;
+  } else {   // pair panel q = rows (32 gate, 32 up); chunk s = K-groups 16s.. of gate then of up
+    const size_t q = r / (2 * PANEL);
+    const int half = (int)((r / PANEL) % 2), m = (int)(r % PANEL);
+    const int s = g / (PAIR_KB / 16), gg = g % (PAIR_KB / 16);
+    dst = q * 2 * PANEL * K + (size_t)s * SLOTW + (size_t)half * (SLOTW / 2) + ((size_t)gg * PANEL + m) * 16;
+  }
+  out[dst / 16] = v;
+}
+
+cudaError_t repack_panels(const int8_t* const* rowptr, int8_t* out, int nrows, int K, bool pair,
+                          cudaStream_t st) {
+  if (nrows % (pair ? 2 * PANEL : PANEL) || (!pair && K % PANEL_KB) || ((uintptr_t)out & 15) ||
+      (pair && K != HID))
+    return cudaErrorInvalidValue;
+  const size_t n = (size_t)nrows * (K / 16);
+  k_repack_panels<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rowptr, reinterpret_cast<int4*>(out), nrows,
+                                                             K, pair ? 1 : 0);
   return cudaGetLastError();
 }
 

@@ -63,20 +63,24 @@ static_assert(VOCAB % HEAD_TM == 0 && HID % HEAD_KS == 0, "head tiling");
 constexpr size_t HEAD_TILE_BYTES = (size_t)VOCAB * HID;
 cudaError_t repack_head_tiles(const int8_t* emb_q, int8_t* tiles, cudaStream_t st);
 
-// Layer GEMVs with K = HID on the tensor cores, same tile format as the head:
-// IN of a DeltaNet layer = [qkv | z] rows (64 tiles), IN of an attention layer =
-// [q | k | v] rows (40 tiles), GATEUP = 56 tiles of (64 gate rows, 64 up rows).
-constexpr int IN_TILES_LIN = (CONVD + VDIM) / HEAD_TM;
-constexpr int IN_TILES_FULL = (QPROJ + 2 * KVPROJ) / HEAD_TM;
-constexpr int GU_TILES = FFN / (HEAD_TM / 2);
-constexpr size_t TILE_BYTES = (size_t)HEAD_TM * HID;
-static_assert((CONVD + VDIM) % HEAD_TM == 0 && (QPROJ + 2 * KVPROJ) % HEAD_TM == 0 &&
-              FFN % (HEAD_TM / 2) == 0, "layer tiling");
-// Re-tile nrows (a multiple of HEAD_TM) rows of HID int8 each: row r of the
-// output tile sequence is read from rowptr[r] (device pointers, device array).
-cudaError_t repack_rows_tiles(const int8_t* const* rowptr, int8_t* out, int nrows, cudaStream_t st);
+// Layer GEMVs on the CUDA cores, lane per row: every projection is re-laid at
+// load time as panels of 32 rows; inside a panel, element (m, k) sits at
+// ((k / 16) * 32 + m) * 16 + k % 16, so one 16-byte K-group of all 32 rows is
+// 512 contiguous bytes (one conflict-free 16-byte load per lane).  A chunk is
+// 16 KB = the panel's 32 rows x 512 bytes of K.  GATEUP uses pair panels: 32
+// gate rows and the same 32 up rows; a chunk is 256 bytes of K of both (gate
+// half, then up half, 8 KB each).
+constexpr int PANEL = 32;
+constexpr int PANEL_KB = 512;                   // K bytes per chunk of a plain panel
+constexpr int PAIR_KB = 256;                    // K bytes per chunk of a pair panel
+constexpr unsigned char CHUNK_PANEL = 0x40;     // Chunk.seg flag: row0 = panel, nrows = K-slice
+static_assert(CONVD % PANEL == 0 && VDIM % PANEL == 0 && QPROJ % PANEL == 0 &&
+              KVPROJ % PANEL == 0 && HID % PANEL == 0 && FFN % PANEL == 0, "panels");
+// Re-lay nrows rows (row r read from rowptr[r], K bytes each) as panels; pair =
+// rows come as (32 gate rows, 32 up rows) per pair panel, K = HID.
+cudaError_t repack_panels(const int8_t* const* rowptr, int8_t* out, int nrows, int K, bool pair,
+                          cudaStream_t st);
 
-bool persist_layer_tiles();   // IN / GATEUP scheduled as tensor-core tiles
 int persist_smem_bytes();
 int persist_num_phases();
 int persist_max_chunks();

@@ -578,44 +578,49 @@ int qwen_create(const char* blob_path, const char* index_path, int n_gpus, const
       if (e != cudaSuccess) { fail(c, QWEN_ERR_CUDA, "head repack: %s", cudaGetErrorString(e)); return bail(QWEN_ERR_CUDA); }
       P.head_tiles = tiles;
     }
-    if (persist_layer_tiles()) {
-      // IN and GATEUP weights of every layer re-tiled for the tensor cores
-      // (second copies; the row-major tensors still serve engine 0)
-      std::vector<const int8_t*> rows;
-      std::vector<size_t> in_off(NLAYER), gu_off(NLAYER);
+    {
+      // every layer projection re-laid as 32-row panels for the persistent
+      // engine (second copies; the row-major tensors still serve engine 0)
+      struct Job { std::vector<const int8_t*> rows; int K; bool pair; const int8_t** slot; };
+      std::vector<Job> jobs;
       for (int l = 0; l < NLAYER; ++l) {
-        const LayerW& L = c->Mh.L[l];
-        in_off[l] = rows.size();
-        if (L.linear) {
-          for (int r = 0; r < CONVD; ++r) rows.push_back(L.qkv_q + (size_t)r * HID);
-          for (int r = 0; r < VDIM; ++r) rows.push_back(L.z_q + (size_t)r * HID);
-        } else {
-          for (int r = 0; r < QPROJ; ++r) rows.push_back(L.q_q + (size_t)r * HID);
-          for (int r = 0; r < KVPROJ; ++r) rows.push_back(L.k_q + (size_t)r * HID);
-          for (int r = 0; r < KVPROJ; ++r) rows.push_back(L.v_q + (size_t)r * HID);
+        LayerW& L = c->Mh.L[l];
+        Job in{{}, HID, false, &L.pin}, out{{}, VDIM, false, &L.pout}, gu{{}, HID, true, &L.pgu},
+            dn{{}, FFN, false, &L.pdown};
+        auto rows = [](std::vector<const int8_t*>& v, const int8_t* w, int n, int K) {
+          for (int r = 0; r < n; ++r) v.push_back(w + (size_t)r * K);
+        };
+        if (L.linear) { rows(in.rows, L.qkv_q, CONVD, HID); rows(in.rows, L.z_q, VDIM, HID); }
+        else { rows(in.rows, L.q_q, QPROJ, HID); rows(in.rows, L.k_q, KVPROJ, HID); rows(in.rows, L.v_q, KVPROJ, HID); }
+        rows(out.rows, L.linear ? L.out_q : L.o_q, HID, VDIM);
+        for (int q = 0; q < FFN / PANEL; ++q) {   // pair panel q: gate rows 32q.., then up rows 32q..
+          rows(gu.rows, L.gate_q + (size_t)q * PANEL * HID, PANEL, HID);
+          rows(gu.rows, L.up_q + (size_t)q * PANEL * HID, PANEL, HID);
         }
-        gu_off[l] = rows.size();
-        for (int u = 0; u < GU_TILES; ++u) {   // tile u: gate rows 64u.., then up rows 64u..
-          for (int m = 0; m < HEAD_TM / 2; ++m) rows.push_back(L.gate_q + (size_t)(u * (HEAD_TM / 2) + m) * HID);
-          for (int m = 0; m < HEAD_TM / 2; ++m) rows.push_back(L.up_q + (size_t)(u * (HEAD_TM / 2) + m) * HID);
-        }
+        rows(dn.rows, L.down_q, HID, FFN);
+        jobs.push_back(std::move(in)); jobs.push_back(std::move(out));
+        jobs.push_back(std::move(gu)); jobs.push_back(std::move(dn));
       }
-      int8_t* lt = nullptr;
+      size_t total = 0, maxrows = 0;
+      for (auto& j : jobs) { total += j.rows.size() * (size_t)j.K; maxrows = std::max(maxrows, j.rows.size()); }
+      int8_t* pbuf = nullptr;
       const int8_t** drows = nullptr;
-      if ((rc = dalloc(c, &lt, rows.size() * (size_t)HID))) return bail(rc);
-      if (cudaMalloc((void**)&drows, rows.size() * sizeof(void*)) != cudaSuccess) {
-        fail(c, QWEN_ERR_CUDA, "layer tile row table");
+      if ((rc = dalloc(c, &pbuf, total))) return bail(rc);
+      if (cudaMalloc((void**)&drows, maxrows * sizeof(void*)) != cudaSuccess) {
+        fail(c, QWEN_ERR_CUDA, "panel row table");
         return bail(QWEN_ERR_CUDA);
       }
-      cudaError_t e = cudaMemcpy(drows, rows.data(), rows.size() * sizeof(void*), cudaMemcpyHostToDevice);
-      if (e == cudaSuccess) e = repack_rows_tiles(drows, lt, (int)rows.size(), c->st);
-      if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);
-      cudaFree(drows);
-      if (e != cudaSuccess) { fail(c, QWEN_ERR_CUDA, "layer repack: %s", cudaGetErrorString(e)); return bail(QWEN_ERR_CUDA); }
-      for (int l = 0; l < NLAYER; ++l) {
-        c->Mh.L[l].in_tiles = lt + in_off[l] * HID;
-        c->Mh.L[l].gu_tiles = lt + gu_off[l] * HID;
+      cudaError_t e = cudaSuccess;
+      size_t off = 0;
+      for (auto& j : jobs) {
+        if (e == cudaSuccess) e = cudaMemcpy(drows, j.rows.data(), j.rows.size() * sizeof(void*), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = repack_panels(drows, pbuf + off, (int)j.rows.size(), j.K, j.pair, c->st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);   // the row table is reused
+        *j.slot = pbuf + off;
+        off += j.rows.size() * (size_t)j.K;
       }
+      cudaFree(drows);
+      if (e != cudaSuccess) { fail(c, QWEN_ERR_CUDA, "panel repack: %s", cudaGetErrorString(e)); return bail(QWEN_ERR_CUDA); }
       e = cudaMemcpy(c->Md, &c->Mh, sizeof(ModelW), cudaMemcpyHostToDevice);
       if (e != cudaSuccess) { fail(c, QWEN_ERR_CUDA, "model table upload: %s", cudaGetErrorString(e)); return bail(QWEN_ERR_CUDA); }
     }
