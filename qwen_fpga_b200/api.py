@@ -155,14 +155,15 @@ class Decoder:
 
     def trace_read(self):
         """Last step's per-CTA, per-phase stamps [entry, ready, first chunk, exit] (ns),
-        shape [n_ctas, n_phases, 4]."""
-        n = 160 * 121 * 4 + 4096
+        shape [n_ctas, n_phases, 4]; CTA 0's per-warp clock stamps land in
+        self.trace_warps, shape [n_phases, 16, 16]."""
+        n = 160 * 121 * 4 + 121 * 16 * 16
         buf = np.zeros(n, np.uint64)
         nc, npz = C.c_int(), C.c_int()
         _check(load().qwen_trace_read(self.h, buf.ctypes.data_as(C.POINTER(C.c_ulonglong)), n,
                                       C.byref(nc), C.byref(npz)), self.h)
         m = nc.value * npz.value * 4
-        self.trace_chunks = buf[m:m + 448 * 4].reshape(448, 4)
+        self.trace_warps = buf[m:m + npz.value * 16 * 16].reshape(npz.value, 16, 16)
         return buf[:m].reshape(nc.value, npz.value, 4)
 
     def reset(self):

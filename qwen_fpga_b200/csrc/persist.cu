@@ -46,7 +46,7 @@ constexpr int NCW = 16;                 // warps per CTA
 constexpr int PT = NCW * 32;            // threads per CTA
 constexpr int NTHREADS = PT;
 constexpr int SLOTW = 16384;            // weight bytes per ring slot
-constexpr int SLOT = SLOTW + 256;       // + row scales of the chunk (two arrays for gate/up)
+constexpr int SLOT = SLOTW;             // slot stride
 constexpr int NSLOT = 11;               // ring depth
 constexpr int MAXCH = 448;              // chunk-list capacity per CTA
 constexpr int NPHASE = PERSIST_NPHASE;  // 121
@@ -58,10 +58,12 @@ constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s bound on any wait
 
 // ---- shared memory layout (dynamic, offsets from the aligned base)
 constexpr int OFF_RING = 0;
-constexpr int OFF_DIG = OFF_RING + NSLOT * SLOT;          // int8 [3][KMAX]
+constexpr int OFF_DIG = OFF_RING + NSLOT * SLOT;          // digit image, 3 * KMAX bytes (see dig_off)
 constexpr int OFF_XF = OFF_DIG + 3 * KMAX;                // float [KMAX]
 constexpr int OFF_HS = OFF_XF + 4 * KMAX;                 // float [HID]
-constexpr int OFF_LAY = OFF_HS + 4 * HID;                 // LayerW [NLAYER]
+constexpr int MAXPAN = NSLOT;                             // panels of one phase on one CTA (at most)
+constexpr int OFF_PART = OFF_HS + 4 * HID;                // int [MAXPAN][6][PANEL] panel digit sums
+constexpr int OFF_LAY = OFF_PART + 4 * MAXPAN * 6 * PANEL; // LayerW [NLAYER]
 constexpr int OFF_CH = OFF_LAY + ((int)sizeof(LayerW) * NLAYER + 15) / 16 * 16;  // Chunk [MAXCH]
 constexpr int OFF_BAR = OFF_CH + 8 * MAXCH;               // u64 mbarriers, see bar_* below
 constexpr int NBAR = 3 * NSLOT + 5;                       // full, empty, mma per slot; acc_full[2], acc_empty[2], fin
@@ -242,11 +244,12 @@ __device__ __forceinline__ void trace_mark(const PCtx& c, int p, int k) {
   if (c.A->trace && threadIdx.x == 0)
     c.A->trace[((size_t)blockIdx.x * NPHASE + p) * TRACE_STAMPS + k] = gtime();
 }
-// per-chunk stamps of CTA 0, warp 0 (after the per-phase block): [chunk][4]
+// per-warp stamps of CTA 0 (after the per-phase block): [phase][warp][TRACE_WARP_STAMPS]
 // SM clock cycles (clock64), finer than the global timer
-__device__ __forceinline__ void trace_chunk(const PCtx& c, int i, int k) {
-  if (c.A->trace && blockIdx.x == 0 && threadIdx.x == 0)
-    c.A->trace[(size_t)gridDim.x * NPHASE * TRACE_STAMPS + (size_t)i * 4 + k] = clock64();
+__device__ __forceinline__ void trace_warp(const PCtx& c, int p, int k) {
+  if (c.A->trace && blockIdx.x == 0 && (threadIdx.x & 31) == 0)
+    c.A->trace[(size_t)gridDim.x * NPHASE * TRACE_STAMPS +
+               ((size_t)p * NCW + (threadIdx.x >> 5)) * TRACE_WARP_STAMPS + k] = clock64();
 }
 
 // A device-side bounds check failed: record the site and the offending value,
@@ -276,18 +279,24 @@ __device__ __forceinline__ bool aborted(const PCtx& c) {
   return *(volatile int*)&c.ms->abort || ld_flag(c.A->abort_flag);
 }
 
-// Sources of chunk k: weight rows (src, and src2 for the up rows of a
-// gate/up pair) and the row-scale arrays (sc, sc2; null for fp32 rows).
-__device__ __forceinline__ void chunk_src(const PCtx& c, const Chunk& k, const char*& src,
-                                          const char*& src2, unsigned& bytes, const float*& sc,
-                                          const float*& sc2) {
+// Source and size of chunk k: one K-slice of a layer panel, one K-slab of a
+// head tile, or (DeltaNet IN) nrows fp32 rows of in_proj_b (seg 2) or
+// in_proj_a (seg 3).  src = null for a chunk outside its matrix.
+__device__ __forceinline__ void chunk_src(const PCtx& c, const Chunk& k, const char*& src, unsigned& bytes) {
   const int p = k.phase;
   const int row0 = (int)k.row0, n = k.nrows;
-  src2 = nullptr;
-  sc = sc2 = nullptr;
-  if (k.seg & CHUNK_PANEL) {   // one K-slice of a panel; row scales are read at the end of the phase
-    const LayerW& L = c.lay[p / 5];
-    const int sub = p % 5;
+  src = nullptr;
+  bytes = 0;
+  if (k.seg & CHUNK_MMA) {   // row scales are read by the epilogue
+    if (p != PH_HEAD || row0 >= HEAD_TILES || n >= HEAD_NSLAB) return;
+    src = (const char*)c.A->head_tiles + ((size_t)row0 * HEAD_NSLAB + n) * SLOTW;
+    bytes = SLOTW;
+    return;
+  }
+  if (p >= PH_HEAD) return;
+  const LayerW& L = c.lay[p / 5];
+  const int sub = p % 5;
+  if (k.seg & CHUNK_PANEL) {   // row scales are read at the end of the phase
     const int8_t* base = nullptr;
     int np = 0;
     size_t pbytes = 0;
@@ -295,107 +304,28 @@ __device__ __forceinline__ void chunk_src(const PCtx& c, const Chunk& k, const c
     else if (sub == 2) { base = L.pout; np = HID / PANEL; pbytes = (size_t)PANEL * VDIM; }
     else if (sub == 3) { base = L.pgu; np = FFN / PANEL; pbytes = (size_t)2 * PANEL * HID; }
     else if (sub == 4) { base = L.pdown; np = HID / PANEL; pbytes = (size_t)PANEL * FFN; }
-    if (!base || row0 >= np || (size_t)(n + 1) * SLOTW > pbytes) { src = nullptr; bytes = 0; return; }
+    if (!base || row0 >= np || (size_t)n * SLOTW >= pbytes) return;
     src = (const char*)base + (size_t)row0 * pbytes + (size_t)n * SLOTW;
-    bytes = SLOTW;
+    const size_t rem = pbytes - (size_t)n * SLOTW;
+    bytes = rem < (size_t)SLOTW ? (unsigned)rem : (unsigned)SLOTW;
     return;
   }
-  if (k.seg & CHUNK_MMA) {   // one K-slab of a head tile; row scales are read by the epilogue
-    if (p != PH_HEAD || row0 >= HEAD_TILES || n >= HEAD_NSLAB) { src = nullptr; bytes = 0; return; }
-    src = (const char*)c.A->head_tiles + ((size_t)row0 * HEAD_NSLAB + n) * SLOTW;
-    bytes = SLOTW;
-    return;
-  }
-  const LayerW& L = c.lay[p / 5];
-  const int sub = p % 5;
-  if (sub == 0) {
-    if (L.linear) {
-      if (k.seg == 0) { src = (const char*)L.qkv_q + (size_t)row0 * HID; bytes = n * HID; sc = L.qkv_s; }
-      else if (k.seg == 1) { src = (const char*)L.z_q + (size_t)row0 * HID; bytes = n * HID; sc = L.z_s; }
-      else if (k.seg == 2) { src = (const char*)(L.b_w + (size_t)row0 * HID); bytes = n * HID * 4; }
-      else { src = (const char*)(L.a_w + (size_t)row0 * HID); bytes = n * HID * 4; }
-    } else {
-      if (k.seg == 0) { src = (const char*)L.q_q + (size_t)row0 * HID; sc = L.q_s; }
-      else if (k.seg == 1) { src = (const char*)L.k_q + (size_t)row0 * HID; sc = L.k_s; }
-      else { src = (const char*)L.v_q + (size_t)row0 * HID; sc = L.v_s; }
-      bytes = n * HID;
-    }
-  } else if (sub == 2) {
-    src = (const char*)(L.linear ? L.out_q : L.o_q) + (size_t)row0 * VDIM;
-    bytes = n * VDIM;
-    sc = L.linear ? L.out_s : L.o_s;
-  } else if (sub == 3) {
-    src = (const char*)L.gate_q + (size_t)row0 * HID;
-    src2 = (const char*)L.up_q + (size_t)row0 * HID;
-    bytes = n * HID;
-    sc = L.gate_s;
-    sc2 = L.up_s;
-  } else {
-    src = (const char*)L.down_q + (size_t)row0 * FFN;
-    bytes = n * FFN;
-    sc = L.down_s;
-  }
+  if (sub != 0 || !L.linear || k.seg < 2 || k.seg > 3 || row0 + n > LH || n * HID * 4 > SLOTW) return;
+  src = (const char*)((k.seg == 2 ? L.b_w : L.a_w) + (size_t)row0 * HID);
+  bytes = (unsigned)(n * HID * 4);
 }
 
-// Scales of rows [row0, row0+n) are copied from the 16-byte aligned start
-// row0 & ~3; row o's scale sits at tail[o - (row0 & ~3)] (second array at +32).
-__device__ __forceinline__ unsigned scale_bytes(int row0, int n) {
-  const int a = row0 & ~3, b = (row0 + n + 3) & ~3;
-  return (unsigned)(b - a) * 4u;
-}
-
-// Issue the bulk copies of chunk i into its slot (one lane).
+// Issue the bulk copy of chunk i into its slot (one lane).
 __device__ __forceinline__ void issue_chunk(const PCtx& c, int i) {
   const int slot = i % NSLOT;
   const Chunk k = c.ch[i];
   const char* src;
-  const char* src2;
   unsigned bytes;
-  const float* sc;
-  const float* sc2;
-  chunk_src(c, k, src, src2, bytes, sc, sc2);
+  chunk_src(c, k, src, bytes);
   if (!src) { check_fail(c, 5, (int)k.row0); return; }
   const unsigned bar = full_bar(c, slot);
-  const unsigned dst = smem_u32(c.sm + OFF_RING + slot * SLOT);
-  const unsigned sb = sc ? scale_bytes((int)k.row0, k.nrows) : 0u;
-  const unsigned total = (src2 ? 2 * bytes : bytes) + (sc ? sb : 0u) + (sc2 ? sb : 0u);
-  mbar_expect(bar, total);
-  bulk_g2s(dst, src, bytes, bar, c.pol);
-  if (src2) bulk_g2s(dst + bytes, src2, bytes, bar, c.pol);
-  const int a = (int)k.row0 & ~3;
-  if (sc) bulk_g2s(dst + SLOTW, sc + a, sb, bar, c.pol);
-  if (sc2) bulk_g2s(dst + SLOTW + 128, sc2 + a, sb, bar, c.pol);
-}
-
-// Warp done reading chunk i: arrive on the slot's `empty` barrier (lane 0,
-// non-blocking).  The slot's refill with chunk i + NSLOT is issued by warp
-// i % NCW once all NCW warps have arrived; that warp waits for the stragglers,
-// the others never wait here.
-__device__ __forceinline__ void release_slot(PCtx& c, int i) {
-  const int s = i % NSLOT;
-  const int lane = threadIdx.x & 31;
-  if (lane == 0) mbar_arrive(empty_bar(c, s));
-  if ((int)(threadIdx.x >> 5) != i % NCW) return;
-  const int nx = i + NSLOT;
-  if (nx >= c.nch) return;
-  if (lane == 0) {
-    const unsigned bar = empty_bar(c, s);
-    const unsigned parity = (unsigned)((i / NSLOT) & 1);
-    const unsigned long long t0 = gtime();
-    int it = 0;
-    bool good = true;
-    while (!mbar_try(bar, parity)) {
-      if (((++it) & 63) == 0) {
-        if (aborted(c)) { good = false; break; }
-        if (gtime() - t0 > WAIT_NS) { raise_abort(c, 10, i); good = false; break; }
-      }
-    }
-    if (good && !*(volatile int*)&c.ms->abort) {
-      issue_chunk(c, nx);
-      c.ms->slot_last[s] = nx;
-    }
-  }
-  __syncwarp();
+  mbar_expect(bar, bytes);
+  bulk_g2s(smem_u32(c.sm + OFF_RING + slot * SLOT), src, bytes, bar, c.pol);
 }
 
 // One thread: bounded wait for phase `parity` of an mbarrier.  false on abort
@@ -437,9 +367,12 @@ __device__ __forceinline__ bool wait_full(PCtx& c, int i) {
 
 // Poll tagged words src[0..n) (n even, n <= KMAX) until all carry `tag`; values
 // into dst (smem).  Each thread issues all its pending loads before checking
-// any.  Collective over the consumer threads.  false on abort.
-__device__ bool wait_tagged(PCtx& c, const unsigned long long* src, int n, unsigned tag,
-                                         float* dst) {
+// any.  Collective over the consumer threads.  false on abort.  One copy in
+// the kernel (not inlined): every phase's input wait runs the same
+// instructions.
+__device__ __noinline__ bool wait_tagged_words(Misc* ms, int* err, int* abort_flag,
+                                               const unsigned long long* src, int n, unsigned tag,
+                                               float* dst) {
   const unsigned long long t0 = gtime();
   const int npair = n >> 1;
   unsigned pend = 0;
@@ -465,15 +398,37 @@ __device__ bool wait_tagged(PCtx& c, const unsigned long long* src, int n, unsig
     if (((++it) & 15) == 0) {
       int bad = 0;
       if (threadIdx.x == 0) {
-        if (aborted(c)) bad = 1;
-        else if (gtime() - t0 > WAIT_NS) { raise_abort(c, 12, (int)(tag & 127u)); bad = 1; }
+        if (*(volatile int*)&ms->abort || ld_flag(abort_flag)) {
+          bad = 1;
+        } else if (gtime() - t0 > WAIT_NS) {
+          if (atomicCAS(err, 0, ERR_WAIT) == 0) {
+            err[1] = 12;
+            err[2] = (int)(tag & 127u);
+            err[3] = (int)blockIdx.x;
+          }
+          atomicExch(abort_flag, 1);
+          *(volatile int*)&ms->abort = 1;
+          bad = 1;
+        }
       }
       if (!consumer_and(!bad)) return false;
     }
   }
 }
+__device__ __forceinline__ bool wait_tagged(PCtx& c, const unsigned long long* src, int n, unsigned tag,
+                                            float* dst) {
+  return wait_tagged_words(c.ms, c.A->err, c.A->abort_flag, src, n, tag, dst);
+}
 
 // ---------------------------------------------------------------- prologues
+
+// The shared digit image of the GEMV input is kept in the B-fragment order of
+// mma.m16n8k32: K-step s (positions 32s .. 32s+31) is 96 bytes, 12 lanes x 8
+// bytes, lane 4d + u = digit d at positions 32s + 4u .. +3, then 32s + 16 + 4u
+// .. +3.  Byte offset of the 4 positions k .. k+3 (k a multiple of 4) of digit d:
+__device__ __forceinline__ int dig_off(int d, int k) {
+  return (k >> 5) * 96 + (d * 4 + ((k >> 2) & 3)) * 8 + ((k >> 4) & 1) * 4;
+}
 
 // Recombine the digit sums in fp32: (a2 * 65536 + a1 * 256 + a0) * (x_scale * s_w).
 // Two fp32 roundings instead of the graph engine's single fp64 one (|rel| < 2e-7).
@@ -486,12 +441,12 @@ __device__ __forceinline__ float finish_f32(int a0, int a1, int a2, int ndig, fl
 // 2^e as a float for -126 <= e <= 127.
 __device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
 
-// Digit image of xf[0..K) into the linear digit planes (W8A32), or the golden
-// _qa int8 quantiser (ACT_INT8).  Same values as encode_x in common.cuh.
-__device__ void encode_lin(PCtx& c, int K, bool act_int8) {
-  float* xf = (float*)(c.sm + OFF_XF);
-  int8_t* dg = (int8_t*)(c.sm + OFF_DIG);
-  Misc* ms = c.ms;
+// Digit image of xf[0..K) (W8A32, three digits), or the golden _qa int8
+// quantiser (ACT_INT8, one digit), into the fragment-ordered digit image.
+// Same values as encode_x in common.cuh.
+__device__ __noinline__ void encode_lin_core(unsigned char* sm, Misc* ms, int K, bool act_int8) {
+  float* xf = (float*)(sm + OFF_XF);
+  int8_t* dg = (int8_t*)(sm + OFF_DIG);
   float m = 0.0f;
   for (int i = threadIdx.x; i < K; i += PT) m = fmaxf(m, fabsf(xf[i]));
   m = warp_max(m);
@@ -516,7 +471,7 @@ __device__ void encode_lin(PCtx& c, int K, bool act_int8) {
         }
         w0 |= ((unsigned)qi & 0xffu) << (8 * e);
       }
-      reinterpret_cast<unsigned*>(dg)[i4] = w0;
+      *reinterpret_cast<unsigned*>(dg + dig_off(0, 4 * i4)) = w0;
     }
     if (threadIdx.x == 0) { ms->scale = (double)s; ms->ndig = 1; }
   } else {
@@ -542,56 +497,33 @@ __device__ void encode_lin(PCtx& c, int K, bool act_int8) {
         w1 |= ((unsigned)a1 & 0xffu) << (8 * e);
         w2 |= ((unsigned)a2 & 0xffu) << (8 * e);
       }
-      reinterpret_cast<unsigned*>(dg)[i4] = w0;
-      reinterpret_cast<unsigned*>(dg + KMAX)[i4] = w1;
-      reinterpret_cast<unsigned*>(dg + 2 * KMAX)[i4] = w2;
+      *reinterpret_cast<unsigned*>(dg + dig_off(0, 4 * i4)) = w0;
+      *reinterpret_cast<unsigned*>(dg + dig_off(1, 4 * i4)) = w1;
+      *reinterpret_cast<unsigned*>(dg + dig_off(2, 4 * i4)) = w2;
     }
     if (threadIdx.x == 0) { ms->scale = ldexp(1.0, -shs); ms->ndig = 3; }
   }
   consumer_sync();
 }
-
-
-// ---------------------------------------------------------------- per-warp K=1024 input
-
-// Sum of squares of hs[0..HID) in numpy's pairwise order (blocks of 128 summed
-// with 8 strided accumulators, then a binary tree of blocks) -- the order of
-// np.mean(x**2) in golden/model.py:74, so the norm is bit-exact when its input
-// is.  One warp; the result in every lane.
-__device__ __forceinline__ float pairwise_sumsq_1024(const float* hs) {
-  const int lane = threadIdx.x & 31;
-  float r[2];
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int ch = lane + 32 * u;            // chain: block ch / 8, accumulator ch % 8
-    const float* a = hs + 128 * (ch >> 3) + (ch & 7);
-    float acc = __fmul_rn(a[0], a[0]);
-#pragma unroll
-    for (int i = 1; i < 16; ++i) acc = __fadd_rn(acc, __fmul_rn(a[8 * i], a[8 * i]));
-    // ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)) within the block
-    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
-    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
-    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
-    // ((B0 + B1) + (B2 + B3)) over the four blocks of this half
-    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
-    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 16));
-    r[u] = acc;
-  }
-  return __fadd_rn(r[0], r[1]);
+__device__ __forceinline__ void encode_lin(PCtx& c, int K, bool act_int8) {
+  encode_lin_core(c.sm, c.ms, K, act_int8);
 }
+
 
 // CTA-level encode of a normed HID input (every thread two elements, 2t and
 // 2t+1): the sum of squares in numpy's pairwise order by warps 0-1 (the order
 // of np.mean(x**2), golden/model.py:74), then 1/rms, x = h * inv * (1 + w), the
 // digit image (the shift from an upper bound of max|x|) or, under ACT_INT8,
 // the golden quantiser with the exact max|x| (golden/model.py:37-45).  Digits
-// land in the shared planes, or (canon) in rows 0-2 (ACT_INT8: row 0) of the
+// land in the fragment-ordered digit image (and x itself, fake-quantised under
+// ACT_INT8, in xf), or (canon) in rows 0-2 (ACT_INT8: row 0) of the
 // tensor-core B tile at OFF_BT with the other rows zeroed; returns inv and
-// (ACT_INT8) s_x.  Two barriers (three under ACT_INT8).
-__device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2 g2, bool act_int8,
-                                                float& inv_out, float& sx_out, bool canon = false) {
-  Misc* ms = c.ms;
-  int8_t* dg = (int8_t*)(c.sm + OFF_DIG);
+// (ACT_INT8) s_x.  Two barriers (three under ACT_INT8).  One copy in the
+// kernel (not inlined), shared by the IN, GATEUP and head phases.
+__device__ __noinline__ float2 encode_normed(unsigned char* sm, Misc* ms, const float* hs, float2 g2,
+                                             bool act_int8, bool canon, unsigned long long* tw) {
+  int8_t* dg = (int8_t*)(sm + OFF_DIG);
+  float inv_out = 0.0f, sx_out = 0.0f;
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
   const float2 h2 = *reinterpret_cast<const float2*>(hs + 2 * t);
   const float w0 = __fadd_rn(1.0f, g2.x), w1 = __fadd_rn(1.0f, g2.y);
@@ -610,9 +542,14 @@ __device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2
   }
   const float mb = warp_max(fmaxf(fabsf(h2.x * w0), fabsf(h2.y * w1)));
   if (lane == 0) ms->red[2 + wid] = mb;
+  if (tw) tw[8] = clock64();
   consumer_sync();
+  if (tw) tw[9] = clock64();
   const float tot = __fadd_rn(ms->red[0], ms->red[1]);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)HID), EPS)));
+  // (tot / HID: HID is a power of two, so the product by 1/HID is the same
+  // number; 1 / sqrt through the correctly rounded reciprocal, the same number
+  // as the correctly rounded quotient)
+  const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(tot, 1.0f / HID), EPS)));
   inv_out = inv;
   const float x0 = __fmul_rn(__fmul_rn(h2.x, inv), w0);
   const float x1 = __fmul_rn(__fmul_rn(h2.y, inv), w1);
@@ -632,7 +569,7 @@ __device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2
     const unsigned short qq = (unsigned short)(((unsigned)q0 & 0xffu) | (((unsigned)q1 & 0xffu) << 8));
     if (canon) {
       // B tile: row 0 = the int8 activations, rows 1-15 zero
-      unsigned char* bt = c.sm + OFF_BT + ((2 * t) >> 4) * 128 + ((2 * t) & 15);
+      unsigned char* bt = sm + OFF_BT + ((2 * t) >> 4) * 128 + ((2 * t) & 15);
       *reinterpret_cast<unsigned short*>(bt) = qq;
 #pragma unroll
       for (int d = 1; d < 8; ++d) *reinterpret_cast<unsigned short*>(bt + 16 * d) = 0;
@@ -640,7 +577,9 @@ __device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2
       for (int d = 0; d < 8; ++d) *reinterpret_cast<unsigned short*>(bt + BT_SBO + 16 * d) = 0;
       fence_async_smem();
     } else {
-      reinterpret_cast<unsigned short*>(dg)[t] = qq;
+      *reinterpret_cast<unsigned short*>(dg + dig_off(0, (2 * t) & ~3) + ((2 * t) & 2)) = qq;
+      // x as the golden fake quantiser rebuilds it, for the fp32 rows
+      *reinterpret_cast<float2*>(sm + OFF_XF + 8 * t) = make_float2(__fmul_rn((float)q0, s), __fmul_rn((float)q1, s));
     }
     if (t == 0) { ms->scale = (double)s; ms->ndig = 1; }
     sx_out = s;
@@ -672,7 +611,7 @@ __device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2
     }
     if (canon) {
       // elements 2t, 2t+1 sit in core-matrix column (2t)/16 of the 8 x HID tile
-      unsigned char* bt = c.sm + OFF_BT + ((2 * t) >> 4) * 128 + ((2 * t) & 15);
+      unsigned char* bt = sm + OFF_BT + ((2 * t) >> 4) * 128 + ((2 * t) & 15);
 #pragma unroll
       for (int d = 0; d < 3; ++d) *reinterpret_cast<unsigned short*>(bt + 16 * d) = (unsigned short)w_[d];
 #pragma unroll
@@ -682,43 +621,45 @@ __device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2
       fence_async_smem();
     } else {
 #pragma unroll
-      for (int d = 0; d < 3; ++d) reinterpret_cast<unsigned short*>(dg + d * KMAX)[t] = (unsigned short)w_[d];
+      for (int d = 0; d < 3; ++d)
+        *reinterpret_cast<unsigned short*>(dg + dig_off(d, (2 * t) & ~3) + ((2 * t) & 2)) = (unsigned short)w_[d];
+      *reinterpret_cast<float2*>(sm + OFF_XF + 8 * t) = make_float2(x0, x1);   // x itself, for the fp32 rows
     }
     if (t == 0) { ms->scale = ldexp(1.0, -sh); ms->ndig = 3; }
     sx_out = 0.0f;
   }
+  if (tw) tw[10] = clock64();
   consumer_sync();
+  return make_float2(inv_out, sx_out);
+}
+__device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2 g2, bool act_int8,
+                                                float& inv_out, float& sx_out, bool canon = false,
+                                                int tp = -1) {
+  unsigned long long* tw = nullptr;
+  if (tp >= 0 && c.A->trace && blockIdx.x == 0 && (threadIdx.x & 31) == 0)
+    tw = c.A->trace + (size_t)gridDim.x * NPHASE * TRACE_STAMPS +
+         ((size_t)tp * NCW + (threadIdx.x >> 5)) * TRACE_WARP_STAMPS;
+  const float2 r = encode_normed(c.sm, c.ms, hs, g2, act_int8, canon, tw);
+  inv_out = r.x;
+  sx_out = r.y;
 }
 
-// fp32 row (HID floats, smem) dotted with x on this lane's positions, x rebuilt
-// from hs, 1/rms and the gains exactly as cta_encode_1024 formed it (and
-// fake-quantised with s_x under ACT_INT8, golden/model.py:37-45); warp sum.
-__device__ __forceinline__ float row_dot_f32_lane(const float* row, const float* hs, const float* gw,
-                                                  float inv, bool act_int8, float sx) {
+// fp32 row (HID floats, smem) dotted with x (xf, written by the encoder of
+// the normed input: x, or under ACT_INT8 x as the golden fake quantiser
+// rebuilds it, golden/model.py:37-45); lane = 4 consecutive positions of each
+// 128; warp sum.
+__device__ __forceinline__ float row_dot_f32(const float* row, const float* xf) {
   const int lane = threadIdx.x & 31;
   float a = 0.0f;
 #pragma unroll
-  for (int q = 0; q < 2; ++q)
-#pragma unroll
-    for (int e4 = 0; e4 < 4; ++e4) {
-      const int pos = 16 * (lane + 32 * q) + 4 * e4;
-      const float4 w = *reinterpret_cast<const float4*>(row + pos);
-      const float4 h4 = *reinterpret_cast<const float4*>(hs + pos);
-      const float4 g4 = __ldg(reinterpret_cast<const float4*>(gw + pos));
-      float x[4] = {__fmul_rn(__fmul_rn(h4.x, inv), __fadd_rn(1.0f, g4.x)),
-                    __fmul_rn(__fmul_rn(h4.y, inv), __fadd_rn(1.0f, g4.y)),
-                    __fmul_rn(__fmul_rn(h4.z, inv), __fadd_rn(1.0f, g4.z)),
-                    __fmul_rn(__fmul_rn(h4.w, inv), __fadd_rn(1.0f, g4.w))};
-      if (act_int8) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          x[e] = __fmul_rn(fminf(fmaxf(rintf(__fdiv_rn(x[e], sx)), -127.0f), 127.0f), sx);
-      }
-      a = fmaf(w.x, x[0], a);
-      a = fmaf(w.y, x[1], a);
-      a = fmaf(w.z, x[2], a);
-      a = fmaf(w.w, x[3], a);
-    }
+  for (int q = 0; q < HID / 128; ++q) {
+    const float4 w = *reinterpret_cast<const float4*>(row + 4 * (lane + 32 * q));
+    const float4 x = *reinterpret_cast<const float4*>(xf + 4 * (lane + 32 * q));
+    a = fmaf(w.x, x.x, a);
+    a = fmaf(w.y, x.y, a);
+    a = fmaf(w.z, x.z, a);
+    a = fmaf(w.w, x.w, a);
+  }
   return warp_sum(a);
 }
 
@@ -754,111 +695,36 @@ __device__ bool prologue(PCtx& c, int p) {
   const int l = p / 5, sub = p % 5;
   const LayerW& L = c.lay[l];
   if (!load_residual(c, p)) return false;
-  if (sub == 2) {
-    if (L.linear) {
-      // gated RMSNorm of the delta-rule output (golden/model.py:183-189):
-      // o from MIX(l) into xf, z from IN(l) parked in the digit region
-      float* zb = (float*)(c.sm + OFF_DIG);
-      const float gw = __ldg(L.gnorm_w + (threadIdx.x % LV));   // element i = tid + 512 j
-      if (!wait_tagged(c, A.tv_o, VDIM, tag_of(c, p - 1), xf)) return false;
-      if (!wait_tagged(c, A.tv_z, VDIM, tag_of(c, p - 2), zb)) return false;
-      const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-      for (int h = wid; h < LH; h += NCW) {
-        float ss = 0.0f;
-        for (int i = lane; i < LV; i += 32) ss = fmaf(xf[h * LV + i], xf[h * LV + i], ss);
-        ss = warp_sum(ss);
-        if (lane == 0) ms->inv_h[h] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)LV), EPS)));
-      }
-      consumer_sync();
-      for (int i = threadIdx.x; i < VDIM; i += PT) {
-        const float v = __fmul_rn(__fmul_rn(xf[i], ms->inv_h[i / LV]), gw);
-        xf[i] = __fmul_rn(v, silu_f(zb[i]));
-      }
-      consumer_sync();
-      encode_lin(c, VDIM, i8);
-    } else {
-      // gated attention output, already o * sigmoid(gate) (written by the merge)
-      if (!wait_tagged(c, A.tv_attn, NH * HD, tag_of(c, p - 1), xf)) return false;
-      encode_lin(c, NH * HD, i8);
+  // the projection's input: the delta-rule output o (DeltaNet OUT, gated
+  // below), the gated attention output o * sigmoid(gate) written by the merge
+  // (attention OUT), or silu(gate) * up (DOWN)
+  const bool gated = sub == 2 && L.linear;
+  const float gw = gated ? __ldg(L.gnorm_w + (threadIdx.x % LV)) : 0.0f;   // element i = tid + 512 j
+  const unsigned long long* src = sub == 4 ? A.tv_act : (L.linear ? A.tv_o : A.tv_attn);
+  const int K = sub == 4 ? FFN : (L.linear ? VDIM : NH * HD);
+  if (!wait_tagged(c, src, K, tag_of(c, p - 1), xf)) return false;
+  if (gated) {
+    // gated RMSNorm of the delta-rule output (golden/model.py:183-189), z from
+    // IN(l) parked in the digit region
+    float* zb = (float*)(c.sm + OFF_DIG);
+    if (!wait_tagged(c, A.tv_z, VDIM, tag_of(c, p - 2), zb)) return false;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    for (int h = wid; h < LH; h += NCW) {
+      float ss = 0.0f;
+      for (int i = lane; i < LV; i += 32) ss = fmaf(xf[h * LV + i], xf[h * LV + i], ss);
+      ss = warp_sum(ss);
+      // (ss / LV: LV is a power of two, so the product by 1/LV is the same number)
+      if (lane == 0) ms->inv_h[h] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / LV), EPS)));
     }
-  } else {  // sub == 4
-    if (!wait_tagged(c, A.tv_act, FFN, tag_of(c, p - 1), xf)) return false;
-    encode_lin(c, FFN, i8);
+    consumer_sync();
+    for (int i = threadIdx.x; i < VDIM; i += PT) {
+      const float v = __fmul_rn(__fmul_rn(xf[i], ms->inv_h[i / LV]), gw);
+      xf[i] = __fmul_rn(v, silu_f(zb[i]));
+    }
+    consumer_sync();
   }
+  encode_lin(c, K, i8);
   return true;
-}
-
-// ---------------------------------------------------------------- GEMV chunks
-
-// Digits of this lane's 16-byte positions; held in registers only for K = 1024.
-template <int NC, int ND>
-struct Dig {
-  int4 d[ND][NC];
-};
-
-template <int NC, int ND>
-__device__ __forceinline__ void load_dig(const PCtx& c, Dig<NC, ND>& D) {
-  const int8_t* dg = (const int8_t*)(c.sm + OFF_DIG);
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int d = 0; d < ND; ++d)
-#pragma unroll
-    for (int q = 0; q < NC; ++q)
-      D.d[d][q] = *reinterpret_cast<const int4*>(dg + d * KMAX + 16 * (lane + 32 * q));
-}
-
-__device__ __forceinline__ void dp16(int& a, const int4 w, const int4 x) {
-  a = __dp4a(w.x, x.x, a);
-  a = __dp4a(w.y, x.y, a);
-  a = __dp4a(w.z, x.z, a);
-  a = __dp4a(w.w, x.w, a);
-}
-
-// Digit sums of one smem weight row (K = NC*512) in every lane (redux.sync);
-// digits from registers.
-template <int NC, int ND>
-__device__ __forceinline__ void row_dot_r(const int8_t* row, const Dig<NC, ND>& D, int (&acc)[3]) {
-  const int lane = threadIdx.x & 31;
-  acc[0] = acc[1] = acc[2] = 0;
-#pragma unroll
-  for (int q = 0; q < NC; ++q) {
-    const int4 w = *reinterpret_cast<const int4*>(row + 16 * (lane + 32 * q));
-#pragma unroll
-    for (int d = 0; d < ND; ++d) dp16(acc[d], w, D.d[d][q]);
-  }
-#pragma unroll
-  for (int d = 0; d < ND; ++d) acc[d] = redux_add(acc[d]);
-}
-// Same, digits read from the shared digit planes, K = nc*512 at run time.
-template <int ND>
-__device__ __forceinline__ void row_dot_s(const int8_t* row, const int8_t* dg, int nc, int (&acc)[3]) {
-  const int lane = threadIdx.x & 31;
-  acc[0] = acc[1] = acc[2] = 0;
-#pragma unroll 1
-  for (int q = 0; q < nc; ++q) {
-    const int off = 16 * (lane + 32 * q);
-    const int4 w = *reinterpret_cast<const int4*>(row + off);
-#pragma unroll
-    for (int d = 0; d < ND; ++d) dp16(acc[d], w, *reinterpret_cast<const int4*>(dg + d * KMAX + off));
-  }
-#pragma unroll
-  for (int d = 0; d < ND; ++d) acc[d] = redux_add(acc[d]);
-}
-
-// fp32 row (K = HID floats) against xf.
-__device__ __forceinline__ float row_dot_f32(const float* row, const float* xf) {
-  const int lane = threadIdx.x & 31;
-  float a = 0.0f;
-#pragma unroll
-  for (int q = 0; q < HID / 128; ++q) {
-    const float4 w = *reinterpret_cast<const float4*>(row + 4 * (lane + 32 * q));
-    const float4 x = *reinterpret_cast<const float4*>(xf + 4 * (lane + 32 * q));
-    a = fmaf(w.x, x.x, a);
-    a = fmaf(w.y, x.y, a);
-    a = fmaf(w.z, x.z, a);
-    a = fmaf(w.w, x.w, a);
-  }
-  return warp_sum(a);
 }
 
 // Block argmax of the head, then the last CTA reduces every block's maximum,
@@ -977,20 +843,6 @@ __device__ int tile_mma(PCtx& c, int i0, int i1, unsigned tmem, int T0) {
   return 1;
 }
 
-// Output row of the epilogue thread for tile `tix` of an IN phase: destination
-// word, index and row scale.
-__device__ __forceinline__ void in_row_target(const PersistArgs& A, const LayerW& L, int row,
-                                              unsigned long long*& out, int& idx, const float*& sc) {
-  if (L.linear) {
-    if (row < CONVD) { out = A.tv_qkv; idx = row; sc = L.qkv_s + row; }
-    else { out = A.tv_z; idx = row - CONVD; sc = L.z_s + idx; }
-  } else {
-    if (row < QPROJ) { out = A.tv_qg; idx = row; sc = L.q_s + row; }
-    else if (row < QPROJ + KVPROJ) { out = A.tv_kvn; idx = row - QPROJ; sc = L.k_s + idx; }
-    else { out = A.tv_kvn + KVPROJ; idx = row - QPROJ - KVPROJ; sc = L.v_s + idx; }
-  }
-}
-
 // The tied head on the tensor cores: chunks [i0, i1) are this CTA's head tile
 // slabs (possibly none: the argmax merge still needs every CTA).  Input: the
 // residual stream after the last layer, final-normed, encoded once into the B
@@ -1062,64 +914,71 @@ __device__ bool phase_head(PCtx& c, int p, int i0, int i1) {
 }
 
 // ---------------------------------------------------------------- panel GEMVs
+//
+// The layer projections run on the warp-level tensor-core MMA, mma.sync
+// m16n8k32 s8 x s8 -> s32 (exact): A = 16 panel rows x 32 K (one ldmatrix.x4;
+// the panel layout makes a K-step 512 contiguous bytes), B = the x digits
+// (column d = digit d, the other columns zero) from the fragment-ordered digit
+// image.  A chunk splits into tasks of 4 KB of weights -- 8 K-steps of a plain
+// chunk, or 4 gate + 4 up K-steps of a pair chunk; an fp32 chunk splits into
+// one task per row.  Task t of a phase runs on warp t % NCW and adds its digit
+// sums into the panel's accumulators in shared memory (int32 adds: exact, so
+// their order does not matter).
 
-// Digit sums of the 32 rows of one plain panel chunk (lane = row), K offset k0
-// of the digit planes: per 16-byte K-group one conflict-free 16-byte load of
-// the lane's row and one broadcast load per digit plane.  Exact int32.
-template <int ND>
-__device__ __forceinline__ void panel_dot(const unsigned char* slot, const int8_t* dg, int k0, int (&sum)[3]) {
-  const int lane = threadIdx.x & 31;
-  const int4* w = reinterpret_cast<const int4*>(slot) + lane;
-  int a[ND][2];
-#pragma unroll
-  for (int d = 0; d < ND; ++d) a[d][0] = a[d][1] = 0;
-#pragma unroll 8
-  for (int g = 0; g < PANEL_KB / 16; ++g) {
-    const int4 wv = w[g * PANEL];
-#pragma unroll
-    for (int d = 0; d < ND; ++d) {
-      const int4 x = *reinterpret_cast<const int4*>(dg + d * KMAX + k0 + 16 * g);
-      int& acc = a[d][g & 1];
-      acc = __dp4a(wv.x, x.x, acc);
-      acc = __dp4a(wv.y, x.y, acc);
-      acc = __dp4a(wv.z, x.z, acc);
-      acc = __dp4a(wv.w, x.w, acc);
-    }
-  }
-  sum[0] = sum[1] = sum[2] = 0;
-#pragma unroll
-  for (int d = 0; d < ND; ++d) sum[d] = a[d][0] + a[d][1];
+__device__ __forceinline__ void ldsm_x4(unsigned addr, unsigned (&a)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]) : "r"(addr) : "memory");
+}
+__device__ __forceinline__ void mma_s8(int (&d)[4], const unsigned (&a)[4], uint2 b) {
+  asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+               "{%0,%1,%2,%3};"
+               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
+}
+__device__ __forceinline__ void red_add_s32(unsigned addr, int v) {
+  asm volatile("red.shared.add.s32 [%0], %1;" :: "r"(addr), "r"(v) : "memory");
 }
 
-// Same for a pair chunk: 32 gate rows (first 8 KB) and the same 32 up rows.
-template <int ND>
-__device__ __forceinline__ void pair_dot(const unsigned char* slot, const int8_t* dg, int k0, int (&gs)[3],
-                                         int (&us)[3]) {
+// Digit sums of the 16 rows of a panel over ns K-steps (a multiple of 4): A at
+// shared address a (K-step s at a + 512 s), B from the digit image fr at
+// K-step s0, nd digits (B columns nd.. read as zero); two accumulator chains
+// (even / odd steps).  The m16n8 accumulator fragment has rows g, g + 8 of
+// columns 2u, 2u + 1 in lane (g, u) = (lane / 4, lane % 4); it comes back
+// rearranged: lane u = 0 holds digits 0-2 of row g, lane u = 1 those of row
+// g + 8, lanes u = 2, 3 nothing.  One body for every GEMV phase and digit
+// count, so the phases share its instructions.
+__device__ __forceinline__ void panel_mma(unsigned a, const unsigned char* fr, int s0, int ns, int nd,
+                                          int (&d3)[3]) {
   const int lane = threadIdx.x & 31;
-  const int4* wg = reinterpret_cast<const int4*>(slot) + lane;
-  const int4* wu = reinterpret_cast<const int4*>(slot + SLOTW / 2) + lane;
-  int ag[ND], au[ND];
+  int c0[4] = {0, 0, 0, 0}, c1[4] = {0, 0, 0, 0};
+  a += 16u * lane;
+  const unsigned char* fb = fr + 96 * s0 + 8 * lane;
+  const bool bl = lane < 4 * nd;
+#pragma unroll 1
+  for (int s = 0; s < ns; s += 4) {
 #pragma unroll
-  for (int d = 0; d < ND; ++d) ag[d] = au[d] = 0;
-#pragma unroll 8
-  for (int g = 0; g < PAIR_KB / 16; ++g) {
-    const int4 vg = wg[g * PANEL], vu = wu[g * PANEL];
-#pragma unroll
-    for (int d = 0; d < ND; ++d) {
-      const int4 x = *reinterpret_cast<const int4*>(dg + d * KMAX + k0 + 16 * g);
-      ag[d] = __dp4a(vg.x, x.x, ag[d]); au[d] = __dp4a(vu.x, x.x, au[d]);
-      ag[d] = __dp4a(vg.y, x.y, ag[d]); au[d] = __dp4a(vu.y, x.y, au[d]);
-      ag[d] = __dp4a(vg.z, x.z, ag[d]); au[d] = __dp4a(vu.z, x.z, au[d]);
-      ag[d] = __dp4a(vg.w, x.w, ag[d]); au[d] = __dp4a(vu.w, x.w, au[d]);
+    for (int u = 0; u < 4; ++u) {
+      unsigned w[4];
+      ldsm_x4(a + 512u * (s + u), w);
+      const uint2 b = bl ? *reinterpret_cast<const uint2*>(fb + 96 * (s + u)) : make_uint2(0u, 0u);
+      if (u & 1) mma_s8(c1, w, b);
+      else mma_s8(c0, w, b);
     }
   }
-  gs[0] = gs[1] = gs[2] = us[0] = us[1] = us[2] = 0;
+  int c[4];
 #pragma unroll
-  for (int d = 0; d < ND; ++d) { gs[d] = ag[d]; us[d] = au[d]; }
+  for (int e = 0; e < 4; ++e) c[e] = c0[e] + c1[e];
+  const int u = lane & 3;
+  const int x = __shfl_xor_sync(0xffffffffu, u == 0 ? c[2] : c[0], 1);
+  const int y = __shfl_xor_sync(0xffffffffu, c[3], 1);
+  d3[0] = u == 0 ? c[0] : x;
+  d3[1] = u == 0 ? c[1] : y;
+  d3[2] = u == 0 ? x : c[2];
 }
 
-// A warp is done with panel chunk i (it alone read it): complete the slot's
-// empty phase for every warp at once and refill the slot itself.
+// A warp is done with chunk i (every task on it finished before the last CTA
+// barrier): complete the slot's empty phase for every warp at once and refill
+// the slot itself.
 __device__ __forceinline__ void release_panel_chunk(PCtx& c, int i) {
   const int s = i % NSLOT;
   if ((threadIdx.x & 31) == 0) {
@@ -1134,12 +993,87 @@ __device__ __forceinline__ void release_panel_chunk(PCtx& c, int i) {
   __syncwarp();
 }
 
+// Tasks of chunk k of GEMV phase `sub`.
+__host__ __device__ __forceinline__ int chunk_tasks(const Chunk& k, int sub) {
+  if (!(k.seg & CHUNK_PANEL)) return k.nrows;
+  if (sub == 3) return PAIR_KB / 128;
+  const int K = sub == 0 ? HID : (sub == 2 ? VDIM : FFN);
+  const int rem = K - (int)k.nrows * PANEL_KB;
+  return (rem < PANEL_KB ? rem : PANEL_KB) / TASK_KB;
+}
+
+// Task map of a GEMV phase over chunks [i0, i0 + nj), nj <= NSLOT, held in
+// registers by every warp (lane = chunk): nq = the chunk's tasks, tb / pv =
+// inclusive prefix sums of tasks / panel starts over the chunks.  Task t lies
+// in the first chunk whose tb exceeds t; panel v starts at the chunk whose pv
+// is v + 1.  Every warp runs exactly its own tasks (t = wid, wid + NCW, ...).
+struct TaskMap {
+  int nq, tb, pv, start, ntask, npan;
+};
+__device__ __forceinline__ TaskMap task_map(const PCtx& c, int sub, int i0, int nj) {
+  const int lane = threadIdx.x & 31;
+  TaskMap m;
+  m.nq = 0;
+  m.start = 0;
+  if (lane < nj) {
+    const Chunk k = c.ch[i0 + lane];
+    m.nq = chunk_tasks(k, sub);
+    if (k.seg & CHUNK_PANEL) {
+      m.start = 1;
+      if (lane > 0) {
+        const Chunk kp = c.ch[i0 + lane - 1];
+        if ((kp.seg & CHUNK_PANEL) && kp.row0 == k.row0) m.start = 0;
+      }
+    }
+  }
+  m.tb = m.nq;
+  m.pv = m.start;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int a = __shfl_up_sync(0xffffffffu, m.tb, o), b = __shfl_up_sync(0xffffffffu, m.pv, o);
+    if (lane >= o) { m.tb += a; m.pv += b; }
+  }
+  m.ntask = __shfl_sync(0xffffffffu, m.tb, 31);
+  m.npan = __shfl_sync(0xffffffffu, m.pv, 31);
+  return m;
+}
+// chunk (of the phase) holding task t < ntask, and t's K-part within it
+__device__ __forceinline__ int task_chunk(const TaskMap& m, int t, int& q) {
+  const int j = __ffs(__ballot_sync(0xffffffffu, m.tb > t)) - 1;
+  q = t - __shfl_sync(0xffffffffu, m.tb - m.nq, j);
+  return j;
+}
+// panel (of the phase) of chunk j
+__device__ __forceinline__ int chunk_panel(const TaskMap& m, int j) {
+  return __shfl_sync(0xffffffffu, m.pv, j) - 1;
+}
+// first chunk of panel v < npan
+__device__ __forceinline__ int panel_chunk(const TaskMap& m, int v) {
+  return __ffs(__ballot_sync(0xffffffffu, m.start && m.pv == v + 1)) - 1;
+}
+
+// Row-scale pointers of panel row r of GEMV phase `sub` (second: the up row of
+// a GATEUP pair, else null).
+__device__ __forceinline__ void row_scales(const LayerW& L, int sub, int r, const float*& s0, const float*& s1) {
+  s1 = nullptr;
+  if (sub == 0) {
+    if (L.linear) s0 = r < CONVD ? L.qkv_s + r : L.z_s + (r - CONVD);
+    else s0 = r < QPROJ ? L.q_s + r : (r < QPROJ + KVPROJ ? L.k_s + (r - QPROJ) : L.v_s + (r - QPROJ - KVPROJ));
+  } else if (sub == 3) {
+    s0 = L.gate_s + r;
+    s1 = L.up_s + r;
+  } else {
+    s0 = (sub == 2 ? (L.linear ? L.out_s : L.o_s) : L.down_s) + r;
+  }
+}
+
 // A GEMV phase over panels (IN, OUT, GATEUP, DOWN).  The input vector is
-// encoded once into the digit planes; chunk j of the phase goes to warp
-// j % NCW, which writes its rows' partial digit sums to shared memory; after a
-// CTA barrier, warp v % NCW adds the partials of the v-th panel in chunk order
-// (exact int32) and writes the panel's 32 outputs: the projection rows (IN),
-// silu(gate) * up (GATEUP, golden/model.py:236), or h + y (OUT, DOWN).
+// encoded once into the digit image; every warp runs its own tasks of the
+// CTA's chunks; after a CTA barrier, warp v % NCW finishes the v-th panel (16
+// rows) of the CTA's phase: the projection rows (IN), silu(gate) * up
+// (GATEUP, golden/model.py:236), or h + y (OUT, DOWN).  The fp32 in_proj_b /
+// in_proj_a rows of a DeltaNet IN (golden/model.py:146-147) are dotted with x
+// in fp32 by their tasks directly.
 __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
@@ -1150,31 +1084,41 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
   const float* gw = sub == 0 ? L.in_norm : L.post_norm;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int nj = i1 - i0;
-  // the row scales of the panels this warp will finish, fetched before the
-  // input wait so that their latency hides behind it (lane = row)
-  constexpr int MPW = 2;
-  float scp_pre[MPW][2];
-  {
-    int v = 0;
-    for (int ja = 0; ja < nj; ++ja) {
-      const Chunk k = c.ch[i0 + ja];
-      if (!(k.seg & CHUNK_PANEL) || (ja > 0 && (c.ch[i0 + ja - 1].seg & CHUNK_PANEL) &&
-                                     c.ch[i0 + ja - 1].row0 == k.row0))
-        continue;
-      if (v % NCW == wid && v / NCW < MPW) {
-        const int r = (int)k.row0 * PANEL + lane;
-        const float* s0;
-        const float* s1 = nullptr;
-        if (sub == 0) {
-          if (L.linear) s0 = r < CONVD ? L.qkv_s + r : L.z_s + (r - CONVD);
-          else s0 = r < QPROJ ? L.q_s + r : (r < QPROJ + KVPROJ ? L.k_s + (r - QPROJ) : L.v_s + (r - QPROJ - KVPROJ));
-        } else if (sub == 3) { s0 = L.gate_s + r; s1 = L.up_s + r; }
-        else s0 = (sub == 2 ? (L.linear ? L.out_s : L.o_s) : L.down_s) + r;
-        scp_pre[v / NCW][0] = __ldg(s0);
-        scp_pre[v / NCW][1] = s1 ? __ldg(s1) : 0.0f;
+  trace_warp(c, p, 0);
+  int good = 1;
+  if (nj > NSLOT) {   // the schedule keeps a phase within the ring (and MAXPAN panels)
+    if (threadIdx.x == 0) check_fail(c, 8, nj);
+    good = 0;
+  }
+  const TaskMap m = task_map(c, sub, i0, good ? nj : 0);
+  // panel row of this lane in the finishing step (lanes with lane & 2 hold none)
+  const bool own = (lane & 2) == 0;
+  const int pr = (lane >> 2) + 8 * (lane & 1);
+  // the row scales of the (at most two) panels this warp will finish, fetched
+  // before the input wait so that their latency hides behind it
+  float sp[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int v = wid + NCW * u;
+    if (v < m.npan) {
+      const int r = (int)c.ch[i0 + panel_chunk(m, v)].row0 * PANEL + pr;
+      const float* s0;
+      const float* s1;
+      row_scales(L, sub, r, s0, s1);
+      if (own) {
+        sp[u][0] = __ldg(s0);
+        if (s1) sp[u][1] = __ldg(s1);
       }
-      ++v;
     }
+  }
+  // this warp's first chunk: its bytes were requested in an earlier phase, so
+  // waiting for them here (before the input wait) cannot hold anything up
+  bool first_in = false;
+  if (good && wid < m.ntask) {
+    int q;
+    first_in = wait_full(c, i0 + task_chunk(m, wid, q));
+    if (!first_in) good = 0;
+    trace_warp(c, p, 3);
   }
   float inv = 0.0f, sx = 0.0f;
   if (sub == 0 || sub == 3) {
@@ -1189,242 +1133,108 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
     } else if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) {
       return false;
     }
+    trace_warp(c, p, 1);
     if (threadIdx.x == 0) ms->hs_tag = tag_of(c, p - 1);   // layer 0: the embedding (tag of "phase -1")
-    cta_encode_1024(c, hs, g2, i8, inv, sx);
+    cta_encode_1024(c, hs, g2, i8, inv, sx, false, p);
   } else if (!prologue(c, p)) {
     return false;
   }
   trace_mark(c, p, 1);
-  const int8_t* dg = (const int8_t*)(c.sm + OFF_DIG);
-  int* part = (int*)(c.sm + OFF_XF);                     // [chunk][3 or 6][32] partial sums
+  trace_warp(c, p, 2);
+  const unsigned char* fr = c.sm + OFF_DIG;
+  const unsigned part = smem_u32(c.sm + OFF_PART);
   const int nd = ms->ndig;
   const float xsf = (float)ms->scale;
   const unsigned tag = tag_of(c, p);
   const bool pair = (sub == 3);
-  const int pw = pair ? 6 : 3;
-  int good = 1;
-  if (nj * pw * 32 * 4 > 4 * KMAX) {
-    if (threadIdx.x == 0) check_fail(c, 8, nj);
-    good = 0;
-  }
-  for (int j = wid; good && j < nj; j += NCW) {
+  for (int t = wid; good && t < m.ntask; t += NCW) {
+    int q;
+    const int j = task_chunk(m, t, q);
     const int i = i0 + j;
     const Chunk k = c.ch[i];
-    const bool f32 = !(k.seg & CHUNK_PANEL);
-    if (f32 && !(sub == 0 && L.linear && k.seg >= 2)) { if (lane == 0) check_fail(c, 9, i); good = 0; break; }
-    if (!wait_full(c, i)) { good = 0; break; }
-    if (j == 0) trace_mark(c, p, 2);
-    const unsigned char* slot = c.sm + OFF_RING + (i % NSLOT) * SLOT;
-    int* pj = part + j * pw * 32;
-    if (f32) {
-      // in_proj_b / in_proj_a rows (fp32, golden/model.py:146-147), one warp
-      for (int r = 0; r < k.nrows; ++r) {
-        const float v = row_dot_f32_lane((const float*)slot + r * HID, hs, gw, inv, i8, sx);
-        if (lane == 0) st_tv(A.tv_ab + (k.seg == 2 ? 0 : LH) + (int)k.row0 + r, v, tag);
-      }
-    } else if (pair) {
-      int gs[3], us[3];
-      const int k0 = k.nrows * PAIR_KB;
-      if (nd == 3) pair_dot<3>(slot, dg, k0, gs, us);
-      else pair_dot<1>(slot, dg, k0, gs, us);
-#pragma unroll
-      for (int d = 0; d < 3; ++d) { pj[d * 32 + lane] = gs[d]; pj[(3 + d) * 32 + lane] = us[d]; }
-    } else {
-      int sm3[3];
-      const int k0 = k.nrows * PANEL_KB;
-      if (nd == 3) panel_dot<3>(slot, dg, k0, sm3);
-      else panel_dot<1>(slot, dg, k0, sm3);
-#pragma unroll
-      for (int d = 0; d < 3; ++d) pj[d * 32 + lane] = sm3[d];
+    const bool pan = (k.seg & CHUNK_PANEL) != 0;
+    if (!pan && !(sub == 0 && L.linear && k.seg >= 2)) {
+      if (lane == 0) check_fail(c, 9, i);
+      good = 0;
+      break;
     }
-    // chunks beyond the ring's depth arrive only as slots free up: release now
-    if (nj > NSLOT) release_panel_chunk(c, i);
+    if (!(t == wid && first_in) && !wait_full(c, i)) { good = 0; break; }
+    if (t == 0) trace_mark(c, p, 2);
+    const unsigned sa = smem_u32(c.sm + OFF_RING + (i % NSLOT) * SLOT);
+    if (!pan) {
+      const float* row = (const float*)(c.sm + OFF_RING + (i % NSLOT) * SLOT) + q * HID;
+      const float y = row_dot_f32(row, (const float*)(c.sm + OFF_XF));
+      if (lane == 0) st_tv(A.tv_ab + (k.seg == 2 ? 0 : LH) + (int)k.row0 + q, y, tag);
+      continue;
+    }
+    // a plain task: 8 K-steps of the slot; a pair task: 4 K-steps of the gate
+    // half, then the same 4 of the up half (SLOTW / 2 further on)
+    const int ns = pair ? PAIR_KB / 128 : TASK_KB / 32;
+    const int s0 = pair ? ((int)k.nrows * PAIR_KB + 128 * q) >> 5 : ((int)k.nrows * PANEL_KB + TASK_KB * q) >> 5;
+    const unsigned pv = part + 4u * (unsigned)(chunk_panel(m, j) * 6 * PANEL + pr);
+#pragma unroll 1
+    for (int h = 0; h < (pair ? 2 : 1); ++h) {
+      int d3[3];
+      panel_mma(sa + (SLOTW / 2) * h + 512u * ns * q, fr, s0, ns, nd, d3);
+      if (own) {
+        const unsigned ph = pv + 4u * PANEL * 3 * h;
+        red_add_s32(ph, d3[0]);
+        if (nd == 3) {
+          red_add_s32(ph + 4u * PANEL, d3[1]);
+          red_add_s32(ph + 4u * PANEL * 2, d3[2]);
+        }
+      }
+    }
   }
+  trace_warp(c, p, 4);
   if (!consumer_and(good)) return false;
-  // panel v = the v-th run of consecutive chunks with the same panel index
-  int v = 0;
-  for (int ja = 0; ja < nj;) {
-    if (!(c.ch[i0 + ja].seg & CHUNK_PANEL)) { ++ja; continue; }   // fp32 rows: written above
-    const unsigned q = c.ch[i0 + ja].row0;
-    int jb = ja + 1;
-    while (jb < nj && (c.ch[i0 + jb].seg & CHUNK_PANEL) && c.ch[i0 + jb].row0 == q) ++jb;
-    if (v % NCW == wid) {
-      int t[6] = {0, 0, 0, 0, 0, 0};
-      for (int j = ja; j < jb; ++j)
+  trace_warp(c, p, 5);
+  for (int v = wid; v < m.npan; v += NCW) {
+    const Chunk k = c.ch[i0 + panel_chunk(m, v)];
+    if (!own) continue;
+    // the panel's sums, and the accumulators zeroed for the next phase
+    int* pv = (int*)(c.sm + OFF_PART) + v * 6 * PANEL + pr;
+    int t[6];
 #pragma unroll
-        for (int e = 0; e < 6; ++e)
-          if (e < pw) t[e] += part[(j * pw + e) * 32 + lane];
-      const int r = (int)q * PANEL + lane;
-      // row scales: prefetched for this warp's first MPW panels
-      float sa = 0.0f, sb = 0.0f;
-      const int u = v / NCW;
-#pragma unroll
-      for (int e = 0; e < MPW; ++e)
-        if (e == u) { sa = scp_pre[e][0]; sb = scp_pre[e][1]; }
-      if (sub == 0) {
-        unsigned long long* out;
-        int o;
-        const float* scp;
-        if (L.linear) {
-          if (r < CONVD) { out = A.tv_qkv; o = r; scp = L.qkv_s + r; }
-          else { out = A.tv_z; o = r - CONVD; scp = L.z_s + o; }
-        } else {
-          if (r < QPROJ) { out = A.tv_qg; o = r; scp = L.q_s + r; }
-          else if (r < QPROJ + KVPROJ) { out = A.tv_kvn; o = r - QPROJ; scp = L.k_s + o; }
-          else { out = A.tv_kvn + KVPROJ; o = r - QPROJ - KVPROJ; scp = L.v_s + o; }
-        }
-        if (u >= MPW) sa = __ldg(scp);
-        st_tv(out + o, finish_f32(t[0], t[1], t[2], nd, xsf * sa), tag);
-      } else if (sub == 3) {
-        if (u >= MPW) { sa = __ldg(L.gate_s + r); sb = __ldg(L.up_s + r); }
-        const float g = finish_f32(t[0], t[1], t[2], nd, xsf * sa);
-        const float uu = finish_f32(t[3], t[4], t[5], nd, xsf * sb);
-        st_tv(A.tv_act + r, __fmul_rn(silu_f(g), uu), tag);
-      } else {
-        if (u >= MPW) sa = __ldg((sub == 2 ? (L.linear ? L.out_s : L.o_s) : L.down_s) + r);
-        const float y = finish_f32(t[0], t[1], t[2], nd, xsf * sa);
-        st_tv(A.tv_h + r, __fadd_rn(hs[r], y), tag);
-      }
+    for (int e = 0; e < 6; ++e) { t[e] = pv[e * PANEL]; pv[e * PANEL] = 0; }
+    const int r = (int)k.row0 * PANEL + pr;
+    float sa, sb;
+    if (v < 2 * NCW) {
+      sa = v < NCW ? sp[0][0] : sp[1][0];
+      sb = v < NCW ? sp[0][1] : sp[1][1];
+    } else {
+      const float* s0;
+      const float* s1;
+      row_scales(L, sub, r, s0, s1);
+      sa = __ldg(s0);
+      sb = s1 ? __ldg(s1) : 0.0f;
     }
-    ++v;
-    ja = jb;
+    if (sub == 0) {
+      unsigned long long* out;
+      int o;
+      if (L.linear) {
+        if (r < CONVD) { out = A.tv_qkv; o = r; }
+        else { out = A.tv_z; o = r - CONVD; }
+      } else {
+        if (r < QPROJ) { out = A.tv_qg; o = r; }
+        else if (r < QPROJ + KVPROJ) { out = A.tv_kvn; o = r - QPROJ; }
+        else { out = A.tv_kvn + KVPROJ; o = r - QPROJ - KVPROJ; }
+      }
+      st_tv(out + o, finish_f32(t[0], t[1], t[2], nd, xsf * sa), tag);
+    } else if (sub == 3) {
+      const float g = finish_f32(t[0], t[1], t[2], nd, xsf * sa);
+      const float uu = finish_f32(t[3], t[4], t[5], nd, xsf * sb);
+      st_tv(A.tv_act + r, __fmul_rn(silu_f(g), uu), tag);
+    } else {
+      const float y = finish_f32(t[0], t[1], t[2], nd, xsf * sa);
+      st_tv(A.tv_h + r, __fadd_rn(hs[r], y), tag);
+    }
   }
+  trace_warp(c, p, 6);
   // the outputs are out: now give the slots back and refill them (off the
-  // phase's critical path; the schedule keeps a phase within the ring's depth)
-  if (nj <= NSLOT)
-    for (int j = wid; j < nj; j += NCW) release_panel_chunk(c, i0 + j);
-  return true;
-}
-
-// GEMV phases whose input is a normed HID vector -- IN (both layer kinds),
-// GATEUP.  Inputs polled into hs once per CTA; then every warp encodes
-// its own register digits (no further CTA synchronisation) and consumes the
-// chunks.  Chunk k's row r goes to warp (rows before k + r) mod 16, so small
-// consecutive chunks are worked on by different warps at the same time.
-__device__ bool phase_1024(PCtx& c, int p, int i0, int i1) {
-  const PersistArgs& A = *c.A;
-  Misc* ms = c.ms;
-  float* hs = (float*)(c.sm + OFF_HS);
-  const int l = p / 5, sub = p % 5;
-  const LayerW& L = c.lay[l];
-  const float* gw = sub == 0 ? L.in_norm : L.post_norm;
-  const float2 g2 = __ldg(reinterpret_cast<const float2*>(gw) + threadIdx.x);
-  if (sub == 0 && l == 0) {
-    // residual stream starts at the dequantised embedding row (golden/model.py:246)
-    const int tok = ms->tok;
-    const float sc = __ldg(A.emb_s + tok);
-    const int8_t* row = A.emb_q + (size_t)tok * HID;
-    for (int i = threadIdx.x; i < HID; i += PT) hs[i] = __fmul_rn((float)row[i], sc);
-    consumer_sync();
-  } else if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) {
-    return false;
-  }
-  if (threadIdx.x == 0) ms->hs_tag = tag_of(c, p - 1);   // layer 0: the embedding (tag of "phase -1")
-  float inv, sx;
-  const bool i8 = ms->act_int8 != 0;
-  cta_encode_1024(c, hs, g2, i8, inv, sx);
-  Dig<2, 3> D;
-  load_dig<2, 3>(c, D);
-  const int nd = ms->ndig;
-  const double xs = ms->scale;
-  trace_mark(c, p, 1);
-  const unsigned tag = tag_of(c, p);
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  int rows_off = 0;
-  for (int i = i0; i < i1; ++i) {
-    const Chunk k = c.ch[i];
-    trace_chunk(c, i, 0);
-    if (!wait_full(c, i)) return false;
-    trace_chunk(c, i, 1);
-    if (i == i0) trace_mark(c, p, 2);
-    const int8_t* buf = (const int8_t*)(c.sm + OFF_RING + (i % NSLOT) * SLOT);
-    const float* tail = (const float*)(buf + SLOTW);
-    const int row0 = (int)k.row0, n = k.nrows, a0 = row0 & ~3;
-    const bool pair = (sub == 3);
-    const bool f32 = (sub == 0) && L.linear && k.seg >= 2;
-    const int r = (wid - rows_off) & (NCW - 1);
-    rows_off += n;
-    int acc[3] = {0, 0, 0}, acc2[3] = {0, 0, 0};
-    float fv = 0.0f, sc = 0.0f, sc2 = 0.0f;
-    const bool mine = r < n;
-    if (mine) {
-      if (f32) {
-        fv = row_dot_f32_lane((const float*)buf + r * HID, hs, gw, inv, i8, sx);
-      } else {
-        row_dot_r<2, 3>(buf + r * HID, D, acc);
-        if (lane == 0) sc = tail[row0 + r - a0];
-        if (pair) {
-          row_dot_r<2, 3>(buf + (n + r) * HID, D, acc2);
-          if (lane == 0) sc2 = tail[32 + row0 + r - a0];
-        }
-      }
-    }
-    __syncwarp();
-    trace_chunk(c, i, 2);
-    release_slot(c, i);
-    trace_chunk(c, i, 3);
-    if (mine && lane == 0) {
-      const int o = row0 + r;
-      const float xsf = (float)xs;
-      if (pair) {
-        const float g = finish_f32(acc[0], acc[1], acc[2], nd, xsf * sc);
-        const float u = finish_f32(acc2[0], acc2[1], acc2[2], nd, xsf * sc2);
-        st_tv(A.tv_act + o, __fmul_rn(silu_f(g), u), tag);
-      } else if (f32) {
-        st_tv(A.tv_ab + (k.seg == 2 ? 0 : LH) + o, fv, tag);
-      } else {
-        const float y = finish_f32(acc[0], acc[1], acc[2], nd, xsf * sc);
-        unsigned long long* out;
-        if (L.linear) out = (k.seg == 0) ? A.tv_qkv : A.tv_z;
-        else out = (k.seg == 0) ? A.tv_qg : (k.seg == 1 ? A.tv_kvn : A.tv_kvn + KVPROJ);
-        st_tv(out + o, y, tag);
-      }
-    }
-  }
-  return true;
-}
-
-// GEMV phases with K = 2048 / 3584 (OUT: out_proj / o_proj, DOWN): digits in
-// the shared planes (written by the CTA prologue), row-parallel projection
-// with the residual add, h = r + y (golden/model.py:259,263).
-__device__ bool phase_wide(PCtx& c, int p, int nc, int i0, int i1) {
-  const PersistArgs& A = *c.A;
-  Misc* ms = c.ms;
-  const float* hs = (const float*)(c.sm + OFF_HS);
-  const int8_t* dg = (const int8_t*)(c.sm + OFF_DIG);
-  const double xs = ms->scale;
-  const int nd = ms->ndig;
-  const unsigned tag = tag_of(c, p);
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  int rows_off = 0;
-  for (int i = i0; i < i1; ++i) {
-    const Chunk k = c.ch[i];
-    trace_chunk(c, i, 0);
-    if (!wait_full(c, i)) return false;
-    trace_chunk(c, i, 1);
-    if (i == i0) trace_mark(c, p, 2);
-    const int8_t* buf = (const int8_t*)(c.sm + OFF_RING + (i % NSLOT) * SLOT);
-    const float* tail = (const float*)(buf + SLOTW);
-    const int row0 = (int)k.row0, n = k.nrows, a0 = row0 & ~3;
-    const int r = (wid - rows_off) & (NCW - 1);
-    rows_off += n;
-    int acc[3] = {0, 0, 0};
-    float sc = 0.0f;
-    const bool mine = r < n;
-    if (mine) {
-      row_dot_s<3>(buf + r * (nc * 512), dg, nc, acc);
-      if (lane == 0) sc = tail[row0 + r - a0];
-    }
-    __syncwarp();
-    release_slot(c, i);
-    trace_chunk(c, i, 2);
-    if (mine && lane == 0) {
-      const int o = row0 + r;
-      const float y = finish_f32(acc[0], acc[1], acc[2], nd, (float)xs * sc);
-      st_tv(A.tv_h + o, __fadd_rn(hs[o], y), tag);
-    }
-    trace_chunk(c, i, 3);
-  }
+  // phase's critical path)
+  for (int j = wid; j < nj; j += NCW) release_panel_chunk(c, i0 + j);
+  trace_warp(c, p, 7);
   return true;
 }
 
@@ -1784,6 +1594,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
     ((int*)c.lay)[i] = ((const int*)A.layers)[i];
   for (int i = threadIdx.x; i < c.nch; i += NTHREADS) chs[i] = A.chunks[(size_t)blockIdx.x * MAXCH + i];
   for (int i = threadIdx.x; i <= NPHASE; i += NTHREADS) ms->pf[i] = A.phase_first[(size_t)blockIdx.x * (NPHASE + 1) + i];
+  for (int i = threadIdx.x; i < MAXPAN * 6 * PANEL; i += NTHREADS) ((int*)(sm + OFF_PART))[i] = 0;
   if (threadIdx.x == 0) {
     ms->abort = 0;
     ms->pos = A.dyn->pos;
@@ -1912,13 +1723,18 @@ static_assert(OFF_DIG + (4 * HD + 2 * HD + 4 * ATT_MAXLEN) * 4 <= OFF_HS,
 int persist_smem_bytes() { return SMEM_BYTES; }
 int persist_num_phases() { return NPHASE; }
 int persist_max_chunks() { return MAXCH; }
+size_t persist_trace_words(int G) {
+  return (size_t)G * NPHASE * TRACE_STAMPS + (size_t)NPHASE * NCW * TRACE_WARP_STAMPS;
+}
 
 
 // Build the per-CTA chunk lists.
-//   IN, OUT, GATEUP, DOWN: whole panels (32 rows; all of a panel's K-slices on
-//     one CTA), each given to the CTA with the fewest bytes so far in the step
-//     (ties: lowest index); the fp32 in_proj_a/b rows of a DeltaNet IN go, 4 rows
-//     per chunk, to the least-loaded CTAs too.
+//   IN, OUT, GATEUP, DOWN: whole panels (16 rows; all of a panel's K-slices on
+//     one CTA).  Each panel goes to the CTA with the fewest 4 KB tasks so far
+//     in the phase, then the fewest bytes so far in the step, then the lowest
+//     index, among the CTAs whose ring still holds the panel's chunks with the
+//     phase's others; the fp32 in_proj_a/b rows of a DeltaNet IN follow, 4 rows
+//     per chunk, by the same rule.
 //   HEAD: contiguous, balanced ranges of the 1940 tiles.
 bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
                     std::vector<unsigned short>& phase_first, std::string& err) {
@@ -1928,7 +1744,7 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
   phase_first.assign((size_t)G * (NPHASE + 1), 0);
   std::vector<int> counts(G, 0);
   std::vector<long long> load(G, 0);
-  auto push = [&](int b, int p, int seg, int n, int row0) -> bool {
+  auto push = [&](int b, int p, int seg, int n, int row0, int bytes) -> bool {
     int& cnt = counts[b];
     if (cnt >= MAXCH) { err = "chunk list overflow"; return false; }
     Chunk& k = chunks[(size_t)b * MAXCH + cnt++];
@@ -1936,7 +1752,7 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
     k.seg = (unsigned char)seg;
     k.nrows = (unsigned char)n;
     k.row0 = (unsigned)row0;
-    load[b] += SLOTW;
+    load[b] += bytes;
     return true;
   };
   for (int p = 0; p < NPHASE; ++p) {
@@ -1949,40 +1765,58 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
         const int t0 = (int)((long long)HEAD_TILES * b / G), t1 = (int)((long long)HEAD_TILES * (b + 1) / G);
         for (int t = t0; t < t1; ++t)
           for (int j = 0; j < HEAD_NSLAB; ++j)
-            if (!push(b, p, CHUNK_MMA, j, t)) return false;
+            if (!push(b, p, CHUNK_MMA, j, t, SLOTW)) return false;
       }
       continue;
     }
     if (sub == 1) continue;
     const bool linear = (p / 5) % 4 != 3;
-    int npan, nslice;
-    if (sub == 0) { npan = (linear ? CONVD + VDIM : QPROJ + 2 * KVPROJ) / PANEL; nslice = HID / PANEL_KB; }
-    else if (sub == 2) { npan = HID / PANEL; nslice = VDIM / PANEL_KB; }
-    else if (sub == 3) { npan = FFN / PANEL; nslice = HID / PAIR_KB; }
-    else { npan = HID / PANEL; nslice = FFN / PANEL_KB; }
-    std::vector<int> inph(G, 0);   // chunks of this phase per CTA: at most NSLOT (all resident at once)
+    int npan, K;
+    if (sub == 0) { npan = (linear ? CONVD + VDIM : QPROJ + 2 * KVPROJ) / PANEL; K = HID; }
+    else if (sub == 2) { npan = HID / PANEL; K = VDIM; }
+    else if (sub == 3) { npan = FFN / PANEL; K = HID; }
+    else { npan = HID / PANEL; K = FFN; }
+    // a panel's K-slices: bytes and tasks of each
+    std::vector<int> sl_bytes, sl_tasks;
+    if (sub == 3) {
+      for (int k0 = 0; k0 < K; k0 += PAIR_KB) { sl_bytes.push_back(2 * PANEL * PAIR_KB); sl_tasks.push_back(PAIR_KB / 128); }
+    } else {
+      for (int k0 = 0; k0 < K; k0 += PANEL_KB) {
+        const int kb = K - k0 < PANEL_KB ? K - k0 : PANEL_KB;
+        sl_bytes.push_back(PANEL * kb);
+        sl_tasks.push_back(kb / TASK_KB);
+      }
+    }
+    const int nslice = (int)sl_bytes.size();
+    int ptasks = 0;
+    for (int x : sl_tasks) ptasks += x;
+    std::vector<int> inph(G, 0), tasks(G, 0);   // chunks (at most NSLOT: all resident at once) and tasks
     auto least_fit = [&](int need) {
       int best = -1;
-      for (int b = 0; b < G; ++b)
-        if (inph[b] + need <= NSLOT && (best < 0 || load[b] < load[best])) best = b;
+      for (int b = 0; b < G; ++b) {
+        if (inph[b] + need > NSLOT) continue;
+        if (best < 0 || tasks[b] < tasks[best] || (tasks[b] == tasks[best] && load[b] < load[best])) best = b;
+      }
       return best;
     };
     for (int q = 0; q < npan; ++q) {
       const int b = least_fit(nslice);
       if (b < 0) { err = "phase does not fit the rings"; return false; }
       inph[b] += nslice;
+      tasks[b] += ptasks;
       for (int j = 0; j < nslice; ++j)
-        if (!push(b, p, CHUNK_PANEL, j, q)) return false;
+        if (!push(b, p, CHUNK_PANEL, j, q, sl_bytes[j])) return false;
     }
     if (sub == 0 && linear) {
-      // in_proj_b (seg 2) and in_proj_a (seg 3): fp32 rows, 4 per chunk
+      // in_proj_b (seg 2) and in_proj_a (seg 3): fp32 rows, 4 per chunk, one task per row
       constexpr int per = SLOTW / (HID * 4);
       for (int seg = 2; seg <= 3; ++seg)
         for (int r = 0; r < LH; r += per) {
           const int b = least_fit(1);
           if (b < 0) { err = "phase does not fit the rings"; return false; }
           inph[b] += 1;
-          if (!push(b, p, seg, per, r)) return false;
+          tasks[b] += per;
+          if (!push(b, p, seg, per, r, per * HID * 4)) return false;
         }
     }
   }
@@ -2025,7 +1859,7 @@ __global__ void k_repack_panels(const int8_t* const* __restrict__ rowptr, int4* 
     const size_t q = r / PANEL;
     const int m = (int)(r % PANEL);
     dst = q * PANEL * K + ((size_t)g * PANEL + m) * 16;
-  } else {   // pair panel q = rows (32 gate, 32 up); chunk s = K-groups 16s.. of gate then of up
+  } else {   // pair panel q = rows (16 gate, 16 up); chunk s = K-groups 32s.. of gate then of up
     const size_t q = r / (2 * PANEL);
     const int half = (int)((r / PANEL) % 2), m = (int)(r % PANEL);
     const int s = g / (PAIR_KB / 16), gg = g % (PAIR_KB / 16);
@@ -2036,8 +1870,7 @@ __global__ void k_repack_panels(const int8_t* const* __restrict__ rowptr, int4* 
 
 cudaError_t repack_panels(const int8_t* const* rowptr, int8_t* out, int nrows, int K, bool pair,
                           cudaStream_t st) {
-  if (nrows % (pair ? 2 * PANEL : PANEL) || (!pair && K % PANEL_KB) || ((uintptr_t)out & 15) ||
-      (pair && K != HID))
+  if (nrows % (pair ? 2 * PANEL : PANEL) || K % TASK_KB || ((uintptr_t)out & 15) || (pair && K != HID))
     return cudaErrorInvalidValue;
   const size_t n = (size_t)nrows * (K / 16);
   k_repack_panels<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rowptr, reinterpret_cast<int4*>(out), nrows,

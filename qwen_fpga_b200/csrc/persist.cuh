@@ -42,13 +42,19 @@ struct PersistArgs {
   float* logits;
   int* io; int* ids; int* err; int* abort_flag;
   StepDyn* dyn;
-  unsigned long long* trace;       // nullable: [G][NPHASE][4] %globaltimer stamps
+  unsigned long long* trace;       // nullable: the trace record (layout above persist_trace_words)
   int max_ctx, max_rope, max_steps;
 };
 
-// Trace record layout: per CTA and phase, stamps at phase entry, inputs ready
-// (prologue done), first weight chunk landed, phase exit.
+// Trace record layout: per CTA and phase, %globaltimer stamps at phase entry,
+// inputs ready (prologue done), first weight chunk landed, phase exit; then,
+// for CTA 0 only, per phase and warp, clock64 stamps of a GEMV phase: 0 entry,
+// 1 input vector in, 2 digit image encoded, 3 first task's chunk landed, 4 own
+// tasks done, 5 CTA barrier passed, 6 panels finished, 7 slots released, and
+// inside the encoder of a normed input 8 norm statistics, 9 their barrier
+// passed, 10 digits written (0 = not reached).
 constexpr int TRACE_STAMPS = 4;
+constexpr int TRACE_WARP_STAMPS = 16;
 
 // Head tiles: embed_tokens.weight [VOCAB, HID] int8 as HEAD_TILES tiles of
 // HEAD_TM rows, each cut into HEAD_NSLAB K-slabs of HEAD_KS bytes.  Slab
@@ -63,27 +69,31 @@ static_assert(VOCAB % HEAD_TM == 0 && HID % HEAD_KS == 0, "head tiling");
 constexpr size_t HEAD_TILE_BYTES = (size_t)VOCAB * HID;
 cudaError_t repack_head_tiles(const int8_t* emb_q, int8_t* tiles, cudaStream_t st);
 
-// Layer GEMVs on the CUDA cores, lane per row: every projection is re-laid at
-// load time as panels of 32 rows; inside a panel, element (m, k) sits at
-// ((k / 16) * 32 + m) * 16 + k % 16, so one 16-byte K-group of all 32 rows is
-// 512 contiguous bytes (one conflict-free 16-byte load per lane).  A chunk is
-// 16 KB = the panel's 32 rows x 512 bytes of K.  GATEUP uses pair panels: 32
-// gate rows and the same 32 up rows; a chunk is 256 bytes of K of both (gate
-// half, then up half, 8 KB each).
-constexpr int PANEL = 32;
-constexpr int PANEL_KB = 512;                   // K bytes per chunk of a plain panel
-constexpr int PAIR_KB = 256;                    // K bytes per chunk of a pair panel
+// Layer GEMVs on the warp-level tensor-core MMA (mma.sync m16n8k32 s8): every
+// projection is re-laid at load time as panels of 16 rows; inside a panel,
+// element (m, k) sits at ((k / 16) * 16 + m) * 16 + k % 16, so one K = 32 step
+// of all 16 rows is 512 contiguous bytes (one ldmatrix.x4 = the MMA's A
+// fragment).  A chunk is one K-slice of a panel: 16 rows x 1024 bytes of K
+// (16 KB; the last slice of a K = 3584 panel is 512 bytes, 8 KB).  GATEUP uses
+// pair panels: 16 gate rows and the same 16 up rows; a chunk is 512 bytes of K
+// of both (gate half, then up half, 8 KB each).
+constexpr int PANEL = 16;
+constexpr int PANEL_KB = 1024;                  // K bytes per chunk of a plain panel
+constexpr int PAIR_KB = 512;                    // K bytes per chunk of a pair panel
+constexpr int TASK_KB = 256;                    // K bytes of one plain task (4 KB of weights)
 constexpr unsigned char CHUNK_PANEL = 0x40;     // Chunk.seg flag: row0 = panel, nrows = K-slice
 static_assert(CONVD % PANEL == 0 && VDIM % PANEL == 0 && QPROJ % PANEL == 0 &&
               KVPROJ % PANEL == 0 && HID % PANEL == 0 && FFN % PANEL == 0, "panels");
+static_assert(HID % TASK_KB == 0 && VDIM % TASK_KB == 0 && FFN % TASK_KB == 0 && HID % PAIR_KB == 0, "tasks");
 // Re-lay nrows rows (row r read from rowptr[r], K bytes each) as panels; pair =
-// rows come as (32 gate rows, 32 up rows) per pair panel, K = HID.
+// rows come as (16 gate rows, 16 up rows) per pair panel, K = HID.
 cudaError_t repack_panels(const int8_t* const* rowptr, int8_t* out, int nrows, int K, bool pair,
                           cudaStream_t st);
 
 int persist_smem_bytes();
 int persist_num_phases();
 int persist_max_chunks();
+size_t persist_trace_words(int G);   // words of the trace record for G CTAs
 int persist_max_blocks_per_sm();
 bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
                     std::vector<unsigned short>& phase_first, std::string& err);

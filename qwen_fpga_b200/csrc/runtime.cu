@@ -378,6 +378,8 @@ int ensure_seq_room(qwen_ctx* c, int launches) {
 // One decode step on the context stream with the selected engine.
 int launch_step(qwen_ctx* c) {
   if (c->engine == 1) {
+    // a traced step starts from a cleared record (0 = stamp not reached)
+    if (c->P.trace) QCUDA(c, cudaMemsetAsync(c->P.trace, 0, persist_trace_words(c->sm_count) * 8, c->st));
     cudaError_t e = launch_persistent(c->P, c->sm_count, c->st);
     if (e != cudaSuccess) return fail(c, QWEN_ERR_CUDA, "persistent launch: %s", cudaGetErrorString(e));
   } else {
@@ -579,7 +581,7 @@ int qwen_create(const char* blob_path, const char* index_path, int n_gpus, const
       P.head_tiles = tiles;
     }
     {
-      // every layer projection re-laid as 32-row panels for the persistent
+      // every layer projection re-laid as 16-row panels for the persistent
       // engine (second copies; the row-major tensors still serve engine 0)
       struct Job { std::vector<const int8_t*> rows; int K; bool pair; const int8_t** slot; };
       std::vector<Job> jobs;
@@ -593,7 +595,7 @@ int qwen_create(const char* blob_path, const char* index_path, int n_gpus, const
         if (L.linear) { rows(in.rows, L.qkv_q, CONVD, HID); rows(in.rows, L.z_q, VDIM, HID); }
         else { rows(in.rows, L.q_q, QPROJ, HID); rows(in.rows, L.k_q, KVPROJ, HID); rows(in.rows, L.v_q, KVPROJ, HID); }
         rows(out.rows, L.linear ? L.out_q : L.o_q, HID, VDIM);
-        for (int q = 0; q < FFN / PANEL; ++q) {   // pair panel q: gate rows 32q.., then up rows 32q..
+        for (int q = 0; q < FFN / PANEL; ++q) {   // pair panel q: gate rows 16q.., then up rows 16q..
           rows(gu.rows, L.gate_q + (size_t)q * PANEL * HID, PANEL, HID);
           rows(gu.rows, L.up_q + (size_t)q * PANEL * HID, PANEL, HID);
         }
@@ -678,8 +680,7 @@ int qwen_trace_enable(qwen_ctx* c, int on) {
   int rc;
   if ((rc = check_ctx(c))) return rc;
   if (on && !c->P.trace) {
-    const size_t words = (size_t)c->sm_count * persist_num_phases() * TRACE_STAMPS +
-                         (size_t)persist_max_chunks() * 4;
+    const size_t words = persist_trace_words(c->sm_count);
     if ((rc = dalloc(c, &c->P.trace, words * 8))) return rc;
   } else if (!on) {
     c->P.trace = nullptr;   // the buffer stays allocated until qwen_destroy
@@ -692,8 +693,7 @@ int qwen_trace_read(qwen_ctx* c, unsigned long long* out, int max_words, int* n_
   int rc;
   if ((rc = check_ctx(c))) return rc;
   if (!c->P.trace) return fail(c, QWEN_ERR_STATE, "tracing is off");
-  const size_t words = (size_t)c->sm_count * persist_num_phases() * TRACE_STAMPS +
-                       (size_t)persist_max_chunks() * 4;
+  const size_t words = persist_trace_words(c->sm_count);
   if (!out || (size_t)max_words < words) return fail(c, QWEN_ERR_ARG, "need %zu words", words);
   QCUDA(c, cudaStreamSynchronize(c->st));
   QCUDA(c, cudaMemcpy(out, c->P.trace, words * 8, cudaMemcpyDeviceToHost));
