@@ -58,12 +58,15 @@ constexpr unsigned long long WAIT_NS = 2000000000ull;  // 2 s bound on any wait
 
 // ---- shared memory layout (dynamic, offsets from the aligned base)
 constexpr int OFF_RING = 0;
-constexpr int OFF_DIG = OFF_RING + NSLOT * SLOT;          // digit image, 3 * KMAX bytes (see dig_off)
-constexpr int OFF_XF = OFF_DIG + 3 * KMAX;                // float [KMAX]
+constexpr int DIG_BYTES = 3 * KMAX;                       // the digit image (see dig_off)
+constexpr int OFF_DIG = OFF_RING + NSLOT * SLOT;
+constexpr int OFF_XF = OFF_DIG + DIG_BYTES;               // float [KMAX]
 constexpr int OFF_HS = OFF_XF + 4 * KMAX;                 // float [HID]
 constexpr int MAXPAN = NSLOT;                             // panels of one phase on one CTA (at most)
-constexpr int OFF_PART = OFF_HS + 4 * HID;                // int [MAXPAN][6][PANEL] panel digit sums
-constexpr int OFF_LAY = OFF_PART + 4 * MAXPAN * 6 * PANEL; // LayerW [NLAYER]
+constexpr int MAXTASK = NSLOT * (PANEL_KB / TASK_KB);     // tasks of one phase on one CTA (at most)
+constexpr int OFF_PART = OFF_HS + 4 * HID;                // int [MAXPAN][3][PANEL]: exact digit sums
+constexpr int OFF_PARTF = OFF_PART + 4 * MAXPAN * 3 * PANEL;  // float [MAXTASK][PANEL]: fp32 row dots
+constexpr int OFF_LAY = OFF_PARTF + 4 * MAXTASK * PANEL;  // LayerW [NLAYER]
 constexpr int OFF_CH = OFF_LAY + ((int)sizeof(LayerW) * NLAYER + 15) / 16 * 16;  // Chunk [MAXCH]
 constexpr int OFF_BAR = OFF_CH + 8 * MAXCH;               // u64 mbarriers, see bar_* below
 constexpr int NBAR = 3 * NSLOT + 5;                       // full, empty, mma per slot; acc_full[2], acc_empty[2], fin
@@ -100,6 +103,8 @@ struct Misc {
   unsigned long long wbest[NCW];
   float inv_h[LH];
   float gate_g, gate_beta;
+  float xinv;              // 1/rms of the current normed GEMV input (W8A32 path)
+  unsigned amax[2];        // bits of max|v| of the GEMV input of phases p with p & 1 = index
 };
 static_assert(sizeof(Misc) <= 1024, "misc");
 static_assert(OFF_MISC % 16 == 0, "tcgen05.alloc destination alignment");
@@ -302,7 +307,7 @@ __device__ __forceinline__ void chunk_src(const PCtx& c, const Chunk& k, const c
     size_t pbytes = 0;
     if (sub == 0) { base = L.pin; np = (L.linear ? CONVD + VDIM : QPROJ + 2 * KVPROJ) / PANEL; pbytes = (size_t)PANEL * HID; }
     else if (sub == 2) { base = L.pout; np = HID / PANEL; pbytes = (size_t)PANEL * VDIM; }
-    else if (sub == 3) { base = L.pgu; np = FFN / PANEL; pbytes = (size_t)2 * PANEL * HID; }
+    else if (sub == 3) { base = L.pgu; np = FFN / PAIR_ROWS; pbytes = (size_t)PANEL * HID; }
     else if (sub == 4) { base = L.pdown; np = HID / PANEL; pbytes = (size_t)PANEL * FFN; }
     if (!base || row0 >= np || (size_t)n * SLOTW >= pbytes) return;
     src = (const char*)base + (size_t)row0 * pbytes + (size_t)n * SLOTW;
@@ -370,15 +375,23 @@ __device__ __forceinline__ bool wait_full(PCtx& c, int i) {
 // any.  Collective over the consumer threads.  false on abort.  One copy in
 // the kernel (not inlined): every phase's input wait runs the same
 // instructions.
+//
+// With amax (a shared word, zero on entry; may be null) the wait also folds
+// max|v| of the values into it (red.shared.max on the bits of a non-negative
+// float orders like the floats), v = the value, or value * (1 + g) with the
+// thread's norm gains g (gain, for n = 2 * PT: one pair per thread).  The
+// barrier that ends the wait publishes it.
 __device__ __noinline__ bool wait_tagged_words(Misc* ms, int* err, int* abort_flag,
                                                const unsigned long long* src, int n, unsigned tag,
-                                               float* dst) {
+                                               float* dst, unsigned* amax, bool gain, float2 g2) {
   const unsigned long long t0 = gtime();
   const int npair = n >> 1;
   unsigned pend = 0;
 #pragma unroll
   for (int j = 0; j < MAXP; ++j)
     if ((int)threadIdx.x + PT * j < npair) pend |= 1u << j;
+  float vmax = 0.0f;
+  bool folded = false;
   int it = 0;
   for (;;) {
     unsigned long long a[MAXP], b[MAXP];
@@ -389,10 +402,22 @@ __device__ __noinline__ bool wait_tagged_words(Misc* ms, int* err, int* abort_fl
     for (int j = 0; j < MAXP; ++j) {
       if ((pend >> j & 1) && tag_ok(a[j], tag) && tag_ok(b[j], tag)) {
         const int q = threadIdx.x + PT * j;
-        dst[2 * q] = tv_val(a[j]);
-        dst[2 * q + 1] = tv_val(b[j]);
+        const float v0 = tv_val(a[j]), v1 = tv_val(b[j]);
+        dst[2 * q] = v0;
+        dst[2 * q + 1] = v1;
+        if (gain) vmax = fmaxf(vmax, fmaxf(fabsf(__fmul_rn(v0, __fadd_rn(1.0f, g2.x))),
+                                           fabsf(__fmul_rn(v1, __fadd_rn(1.0f, g2.y)))));
+        else vmax = fmaxf(vmax, fmaxf(fabsf(v0), fabsf(v1)));
         pend &= ~(1u << j);
       }
+    }
+    if (amax) {
+      // lanes whose values all arrived fold their max once: one shared atomic per warp
+      const bool nw = pend == 0 && !folded;
+      const unsigned wm = __reduce_max_sync(0xffffffffu, nw ? __float_as_uint(vmax) : 0u);
+      if (nw) folded = true;
+      if ((threadIdx.x & 31) == 0 && wm)
+        asm volatile("red.shared.max.u32 [%0], %1;" :: "r"(smem_u32(amax)), "r"(wm) : "memory");
     }
     if (consumer_and(pend == 0)) return true;
     if (((++it) & 15) == 0) {
@@ -417,7 +442,13 @@ __device__ __noinline__ bool wait_tagged_words(Misc* ms, int* err, int* abort_fl
 }
 __device__ __forceinline__ bool wait_tagged(PCtx& c, const unsigned long long* src, int n, unsigned tag,
                                             float* dst) {
-  return wait_tagged_words(c.ms, c.A->err, c.A->abort_flag, src, n, tag, dst);
+  return wait_tagged_words(c.ms, c.A->err, c.A->abort_flag, src, n, tag, dst, nullptr, false,
+                           make_float2(0.0f, 0.0f));
+}
+// The same, folding max|v| into *amax (see above).
+__device__ __forceinline__ bool wait_tagged_max(PCtx& c, const unsigned long long* src, int n, unsigned tag,
+                                                float* dst, unsigned* amax, bool gain, float2 g2) {
+  return wait_tagged_words(c.ms, c.A->err, c.A->abort_flag, src, n, tag, dst, amax, gain, g2);
 }
 
 // ---------------------------------------------------------------- prologues
@@ -426,8 +457,51 @@ __device__ __forceinline__ bool wait_tagged(PCtx& c, const unsigned long long* s
 // mma.m16n8k32: K-step s (positions 32s .. 32s+31) is 96 bytes, 12 lanes x 8
 // bytes, lane 4d + u = digit d at positions 32s + 4u .. +3, then 32s + 16 + 4u
 // .. +3.  Byte offset of the 4 positions k .. k+3 (k a multiple of 4) of digit d:
+// 2^e as a float for -126 <= e <= 127.
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
+
 __device__ __forceinline__ int dig_off(int d, int k) {
   return (k >> 5) * 96 + (d * 4 + ((k >> 2) & 3)) * 8 + ((k >> 4) & 1) * 4;
+}
+
+// W8A32 digit image of v = src[0 .. K) (a normed input: v = src * (1 + g),
+// K = 2 PT, the thread's gains g2) into the CTA's image, shift from the exact
+// max|v| whose bits the input wait folded into amax: |X| <= 2^22 (the rule of
+// the other encoders), three int8 digits per position; an input whose max is
+// below 2^-104 encodes as zero (its share of any output is below 2^-104 * 127 *
+// K of the row scale).  Thread = position pairs tid + PT j.  Returns 2^-shift
+// (0: all zero).  Ends with a CTA barrier.  One copy (not inlined), shared by
+// the four GEMV phases.
+__device__ __noinline__ float encode_fixed(unsigned char* sm, const float* src, int K, unsigned amax, bool gain,
+                                           float2 g2) {
+  int8_t* dg = (int8_t*)(sm + OFF_DIG);
+  const int sh = 22 - ((int)((amax >> 23) & 0xffu) - 126);   // max in [2^(ex-1), 2^ex)
+  const bool live = amax != 0u && sh <= 126;
+  const float p2 = live ? pow2f(sh) : 0.0f;
+  for (int q = threadIdx.x; 2 * q < K; q += PT) {
+    float v0 = src[2 * q], v1 = src[2 * q + 1];
+    if (gain) {
+      v0 = __fmul_rn(v0, __fadd_rn(1.0f, g2.x));
+      v1 = __fmul_rn(v1, __fadd_rn(1.0f, g2.y));
+    }
+    const int X[2] = {__float2int_rn(v0 * p2), __float2int_rn(v1 * p2)};   // exact products
+    unsigned w_[3] = {0u, 0u, 0u};
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int a0 = (X[e] << 24) >> 24;
+      const int X1 = (X[e] - a0) >> 8;
+      const int a1 = (X1 << 24) >> 24;
+      const int a2 = (X1 - a1) >> 8;
+      w_[0] |= ((unsigned)a0 & 0xffu) << (8 * e);
+      w_[1] |= ((unsigned)a1 & 0xffu) << (8 * e);
+      w_[2] |= ((unsigned)a2 & 0xffu) << (8 * e);
+    }
+#pragma unroll
+    for (int d = 0; d < 3; ++d)
+      *reinterpret_cast<unsigned short*>(dg + dig_off(d, (2 * q) & ~3) + ((2 * q) & 2)) = (unsigned short)w_[d];
+  }
+  consumer_sync();
+  return live ? pow2f(-sh) : 0.0f;
 }
 
 // Recombine the digit sums in fp32: (a2 * 65536 + a1 * 256 + a0) * (x_scale * s_w).
@@ -438,8 +512,6 @@ __device__ __forceinline__ float finish_f32(int a0, int a1, int a2, int ndig, fl
   return y * xs_sw;
 }
 
-// 2^e as a float for -126 <= e <= 127.
-__device__ __forceinline__ float pow2f(int e) { return __int_as_float((e + 127) << 23); }
 
 // Digit image of xf[0..K) (W8A32, three digits), or the golden _qa int8
 // quantiser (ACT_INT8, one digit), into the fragment-ordered digit image.
@@ -685,9 +757,11 @@ __device__ bool load_residual(PCtx& c, int p) {
   return true;
 }
 
-// Prologue of the OUT (sub 2) and DOWN (sub 4) phases: the residual rows, the
-// inputs into xf, encoded into the shared digit planes.  false on abort.
-__device__ bool prologue(PCtx& c, int p) {
+// Prologue of the OUT (sub 2) and DOWN (sub 4) phases: the residual rows and
+// the K inputs into xf.  ACT_INT8 (amax null): their digit image for the whole
+// CTA as well (encode_lin); W8A32: max|x| folded into *amax instead, for
+// encode_fixed.  false on abort.
+__device__ bool prologue(PCtx& c, int p, unsigned* amax, int& K_out) {
   float* xf = (float*)(c.sm + OFF_XF);
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
@@ -702,7 +776,9 @@ __device__ bool prologue(PCtx& c, int p) {
   const float gw = gated ? __ldg(L.gnorm_w + (threadIdx.x % LV)) : 0.0f;   // element i = tid + 512 j
   const unsigned long long* src = sub == 4 ? A.tv_act : (L.linear ? A.tv_o : A.tv_attn);
   const int K = sub == 4 ? FFN : (L.linear ? VDIM : NH * HD);
-  if (!wait_tagged(c, src, K, tag_of(c, p - 1), xf)) return false;
+  K_out = K;
+  if (!wait_tagged_max(c, src, K, tag_of(c, p - 1), xf, gated ? nullptr : amax, false, make_float2(0.0f, 0.0f)))
+    return false;
   if (gated) {
     // gated RMSNorm of the delta-rule output (golden/model.py:183-189), z from
     // IN(l) parked in the digit region
@@ -717,13 +793,20 @@ __device__ bool prologue(PCtx& c, int p) {
       if (lane == 0) ms->inv_h[h] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / LV), EPS)));
     }
     consumer_sync();
+    float vmax = 0.0f;
     for (int i = threadIdx.x; i < VDIM; i += PT) {
       const float v = __fmul_rn(__fmul_rn(xf[i], ms->inv_h[i / LV]), gw);
       xf[i] = __fmul_rn(v, silu_f(zb[i]));
+      vmax = fmaxf(vmax, fabsf(xf[i]));
+    }
+    if (amax) {
+      const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(vmax));
+      if ((threadIdx.x & 31) == 0 && wm)
+        asm volatile("red.shared.max.u32 [%0], %1;" :: "r"(smem_u32(amax)), "r"(wm) : "memory");
     }
     consumer_sync();
   }
-  encode_lin(c, K, i8);
+  if (!amax) encode_lin(c, K, i8);
   return true;
 }
 
@@ -996,7 +1079,6 @@ __device__ __forceinline__ void release_panel_chunk(PCtx& c, int i) {
 // Tasks of chunk k of GEMV phase `sub`.
 __host__ __device__ __forceinline__ int chunk_tasks(const Chunk& k, int sub) {
   if (!(k.seg & CHUNK_PANEL)) return k.nrows;
-  if (sub == 3) return PAIR_KB / 128;
   const int K = sub == 0 ? HID : (sub == 2 ? VDIM : FFN);
   const int rem = K - (int)k.nrows * PANEL_KB;
   return (rem < PANEL_KB ? rem : PANEL_KB) / TASK_KB;
@@ -1008,17 +1090,19 @@ __host__ __device__ __forceinline__ int chunk_tasks(const Chunk& k, int sub) {
 // in the first chunk whose tb exceeds t; panel v starts at the chunk whose pv
 // is v + 1.  Every warp runs exactly its own tasks (t = wid, wid + NCW, ...).
 struct TaskMap {
-  int nq, tb, pv, start, ntask, npan;
+  int nq, tb, pv, start, pan, ntask, npan;
 };
 __device__ __forceinline__ TaskMap task_map(const PCtx& c, int sub, int i0, int nj) {
   const int lane = threadIdx.x & 31;
   TaskMap m;
   m.nq = 0;
   m.start = 0;
+  m.pan = 0;
   if (lane < nj) {
     const Chunk k = c.ch[i0 + lane];
     m.nq = chunk_tasks(k, sub);
     if (k.seg & CHUNK_PANEL) {
+      m.pan = 1;
       m.start = 1;
       if (lane > 0) {
         const Chunk kp = c.ch[i0 + lane - 1];
@@ -1051,103 +1135,148 @@ __device__ __forceinline__ int chunk_panel(const TaskMap& m, int j) {
 __device__ __forceinline__ int panel_chunk(const TaskMap& m, int v) {
   return __ffs(__ballot_sync(0xffffffffu, m.start && m.pv == v + 1)) - 1;
 }
-
-// Row-scale pointers of panel row r of GEMV phase `sub` (second: the up row of
-// a GATEUP pair, else null).
-__device__ __forceinline__ void row_scales(const LayerW& L, int sub, int r, const float*& s0, const float*& s1) {
-  s1 = nullptr;
+// Row scale of row pr of panel q of GEMV phase `sub` (a pair panel: rows 0-7
+// gate rows 8q.., rows 8-15 the same up rows).
+__device__ __forceinline__ const float* row_scale(const LayerW& L, int sub, int q, int pr) {
+  if (sub == 3) return (pr < PAIR_ROWS ? L.gate_s : L.up_s) + q * PAIR_ROWS + pr % PAIR_ROWS;
+  const int r = q * PANEL + pr;
   if (sub == 0) {
-    if (L.linear) s0 = r < CONVD ? L.qkv_s + r : L.z_s + (r - CONVD);
-    else s0 = r < QPROJ ? L.q_s + r : (r < QPROJ + KVPROJ ? L.k_s + (r - QPROJ) : L.v_s + (r - QPROJ - KVPROJ));
-  } else if (sub == 3) {
-    s0 = L.gate_s + r;
-    s1 = L.up_s + r;
-  } else {
-    s0 = (sub == 2 ? (L.linear ? L.out_s : L.o_s) : L.down_s) + r;
+    if (L.linear) return r < CONVD ? L.qkv_s + r : L.z_s + (r - CONVD);
+    return r < QPROJ ? L.q_s + r : (r < QPROJ + KVPROJ ? L.k_s + (r - QPROJ) : L.v_s + (r - QPROJ - KVPROJ));
   }
+  return (sub == 2 ? (L.linear ? L.out_s : L.o_s) : L.down_s) + r;
 }
 
 // A GEMV phase over panels (IN, OUT, GATEUP, DOWN).  The input vector is
-// encoded once into the digit image; every warp runs its own tasks of the
-// CTA's chunks; after a CTA barrier, warp v % NCW finishes the v-th panel (16
-// rows) of the CTA's phase: the projection rows (IN), silu(gate) * up
-// (GATEUP, golden/model.py:236), or h + y (OUT, DOWN).  The fp32 in_proj_b /
+// encoded once into the CTA's digit image:
+//   W8A32 (default): the input wait folds max|v| of the values as they arrive
+//     (v = z = h * (1 + w) for the normed input of IN / GATEUP, else x), so one
+//     barrier after the wait (encode_fixed) completes the image.  The 1/rms of
+//     a normed input (sum of squares in numpy's pairwise order,
+//     golden/model.py:74) is computed by warp 0 while the other warps run the
+//     tasks, and applied with 2^-shift when the panel finishes.
+//   ACT_INT8: the golden per-vector quantiser of x itself (cta_encode_1024,
+//     encode_lin).
+// Every warp runs its own tasks; a task adds exact int32 digit sums into its
+// panel's accumulators.  After a CTA barrier, warp v % NCW finishes the v-th
+// panel of the CTA's phase: the projection rows (IN), silu(gate) * up
+// (GATEUP, golden/model.py:236), or h + y (OUT, DOWN); the fp32 in_proj_b /
 // in_proj_a rows of a DeltaNet IN (golden/model.py:146-147) are dotted with x
-// in fp32 by their tasks directly.
+// by their tasks.
 __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
   float* hs = (float*)(c.sm + OFF_HS);
+  const float* xf = (const float*)(c.sm + OFF_XF);
   const int l = p / 5, sub = p % 5;
   const LayerW& L = c.lay[l];
   const bool i8 = ms->act_int8 != 0;
+  const bool normed = sub == 0 || sub == 3;
   const float* gw = sub == 0 ? L.in_norm : L.post_norm;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int nj = i1 - i0;
   trace_warp(c, p, 0);
   int good = 1;
-  if (nj > NSLOT) {   // the schedule keeps a phase within the ring (and MAXPAN panels)
+  if (nj > NSLOT) {   // the schedule keeps a phase within the ring (MAXPAN panels, MAXTASK tasks)
     if (threadIdx.x == 0) check_fail(c, 8, nj);
     good = 0;
   }
   const TaskMap m = task_map(c, sub, i0, good ? nj : 0);
+  // W8A32 normed inputs: warp 0 computes 1/rms, so tasks start at warp 1
+  const int off = (normed && !i8) ? 1 : 0;
+  const int t_first = (wid + NCW - off) % NCW;
   // panel row of this lane in the finishing step (lanes with lane & 2 hold none)
   const bool own = (lane & 2) == 0;
   const int pr = (lane >> 2) + 8 * (lane & 1);
-  // the row scales of the (at most two) panels this warp will finish, fetched
-  // before the input wait so that their latency hides behind it
-  float sp[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+  // before the input wait, so that their latency hides behind it: the row
+  // scales of the (at most two) panels this warp finishes, the norm gains of
+  // its first task's positions, and its first chunk (requested in an earlier
+  // phase, so waiting for it here cannot hold anything up)
+  float sp[2] = {0.0f, 0.0f};
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
     const int v = wid + NCW * u;
     if (v < m.npan) {
-      const int r = (int)c.ch[i0 + panel_chunk(m, v)].row0 * PANEL + pr;
-      const float* s0;
-      const float* s1;
-      row_scales(L, sub, r, s0, s1);
-      if (own) {
-        sp[u][0] = __ldg(s0);
-        if (s1) sp[u][1] = __ldg(s1);
-      }
+      const float* sc = row_scale(L, sub, (int)c.ch[i0 + panel_chunk(m, v)].row0, pr);
+      if (own) sp[u] = __ldg(sc);
     }
   }
-  // this warp's first chunk: its bytes were requested in an earlier phase, so
-  // waiting for them here (before the input wait) cannot hold anything up
+  const float2 g2 = normed ? __ldg(reinterpret_cast<const float2*>(gw) + threadIdx.x) : make_float2(0.f, 0.f);
   bool first_in = false;
-  if (good && wid < m.ntask) {
+  if (good && t_first < m.ntask) {
     int q;
-    first_in = wait_full(c, i0 + task_chunk(m, wid, q));
+    first_in = wait_full(c, i0 + task_chunk(m, t_first, q));
     if (!first_in) good = 0;
     trace_warp(c, p, 3);
   }
-  float inv = 0.0f, sx = 0.0f;
-  if (sub == 0 || sub == 3) {
-    const float2 g2 = __ldg(reinterpret_cast<const float2*>(gw) + threadIdx.x);
+  // the input vector (W8A32: its max folded into amax by the wait)
+  float sx = 0.0f, xs = 0.0f;
+  unsigned* amax = i8 ? nullptr : &ms->amax[p & 1];
+  int K = HID;
+  if (normed) {
     if (sub == 0 && l == 0) {
       // residual stream starts at the dequantised embedding row (golden/model.py:246)
       const int tok = ms->tok;
       const float sc = __ldg(A.emb_s + tok);
       const int8_t* row = A.emb_q + (size_t)tok * HID;
-      for (int i = threadIdx.x; i < HID; i += PT) hs[i] = __fmul_rn((float)row[i], sc);
+      const float h0 = __fmul_rn((float)row[2 * threadIdx.x], sc), h1 = __fmul_rn((float)row[2 * threadIdx.x + 1], sc);
+      hs[2 * threadIdx.x] = h0;
+      hs[2 * threadIdx.x + 1] = h1;
+      if (amax) {
+        const float vm = fmaxf(fabsf(__fmul_rn(h0, __fadd_rn(1.0f, g2.x))), fabsf(__fmul_rn(h1, __fadd_rn(1.0f, g2.y))));
+        const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(vm));
+        if (lane == 0 && wm) asm volatile("red.shared.max.u32 [%0], %1;" :: "r"(smem_u32(amax)), "r"(wm) : "memory");
+      }
       consumer_sync();
-    } else if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) {
+    } else if (!wait_tagged_max(c, A.tv_h, HID, tag_of(c, p - 1), hs, amax, true, g2)) {
       return false;
     }
     trace_warp(c, p, 1);
     if (threadIdx.x == 0) ms->hs_tag = tag_of(c, p - 1);   // layer 0: the embedding (tag of "phase -1")
-    cta_encode_1024(c, hs, g2, i8, inv, sx, false, p);
-  } else if (!prologue(c, p)) {
-    return false;
+    if (i8) {
+      float inv;
+      cta_encode_1024(c, hs, g2, true, inv, sx, false, p);
+    } else {
+      xs = encode_fixed(c.sm, hs, HID, *amax, true, g2);
+    }
+    if (!i8 && wid == 0) {
+      // sum of squares in numpy's pairwise order: chain ch = block ch / 8,
+      // accumulator ch % 8 (lane = chains lane, lane + 32: blocks 0-3, 4-7),
+      // ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)) in a block, then the
+      // blocks pairwise; the two halves summed last
+      float r[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int ch = lane + 32 * u;
+        const float* a = hs + 128 * (ch >> 3) + (ch & 7);
+        float acc = __fmul_rn(a[0], a[0]);
+#pragma unroll
+        for (int i = 1; i < 16; ++i) acc = __fadd_rn(acc, __fmul_rn(a[8 * i], a[8 * i]));
+        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
+        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
+        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
+        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
+        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 16));
+        r[u] = acc;
+      }
+      const float tot = __fadd_rn(r[0], r[1]);
+      // tot / HID as the product by 1/HID (HID a power of two: the same
+      // number); 1/sqrt through the correctly rounded reciprocal
+      if (lane == 0) ms->xinv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(tot, 1.0f / HID), EPS)));
+      trace_warp(c, p, 8);
+    }
+  } else {
+    if (!prologue(c, p, amax, K)) return false;
+    if (!i8) xs = encode_fixed(c.sm, xf, K, *amax, false, g2);
   }
   trace_mark(c, p, 1);
   trace_warp(c, p, 2);
-  const unsigned char* fr = c.sm + OFF_DIG;
+  const unsigned char* fr = c.sm + OFF_DIG;                   // the CTA's digit image
+  float* part_f = (float*)(c.sm + OFF_PARTF);
   const unsigned part = smem_u32(c.sm + OFF_PART);
-  const int nd = ms->ndig;
-  const float xsf = (float)ms->scale;
+  const int nd = i8 ? ms->ndig : 3;
   const unsigned tag = tag_of(c, p);
-  const bool pair = (sub == 3);
-  for (int t = wid; good && t < m.ntask; t += NCW) {
+  for (int t = t_first; good && t < m.ntask; t += NCW) {
     int q;
     const int j = task_chunk(m, t, q);
     const int i = i0 + j;
@@ -1158,77 +1287,100 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
       good = 0;
       break;
     }
-    if (!(t == wid && first_in) && !wait_full(c, i)) { good = 0; break; }
+    if (!(t == t_first && first_in) && !wait_full(c, i)) { good = 0; break; }
     if (t == 0) trace_mark(c, p, 2);
-    const unsigned sa = smem_u32(c.sm + OFF_RING + (i % NSLOT) * SLOT);
+    const unsigned char* slot = c.sm + OFF_RING + (i % NSLOT) * SLOT;
     if (!pan) {
-      const float* row = (const float*)(c.sm + OFF_RING + (i % NSLOT) * SLOT) + q * HID;
-      const float y = row_dot_f32(row, (const float*)(c.sm + OFF_XF));
-      if (lane == 0) st_tv(A.tv_ab + (k.seg == 2 ? 0 : LH) + (int)k.row0 + q, y, tag);
+      // row q of the chunk, dotted with x: under ACT_INT8 the encoder's x in
+      // xf; else z = h (1 + w), its 1/rms applied when the phase finishes
+      const float* row = (const float*)slot + q * HID;
+      float a = 0.0f;
+#pragma unroll
+      for (int u = 0; u < HID / 128; ++u) {
+        const int pos = 4 * (lane + 32 * u);
+        const float4 w4 = *reinterpret_cast<const float4*>(row + pos);
+        float4 x4;
+        if (i8) {
+          x4 = *reinterpret_cast<const float4*>(xf + pos);
+        } else {
+          const float4 h4 = *reinterpret_cast<const float4*>(hs + pos);
+          const float4 g4 = __ldg(reinterpret_cast<const float4*>(gw + pos));
+          x4 = make_float4(__fmul_rn(h4.x, __fadd_rn(1.0f, g4.x)), __fmul_rn(h4.y, __fadd_rn(1.0f, g4.y)),
+                           __fmul_rn(h4.z, __fadd_rn(1.0f, g4.z)), __fmul_rn(h4.w, __fadd_rn(1.0f, g4.w)));
+        }
+        a = fmaf(w4.x, x4.x, a);
+        a = fmaf(w4.y, x4.y, a);
+        a = fmaf(w4.z, x4.z, a);
+        a = fmaf(w4.w, x4.w, a);
+      }
+      a = warp_sum(a);
+      if (lane == 0) part_f[t * PANEL] = a;
       continue;
     }
-    // a plain task: 8 K-steps of the slot; a pair task: 4 K-steps of the gate
-    // half, then the same 4 of the up half (SLOTW / 2 further on)
-    const int ns = pair ? PAIR_KB / 128 : TASK_KB / 32;
-    const int s0 = pair ? ((int)k.nrows * PAIR_KB + 128 * q) >> 5 : ((int)k.nrows * PANEL_KB + TASK_KB * q) >> 5;
-    const unsigned pv = part + 4u * (unsigned)(chunk_panel(m, j) * 6 * PANEL + pr);
-#pragma unroll 1
-    for (int h = 0; h < (pair ? 2 : 1); ++h) {
-      int d3[3];
-      panel_mma(sa + (SLOTW / 2) * h + 512u * ns * q, fr, s0, ns, nd, d3);
-      if (own) {
-        const unsigned ph = pv + 4u * PANEL * 3 * h;
-        red_add_s32(ph, d3[0]);
-        if (nd == 3) {
-          red_add_s32(ph + 4u * PANEL, d3[1]);
-          red_add_s32(ph + 4u * PANEL * 2, d3[2]);
-        }
+    const int kb = (int)k.nrows * PANEL_KB + TASK_KB * q;   // the task's first K position
+    const unsigned sa = smem_u32(slot) + 512u * (TASK_KB / 32) * q;
+    int d3[3];
+    panel_mma(sa, fr, kb >> 5, TASK_KB / 32, nd, d3);
+    const int vp = chunk_panel(m, j);
+    if (own) {
+      const unsigned pv = part + 4u * (unsigned)(vp * 3 * PANEL + pr);
+      red_add_s32(pv, d3[0]);
+      if (nd == 3) {
+        red_add_s32(pv + 4u * PANEL, d3[1]);
+        red_add_s32(pv + 8u * PANEL, d3[2]);
       }
     }
   }
   trace_warp(c, p, 4);
   if (!consumer_and(good)) return false;
   trace_warp(c, p, 5);
+  // x scale of the digit sums: ACT_INT8 the quantiser's s_x; W8A32 2^-shift,
+  // times 1/rms for a normed input (exact: a power of two times a float)
+  const float xinv = (normed && !i8) ? ms->xinv : 1.0f;
+  const float xsc = i8 ? (float)ms->scale : __fmul_rn(xs, xinv);
+  if (threadIdx.x == 0 && amax) *amax = 0u;   // read by every thread before the task barrier
   for (int v = wid; v < m.npan; v += NCW) {
-    const Chunk k = c.ch[i0 + panel_chunk(m, v)];
-    if (!own) continue;
-    // the panel's sums, and the accumulators zeroed for the next phase
-    int* pv = (int*)(c.sm + OFF_PART) + v * 6 * PANEL + pr;
-    int t[6];
-#pragma unroll
-    for (int e = 0; e < 6; ++e) { t[e] = pv[e * PANEL]; pv[e * PANEL] = 0; }
-    const int r = (int)k.row0 * PANEL + pr;
-    float sa, sb;
-    if (v < 2 * NCW) {
-      sa = v < NCW ? sp[0][0] : sp[1][0];
-      sb = v < NCW ? sp[0][1] : sp[1][1];
-    } else {
-      const float* s0;
-      const float* s1;
-      row_scales(L, sub, r, s0, s1);
-      sa = __ldg(s0);
-      sb = s1 ? __ldg(s1) : 0.0f;
+    const int q = (int)c.ch[i0 + panel_chunk(m, v)].row0;
+    float y = 0.0f;
+    if (own) {
+      const float s_row = v < NCW ? sp[0] : (v < 2 * NCW ? sp[1] : __ldg(row_scale(L, sub, q, pr)));
+      // the panel's exact sums, and the accumulators zeroed for the next phase
+      int* pv = (int*)(c.sm + OFF_PART) + v * 3 * PANEL + pr;
+      const int a0 = pv[0], a1 = pv[PANEL], a2 = pv[2 * PANEL];
+      pv[0] = 0;
+      pv[PANEL] = 0;
+      pv[2 * PANEL] = 0;
+      y = finish_f32(a0, a1, a2, nd, xsc * s_row);
     }
-    if (sub == 0) {
-      unsigned long long* out;
-      int o;
-      if (L.linear) {
-        if (r < CONVD) { out = A.tv_qkv; o = r; }
-        else { out = A.tv_z; o = r - CONVD; }
+    if (sub == 3) {
+      // pair panel: lane pr = g holds gate row 8q + g, its neighbour the up row
+      const float up = __shfl_xor_sync(0xffffffffu, y, 1);
+      if (own && (lane & 1) == 0) st_tv(A.tv_act + q * PAIR_ROWS + pr, __fmul_rn(silu_f(y), up), tag);
+    } else if (own) {
+      const int r = q * PANEL + pr;
+      if (sub == 0) {
+        unsigned long long* out;
+        int o;
+        if (L.linear) {
+          if (r < CONVD) { out = A.tv_qkv; o = r; }
+          else { out = A.tv_z; o = r - CONVD; }
+        } else {
+          if (r < QPROJ) { out = A.tv_qg; o = r; }
+          else if (r < QPROJ + KVPROJ) { out = A.tv_kvn; o = r - QPROJ; }
+          else { out = A.tv_kvn + KVPROJ; o = r - QPROJ - KVPROJ; }
+        }
+        st_tv(out + o, y, tag);
       } else {
-        if (r < QPROJ) { out = A.tv_qg; o = r; }
-        else if (r < QPROJ + KVPROJ) { out = A.tv_kvn; o = r - QPROJ; }
-        else { out = A.tv_kvn + KVPROJ; o = r - QPROJ - KVPROJ; }
+        st_tv(A.tv_h + r, __fadd_rn(hs[r], y), tag);
       }
-      st_tv(out + o, finish_f32(t[0], t[1], t[2], nd, xsf * sa), tag);
-    } else if (sub == 3) {
-      const float g = finish_f32(t[0], t[1], t[2], nd, xsf * sa);
-      const float uu = finish_f32(t[3], t[4], t[5], nd, xsf * sb);
-      st_tv(A.tv_act + r, __fmul_rn(silu_f(g), uu), tag);
-    } else {
-      const float y = finish_f32(t[0], t[1], t[2], nd, xsf * sa);
-      st_tv(A.tv_h + r, __fadd_rn(hs[r], y), tag);
     }
+  }
+  // the fp32 rows (W8A32: times 1/rms)
+  for (int t = wid; t < m.ntask; t += NCW) {
+    int q;
+    const Chunk k = c.ch[i0 + task_chunk(m, t, q)];
+    if (k.seg & CHUNK_PANEL) continue;
+    if (lane == 0) st_tv(A.tv_ab + (k.seg == 2 ? 0 : LH) + (int)k.row0 + q, __fmul_rn(part_f[t * PANEL], xinv), tag);
   }
   trace_warp(c, p, 6);
   // the outputs are out: now give the slots back and refill them (off the
@@ -1594,8 +1746,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
     ((int*)c.lay)[i] = ((const int*)A.layers)[i];
   for (int i = threadIdx.x; i < c.nch; i += NTHREADS) chs[i] = A.chunks[(size_t)blockIdx.x * MAXCH + i];
   for (int i = threadIdx.x; i <= NPHASE; i += NTHREADS) ms->pf[i] = A.phase_first[(size_t)blockIdx.x * (NPHASE + 1) + i];
-  for (int i = threadIdx.x; i < MAXPAN * 6 * PANEL; i += NTHREADS) ((int*)(sm + OFF_PART))[i] = 0;
+  for (int i = threadIdx.x; i < MAXPAN * 3 * PANEL; i += NTHREADS) ((int*)(sm + OFF_PART))[i] = 0;
   if (threadIdx.x == 0) {
+    ms->amax[0] = 0u;
+    ms->amax[1] = 0u;
     ms->abort = 0;
     ms->pos = A.dyn->pos;
     ms->T = A.dyn->T;
@@ -1729,7 +1883,7 @@ size_t persist_trace_words(int G) {
 
 
 // Build the per-CTA chunk lists.
-//   IN, OUT, GATEUP, DOWN: whole panels (16 rows; all of a panel's K-slices on
+//   IN, OUT, GATEUP, DOWN: whole panels (16 rows, GATEUP 8 gate + 8 up; all of a panel's K-slices on
 //     one CTA).  Each panel goes to the CTA with the fewest 4 KB tasks so far
 //     in the phase, then the fewest bytes so far in the step, then the lowest
 //     index, among the CTAs whose ring still holds the panel's chunks with the
@@ -1774,18 +1928,14 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
     int npan, K;
     if (sub == 0) { npan = (linear ? CONVD + VDIM : QPROJ + 2 * KVPROJ) / PANEL; K = HID; }
     else if (sub == 2) { npan = HID / PANEL; K = VDIM; }
-    else if (sub == 3) { npan = FFN / PANEL; K = HID; }
+    else if (sub == 3) { npan = FFN / PAIR_ROWS; K = HID; }
     else { npan = HID / PANEL; K = FFN; }
     // a panel's K-slices: bytes and tasks of each
     std::vector<int> sl_bytes, sl_tasks;
-    if (sub == 3) {
-      for (int k0 = 0; k0 < K; k0 += PAIR_KB) { sl_bytes.push_back(2 * PANEL * PAIR_KB); sl_tasks.push_back(PAIR_KB / 128); }
-    } else {
-      for (int k0 = 0; k0 < K; k0 += PANEL_KB) {
-        const int kb = K - k0 < PANEL_KB ? K - k0 : PANEL_KB;
-        sl_bytes.push_back(PANEL * kb);
-        sl_tasks.push_back(kb / TASK_KB);
-      }
+    for (int k0 = 0; k0 < K; k0 += PANEL_KB) {
+      const int kb = K - k0 < PANEL_KB ? K - k0 : PANEL_KB;
+      sl_bytes.push_back(PANEL * kb);
+      sl_tasks.push_back(kb / TASK_KB);
     }
     const int nslice = (int)sl_bytes.size();
     int ptasks = 0;
@@ -1845,36 +1995,24 @@ cudaError_t repack_head_tiles(const int8_t* emb_q, int8_t* tiles, cudaStream_t s
   return cudaGetLastError();
 }
 
-// Re-lay rows as panels: thread = one 16-byte K-group of one row.
+// Re-lay rows as 16-row panels: thread = one 16-byte K-group of one row.
 __global__ void k_repack_panels(const int8_t* const* __restrict__ rowptr, int4* __restrict__ out, int nrows,
-                                int K, int pair) {
+                                int K) {
   const size_t id = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int G16 = K / 16;
   if (id >= (size_t)nrows * G16) return;
   const int g = (int)(id % G16);
   const size_t r = id / G16;
   const int4 v = reinterpret_cast<const int4*>(rowptr[r])[g];
-  size_t dst;
-  if (!pair) {
-    const size_t q = r / PANEL;
-    const int m = (int)(r % PANEL);
-    dst = q * PANEL * K + ((size_t)g * PANEL + m) * 16;
-  } else {   // pair panel q = rows (16 gate, 16 up); chunk s = K-groups 32s.. of gate then of up
-    const size_t q = r / (2 * PANEL);
-    const int half = (int)((r / PANEL) % 2), m = (int)(r % PANEL);
-    const int s = g / (PAIR_KB / 16), gg = g % (PAIR_KB / 16);
-    dst = q * 2 * PANEL * K + (size_t)s * SLOTW + (size_t)half * (SLOTW / 2) + ((size_t)gg * PANEL + m) * 16;
-  }
-  out[dst / 16] = v;
+  const size_t q = r / PANEL;
+  const int m = (int)(r % PANEL);
+  out[(q * PANEL * K + ((size_t)g * PANEL + m) * 16) / 16] = v;
 }
 
-cudaError_t repack_panels(const int8_t* const* rowptr, int8_t* out, int nrows, int K, bool pair,
-                          cudaStream_t st) {
-  if (nrows % (pair ? 2 * PANEL : PANEL) || K % TASK_KB || ((uintptr_t)out & 15) || (pair && K != HID))
-    return cudaErrorInvalidValue;
+cudaError_t repack_panels(const int8_t* const* rowptr, int8_t* out, int nrows, int K, cudaStream_t st) {
+  if (nrows % PANEL || K % TASK_KB || ((uintptr_t)out & 15)) return cudaErrorInvalidValue;
   const size_t n = (size_t)nrows * (K / 16);
-  k_repack_panels<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rowptr, reinterpret_cast<int4*>(out), nrows,
-                                                             K, pair ? 1 : 0);
+  k_repack_panels<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(rowptr, reinterpret_cast<int4*>(out), nrows, K);
   return cudaGetLastError();
 }
 

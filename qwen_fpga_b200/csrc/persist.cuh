@@ -74,21 +74,21 @@ cudaError_t repack_head_tiles(const int8_t* emb_q, int8_t* tiles, cudaStream_t s
 // element (m, k) sits at ((k / 16) * 16 + m) * 16 + k % 16, so one K = 32 step
 // of all 16 rows is 512 contiguous bytes (one ldmatrix.x4 = the MMA's A
 // fragment).  A chunk is one K-slice of a panel: 16 rows x 1024 bytes of K
-// (16 KB; the last slice of a K = 3584 panel is 512 bytes, 8 KB).  GATEUP uses
-// pair panels: 16 gate rows and the same 16 up rows; a chunk is 512 bytes of K
-// of both (gate half, then up half, 8 KB each).
+// (16 KB; the last slice of a K = 3584 panel is 512 bytes, 8 KB); a task is
+// 256 bytes of K of a chunk (4 KB of weights, 8 MMA K-steps).  GATEUP uses
+// pair panels: rows 0-7 are gate rows 8q .. 8q+7, rows 8-15 the same up rows,
+// so a gate row and its up row finish in neighbouring lanes.
 constexpr int PANEL = 16;
-constexpr int PANEL_KB = 1024;                  // K bytes per chunk of a plain panel
-constexpr int PAIR_KB = 512;                    // K bytes per chunk of a pair panel
-constexpr int TASK_KB = 256;                    // K bytes of one plain task (4 KB of weights)
+constexpr int PANEL_KB = 1024;                  // K bytes per chunk
+constexpr int TASK_KB = 256;                    // K bytes per task
+constexpr int PAIR_ROWS = 8;                    // gate (and up) rows per pair panel
 constexpr unsigned char CHUNK_PANEL = 0x40;     // Chunk.seg flag: row0 = panel, nrows = K-slice
 static_assert(CONVD % PANEL == 0 && VDIM % PANEL == 0 && QPROJ % PANEL == 0 &&
-              KVPROJ % PANEL == 0 && HID % PANEL == 0 && FFN % PANEL == 0, "panels");
-static_assert(HID % TASK_KB == 0 && VDIM % TASK_KB == 0 && FFN % TASK_KB == 0 && HID % PAIR_KB == 0, "tasks");
-// Re-lay nrows rows (row r read from rowptr[r], K bytes each) as panels; pair =
-// rows come as (16 gate rows, 16 up rows) per pair panel, K = HID.
-cudaError_t repack_panels(const int8_t* const* rowptr, int8_t* out, int nrows, int K, bool pair,
-                          cudaStream_t st);
+              KVPROJ % PANEL == 0 && HID % PANEL == 0 && FFN % PAIR_ROWS == 0, "panels");
+static_assert(HID % TASK_KB == 0 && VDIM % TASK_KB == 0 && FFN % TASK_KB == 0, "tasks");
+// Re-lay nrows rows (row r read from rowptr[r], K bytes each) as 16-row panels
+// (for GATEUP the caller orders the rows 8 gate, 8 up per panel).
+cudaError_t repack_panels(const int8_t* const* rowptr, int8_t* out, int nrows, int K, cudaStream_t st);
 
 int persist_smem_bytes();
 int persist_num_phases();

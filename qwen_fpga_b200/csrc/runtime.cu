@@ -583,21 +583,20 @@ int qwen_create(const char* blob_path, const char* index_path, int n_gpus, const
     {
       // every layer projection re-laid as 16-row panels for the persistent
       // engine (second copies; the row-major tensors still serve engine 0)
-      struct Job { std::vector<const int8_t*> rows; int K; bool pair; const int8_t** slot; };
+      struct Job { std::vector<const int8_t*> rows; int K; const int8_t** slot; };
       std::vector<Job> jobs;
       for (int l = 0; l < NLAYER; ++l) {
         LayerW& L = c->Mh.L[l];
-        Job in{{}, HID, false, &L.pin}, out{{}, VDIM, false, &L.pout}, gu{{}, HID, true, &L.pgu},
-            dn{{}, FFN, false, &L.pdown};
+        Job in{{}, HID, &L.pin}, out{{}, VDIM, &L.pout}, gu{{}, HID, &L.pgu}, dn{{}, FFN, &L.pdown};
         auto rows = [](std::vector<const int8_t*>& v, const int8_t* w, int n, int K) {
           for (int r = 0; r < n; ++r) v.push_back(w + (size_t)r * K);
         };
         if (L.linear) { rows(in.rows, L.qkv_q, CONVD, HID); rows(in.rows, L.z_q, VDIM, HID); }
         else { rows(in.rows, L.q_q, QPROJ, HID); rows(in.rows, L.k_q, KVPROJ, HID); rows(in.rows, L.v_q, KVPROJ, HID); }
         rows(out.rows, L.linear ? L.out_q : L.o_q, HID, VDIM);
-        for (int q = 0; q < FFN / PANEL; ++q) {   // pair panel q: gate rows 16q.., then up rows 16q..
-          rows(gu.rows, L.gate_q + (size_t)q * PANEL * HID, PANEL, HID);
-          rows(gu.rows, L.up_q + (size_t)q * PANEL * HID, PANEL, HID);
+        for (int q = 0; q < FFN / PAIR_ROWS; ++q) {   // pair panel q: gate rows 8q.., then up rows 8q..
+          rows(gu.rows, L.gate_q + (size_t)q * PAIR_ROWS * HID, PAIR_ROWS, HID);
+          rows(gu.rows, L.up_q + (size_t)q * PAIR_ROWS * HID, PAIR_ROWS, HID);
         }
         rows(dn.rows, L.down_q, HID, FFN);
         jobs.push_back(std::move(in)); jobs.push_back(std::move(out));
@@ -616,7 +615,7 @@ int qwen_create(const char* blob_path, const char* index_path, int n_gpus, const
       size_t off = 0;
       for (auto& j : jobs) {
         if (e == cudaSuccess) e = cudaMemcpy(drows, j.rows.data(), j.rows.size() * sizeof(void*), cudaMemcpyHostToDevice);
-        if (e == cudaSuccess) e = repack_panels(drows, pbuf + off, (int)j.rows.size(), j.K, j.pair, c->st);
+        if (e == cudaSuccess) e = repack_panels(drows, pbuf + off, (int)j.rows.size(), j.K, c->st);
         if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);   // the row table is reused
         *j.slot = pbuf + off;
         off += j.rows.size() * (size_t)j.K;
