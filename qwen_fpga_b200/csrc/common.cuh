@@ -52,7 +52,7 @@ constexpr int DSLICE = 16;
 constexpr int NDSLICE = LV / DSLICE;      // 8
 // attention split-KV bounds
 constexpr int ATT_MAXCH = 64;            // chunks per kv head
-constexpr int ATT_MINLEN = 64;           // positions per chunk (at least)
+constexpr int ATT_MINLEN = 8;            // positions per chunk (at least)
 constexpr int ATT_MAXLEN = 1024;         // positions per chunk (at most, smem bound)
 constexpr int AM_PARTS = 4096;           // argmax partial slots (>= head grid)
 

@@ -250,11 +250,17 @@ __device__ __forceinline__ void trace_mark(const PCtx& c, int p, int k) {
     c.A->trace[((size_t)blockIdx.x * NPHASE + p) * TRACE_STAMPS + k] = gtime();
 }
 // per-warp stamps of CTA 0 (after the per-phase block): [phase][warp][TRACE_WARP_STAMPS]
-// SM clock cycles (clock64), finer than the global timer
+// SM clock cycles (clock64), finer than the global timer.  Compiled in only
+// with QB_WARP_TRACE defined (every call site costs instructions on the hot
+// path, traced or not); otherwise that part of the record stays zero.
 __device__ __forceinline__ void trace_warp(const PCtx& c, int p, int k) {
+#ifdef QB_WARP_TRACE
   if (c.A->trace && blockIdx.x == 0 && (threadIdx.x & 31) == 0)
     c.A->trace[(size_t)gridDim.x * NPHASE * TRACE_STAMPS +
                ((size_t)p * NCW + (threadIdx.x >> 5)) * TRACE_WARP_STAMPS + k] = clock64();
+#else
+  (void)c; (void)p; (void)k;
+#endif
 }
 
 // A device-side bounds check failed: record the site and the offending value,
@@ -287,19 +293,20 @@ __device__ __forceinline__ bool aborted(const PCtx& c) {
 // Source and size of chunk k: one K-slice of a layer panel, one K-slab of a
 // head tile, or (DeltaNet IN) nrows fp32 rows of in_proj_b (seg 2) or
 // in_proj_a (seg 3).  src = null for a chunk outside its matrix.
-__device__ __forceinline__ void chunk_src(const PCtx& c, const Chunk& k, const char*& src, unsigned& bytes) {
+__device__ __forceinline__ void chunk_src(const LayerW* lay, const int8_t* head_tiles, const Chunk& k,
+                                          const char*& src, unsigned& bytes) {
   const int p = k.phase;
   const int row0 = (int)k.row0, n = k.nrows;
   src = nullptr;
   bytes = 0;
   if (k.seg & CHUNK_MMA) {   // row scales are read by the epilogue
     if (p != PH_HEAD || row0 >= HEAD_TILES || n >= HEAD_NSLAB) return;
-    src = (const char*)c.A->head_tiles + ((size_t)row0 * HEAD_NSLAB + n) * SLOTW;
+    src = (const char*)head_tiles + ((size_t)row0 * HEAD_NSLAB + n) * SLOTW;
     bytes = SLOTW;
     return;
   }
   if (p >= PH_HEAD) return;
-  const LayerW& L = c.lay[p / 5];
+  const LayerW& L = lay[p / 5];
   const int sub = p % 5;
   if (k.seg & CHUNK_PANEL) {   // row scales are read at the end of the phase
     const int8_t* base = nullptr;
@@ -320,17 +327,31 @@ __device__ __forceinline__ void chunk_src(const PCtx& c, const Chunk& k, const c
   bytes = (unsigned)(n * HID * 4);
 }
 
-// Issue the bulk copy of chunk i into its slot (one lane).
-__device__ __forceinline__ void issue_chunk(const PCtx& c, int i) {
+// Issue the bulk copy of chunk i into its slot (one lane).  One copy in the
+// kernel (not inlined, plain arguments): every refill site calls it.
+__device__ __noinline__ void issue_chunk_core(const Chunk* ch, const LayerW* lay, const int8_t* head_tiles,
+                                              unsigned char* sm, unsigned long long pol, int* err,
+                                              int* abort_flag, int i) {
   const int slot = i % NSLOT;
-  const Chunk k = c.ch[i];
+  const Chunk k = ch[i];
   const char* src;
   unsigned bytes;
-  chunk_src(c, k, src, bytes);
-  if (!src) { check_fail(c, 5, (int)k.row0); return; }
-  const unsigned bar = full_bar(c, slot);
+  chunk_src(lay, head_tiles, k, src, bytes);
+  if (!src) {   // a chunk outside its matrix: ERR_CHECK site 5, every CTA stops
+    if (atomicCAS(err, 0, ERR_CHECK) == 0) {
+      err[1] = 5;
+      err[2] = (int)k.row0;
+    }
+    atomicExch(abort_flag, 1);
+    *(volatile int*)&((Misc*)(sm + OFF_MISC))->abort = 1;
+    return;
+  }
+  const unsigned bar = smem_u32(sm + OFF_BAR + 8 * slot);   // full_bar
   mbar_expect(bar, bytes);
-  bulk_g2s(smem_u32(c.sm + OFF_RING + slot * SLOT), src, bytes, bar, c.pol);
+  bulk_g2s(smem_u32(sm + OFF_RING + slot * SLOT), src, bytes, bar, pol);
+}
+__device__ __forceinline__ void issue_chunk(const PCtx& c, int i) {
+  issue_chunk_core(c.ch, c.lay, c.A->head_tiles, c.sm, c.pol, c.A->err, c.A->abort_flag, i);
 }
 
 // One thread: bounded wait for phase `parity` of an mbarrier.  false on abort
@@ -708,9 +729,11 @@ __device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2
                                                 float& inv_out, float& sx_out, bool canon = false,
                                                 int tp = -1) {
   unsigned long long* tw = nullptr;
+#ifdef QB_WARP_TRACE
   if (tp >= 0 && c.A->trace && blockIdx.x == 0 && (threadIdx.x & 31) == 0)
     tw = c.A->trace + (size_t)gridDim.x * NPHASE * TRACE_STAMPS +
          ((size_t)tp * NCW + (threadIdx.x >> 5)) * TRACE_WARP_STAMPS;
+#endif
   const float2 r = encode_normed(c.sm, c.ms, hs, g2, act_int8, canon, tw);
   inv_out = r.x;
   sx_out = r.y;
@@ -1295,7 +1318,7 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
       // xf; else z = h (1 + w), its 1/rms applied when the phase finishes
       const float* row = (const float*)slot + q * HID;
       float a = 0.0f;
-#pragma unroll
+#pragma unroll 1
       for (int u = 0; u < HID / 128; ++u) {
         const int pos = 4 * (lane + 32 * u);
         const float4 w4 = *reinterpret_cast<const float4*>(row + pos);
@@ -1615,8 +1638,7 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
       }
     }
   }
-  if (wid < 4) warp_norm_rope_v(raw + wid * HD, nw, rco, rsi, qn + wid * HD);
-  else if (wid == 4) warp_norm_rope_v(raw + 4 * HD, nw, rco, rsi, kn);
+  if (wid < 5) warp_norm_rope_v(raw + wid * HD, nw, rco, rsi, wid < 4 ? qn + wid * HD : kn);   // kn follows qn
   else if (wid == 5) for (int d = lane; d < HD; d += 32) vn[d] = raw[5 * HD + d];
   consumer_sync();
   float* kc = A.kcache + (size_t)fi * A.max_ctx * KVPROJ;
@@ -1625,17 +1647,13 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
     kc[(size_t)T * KVPROJ + g * HD + threadIdx.x] = kn[threadIdx.x];
     vc[(size_t)T * KVPROJ + g * HD + threadIdx.x] = vn[threadIdx.x];
   }
+  // scores of this chunk's positions: warp = position (cached K, or the new
+  // key for position T), lane = 8 of the 256 dims, 4 query heads
   for (int i = wid; i < n; i += NCW) {
     const int tt = t0 + i;
-    float4 k0, k1;
-    if (tt < T) {
-      const float* kp = kc + (size_t)tt * KVPROJ + g * HD;
-      k0 = *reinterpret_cast<const float4*>(kp + 4 * lane);
-      k1 = *reinterpret_cast<const float4*>(kp + 128 + 4 * lane);
-    } else {
-      k0 = *reinterpret_cast<const float4*>(kn + 4 * lane);
-      k1 = *reinterpret_cast<const float4*>(kn + 128 + 4 * lane);
-    }
+    const float* kp = tt < T ? kc + (size_t)tt * KVPROJ + g * HD : kn;
+    const float4 k0 = *reinterpret_cast<const float4*>(kp + 4 * lane);
+    const float4 k1 = *reinterpret_cast<const float4*>(kp + 128 + 4 * lane);
 #pragma unroll
     for (int hq = 0; hq < 4; ++hq) {
       const float4 q0 = *reinterpret_cast<const float4*>(qn + hq * HD + 4 * lane);
@@ -1662,19 +1680,34 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
     if (lane == 0) { mh[wid] = m; mh[4 + wid] = lsum; }
   }
   consumer_sync();
-  const int d = threadIdx.x;          // threads 0..255: one head dimension each
-  float* part = A.att_part + ((size_t)(g * ATT_MAXCH + cc) * 4) * (2 + HD);
-  if (d < HD) {
-    float o[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int i = 0; i < n; ++i) {
-      const int tt = t0 + i;
-      const float v = (tt < T) ? vc[(size_t)tt * KVPROJ + g * HD + d] : vn[d];
+  // P V: thread = one dim d of one half of the positions (all V loads of a
+  // thread independent, four in flight); halves summed through shared memory
+  const int d = threadIdx.x & (HD - 1), half = threadIdx.x >> 8;
+  float o[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    const int ncache = min(n, T - t0);     // positions with a cached V
+#pragma unroll 4
+    for (int i = half; i < ncache; i += 2) {
+      const float v = vc[(size_t)(t0 + i) * KVPROJ + g * HD + d];
 #pragma unroll
       for (int hq = 0; hq < 4; ++hq) o[hq] = fmaf(sc[hq * ATT_MAXLEN + i], v, o[hq]);
     }
+    if (t1 == Tn && ((n - 1) & 1) == half) {   // the new position T
+#pragma unroll
+      for (int hq = 0; hq < 4; ++hq) o[hq] = fmaf(sc[hq * ATT_MAXLEN + n - 1], vn[d], o[hq]);
+    }
+  }
+  float* ox = qn;                       // [4][256], the queries are consumed
+  if (half == 1) {
+#pragma unroll
+    for (int hq = 0; hq < 4; ++hq) ox[hq * HD + d] = o[hq];
+  }
+  consumer_sync();
+  float* part = A.att_part + ((size_t)(g * ATT_MAXCH + cc) * 4) * (2 + HD);
+  if (half == 0) {
 #pragma unroll
     for (int hq = 0; hq < 4; ++hq) {
-      part[hq * (2 + HD) + 2 + d] = o[hq];
+      part[hq * (2 + HD) + 2 + d] = __fadd_rn(o[hq], ox[hq * HD + d]);
       if (d == 0) { part[hq * (2 + HD)] = mh[hq]; part[hq * (2 + HD) + 1] = mh[4 + hq]; }
     }
   }
@@ -1686,41 +1719,67 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
   if (!ms->last) return true;
   __threadfence();
   if (threadIdx.x == 0) *cnt = 0;
-  if (d >= HD) { consumer_sync(); return true; }
-  // gates of the 4 heads (tagged, from IN): all four polls issued together
-  const unsigned long long tg0 = gtime();
-  float gv[4] = {0.f, 0.f, 0.f, 0.f};
+  // merge of the group's chunks (this CTA holds the last one): every chunk's
+  // maxima and sums staged in shared memory, the overall max and the weights
+  // exp(m_q - M) once per (head, chunk), then thread = (head, two dims) with
+  // the partial outputs of all chunks read independently
+  float* mq = sc;                       // [4][nch]: chunk maxima, then weights
+  float* lq = sc + 4 * ATT_MAXCH;       // [4][nch]: chunk sums
+  float* Mh = sc + 8 * ATT_MAXCH;       // [4] overall maxima, [4..8) total sums
+  for (int i = threadIdx.x; i < 4 * nch; i += PT) {
+    const int hq = i / nch, q = i % nch;
+    const float* pb = A.att_part + ((size_t)(g * ATT_MAXCH + q) * 4 + hq) * (2 + HD);
+    mq[i] = __ldcg(pb);
+    lq[i] = __ldcg(pb + 1);
+  }
+  consumer_sync();
+  if (threadIdx.x < 4) {
+    float M = -INFINITY;
+    for (int q = 0; q < nch; ++q) M = fmaxf(M, mq[threadIdx.x * nch + q]);
+    Mh[threadIdx.x] = M;
+  }
+  consumer_sync();
+  for (int i = threadIdx.x; i < 4 * nch; i += PT) mq[i] = expf(mq[i] - Mh[i / nch]);
+  consumer_sync();
+  if (threadIdx.x < 4) {
+    float Ls = 0.0f;
+    for (int q = 0; q < nch; ++q) Ls = fmaf(lq[threadIdx.x * nch + q], mq[threadIdx.x * nch + q], Ls);
+    Mh[4 + threadIdx.x] = Ls;
+  }
+  consumer_sync();
+  const int hq = threadIdx.x >> 7, d2 = 2 * (threadIdx.x & 127);
+  // the gates of head 4g + hq at dims d2, d2 + 1 (tagged, from IN), polled
+  // while the partial outputs load
+  const unsigned long long* gsrc = A.tv_qg + (size_t)(4 * g + hq) * 2 * HD + HD + d2;
+  unsigned long long ga, gb;
+  ld_tv2(gsrc, ga, gb);
+  float O0 = 0.0f, O1 = 0.0f;
   {
-    unsigned pend = 0xf;
+    const float* pb = A.att_part + ((size_t)(g * ATT_MAXCH) * 4 + hq) * (2 + HD) + 2 + d2;
+    const size_t stride = 4 * (2 + HD);
+#pragma unroll 4
+    for (int q = 0; q < nch; ++q) {
+      const float2 ov = __ldcg(reinterpret_cast<const float2*>(pb + q * stride));
+      const float f = mq[hq * nch + q];
+      O0 = fmaf(ov.x, f, O0);
+      O1 = fmaf(ov.y, f, O1);
+    }
+  }
+  {
+    const unsigned long long tg0 = gtime();
     int it = 0;
-    unsigned long long w[4];
-    while (pend) {
-#pragma unroll
-      for (int hq = 0; hq < 4; ++hq)
-        if (pend >> hq & 1) w[hq] = ld_tv(A.tv_qg + (size_t)(4 * g + hq) * 2 * HD + HD + d);
-#pragma unroll
-      for (int hq = 0; hq < 4; ++hq)
-        if ((pend >> hq & 1) && tag_ok(w[hq], tin)) { gv[hq] = tv_val(w[hq]); pend &= ~(1u << hq); }
-      if (pend && ((++it) & 63) == 0) {
+    while (!(tag_ok(ga, tin) && tag_ok(gb, tin))) {
+      if (((++it) & 63) == 0) {
         if (aborted(c)) break;
         if (gtime() - tg0 > WAIT_NS) { raise_abort(c, 20, p); break; }
       }
+      ld_tv2(gsrc, ga, gb);
     }
   }
   const unsigned tout = tag_of(c, p);
-  for (int hq = 0; hq < 4; ++hq) {
-    const float* pb = A.att_part + ((size_t)(g * ATT_MAXCH) * 4 + hq) * (2 + HD);
-    const size_t stride = 4 * (2 + HD);
-    float M = -INFINITY;
-    for (int q = 0; q < nch; ++q) M = fmaxf(M, __ldcg(pb + q * stride));
-    float Ls = 0.0f, O = 0.0f;
-    for (int q = 0; q < nch; ++q) {
-      const float f = expf(__ldcg(pb + q * stride) - M);
-      Ls = fmaf(__ldcg(pb + q * stride + 1), f, Ls);
-      O = fmaf(__ldcg(pb + q * stride + 2 + d), f, O);
-    }
-    st_tv(A.tv_attn + (4 * g + hq) * HD + d, __fmul_rn(__fdiv_rn(O, Ls), sigmoid_f(gv[hq])), tout);
-  }
+  const float Ls = Mh[4 + hq];
+  st_tv(A.tv_attn + (4 * g + hq) * HD + d2, __fmul_rn(__fdiv_rn(O0, Ls), sigmoid_f(tv_val(ga))), tout);
+  st_tv(A.tv_attn + (4 * g + hq) * HD + d2 + 1, __fmul_rn(__fdiv_rn(O1, Ls), sigmoid_f(tv_val(gb))), tout);
   consumer_sync();
   return true;
 }
