@@ -74,13 +74,16 @@ int qwen_get_engine(qwen_ctx* ctx);
 /* Per-phase tracing of the persistent engine (no counterpart in the reference,
  * which times steps with perf_counter at run_prompt.py:80-98): when on, every
  * step records, per CTA and per phase, %globaltimer stamps [entry, inputs
- * ready, first weight chunk landed, exit] (ns), n_ctas * n_phases * 4 words;
+ * arrived, outputs written, exit] (ns; 0 where a phase has no such point),
+ * n_ctas * n_phases * 4 words;
  * then, for CTA 0, per phase and per warp (16), 16 SM-clock stamps of a GEMV
  * phase [entry, input in, input encoded, first chunk landed, own tasks done,
  * CTA barrier passed, outputs written, slots released, encoder: statistics,
  * their barrier, digits written, 5 unused] (0 = not reached), n_phases * 16 *
- * 16 words.  qwen_trace_read copies the last step's record to
- * host memory; max_words must cover both parts. */
+ * 16 words; this second part is filled only by a library built with
+ * QB_WARP_TRACE defined (its stamps cost instructions on the hot path).
+ * qwen_trace_read copies the last step's record to host memory; max_words
+ * must cover both parts. */
 int qwen_trace_enable(qwen_ctx* ctx, int on);
 int qwen_trace_read(qwen_ctx* ctx, unsigned long long* out, int max_words, int* n_ctas,
                     int* n_phases);

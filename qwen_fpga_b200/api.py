@@ -154,7 +154,7 @@ class Decoder:
         _check(load().qwen_trace_enable(self.h, 1 if on else 0), self.h)
 
     def trace_read(self):
-        """Last step's per-CTA, per-phase stamps [entry, ready, first chunk, exit] (ns),
+        """Last step's per-CTA, per-phase stamps [entry, inputs arrived, outputs written, exit] (ns),
         shape [n_ctas, n_phases, 4]; CTA 0's per-warp clock stamps land in
         self.trace_warps, shape [n_phases, 16, 16]."""
         n = 160 * 121 * 4 + 121 * 16 * 16

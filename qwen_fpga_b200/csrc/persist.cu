@@ -33,6 +33,7 @@
 // loops; the schedule stores where every phase starts).  Arithmetic (and its rounding order)
 // is that of decode.cu, so both engines agree bit for bit; the contract is
 // golden/model.py:243-267.
+#include <algorithm>
 #include <cstdio>
 #include <string>
 #include <vector>
@@ -959,9 +960,9 @@ __device__ bool phase_head(PCtx& c, int p, int i0, int i1) {
   float* hs = (float*)(c.sm + OFF_HS);
   const float2 g2 = __ldg(reinterpret_cast<const float2*>(A.final_norm) + threadIdx.x);
   if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) return false;
+  trace_mark(c, p, 1);
   float inv, sx;
   cta_encode_1024(c, hs, g2, false, inv, sx, true);
-  trace_mark(c, p, 1);
   const float xsf = (float)ms->scale;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int ntiles = (i1 - i0) / HEAD_NSLAB;
@@ -1254,6 +1255,7 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
     } else if (!wait_tagged_max(c, A.tv_h, HID, tag_of(c, p - 1), hs, amax, true, g2)) {
       return false;
     }
+    trace_mark(c, p, 1);
     trace_warp(c, p, 1);
     if (threadIdx.x == 0) ms->hs_tag = tag_of(c, p - 1);   // layer 0: the embedding (tag of "phase -1")
     if (i8) {
@@ -1290,9 +1292,9 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
     }
   } else {
     if (!prologue(c, p, amax, K)) return false;
+    trace_mark(c, p, 1);
     if (!i8) xs = encode_fixed(c.sm, xf, K, *amax, false, g2);
   }
-  trace_mark(c, p, 1);
   trace_warp(c, p, 2);
   const unsigned char* fr = c.sm + OFF_DIG;                   // the CTA's digit image
   float* part_f = (float*)(c.sm + OFF_PARTF);
@@ -1311,7 +1313,6 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
       break;
     }
     if (!(t == t_first && first_in) && !wait_full(c, i)) { good = 0; break; }
-    if (t == 0) trace_mark(c, p, 2);
     const unsigned char* slot = c.sm + OFF_RING + (i % NSLOT) * SLOT;
     if (!pan) {
       // row q of the chunk, dotted with x: under ACT_INT8 the encoder's x in
@@ -1405,6 +1406,7 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
     if (k.seg & CHUNK_PANEL) continue;
     if (lane == 0) st_tv(A.tv_ab + (k.seg == 2 ? 0 : LH) + (int)k.row0 + q, __fmul_rn(part_f[t * PANEL], xinv), tag);
   }
+  trace_mark(c, p, 2);
   trace_warp(c, p, 6);
   // the outputs are out: now give the slots back and refill them (off the
   // phase's critical path)
@@ -1968,6 +1970,18 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
     load[b] += bytes;
     return true;
   };
+  // Time model of the step (us, from traces of this kernel): an idle CTA sees
+  // a phase's input T_PROP after the last producer wrote it; a CTA that worked
+  // in a phase is free again T_REL after its outputs (slot refills, phase
+  // exit, the next phase's set-up); a GEMV phase costs T_ENC + T_ROUND per
+  // round of NCW tasks + T_TAIL from its start; the DeltaNet / attention MIX
+  // items take T_DELTA / T_ATTN.  Panels go to the CTA that would finish the
+  // phase earliest, so a phase's work avoids the CTAs still busy with the last.
+  constexpr double T_PROP = 0.6, T_REL = 1.8, T_ENC = 0.5, T_ROUND = 0.7, T_TAIL = 0.45;
+  constexpr double T_DELTA = 2.4, T_ATTN = 4.0;
+  constexpr int ATT_CTAS = 20;   // CTAs running attention items at short contexts
+  std::vector<double> freeb(G, 0.0);
+  double ready = 0.0;            // when the current phase's input reaches an idle CTA
   for (int p = 0; p < NPHASE; ++p) {
     // every CTA's chunks of phase p start where its list stands now
     for (int b = 0; b < G; ++b) phase_first[(size_t)b * (NPHASE + 1) + p] = (unsigned short)counts[b];
@@ -1982,8 +1996,17 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
       }
       continue;
     }
-    if (sub == 1) continue;
     const bool linear = (p / 5) % 4 != 3;
+    if (sub == 1) {
+      double last = ready;
+      for (int b = 0; b < G; ++b)
+        if (linear ? b < LH * NDSLICE : b < ATT_CTAS) {
+          freeb[b] = std::max(freeb[b], ready) + (linear ? T_DELTA : T_ATTN);
+          last = std::max(last, freeb[b]);
+        }
+      ready = last + T_PROP;
+      continue;
+    }
     int npan, K;
     if (sub == 0) { npan = (linear ? CONVD + VDIM : QPROJ + 2 * KVPROJ) / PANEL; K = HID; }
     else if (sub == 2) { npan = HID / PANEL; K = VDIM; }
@@ -2000,16 +2023,25 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
     int ptasks = 0;
     for (int x : sl_tasks) ptasks += x;
     std::vector<int> inph(G, 0), tasks(G, 0);   // chunks (at most NSLOT: all resident at once) and tasks
-    auto least_fit = [&](int need) {
+    auto fin_of = [&](int b, int t) {
+      return std::max(freeb[b], ready) + T_ENC + T_ROUND * ((t + NCW - 1) / NCW) + T_TAIL;
+    };
+    auto least_fit = [&](int need, int add) {
       int best = -1;
+      double fb = 0.0;
       for (int b = 0; b < G; ++b) {
         if (inph[b] + need > NSLOT) continue;
-        if (best < 0 || tasks[b] < tasks[best] || (tasks[b] == tasks[best] && load[b] < load[best])) best = b;
+        const double f = fin_of(b, tasks[b] + add);
+        if (best < 0 || f < fb - 1e-9 ||
+            (f < fb + 1e-9 && (tasks[b] < tasks[best] || (tasks[b] == tasks[best] && load[b] < load[best])))) {
+          best = b;
+          fb = f;
+        }
       }
       return best;
     };
     for (int q = 0; q < npan; ++q) {
-      const int b = least_fit(nslice);
+      const int b = least_fit(nslice, ptasks);
       if (b < 0) { err = "phase does not fit the rings"; return false; }
       inph[b] += nslice;
       tasks[b] += ptasks;
@@ -2021,13 +2053,21 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
       constexpr int per = SLOTW / (HID * 4);
       for (int seg = 2; seg <= 3; ++seg)
         for (int r = 0; r < LH; r += per) {
-          const int b = least_fit(1);
+          const int b = least_fit(1, per);
           if (b < 0) { err = "phase does not fit the rings"; return false; }
           inph[b] += 1;
           tasks[b] += per;
           if (!push(b, p, seg, per, r, per * HID * 4)) return false;
         }
     }
+    double last = ready;
+    for (int b = 0; b < G; ++b)
+      if (tasks[b]) {
+        const double f = fin_of(b, tasks[b]);
+        freeb[b] = f + T_REL;
+        last = std::max(last, f);
+      }
+    ready = last + T_PROP;
   }
   for (int b = 0; b < G; ++b) phase_first[(size_t)b * (NPHASE + 1) + NPHASE] = (unsigned short)counts[b];
   return true;

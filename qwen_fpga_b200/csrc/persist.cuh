@@ -47,7 +47,8 @@ struct PersistArgs {
 };
 
 // Trace record layout: per CTA and phase, %globaltimer stamps at phase entry,
-// inputs ready (prologue done), first weight chunk landed, phase exit; then,
+// inputs arrived (the input wait done), outputs written (a GEMV phase; the
+// head: its first slab landed), phase exit; then,
 // for CTA 0 only, per phase and warp, clock64 stamps of a GEMV phase: 0 entry,
 // 1 input vector in, 2 digit image encoded, 3 first task's chunk landed, 4 own
 // tasks done, 5 CTA barrier passed, 6 panels finished, 7 slots released, and
