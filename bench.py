@@ -204,6 +204,76 @@ def run_reference(args, rank):
     return 0
 
 
+GEMV_SHAPES = [(6144, 1024), (2048, 1024), (7168, 1024), (1024, 3584), (1024, 2048), (4096, 1024),
+               (248320, 1024)]
+
+
+def run_gemv(args):
+    """Config 1 (GEMV microbench): qwen_gemv_i8_i8 on every shape, W int8
+    rng.integers(-127, 128), scales U[1e-3, 1e-2], x int8 U[-127, 127] with s_x
+    U[1e-3, 1e-2], seed 0 per shape.  Bytes per call = N*K + 4N + K + 4 + 4N
+    (+ 4N for the int32 accumulators also written).  Each timed call reads a
+    different copy of the weights, enough copies that a pass reads more than
+    L2, so the weights come from HBM.  The int32 accumulators of one call per
+    shape are checked against numpy exactly.  One JSON line."""
+    import torch
+    from qwen_fpga_b200 import api
+    torch.cuda.set_device(0)
+    peak, src = peaks()
+    rows = []
+    for N, K in GEMV_SHAPES:
+        if args.gemv_n and N != args.gemv_n:
+            continue
+        rng = np.random.default_rng(0)
+        w = rng.integers(-127, 128, (N, K), dtype=np.int8)
+        sw = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+        xq = rng.integers(-127, 128, K, dtype=np.int8)
+        sx = float(rng.uniform(1e-3, 1e-2))
+        ncopy = max(1, min(128, -(-(256 << 20) // (N * K))))    # > 2x L2 (126 MB) per pass
+        ws = [torch.from_numpy(w).cuda() for _ in range(ncopy)]
+        dsw, dxq = torch.from_numpy(sw).cuda(), torch.from_numpy(xq).cuda()
+        acc = torch.empty(N, dtype=torch.int32, device="cuda")
+        y = torch.empty(N, dtype=torch.float32, device="cuda")
+        api.gemv_i8_i8(ws[0], dsw, dxq, sx, acc=acc, y=y)
+        torch.cuda.synchronize()
+        ref = w.astype(np.int64) @ xq.astype(np.int64)
+        exact = bool(np.array_equal(acc.cpu().numpy().astype(np.int64), ref))
+        # one pass over every copy, captured once as a CUDA graph so that host
+        # launch overhead stays out of the timed region
+        st = torch.cuda.Stream()
+        n = max(8, ncopy)
+        with torch.cuda.stream(st):
+            for i in range(max(args.warmup, 3)):
+                api.gemv_i8_i8(ws[i % ncopy], dsw, dxq, sx, acc=acc, y=y, stream=st)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for i in range(n):
+                api.gemv_i8_i8(ws[i % ncopy], dsw, dxq, sx, acc=acc, y=y, stream=st)
+        reps = 3
+        with torch.cuda.stream(st):
+            g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        with torch.cuda.stream(st):
+            for _ in range(reps):
+                g.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        n *= reps
+        us = e0.elapsed_time(e1) * 1e3 / n
+        nbytes = N * K + 4 * N + K + 4 + 4 * N + 4 * N
+        gbs = nbytes / (us * 1e-6) / 1e9
+        rows.append({"N": N, "K": K, "us": round(us, 3), "bytes": nbytes, "GB_s": round(gbs, 1),
+                     "frac": round(gbs / peak, 4), "acc_exact": exact, "weight_copies": ncopy})
+        del ws
+        torch.cuda.empty_cache()
+    print(json.dumps({"metric": "config-1 int8 GEMV achieved HBM GB/s", "unit": "GB/s", "peak": peak,
+                      "peak_source": src, "kernel": "k_gemv (qwen_gemv_i8_i8)", "shapes": rows}))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -215,11 +285,15 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--engine", type=int, default=1,
                     help="1 = persistent weight-streaming kernel, 0 = graph of phase kernels")
+    ap.add_argument("--gemv", action="store_true", help="config-1 GEMV microbench (one JSON line)")
+    ap.add_argument("--gemv-n", type=int, default=0, help="with --gemv: only the shape with this N")
     ap.add_argument("--profile", type=int, default=0,
                     help="run N decode steps of the config-0 prompt (no timing, no JSON) for ncu")
     args = ap.parse_args()
     if args.profile:
         return run_profile(args)
+    if args.gemv:
+        return run_gemv(args)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

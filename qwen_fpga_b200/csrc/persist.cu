@@ -264,28 +264,25 @@ __device__ __forceinline__ void trace_warp(const PCtx& c, int p, int k) {
 #endif
 }
 
-// A device-side bounds check failed: record the site and the offending value,
-// stop every CTA (the access itself is skipped by the caller).
-__device__ __forceinline__ void check_fail(const PCtx& c, int site, int value) {
-  if (atomicCAS(c.A->err, 0, ERR_CHECK) == 0) {
-    c.A->err[1] = site;
-    c.A->err[2] = value;
+// Record a device error (first one wins: code, site, value and, for ERR_WAIT,
+// the CTA in err[1..3]) and stop every CTA.  One copy in the kernel (not
+// inlined, plain arguments): the error paths of every site share it.
+__device__ __noinline__ void record_error(int* err, int* abort_flag, Misc* ms, int code, int site, int value) {
+  if (atomicCAS(err, 0, code) == 0) {
+    err[1] = site;
+    err[2] = value;
+    if (code == ERR_WAIT) err[3] = (int)blockIdx.x;
   }
-  atomicExch(c.A->abort_flag, 1);
-  *(volatile int*)&c.ms->abort = 1;
+  atomicExch(abort_flag, 1);
+  *(volatile int*)&ms->abort = 1;
 }
-
-// A bounded wait ran out (or the schedule is unusable): record ERR_WAIT with
-// the site, a site-specific value and the CTA (err[1..3], first one wins), and
-// stop every CTA.
-__device__ void raise_abort(const PCtx& c, int site = 0, int value = 0) {
-  if (atomicCAS(c.A->err, 0, ERR_WAIT) == 0) {
-    c.A->err[1] = site;
-    c.A->err[2] = value;
-    c.A->err[3] = (int)blockIdx.x;
-  }
-  atomicExch(c.A->abort_flag, 1);
-  *(volatile int*)&c.ms->abort = 1;
+// A device-side bounds check failed (the access itself is skipped by the caller).
+__device__ __forceinline__ void check_fail(const PCtx& c, int site, int value) {
+  record_error(c.A->err, c.A->abort_flag, c.ms, ERR_CHECK, site, value);
+}
+// A bounded wait ran out (or the schedule is unusable).
+__device__ __forceinline__ void raise_abort(const PCtx& c, int site = 0, int value = 0) {
+  record_error(c.A->err, c.A->abort_flag, c.ms, ERR_WAIT, site, value);
 }
 __device__ __forceinline__ bool aborted(const PCtx& c) {
   return *(volatile int*)&c.ms->abort || ld_flag(c.A->abort_flag);
@@ -339,12 +336,7 @@ __device__ __noinline__ void issue_chunk_core(const Chunk* ch, const LayerW* lay
   unsigned bytes;
   chunk_src(lay, head_tiles, k, src, bytes);
   if (!src) {   // a chunk outside its matrix: ERR_CHECK site 5, every CTA stops
-    if (atomicCAS(err, 0, ERR_CHECK) == 0) {
-      err[1] = 5;
-      err[2] = (int)k.row0;
-    }
-    atomicExch(abort_flag, 1);
-    *(volatile int*)&((Misc*)(sm + OFF_MISC))->abort = 1;
+    record_error(err, abort_flag, (Misc*)(sm + OFF_MISC), ERR_CHECK, 5, (int)k.row0);
     return;
   }
   const unsigned bar = smem_u32(sm + OFF_BAR + 8 * slot);   // full_bar
@@ -448,13 +440,7 @@ __device__ __noinline__ bool wait_tagged_words(Misc* ms, int* err, int* abort_fl
         if (*(volatile int*)&ms->abort || ld_flag(abort_flag)) {
           bad = 1;
         } else if (gtime() - t0 > WAIT_NS) {
-          if (atomicCAS(err, 0, ERR_WAIT) == 0) {
-            err[1] = 12;
-            err[2] = (int)(tag & 127u);
-            err[3] = (int)blockIdx.x;
-          }
-          atomicExch(abort_flag, 1);
-          *(volatile int*)&ms->abort = 1;
+          record_error(err, abort_flag, ms, ERR_WAIT, 12, (int)(tag & 127u));
           bad = 1;
         }
       }
