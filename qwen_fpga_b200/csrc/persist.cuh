@@ -76,12 +76,12 @@ cudaError_t repack_head_tiles(const int8_t* emb_q, int8_t* tiles, cudaStream_t s
 // of all 16 rows is 512 contiguous bytes (one ldmatrix.x4 = the MMA's A
 // fragment).  A chunk is one K-slice of a panel: 16 rows x 1024 bytes of K
 // (16 KB; the last slice of a K = 3584 panel is 512 bytes, 8 KB); a task is
-// 256 bytes of K of a chunk (4 KB of weights, 8 MMA K-steps).  GATEUP uses
+// 512 bytes of K of a chunk (8 KB of weights, 16 MMA K-steps).  GATEUP uses
 // pair panels: rows 0-7 are gate rows 8q .. 8q+7, rows 8-15 the same up rows,
 // so a gate row and its up row finish in neighbouring lanes.
 constexpr int PANEL = 16;
 constexpr int PANEL_KB = 1024;                  // K bytes per chunk
-constexpr int TASK_KB = 256;                    // K bytes per task
+constexpr int TASK_KB = 512;                    // K bytes per task
 constexpr int PAIR_ROWS = 8;                    // gate (and up) rows per pair panel
 constexpr unsigned char CHUNK_PANEL = 0x40;     // Chunk.seg flag: row0 = panel, nrows = K-slice
 static_assert(CONVD % PANEL == 0 && VDIM % PANEL == 0 && QPROJ % PANEL == 0 &&
