@@ -11,8 +11,12 @@ argmax.  Algorithmic bytes of a step attending T positions:
 B(T) = 758,248,704 + 24,576 * T (int8 weights + row scales + fp32 small
 tensors, plus fp32 K/V reads of the 6 attention layers).
 
-Under torchrun each rank decodes its own sequence on its own GPU (independent
-replicas; no collective on the data path) and the throughput is summed.
+Under torchrun (N > 1) the N ranks decode ONE sequence with tensor
+parallelism (qwen_fpga_b200.tp: heads, FFN columns and the vocab split across
+the GPUs, the row-parallel partial sums and the argmax exchanged inside the
+decode kernel over NVLink); the throughput is that sequence's tokens/s
+(strong scaling).  --replicas instead runs N independent sequences, one per
+GPU, and sums their throughput (weak scaling).
 
 --impl reference times the reference's own CPU decoder (the HLS C++ qwen_top
 compiled from the reference sources into oracle/_ref, single thread) on a
@@ -283,6 +287,8 @@ def main():
     ap.add_argument("--e2e-episodes", type=int, default=8)
     ap.add_argument("--cpu-steps", type=int, default=24)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: independent sequences per GPU instead of tensor parallelism")
     ap.add_argument("--engine", type=int, default=1,
                     help="1 = persistent weight-streaming kernel, 0 = graph of phase kernels")
     ap.add_argument("--gemv", action="store_true", help="config-1 GEMV microbench (one JSON line)")
@@ -318,9 +324,16 @@ def main():
 
     episodes = max(1, args.steps // EPISODE)
     K = episodes * EPISODE
-    dec = api.Decoder(blob_path, device=local, max_ctx=PROMPT_LEN + EPISODE + 64)
-    dec.set_engine(args.engine)
+    tp = world > 1 and not args.replicas
+    if tp:
+        from qwen_fpga_b200.tp import TPDecoder
+        tpd = TPDecoder(blob_path, device=local, max_ctx=PROMPT_LEN + EPISODE + 64)
+        dec = tpd.dec
+    else:
+        dec = api.Decoder(blob_path, device=local, max_ctx=PROMPT_LEN + EPISODE + 64)
+        dec.set_engine(args.engine)
     engine = dec.engine
+    seqs = 1 if tp else world   # sequences decoded by the whole job
     launches_per_step = 1 if engine == 1 else 24 * 5 + 2
     kernel_name = ("k_decode_persistent (one cooperative launch per step)" if engine == 1
                    else "whole decode step (CUDA graph of 122 kernels)")
@@ -328,6 +341,8 @@ def main():
 
     # warm-up: W untimed steps
     dec.reset()
+    if world > 1:
+        dist.barrier()
     dec.generate(prompt[:1], max(args.warmup, 3))
 
     # timed: K decode steps in episodes of (16-token prefill untimed, 64 decode timed)
@@ -339,6 +354,8 @@ def main():
     with ClockSampler(local if world == 1 else local) as clk:
         for e in range(episodes):
             dec.reset()
+            if tp:
+                dist.barrier()
             ids, sec = dec.generate(prompt, EPISODE)
             dev_sec += sec
             if ids0 is None:
@@ -352,13 +369,15 @@ def main():
         dev_sec = float(t.item())
         dist.barrier()
     ms_per_step = dev_sec / K * 1e3
-    value = world * K / dev_sec
+    value = seqs * K / dev_sec
 
     # end to end through the C ABI: host token in, host argmax out, every step
     e2e_sec = 0.0
     e2e_steps = 0
     for e in range(max(1, args.e2e_episodes)):
         dec.reset()
+        if tp:
+            dist.barrier()
         am = 0
         for t in prompt:
             am, _ = dec.decode_step(int(t), want_logits=False)
@@ -367,8 +386,11 @@ def main():
             am, _ = dec.decode_step(am, want_logits=False)
         e2e_sec += time.perf_counter() - t0
         e2e_steps += EPISODE
-    # with the fp32 logits returned to host memory each step (what golden decode_step returns)
+    # with the fp32 logits returned to host memory each step (what golden decode_step returns;
+    # under TP each rank returns its vocab slice)
     dec.reset()
+    if tp:
+        dist.barrier()
     am = 0
     for t in prompt:
         am, _ = dec.decode_step(int(t), want_logits=False)
@@ -380,6 +402,8 @@ def main():
         t = torch.tensor([e2e_sec, lg_sec], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_sec, lg_sec = (float(v) for v in t.tolist())
+    if world > 1:
+        dist.barrier()   # every rank's last step is done before any context goes away
     dec.close()
 
     clocks = clk.summary()
@@ -393,22 +417,27 @@ def main():
     t_mean = PROMPT_LEN + 1 + (EPISODE - 1) / 2.0
     bstep = bytes_per_step(t_mean)
     achieved = bstep / (ms_per_step * 1e-3) / 1e9
+    if tp:
+        peak = peak * world   # one step's bytes are spread over every rank's HBM
+        peak_src = f"{peak_src} x {world} GPUs (aggregate)"
     traffic = load_traffic()
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None,
+        "scaling": "strong" if tp else "weak", "vs_baseline": None,
         "dtype": "int8 weights x fp32 activations -> int32 digit accumulators",
         "data": "synthetic (random-init Qwen3.5-0.8B, seed 1234)",
         "config": {"workload": "config0: 16-token prompt prefill (untimed) + 64 greedy decode "
                                "steps (timed), repeated", "model": "Qwen3.5-0.8B (random init)",
-                   "batch": 1, "global_batch": world, "episodes": episodes,
+                   "batch": 1, "global_batch": seqs, "episodes": episodes,
                    "T_ctx": f"{PROMPT_LEN + 1}..{PROMPT_LEN + EPISODE}",
                    "l2": "no flush: 758 MB of weights per step > 126 MB L2",
-                   "parallelism": "1 GPU" if world == 1 else f"{world} independent replicas"},
-        "e2e": {"value": world * e2e_steps / e2e_sec, "unit": UNIT, "h2d_bytes_per_step": 44,
+                   "parallelism": ("1 GPU" if world == 1 else
+                                   f"tp{world} (tensor parallel, one sequence)" if tp else
+                                   f"{world} independent replicas")},
+        "e2e": {"value": seqs * e2e_steps / e2e_sec, "unit": UNIT, "h2d_bytes_per_step": 44,
                 "d2h_bytes_per_step": 20,
-                "with_logits": {"value": world * EPISODE / lg_sec, "unit": UNIT,
+                "with_logits": {"value": seqs * EPISODE / lg_sec, "unit": UNIT,
                                 "d2h_bytes_per_step": 20 + 4 * VOCAB}},
         "gpu_launches": K * launches_per_step,
         "engine": "persistent" if engine == 1 else "graph",

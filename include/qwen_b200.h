@@ -38,6 +38,41 @@ typedef struct CUstream_st* qwen_stream_t; /* same handle as cudaStream_t */
 int qwen_create(const char* blob_path, const char* index_path, int n_gpus,
                 const int* device_ids, int max_ctx, int max_batch, qwen_ctx** out);
 
+/* Tensor parallelism over tp_world (1, 2, 4 or 8) GPUs of one node, one
+ * process and one context per GPU: the weight sharding of a multi-device
+ * decode step (the reference runs one device; BASELINE north_star names the
+ * split).  Rank tp_rank of the job keeps the full weights on device
+ * device_id and computes its shard: DeltaNet heads, attention KV groups (all
+ * four query heads of each), gate/up rows and down columns in 128-column
+ * blocks, out/o columns by head, and a vocab slice of the head.  Row-parallel
+ * projections add their partial rows across ranks inside the decode kernel
+ * (stores into every rank's exchange buffer over NVLink, then a sum in rank
+ * order, so every rank holds the same residual stream bit for bit); the head
+ * exchanges (max, index) pairs.
+ *
+ * Set-up: qwen_create_tp on every rank; qwen_tp_export writes this rank's
+ * exchange-buffer handle (QWEN_TP_HANDLE_BYTES bytes, a CUDA IPC handle);
+ * the caller gathers every rank's handle in rank order (any host transport)
+ * and passes the array to qwen_tp_connect.  Every rank then makes the same
+ * decode calls in the same order (like collectives); a rank that stops makes
+ * the others' next step fail after the 2 s device wait bound with
+ * QWEN_ERR_DEVICE.  ACT_INT8 and engine 0 are not available under TP.
+ * Logits: each rank fills only its vocab slice [lo, hi) of logits_out
+ * (qwen_tp_vocab_range).  State import/export move the full arrays; a rank
+ * uses and updates only its heads' parts.
+ *
+ * qwen_tp_plan writes the shard of (tp_rank, tp_world) without a context:
+ * QWEN_TP_PLAN_INTS ints = DeltaNet heads [h0, h1), KV groups [g0, g1), OUT
+ * input columns [o0, o1), FFN columns [f0, f1), vocab rows [v0, v1). */
+#define QWEN_TP_HANDLE_BYTES 64
+#define QWEN_TP_PLAN_INTS 10
+int qwen_create_tp(const char* blob_path, const char* index_path, int device_id, int tp_rank,
+                   int tp_world, int max_ctx, int max_batch, qwen_ctx** out);
+int qwen_tp_export(qwen_ctx* ctx, void* handle_out);
+int qwen_tp_connect(qwen_ctx* ctx, const void* handles);
+int qwen_tp_vocab_range(qwen_ctx* ctx, int* lo, int* hi);
+int qwen_tp_plan(int tp_rank, int tp_world, int* out);
+
 /* Free every device and host resource of the context. */
 int qwen_destroy(qwen_ctx* ctx);
 

@@ -64,6 +64,12 @@ def load() -> C.CDLL:
     L.qwen_last_error.argtypes = [_vp]
     L.qwen_create.argtypes = [C.c_char_p, C.c_char_p, C.c_int, _ip, C.c_int, C.c_int,
                               C.POINTER(_vp)]
+    L.qwen_create_tp.argtypes = [C.c_char_p, C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                 C.POINTER(_vp)]
+    L.qwen_tp_export.argtypes = [_vp, _vp]
+    L.qwen_tp_connect.argtypes = [_vp, _vp]
+    L.qwen_tp_vocab_range.argtypes = [_vp, _ip, _ip]
+    L.qwen_tp_plan.argtypes = [C.c_int, C.c_int, _ip]
     L.qwen_destroy.argtypes = [_vp]
     L.qwen_reset.argtypes = [_vp, C.c_int]
     L.qwen_state_import.argtypes = [_vp, C.c_int, _fp, _fp, _fp, _fp, C.c_int, C.c_int]
@@ -93,6 +99,20 @@ def _fptr(a):
     return a.ctypes.data_as(_fp) if a is not None else None
 
 
+TP_HANDLE_BYTES = 64
+
+
+def tp_plan(rank: int, world: int) -> dict:
+    """The tensor-parallel shard of `rank` among `world` GPUs (no GPU needed):
+    DeltaNet heads, attention KV groups, OUT input columns, FFN columns and
+    vocab rows, each as a half-open [lo, hi) pair."""
+    out = (C.c_int * 10)()
+    _check(load().qwen_tp_plan(int(rank), int(world), out))
+    v = list(out)
+    return {"dn_heads": (v[0], v[1]), "kv_groups": (v[2], v[3]), "out_cols": (v[4], v[5]),
+            "ffn_cols": (v[6], v[7]), "vocab": (v[8], v[9])}
+
+
 class DecodeStateView:
     """Host copy of the decode state, field for field the golden DecodeState
     (golden/model.py:86-95): conv [18,6144,4], rec [18,16,128,128], kc/vc lists
@@ -106,15 +126,23 @@ class Decoder:
     """One GPU context: weights resident in HBM + one batch-1 decode state."""
 
     def __init__(self, blob_path: str, index_path: str | None = None, device: int = 0,
-                 max_ctx: int = 4096, act_int8: bool = False):
+                 max_ctx: int = 4096, act_int8: bool = False, tp_rank: int = 0, tp_world: int = 1):
+        """tp_world > 1: rank tp_rank of a tensor-parallel job (one Decoder per
+        GPU and process); connect the ranks with tp_handle / tp_connect before
+        decoding (qwen_fpga_b200.tp does it over torch.distributed)."""
         L = load()
         if index_path is None:
             index_path = os.path.splitext(blob_path)[0] + ".idx"
         self.max_ctx = max_ctx
-        dev = (C.c_int * 1)(device)
+        self.tp_rank, self.tp_world = int(tp_rank), int(tp_world)
         h = _vp()
-        rc = L.qwen_create(blob_path.encode(), index_path.encode(), 1, dev, max_ctx, 1,
-                           C.byref(h))
+        if self.tp_world == 1:
+            dev = (C.c_int * 1)(device)
+            rc = L.qwen_create(blob_path.encode(), index_path.encode(), 1, dev, max_ctx, 1,
+                               C.byref(h))
+        else:
+            rc = L.qwen_create_tp(blob_path.encode(), index_path.encode(), int(device), self.tp_rank,
+                                  self.tp_world, max_ctx, 1, C.byref(h))
         _check(rc)
         self.h = h
         self.act_int8 = False
@@ -137,6 +165,26 @@ class Decoder:
             self.close()
         except Exception:
             pass
+
+    def tp_handle(self) -> bytes:
+        """This rank's exchange-buffer handle (TP_HANDLE_BYTES bytes)."""
+        buf = C.create_string_buffer(TP_HANDLE_BYTES)
+        _check(load().qwen_tp_export(self.h, buf), self.h)
+        return buf.raw
+
+    def tp_connect(self, handles):
+        """handles: every rank's tp_handle() in rank order."""
+        if len(handles) != self.tp_world or any(len(x) != TP_HANDLE_BYTES for x in handles):
+            raise ValueError("need tp_world handles of TP_HANDLE_BYTES bytes")
+        buf = C.create_string_buffer(b"".join(handles), TP_HANDLE_BYTES * self.tp_world)
+        _check(load().qwen_tp_connect(self.h, buf), self.h)
+
+    @property
+    def vocab_range(self) -> tuple[int, int]:
+        """Rows of the logits this context fills: all of them, or the rank's vocab slice."""
+        lo, hi = C.c_int(), C.c_int()
+        _check(load().qwen_tp_vocab_range(self.h, C.byref(lo), C.byref(hi)), self.h)
+        return lo.value, hi.value
 
     def set_act_int8(self, on: bool):
         _check(load().qwen_set_act_int8(self.h, 1 if on else 0), self.h)

@@ -152,6 +152,17 @@ __device__ __forceinline__ void st_tv(unsigned long long* p, float v, unsigned t
   const unsigned long long w = ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
   asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" :: "l"(p), "l"(w) : "memory");
 }
+// Tagged words crossing GPUs (the TP exchange buffers, written over NVLink):
+// system scope.
+__device__ __forceinline__ unsigned long long ld_tv_sys(const unsigned long long* p) {
+  unsigned long long a;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
+  return a;
+}
+__device__ __forceinline__ void st_tv_sys(unsigned long long* p, float v, unsigned tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" :: "l"(p), "l"(w) : "memory");
+}
 __device__ __forceinline__ int ld_flag(const int* p) {
   int v;
   asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -288,11 +299,22 @@ __device__ __forceinline__ bool aborted(const PCtx& c) {
   return *(volatile int*)&c.ms->abort || ld_flag(c.A->abort_flag);
 }
 
-// Source and size of chunk k: one K-slice of a layer panel, one K-slab of a
-// head tile, or (DeltaNet IN) nrows fp32 rows of in_proj_b (seg 2) or
-// in_proj_a (seg 3).  src = null for a chunk outside its matrix.
+// K window [k0, k1) of GEMV phase `sub` packed as k0 | k1 << 16: the whole
+// input (IN, GATEUP), or the rank's input columns of a row-parallel OUT / DOWN.
+__host__ __device__ __forceinline__ unsigned kwin_of(int sub, unsigned kw_out, unsigned kw_down) {
+  return sub == 2 ? kw_out : (sub == 4 ? kw_down : (unsigned)HID << 16);
+}
+__device__ __forceinline__ unsigned kwin(const PersistArgs& A, int sub) {
+  return kwin_of(sub, (unsigned)A.ok0 | (unsigned)A.ok1 << 16, (unsigned)A.dk0 | (unsigned)A.dk1 << 16);
+}
+
+// Source and size of chunk k: one K-slice of a layer panel (slice n covers
+// K [k0 + 1024 n, min(k0 + 1024 (n + 1), k1)) of the phase's window), one
+// K-slab of a head tile, or (DeltaNet IN) nrows fp32 rows of in_proj_b (seg 2)
+// or in_proj_a (seg 3).  src = null for a chunk outside its matrix.
 __device__ __forceinline__ void chunk_src(const LayerW* lay, const int8_t* head_tiles, const Chunk& k,
-                                          const char*& src, unsigned& bytes) {
+                                          unsigned kw_out, unsigned kw_down, const char*& src,
+                                          unsigned& bytes) {
   const int p = k.phase;
   const int row0 = (int)k.row0, n = k.nrows;
   src = nullptr;
@@ -314,10 +336,12 @@ __device__ __forceinline__ void chunk_src(const LayerW* lay, const int8_t* head_
     else if (sub == 2) { base = L.pout; np = HID / PANEL; pbytes = (size_t)PANEL * VDIM; }
     else if (sub == 3) { base = L.pgu; np = FFN / PAIR_ROWS; pbytes = (size_t)PANEL * HID; }
     else if (sub == 4) { base = L.pdown; np = HID / PANEL; pbytes = (size_t)PANEL * FFN; }
-    if (!base || row0 >= np || (size_t)n * SLOTW >= pbytes) return;
-    src = (const char*)base + (size_t)row0 * pbytes + (size_t)n * SLOTW;
-    const size_t rem = pbytes - (size_t)n * SLOTW;
-    bytes = rem < (size_t)SLOTW ? (unsigned)rem : (unsigned)SLOTW;
+    const unsigned kw = kwin_of(sub, kw_out, kw_down);
+    const int k0 = (int)(kw & 0xffffu) + n * PANEL_KB, k1 = (int)(kw >> 16);
+    if (!base || row0 >= np || k0 >= k1 || (size_t)k1 * PANEL > pbytes) return;
+    src = (const char*)base + (size_t)row0 * pbytes + (size_t)k0 * PANEL;
+    const int kl = k1 - k0 < PANEL_KB ? k1 - k0 : PANEL_KB;
+    bytes = (unsigned)(kl * PANEL);
     return;
   }
   if (sub != 0 || !L.linear || k.seg < 2 || k.seg > 3 || row0 + n > LH || n * HID * 4 > SLOTW) return;
@@ -328,13 +352,13 @@ __device__ __forceinline__ void chunk_src(const LayerW* lay, const int8_t* head_
 // Issue the bulk copy of chunk i into its slot (one lane).  One copy in the
 // kernel (not inlined, plain arguments): every refill site calls it.
 __device__ __noinline__ void issue_chunk_core(const Chunk* ch, const LayerW* lay, const int8_t* head_tiles,
-                                              unsigned char* sm, unsigned long long pol, int* err,
-                                              int* abort_flag, int i) {
+                                              unsigned kw_out, unsigned kw_down, unsigned char* sm,
+                                              unsigned long long pol, int* err, int* abort_flag, int i) {
   const int slot = i % NSLOT;
   const Chunk k = ch[i];
   const char* src;
   unsigned bytes;
-  chunk_src(lay, head_tiles, k, src, bytes);
+  chunk_src(lay, head_tiles, k, kw_out, kw_down, src, bytes);
   if (!src) {   // a chunk outside its matrix: ERR_CHECK site 5, every CTA stops
     record_error(err, abort_flag, (Misc*)(sm + OFF_MISC), ERR_CHECK, 5, (int)k.row0);
     return;
@@ -344,7 +368,8 @@ __device__ __noinline__ void issue_chunk_core(const Chunk* ch, const LayerW* lay
   bulk_g2s(smem_u32(sm + OFF_RING + slot * SLOT), src, bytes, bar, pol);
 }
 __device__ __forceinline__ void issue_chunk(const PCtx& c, int i) {
-  issue_chunk_core(c.ch, c.lay, c.A->head_tiles, c.sm, c.pol, c.A->err, c.A->abort_flag, i);
+  issue_chunk_core(c.ch, c.lay, c.A->head_tiles, kwin(*c.A, 2), kwin(*c.A, 4), c.sm, c.pol, c.A->err,
+                   c.A->abort_flag, i);
 }
 
 // One thread: bounded wait for phase `parity` of an mbarrier.  false on abort
@@ -472,21 +497,21 @@ __device__ __forceinline__ int dig_off(int d, int k) {
   return (k >> 5) * 96 + (d * 4 + ((k >> 2) & 3)) * 8 + ((k >> 4) & 1) * 4;
 }
 
-// W8A32 digit image of v = src[0 .. K) (a normed input: v = src * (1 + g),
-// K = 2 PT, the thread's gains g2) into the CTA's image, shift from the exact
+// W8A32 digit image of v = src[k0 .. k1) (positions of the image; a normed
+// input: v = src * (1 + g), [0, 2 PT), the thread's gains g2) into the CTA's image, shift from the exact
 // max|v| whose bits the input wait folded into amax: |X| <= 2^22 (the rule of
 // the other encoders), three int8 digits per position; an input whose max is
 // below 2^-104 encodes as zero (its share of any output is below 2^-104 * 127 *
 // K of the row scale).  Thread = position pairs tid + PT j.  Returns 2^-shift
 // (0: all zero).  Ends with a CTA barrier.  One copy (not inlined), shared by
 // the four GEMV phases.
-__device__ __noinline__ float encode_fixed(unsigned char* sm, const float* src, int K, unsigned amax, bool gain,
-                                           float2 g2) {
+__device__ __noinline__ float encode_fixed(unsigned char* sm, const float* src, int k0, int k1, unsigned amax,
+                                           bool gain, float2 g2) {
   int8_t* dg = (int8_t*)(sm + OFF_DIG);
   const int sh = 22 - ((int)((amax >> 23) & 0xffu) - 126);   // max in [2^(ex-1), 2^ex)
   const bool live = amax != 0u && sh <= 126;
   const float p2 = live ? pow2f(sh) : 0.0f;
-  for (int q = threadIdx.x; 2 * q < K; q += PT) {
+  for (int q = (k0 >> 1) + threadIdx.x; 2 * q < k1; q += PT) {
     float v0 = src[2 * q], v1 = src[2 * q + 1];
     if (gain) {
       v0 = __fmul_rn(v0, __fadd_rn(1.0f, g2.x));
@@ -768,10 +793,12 @@ __device__ bool load_residual(PCtx& c, int p) {
 }
 
 // Prologue of the OUT (sub 2) and DOWN (sub 4) phases: the residual rows and
-// the K inputs into xf.  ACT_INT8 (amax null): their digit image for the whole
+// the inputs of the phase's K window [k0, k1) (kwin: all of them, or the
+// rank's columns under tensor parallelism) into xf at their positions.
+// ACT_INT8 (amax null; whole inputs only): their digit image for the whole
 // CTA as well (encode_lin); W8A32: max|x| folded into *amax instead, for
 // encode_fixed.  false on abort.
-__device__ bool prologue(PCtx& c, int p, unsigned* amax, int& K_out) {
+__device__ bool prologue(PCtx& c, int p, unsigned* amax, int& k0, int& k1) {
   float* xf = (float*)(c.sm + OFF_XF);
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
@@ -783,19 +810,22 @@ __device__ bool prologue(PCtx& c, int p, unsigned* amax, int& K_out) {
   // below), the gated attention output o * sigmoid(gate) written by the merge
   // (attention OUT), or silu(gate) * up (DOWN)
   const bool gated = sub == 2 && L.linear;
-  const float gw = gated ? __ldg(L.gnorm_w + (threadIdx.x % LV)) : 0.0f;   // element i = tid + 512 j
+  // element i = k0 + tid + 512 j, and k0 is a multiple of LV
+  const float gw = gated ? __ldg(L.gnorm_w + (threadIdx.x % LV)) : 0.0f;
   const unsigned long long* src = sub == 4 ? A.tv_act : (L.linear ? A.tv_o : A.tv_attn);
-  const int K = sub == 4 ? FFN : (L.linear ? VDIM : NH * HD);
-  K_out = K;
-  if (!wait_tagged_max(c, src, K, tag_of(c, p - 1), xf, gated ? nullptr : amax, false, make_float2(0.0f, 0.0f)))
+  const unsigned kw = kwin(A, sub);
+  k0 = (int)(kw & 0xffffu);
+  k1 = (int)(kw >> 16);
+  if (!wait_tagged_max(c, src + k0, k1 - k0, tag_of(c, p - 1), xf + k0, gated ? nullptr : amax, false,
+                       make_float2(0.0f, 0.0f)))
     return false;
   if (gated) {
-    // gated RMSNorm of the delta-rule output (golden/model.py:183-189), z from
-    // IN(l) parked in the digit region
+    // gated RMSNorm of the delta-rule output (golden/model.py:183-189) over the
+    // window's heads, z from IN(l) parked in the digit region
     float* zb = (float*)(c.sm + OFF_DIG);
-    if (!wait_tagged(c, A.tv_z, VDIM, tag_of(c, p - 2), zb)) return false;
+    if (!wait_tagged(c, A.tv_z + k0, k1 - k0, tag_of(c, p - 2), zb + k0)) return false;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    for (int h = wid; h < LH; h += NCW) {
+    for (int h = k0 / LV + wid; h < k1 / LV; h += NCW) {
       float ss = 0.0f;
       for (int i = lane; i < LV; i += 32) ss = fmaf(xf[h * LV + i], xf[h * LV + i], ss);
       ss = warp_sum(ss);
@@ -804,7 +834,7 @@ __device__ bool prologue(PCtx& c, int p, unsigned* amax, int& K_out) {
     }
     consumer_sync();
     float vmax = 0.0f;
-    for (int i = threadIdx.x; i < VDIM; i += PT) {
+    for (int i = k0 + threadIdx.x; i < k1; i += PT) {
       const float v = __fmul_rn(__fmul_rn(xf[i], ms->inv_h[i / LV]), gw);
       xf[i] = __fmul_rn(v, silu_f(zb[i]));
       vmax = fmaxf(vmax, fabsf(xf[i]));
@@ -816,8 +846,39 @@ __device__ bool prologue(PCtx& c, int p, unsigned* amax, int& K_out) {
     }
     consumer_sync();
   }
-  if (!amax) encode_lin(c, K, i8);
+  if (!amax) encode_lin(c, k1, i8);
   return true;
+}
+
+// Tensor parallelism: this rank's packed (value, index) maximum of its vocab
+// slice to every rank, then the maximum over all ranks' (one thread, bounded
+// wait).  Packed maxima order by value, then by the lower index, so the
+// result is the first index of the global maximum on every rank.
+__device__ unsigned long long tp_argmax(PCtx& c, unsigned long long b) {
+  const PersistArgs& A = *c.A;
+  const unsigned tag = tag_of(c, PH_HEAD);
+  const size_t off = XB_HEAD + 2 * (size_t)A.tp_rank;
+  for (int rr = 0; rr < A.tp_world; ++rr) {
+    st_tv_sys(A.xbuf[rr] + off, __uint_as_float((unsigned)(b >> 32)), tag);
+    st_tv_sys(A.xbuf[rr] + off + 1, __uint_as_float((unsigned)b), tag);
+  }
+  const unsigned long long* xb = A.xbuf[A.tp_rank] + XB_HEAD;
+  const unsigned long long t0 = gtime();
+  int it = 0;
+  for (;;) {
+    unsigned long long g = 0ull;
+    bool all = true;
+    for (int rr = 0; rr < A.tp_world && all; ++rr) {
+      const unsigned long long hi = ld_tv_sys(xb + 2 * rr), lo = ld_tv_sys(xb + 2 * rr + 1);
+      all = tag_ok(hi, tag) && tag_ok(lo, tag);
+      g = umax64(g, (unsigned long long)(unsigned)hi << 32 | (unsigned)lo);
+    }
+    if (all) return g;
+    if (((++it) & 63) == 0) {
+      if (aborted(c)) return b;
+      if (gtime() - t0 > WAIT_NS) { raise_abort(c, 24, A.tp_rank); return b; }
+    }
+  }
 }
 
 // Block argmax of the head, then the last CTA reduces every block's maximum,
@@ -848,6 +909,7 @@ __device__ void head_finish(PCtx& c, unsigned long long best) {
     consumer_sync();
     if (threadIdx.x == 0) {
       for (int w = 0; w < NCW; ++w) b = umax64(b, ms->wbest[w]);
+      if (A.tp_world > 1) b = tp_argmax(c, b);
       const int step = ms->step;
       if (step < A.max_steps) A.ids[step] = am_index(b);
       else atomicCAS(A.err, 0, ERR_CTX);
@@ -1086,12 +1148,12 @@ __device__ __forceinline__ void release_panel_chunk(PCtx& c, int i) {
   __syncwarp();
 }
 
-// Tasks of chunk k of GEMV phase `sub`.
-__host__ __device__ __forceinline__ int chunk_tasks(const Chunk& k, int sub) {
+// Tasks of chunk k of a GEMV phase with K window kw (kwin_of): a panel
+// slice's K in pieces of at most TASK_KB (multiples of 128).
+__host__ __device__ __forceinline__ int chunk_tasks(const Chunk& k, unsigned kw) {
   if (!(k.seg & CHUNK_PANEL)) return k.nrows;
-  const int K = sub == 0 ? HID : (sub == 2 ? VDIM : FFN);
-  const int rem = K - (int)k.nrows * PANEL_KB;
-  return (rem < PANEL_KB ? rem : PANEL_KB) / TASK_KB;
+  const int rem = (int)(kw >> 16) - (int)(kw & 0xffffu) - (int)k.nrows * PANEL_KB;
+  return ((rem < PANEL_KB ? rem : PANEL_KB) + TASK_KB - 1) / TASK_KB;
 }
 
 // Task map of a GEMV phase over chunks [i0, i0 + nj), nj <= NSLOT, held in
@@ -1110,7 +1172,7 @@ __device__ __forceinline__ TaskMap task_map(const PCtx& c, int sub, int i0, int 
   m.pan = 0;
   if (lane < nj) {
     const Chunk k = c.ch[i0 + lane];
-    m.nq = chunk_tasks(k, sub);
+    m.nq = chunk_tasks(k, kwin(*c.A, sub));
     if (k.seg & CHUNK_PANEL) {
       m.pan = 1;
       m.start = 1;
@@ -1155,6 +1217,54 @@ __device__ __forceinline__ const float* row_scale(const LayerW& L, int sub, int 
     return r < QPROJ ? L.q_s + r : (r < QPROJ + KVPROJ ? L.k_s + (r - QPROJ) : L.v_s + (r - QPROJ - KVPROJ));
   }
   return (sub == 2 ? (L.linear ? L.out_s : L.o_s) : L.down_s) + r;
+}
+
+// Row-parallel OUT / DOWN under tensor parallelism: the residual rows of this
+// CTA's panels once every rank's partial of them is in this rank's exchange
+// buffer, h = r + ((y_0 + y_1) + ...) in rank order (bit-identical on every
+// rank), written as tagged words.  Per warp (the panels it finished), bounded
+// wait; false on abort.
+__device__ bool tp_reduce_rows(PCtx& c, int sub, int i0, const TaskMap& m, bool own, int pr, unsigned tag) {
+  const PersistArgs& A = *c.A;
+  const float* hs = (const float*)(c.sm + OFF_HS);
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned long long* xb = A.xbuf[A.tp_rank] + XB_PART + (size_t)(sub == 4) * TP_MAX * HID;
+  const int P = A.tp_world;
+  int good = 1;
+  for (int v = wid; v < m.npan && good; v += NCW) {
+    const int r = (int)c.ch[i0 + panel_chunk(m, v)].row0 * PANEL + pr;
+    const unsigned long long t0 = gtime();
+    int it = 0;
+    float sum = 0.0f;
+    bool done = !own;
+    for (;;) {
+      if (!done) {
+        unsigned long long w[TP_MAX];
+        bool all = true;
+#pragma unroll
+        for (int rr = 0; rr < TP_MAX; ++rr)
+          if (rr < P) { w[rr] = ld_tv_sys(xb + (size_t)rr * HID + r); all = all && tag_ok(w[rr], tag); }
+        if (all) {
+          sum = tv_val(w[0]);
+#pragma unroll
+          for (int rr = 1; rr < TP_MAX; ++rr)
+            if (rr < P) sum = __fadd_rn(sum, tv_val(w[rr]));
+          done = true;
+        }
+      }
+      if (__all_sync(0xffffffffu, done)) break;
+      if (((++it) & 63) == 0) {
+        int bad = 0;
+        if (lane == 0) {
+          if (aborted(c)) bad = 1;
+          else if (gtime() - t0 > WAIT_NS) { raise_abort(c, 23, sub); bad = 1; }
+        }
+        if (__shfl_sync(0xffffffffu, bad, 0)) { good = 0; break; }
+      }
+    }
+    if (good && own) st_tv(A.tv_h + r, __fadd_rn(hs[r], sum), tag);
+  }
+  return good != 0;
 }
 
 // A GEMV phase over panels (IN, OUT, GATEUP, DOWN).  The input vector is
@@ -1222,7 +1332,7 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
   // the input vector (W8A32: its max folded into amax by the wait)
   float sx = 0.0f, xs = 0.0f;
   unsigned* amax = i8 ? nullptr : &ms->amax[p & 1];
-  int K = HID;
+  int k0 = 0, k1 = HID;   // the input window (positions of the digit image)
   if (normed) {
     if (sub == 0 && l == 0) {
       // residual stream starts at the dequantised embedding row (golden/model.py:246)
@@ -1248,7 +1358,7 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
       float inv;
       cta_encode_1024(c, hs, g2, true, inv, sx, false, p);
     } else {
-      xs = encode_fixed(c.sm, hs, HID, *amax, true, g2);
+      xs = encode_fixed(c.sm, hs, 0, HID, *amax, true, g2);
     }
     if (!i8 && wid == 0) {
       // sum of squares in numpy's pairwise order: chain ch = block ch / 8,
@@ -1277,9 +1387,9 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
       trace_warp(c, p, 8);
     }
   } else {
-    if (!prologue(c, p, amax, K)) return false;
+    if (!prologue(c, p, amax, k0, k1)) return false;
     trace_mark(c, p, 1);
-    if (!i8) xs = encode_fixed(c.sm, xf, K, *amax, false, g2);
+    if (!i8) xs = encode_fixed(c.sm, xf, k0, k1, *amax, false, g2);
   }
   trace_warp(c, p, 2);
   const unsigned char* fr = c.sm + OFF_DIG;                   // the CTA's digit image
@@ -1327,10 +1437,11 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
       if (lane == 0) part_f[t * PANEL] = a;
       continue;
     }
-    const int kb = (int)k.nrows * PANEL_KB + TASK_KB * q;   // the task's first K position
+    const int kb = k0 + (int)k.nrows * PANEL_KB + TASK_KB * q;   // the task's first K position
     const unsigned sa = smem_u32(slot) + 512u * (TASK_KB / 32) * q;
+    const int kl = k1 - kb < TASK_KB ? k1 - kb : TASK_KB;         // a multiple of 128
     int d3[3];
-    panel_mma(sa, fr, kb >> 5, TASK_KB / 32, nd, d3);
+    panel_mma(sa, fr, kb >> 5, kl >> 5, nd, d3);
     const int vp = chunk_panel(m, j);
     if (own) {
       const unsigned pv = part + 4u * (unsigned)(vp * 3 * PANEL + pr);
@@ -1380,11 +1491,16 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
           else { out = A.tv_kvn + KVPROJ; o = r - QPROJ - KVPROJ; }
         }
         st_tv(out + o, y, tag);
-      } else {
+      } else if (A.tp_world == 1) {
         st_tv(A.tv_h + r, __fadd_rn(hs[r], y), tag);
+      } else {
+        // row-parallel: this rank's partial row into every rank's exchange buffer
+        const size_t off = XB_PART + ((size_t)(sub == 4) * TP_MAX + A.tp_rank) * HID + r;
+        for (int rr = 0; rr < A.tp_world; ++rr) st_tv_sys(A.xbuf[rr] + off, y, tag);
       }
     }
   }
+  if ((sub == 2 || sub == 4) && A.tp_world > 1 && !tp_reduce_rows(c, sub, i0, m, own, pr, tag)) return false;
   // the fp32 rows (W8A32: times 1/rms)
   for (int t = wid; t < m.ntask; t += NCW) {
     int q;
@@ -1858,15 +1974,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
       if (p != PH_HEAD && sub == 1) {
         const LayerW& L = c.lay[p / 5];
         if (L.linear) {
-          if ((int)blockIdx.x < LH * NDSLICE) ok = delta_item(c, p, blockIdx.x);
+          // this rank's heads [dn_h0, dn_h1): one CTA per (head, value slice)
+          if ((int)blockIdx.x < (A.dn_h1 - A.dn_h0) * NDSLICE) ok = delta_item(c, p, A.dn_h0 * NDSLICE + blockIdx.x);
         } else {
           const int Tn = ms->T + 1;
           int nch = (Tn + ATT_MINLEN - 1) / ATT_MINLEN;
           nch = nch < 1 ? 1 : (nch > ATT_MAXCH ? ATT_MAXCH : nch);
           const int cl = (Tn + nch - 1) / nch;
           if (cl > ATT_MAXLEN) { if (threadIdx.x == 0) raise_abort(c, 21, p); ok = false; break; }
-          for (int it = blockIdx.x; it < NKV * nch && ok; it += gridDim.x)
-            ok = attn_item(c, p, it % NKV, it / NKV, nch, cl);
+          const int ng = A.kv_g1 - A.kv_g0;   // this rank's KV groups
+          for (int it = blockIdx.x; it < ng * nch && ok; it += gridDim.x)
+            ok = attn_item(c, p, A.kv_g0 + it % ng, it / ng, nch, cl);
         }
         trace_mark(c, p, 3);
         continue;
@@ -1937,7 +2055,33 @@ size_t persist_trace_words(int G) {
 //     phase's others; the fp32 in_proj_a/b rows of a DeltaNet IN follow, 4 rows
 //     per chunk, by the same rule.
 //   HEAD: contiguous, balanced ranges of the 1940 tiles.
-bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
+bool tp_plan(int rank, int world, TpPlan& out, std::string& err) {
+  if (world != 1 && world != 2 && world != 4 && world != TP_MAX) { err = "tp world must be 1, 2, 4 or 8"; return false; }
+  if (rank < 0 || rank >= world) { err = "tp rank outside [0, world)"; return false; }
+  TpPlan t;
+  t.rank = rank;
+  t.world = world;
+  t.dn_h0 = LH * rank / world;
+  t.dn_h1 = LH * (rank + 1) / world;
+  if (world <= NKV) {
+    t.kv_g0 = NKV * rank / world;
+    t.kv_g1 = NKV * (rank + 1) / world;
+  } else {   // the KV group of this rank's query heads (computed by world / NKV ranks)
+    t.kv_g0 = (NH * rank / world) / (NH / NKV);
+    t.kv_g1 = t.kv_g0 + 1;
+  }
+  t.ok0 = VDIM * rank / world;   // = the rank's DeltaNet heads x LV = its query heads x HD
+  t.ok1 = VDIM * (rank + 1) / world;
+  constexpr int NB = FFN / 128;  // FFN columns in blocks of 128 (whole MMA task pieces)
+  t.dk0 = 128 * (NB * rank / world);
+  t.dk1 = 128 * (NB * (rank + 1) / world);
+  t.t0 = (int)((long long)HEAD_TILES * rank / world);
+  t.t1 = (int)((long long)HEAD_TILES * (rank + 1) / world);
+  out = t;
+  return true;
+}
+
+bool build_schedule(const ModelW& M, int G, const TpPlan& tp, std::vector<Chunk>& chunks,
                     std::vector<unsigned short>& phase_first, std::string& err) {
   (void)M;
   if (G < 1) { err = "no CTAs"; return false; }
@@ -1963,7 +2107,8 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
   // round of NCW tasks + T_TAIL from its start; the DeltaNet / attention MIX
   // items take T_DELTA / T_ATTN.  Panels go to the CTA that would finish the
   // phase earliest, so a phase's work avoids the CTAs still busy with the last.
-  constexpr double T_PROP = 0.6, T_REL = 1.8, T_ENC = 0.5, T_ROUND = 0.7, T_TAIL = 0.45;
+  constexpr double T_PROP = 0.6, T_REL = 1.8, T_ENC = 0.5, T_TAIL = 0.45;
+  constexpr double T_ROUND = 0.2 + 0.5 * TASK_KB / 512.0;   // one task per warp
   constexpr double T_DELTA = 2.4, T_ATTN = 4.0;
   constexpr int ATT_CTAS = 20;   // CTAs running attention items at short contexts
   std::vector<double> freeb(G, 0.0);
@@ -1974,8 +2119,9 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
     const int sub = p % 5;
     if (p == PH_HEAD) {
       // whole tiles per CTA (a tile's K-slabs accumulate in one CTA's TMEM)
+      const int nt = tp.t1 - tp.t0;   // this rank's vocab slice
       for (int b = 0; b < G; ++b) {
-        const int t0 = (int)((long long)HEAD_TILES * b / G), t1 = (int)((long long)HEAD_TILES * (b + 1) / G);
+        const int t0 = tp.t0 + (int)((long long)nt * b / G), t1 = tp.t0 + (int)((long long)nt * (b + 1) / G);
         for (int t = t0; t < t1; ++t)
           for (int j = 0; j < HEAD_NSLAB; ++j)
             if (!push(b, p, CHUNK_MMA, j, t, SLOTW)) return false;
@@ -1986,24 +2132,41 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
     if (sub == 1) {
       double last = ready;
       for (int b = 0; b < G; ++b)
-        if (linear ? b < LH * NDSLICE : b < ATT_CTAS) {
+        if (linear ? b < (tp.dn_h1 - tp.dn_h0) * NDSLICE : b < ATT_CTAS) {
           freeb[b] = std::max(freeb[b], ready) + (linear ? T_DELTA : T_ATTN);
           last = std::max(last, freeb[b]);
         }
       ready = last + T_PROP;
       continue;
     }
-    int npan, K;
-    if (sub == 0) { npan = (linear ? CONVD + VDIM : QPROJ + 2 * KVPROJ) / PANEL; K = HID; }
-    else if (sub == 2) { npan = HID / PANEL; K = VDIM; }
-    else if (sub == 3) { npan = FFN / PAIR_ROWS; K = HID; }
-    else { npan = HID / PANEL; K = FFN; }
-    // a panel's K-slices: bytes and tasks of each
+    // this rank's panels of the phase and its K window
+    std::vector<int> pans;
+    int kw0 = 0, kw1 = HID;
+    if (sub == 0) {
+      if (linear) {   // q, k, v, z blocks of 2048 rows; head h = 8 panels of each
+        for (int blk = 0; blk < 4; ++blk)
+          for (int h = tp.dn_h0; h < tp.dn_h1; ++h)
+            for (int j = 0; j < LK / PANEL; ++j) pans.push_back(blk * (KDIM / PANEL) + h * (LK / PANEL) + j);
+      } else {        // the KV groups' query heads ([q | gate] rows), k and v rows
+        for (int g = tp.kv_g0; g < tp.kv_g1; ++g) {
+          for (int j = 0; j < QPROJ / NKV / PANEL; ++j) pans.push_back(g * (QPROJ / NKV / PANEL) + j);
+          for (int kv = 0; kv < 2; ++kv)
+            for (int j = 0; j < HD / PANEL; ++j) pans.push_back((QPROJ + kv * KVPROJ + g * HD) / PANEL + j);
+        }
+      }
+    } else if (sub == 3) {
+      for (int q = tp.dk0 / PAIR_ROWS; q < tp.dk1 / PAIR_ROWS; ++q) pans.push_back(q);
+    } else {
+      for (int q = 0; q < HID / PANEL; ++q) pans.push_back(q);
+      kw0 = sub == 2 ? tp.ok0 : tp.dk0;
+      kw1 = sub == 2 ? tp.ok1 : tp.dk1;
+    }
+    // a panel's K-slices of the window: bytes and tasks of each
     std::vector<int> sl_bytes, sl_tasks;
-    for (int k0 = 0; k0 < K; k0 += PANEL_KB) {
-      const int kb = K - k0 < PANEL_KB ? K - k0 : PANEL_KB;
+    for (int k0 = kw0; k0 < kw1; k0 += PANEL_KB) {
+      const int kb = kw1 - k0 < PANEL_KB ? kw1 - k0 : PANEL_KB;
       sl_bytes.push_back(PANEL * kb);
-      sl_tasks.push_back(kb / TASK_KB);
+      sl_tasks.push_back((kb + TASK_KB - 1) / TASK_KB);
     }
     const int nslice = (int)sl_bytes.size();
     int ptasks = 0;
@@ -2026,7 +2189,7 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
       }
       return best;
     };
-    for (int q = 0; q < npan; ++q) {
+    for (int q : pans) {
       const int b = least_fit(nslice, ptasks);
       if (b < 0) { err = "phase does not fit the rings"; return false; }
       inph[b] += nslice;
@@ -2038,12 +2201,13 @@ bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
       // in_proj_b (seg 2) and in_proj_a (seg 3): fp32 rows, 4 per chunk, one task per row
       constexpr int per = SLOTW / (HID * 4);
       for (int seg = 2; seg <= 3; ++seg)
-        for (int r = 0; r < LH; r += per) {
-          const int b = least_fit(1, per);
+        for (int r = tp.dn_h0; r < tp.dn_h1; r += per) {
+          const int n = std::min(per, tp.dn_h1 - r);
+          const int b = least_fit(1, n);
           if (b < 0) { err = "phase does not fit the rings"; return false; }
           inph[b] += 1;
-          tasks[b] += per;
-          if (!push(b, p, seg, per, r, per * HID * 4)) return false;
+          tasks[b] += n;
+          if (!push(b, p, seg, n, r, n * HID * 4)) return false;
         }
     }
     double last = ready;

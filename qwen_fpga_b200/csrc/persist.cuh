@@ -25,27 +25,6 @@ constexpr unsigned char CHUNK_MMA = 0x80;
 // Phases of one decode step: 5 per layer (IN, MIX, OUT, GATEUP, DOWN) + the head.
 constexpr int PERSIST_NPHASE = NLAYER * 5 + 1;
 
-// Everything the persistent kernel reads; tv_* are tagged {value, tag} words.
-struct PersistArgs {
-  const LayerW* layers;        // [NLAYER] (device copy of ModelW::L)
-  const int8_t* emb_q; const float* emb_s; const float* final_norm;
-  const int8_t* head_tiles;    // embed_tokens.weight re-tiled for the tensor cores (repack_head_tiles)
-  const Chunk* chunks;         // [G][MAXCH]
-  const unsigned short* phase_first;  // [G][PERSIST_NPHASE + 1]: a phase's chunks are
-                                      // [first[p], first[p + 1]) of the CTA's list
-  unsigned long long *tv_h, *tv_qkv, *tv_z, *tv_ab, *tv_o, *tv_qg, *tv_kvn, *tv_attn, *tv_act;
-  float* conv; float* rec; float* kcache; float* vcache;
-  float* att_part; int* att_cnt;   // att_cnt: [NFULL][NKV]
-  int* head_cnt;
-  unsigned long long* am_part;     // [G]
-  const float* rope;
-  float* logits;
-  int* io; int* ids; int* err; int* abort_flag;
-  StepDyn* dyn;
-  unsigned long long* trace;       // nullable: the trace record (layout above persist_trace_words)
-  int max_ctx, max_rope, max_steps;
-};
-
 // Trace record layout: per CTA and phase, %globaltimer stamps at phase entry,
 // inputs arrived (the input wait done), outputs written (a GEMV phase; the
 // head: its first slab landed), phase exit; then,
@@ -70,6 +49,62 @@ static_assert(VOCAB % HEAD_TM == 0 && HID % HEAD_KS == 0, "head tiling");
 constexpr size_t HEAD_TILE_BYTES = (size_t)VOCAB * HID;
 cudaError_t repack_head_tiles(const int8_t* emb_q, int8_t* tiles, cudaStream_t st);
 
+// Tensor parallelism over tp_world GPUs of one node, one process (and one
+// context) per GPU.  Every rank keeps the full weights and the global index
+// space of every activation; its schedule covers only its shard:
+//   DeltaNet heads [dn_h0, dn_h1) (in_proj_qkv / z / a / b rows, conv, state,
+//     gated norm: column-parallel, no exchange inside the mixer);
+//   attention KV groups [kv_g0, kv_g1) with all four query heads of each (for
+//     tp_world 4 and 8 the ranks sharing a group compute it redundantly);
+//   OUT (out_proj / o_proj) row-parallel over input columns [ok0, ok1) (the
+//     rank's heads), DOWN row-parallel over FFN columns [dk0, dk1) (128-column
+//     blocks), gate/up column-parallel over the same FFN rows;
+//   head tiles [t0, t1) (vocab slice).
+// An OUT or DOWN phase adds its partial rows across ranks (P2P stores into
+// every rank's exchange buffer, then a fixed-order sum: bit-identical on all
+// ranks); the head exchanges each rank's (max, index).
+constexpr int TP_MAX = 8;
+struct TpPlan {
+  int rank = 0, world = 1;
+  int dn_h0 = 0, dn_h1 = LH;
+  int kv_g0 = 0, kv_g1 = NKV;
+  int ok0 = 0, ok1 = VDIM;
+  int dk0 = 0, dk1 = FFN;
+  int t0 = 0, t1 = HEAD_TILES;
+};
+// The shard of `rank` among `world` (1, 2, 4 or 8); false (with err) otherwise.
+bool tp_plan(int rank, int world, TpPlan& out, std::string& err);
+// Exchange buffer of one rank (tagged words): [2 (OUT, DOWN)][TP_MAX source
+// ranks][HID] partial rows, then [TP_MAX source ranks][2] head (max, index) words.
+constexpr size_t XB_PART = 0;
+constexpr size_t XB_HEAD = 2 * (size_t)TP_MAX * HID;
+constexpr size_t XB_WORDS = XB_HEAD + 2 * TP_MAX;
+
+// Everything the persistent kernel reads; tv_* are tagged {value, tag} words.
+struct PersistArgs {
+  const LayerW* layers;        // [NLAYER] (device copy of ModelW::L)
+  const int8_t* emb_q; const float* emb_s; const float* final_norm;
+  const int8_t* head_tiles;    // embed_tokens.weight re-tiled for the tensor cores (repack_head_tiles)
+  const Chunk* chunks;         // [G][MAXCH]
+  const unsigned short* phase_first;  // [G][PERSIST_NPHASE + 1]: a phase's chunks are
+                                      // [first[p], first[p + 1]) of the CTA's list
+  unsigned long long *tv_h, *tv_qkv, *tv_z, *tv_ab, *tv_o, *tv_qg, *tv_kvn, *tv_attn, *tv_act;
+  float* conv; float* rec; float* kcache; float* vcache;
+  float* att_part; int* att_cnt;   // att_cnt: [NFULL][NKV]
+  int* head_cnt;
+  unsigned long long* am_part;     // [G]
+  const float* rope;
+  float* logits;
+  int* io; int* ids; int* err; int* abort_flag;
+  StepDyn* dyn;
+  unsigned long long* trace;       // nullable: the trace record (layout above persist_trace_words)
+  int max_ctx, max_rope, max_steps;
+  // tensor parallelism (tp_world = 1: none; see TpPlan)
+  int tp_rank, tp_world;
+  int dn_h0, dn_h1, kv_g0, kv_g1, ok0, ok1, dk0, dk1;
+  unsigned long long* xbuf[TP_MAX];   // every rank's exchange buffer, mapped here (rank order)
+};
+
 // Layer GEMVs on the warp-level tensor-core MMA (mma.sync m16n8k32 s8): every
 // projection is re-laid at load time as panels of 16 rows; inside a panel,
 // element (m, k) sits at ((k / 16) * 16 + m) * 16 + k % 16, so one K = 32 step
@@ -87,6 +122,8 @@ constexpr unsigned char CHUNK_PANEL = 0x40;     // Chunk.seg flag: row0 = panel,
 static_assert(CONVD % PANEL == 0 && VDIM % PANEL == 0 && QPROJ % PANEL == 0 &&
               KVPROJ % PANEL == 0 && HID % PANEL == 0 && FFN % PAIR_ROWS == 0, "panels");
 static_assert(HID % TASK_KB == 0 && VDIM % TASK_KB == 0 && FFN % TASK_KB == 0, "tasks");
+static_assert(VDIM == NH * HD && FFN % 128 == 0 && VDIM % (TP_MAX * 128) == 0, "TP column windows");
+static_assert(KDIM == VDIM && LK == LV && LH % TP_MAX == 0 && NH % TP_MAX == 0, "TP head blocks");
 // Re-lay nrows rows (row r read from rowptr[r], K bytes each) as 16-row panels
 // (for GATEUP the caller orders the rows 8 gate, 8 up per panel).
 cudaError_t repack_panels(const int8_t* const* rowptr, int8_t* out, int nrows, int K, cudaStream_t st);
@@ -96,7 +133,7 @@ int persist_num_phases();
 int persist_max_chunks();
 size_t persist_trace_words(int G);   // words of the trace record for G CTAs
 int persist_max_blocks_per_sm();
-bool build_schedule(const ModelW& M, int G, std::vector<Chunk>& chunks,
+bool build_schedule(const ModelW& M, int G, const TpPlan& tp, std::vector<Chunk>& chunks,
                     std::vector<unsigned short>& phase_first, std::string& err);
 cudaError_t launch_persistent(const PersistArgs& args, int G, cudaStream_t st);
 

@@ -198,6 +198,10 @@ struct qwen_ctx {
   int act_int8 = 0;
   int engine = 1;             // 1 = persistent weight-streaming kernel, 0 = graph of phase kernels
   PersistArgs P{};
+  TpPlan tp{};                // tensor-parallel shard of this context (world 1: everything)
+  unsigned long long* xbuf = nullptr;   // this rank's exchange buffer (IPC-exported)
+  std::vector<void*> ipc_open;          // peers' exchange buffers mapped into this process
+  bool tp_ready = true;                 // world 1, or qwen_tp_connect done
   unsigned long long* tv_base = nullptr;
   size_t tv_words = 0;
   cudaGraphExec_t graph = nullptr;
@@ -445,6 +449,7 @@ int qwen_destroy(qwen_ctx* c) {
   cudaSetDevice(c->dev);
   if (c->st) cudaStreamSynchronize(c->st);
   if (c->graph) cudaGraphExecDestroy(c->graph);
+  for (void* p : c->ipc_open) cudaIpcCloseMemHandle(p);
   for (void* p : c->allocs) cudaFree(p);
   if (c->h_ctl) cudaFreeHost(c->h_ctl);
   if (c->h_err) cudaFreeHost(c->h_err);
@@ -455,17 +460,28 @@ int qwen_destroy(qwen_ctx* c) {
   return QWEN_OK;
 }
 
-int qwen_create(const char* blob_path, const char* index_path, int n_gpus, const int* device_ids,
+}  // extern "C"
+
+namespace {
+
+// A context on device `dev` holding tensor-parallel shard (tp_rank, tp_world).
+int create_impl(const char* blob_path, const char* index_path, int dev, int tp_rank, int tp_world,
                 int max_ctx, int max_batch, qwen_ctx** out) {
   if (!out) return fail(nullptr, QWEN_ERR_ARG, "out is null");
   *out = nullptr;
   if (!blob_path || !index_path) return fail(nullptr, QWEN_ERR_ARG, "blob_path / index_path is null");
-  if (n_gpus != 1) return fail(nullptr, QWEN_ERR_ARG, "n_gpus must be 1 (one context per GPU)");
   if (max_batch != 1) return fail(nullptr, QWEN_ERR_ARG, "max_batch must be 1");
   if (max_ctx < 1 || max_ctx > ATT_MAXCH * ATT_MAXLEN)
     return fail(nullptr, QWEN_ERR_ARG, "max_ctx must be in [1, %d]", ATT_MAXCH * ATT_MAXLEN);
+  TpPlan plan;
+  {
+    std::string perr;
+    if (!tp_plan(tp_rank, tp_world, plan, perr)) return fail(nullptr, QWEN_ERR_ARG, "%s", perr.c_str());
+  }
   qwen_ctx* c = new qwen_ctx();
-  c->dev = device_ids ? device_ids[0] : 0;
+  c->dev = dev;
+  c->tp = plan;
+  c->tp_ready = tp_world == 1;
   int rc = QWEN_OK;
   auto bail = [&](int code) { std::string m = c->err; qwen_destroy(c); g_last_error = m; return code; };
   {
@@ -550,7 +566,7 @@ int qwen_create(const char* blob_path, const char* index_path, int n_gpus, const
     std::vector<Chunk> chunks;
     std::vector<unsigned short> first;
     std::string serr;
-    if (!build_schedule(c->Mh, c->sm_count, chunks, first, serr)) {
+    if (!build_schedule(c->Mh, c->sm_count, c->tp, chunks, first, serr)) {
       fail(c, QWEN_ERR_STATE, "schedule: %s", serr.c_str());
       return bail(QWEN_ERR_STATE);
     }
@@ -633,15 +649,101 @@ int qwen_create(const char* blob_path, const char* index_path, int n_gpus, const
     P.logits = S.logits;
     P.io = S.io; P.ids = S.ids; P.err = S.err; P.dyn = S.dyn;
     P.max_ctx = S.max_ctx; P.max_rope = S.max_rope; P.max_steps = S.max_steps;
+    P.tp_rank = c->tp.rank;
+    P.tp_world = c->tp.world;
+    P.dn_h0 = c->tp.dn_h0; P.dn_h1 = c->tp.dn_h1;
+    P.kv_g0 = c->tp.kv_g0; P.kv_g1 = c->tp.kv_g1;
+    P.ok0 = c->tp.ok0; P.ok1 = c->tp.ok1;
+    P.dk0 = c->tp.dk0; P.dk1 = c->tp.dk1;
+    if (c->tp.world > 1) {
+      // the exchange buffer peers store into (its own allocation: IPC maps whole allocations)
+      if ((rc = dalloc(c, &c->xbuf, XB_WORDS * 8))) return bail(rc);
+      P.xbuf[c->tp.rank] = c->xbuf;
+    }
     const char* env = getenv("QWEN_B200_ENGINE");
-    c->engine = (env && env[0] == '0') ? 0 : 1;
-    if (c->engine == 1 && persist_max_blocks_per_sm() < 1) c->engine = 0;
+    c->engine = (env && env[0] == '0' && c->tp.world == 1) ? 0 : 1;
+    if (c->engine == 1 && persist_max_blocks_per_sm() < 1) {
+      if (c->tp.world > 1) { fail(c, QWEN_ERR_STATE, "persistent kernel does not fit"); return bail(QWEN_ERR_STATE); }
+      c->engine = 0;
+    }
   }
   {
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) { fail(c, QWEN_ERR_CUDA, "create: %s", cudaGetErrorString(e)); return bail(QWEN_ERR_CUDA); }
   }
   *out = c;
+  return QWEN_OK;
+}
+
+// Every entry point that launches a step: a TP context must be connected.
+int check_tp(qwen_ctx* c) {
+  if (!c->tp_ready) return fail(c, QWEN_ERR_STATE, "tensor-parallel context not connected (qwen_tp_connect)");
+  return QWEN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qwen_create(const char* blob_path, const char* index_path, int n_gpus, const int* device_ids,
+                int max_ctx, int max_batch, qwen_ctx** out) {
+  if (n_gpus != 1)
+    return fail(nullptr, QWEN_ERR_ARG, "n_gpus must be 1 (tensor parallelism: qwen_create_tp, one context per GPU)");
+  return create_impl(blob_path, index_path, device_ids ? device_ids[0] : 0, 0, 1, max_ctx, max_batch, out);
+}
+
+int qwen_create_tp(const char* blob_path, const char* index_path, int device_id, int tp_rank, int tp_world,
+                   int max_ctx, int max_batch, qwen_ctx** out) {
+  return create_impl(blob_path, index_path, device_id, tp_rank, tp_world, max_ctx, max_batch, out);
+}
+
+int qwen_tp_plan(int tp_rank, int tp_world, int* out) {
+  if (!out) return fail(nullptr, QWEN_ERR_ARG, "out is null");
+  TpPlan t;
+  std::string err;
+  if (!tp_plan(tp_rank, tp_world, t, err)) return fail(nullptr, QWEN_ERR_ARG, "%s", err.c_str());
+  const int v[QWEN_TP_PLAN_INTS] = {t.dn_h0, t.dn_h1, t.kv_g0, t.kv_g1, t.ok0, t.ok1, t.dk0, t.dk1, t.t0 * 128,
+                                    t.t1 * 128};
+  memcpy(out, v, sizeof v);
+  return QWEN_OK;
+}
+
+int qwen_tp_export(qwen_ctx* c, void* handle_out) {
+  int rc;
+  if ((rc = check_ctx(c))) return rc;
+  if (!handle_out) return fail(c, QWEN_ERR_ARG, "handle_out is null");
+  if (c->tp.world == 1) return fail(c, QWEN_ERR_STATE, "not a tensor-parallel context");
+  static_assert(sizeof(cudaIpcMemHandle_t) == QWEN_TP_HANDLE_BYTES, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  QCUDA(c, cudaIpcGetMemHandle(&h, c->xbuf));
+  memcpy(handle_out, &h, sizeof h);
+  return QWEN_OK;
+}
+
+int qwen_tp_connect(qwen_ctx* c, const void* handles) {
+  int rc;
+  if ((rc = check_ctx(c))) return rc;
+  if (!handles) return fail(c, QWEN_ERR_ARG, "handles is null");
+  if (c->tp.world == 1) return fail(c, QWEN_ERR_STATE, "not a tensor-parallel context");
+  if (c->tp_ready) return fail(c, QWEN_ERR_STATE, "already connected");
+  const char* hb = static_cast<const char*>(handles);
+  for (int r = 0; r < c->tp.world; ++r) {
+    if (r == c->tp.rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, hb + (size_t)r * QWEN_TP_HANDLE_BYTES, sizeof h);
+    void* p = nullptr;
+    QCUDA(c, cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    c->ipc_open.push_back(p);
+    c->P.xbuf[r] = static_cast<unsigned long long*>(p);
+  }
+  c->tp_ready = true;
+  return QWEN_OK;
+}
+
+int qwen_tp_vocab_range(qwen_ctx* c, int* lo, int* hi) {
+  if (!c) return fail(nullptr, QWEN_ERR_ARG, "null context");
+  if (lo) *lo = c->tp.t0 * HEAD_TM;
+  if (hi) *hi = c->tp.t1 * HEAD_TM;
   return QWEN_OK;
 }
 
@@ -659,6 +761,9 @@ int qwen_reset(qwen_ctx* c, int seq) {
 int qwen_set_act_int8(qwen_ctx* c, int on) {
   int rc;
   if ((rc = check_ctx(c))) return rc;
+  // the golden W8A8 quantiser needs the max over a whole input vector, which a
+  // row-parallel rank does not hold
+  if (on && c->tp.world > 1) return fail(c, QWEN_ERR_STATE, "ACT_INT8 is not available with tensor parallelism");
   c->act_int8 = on ? 1 : 0;
   return QWEN_OK;
 }
@@ -667,6 +772,7 @@ int qwen_set_engine(qwen_ctx* c, int engine) {
   int rc;
   if ((rc = check_ctx(c))) return rc;
   if (engine != 0 && engine != 1) return fail(c, QWEN_ERR_ARG, "engine must be 0 or 1");
+  if (engine == 0 && c->tp.world > 1) return fail(c, QWEN_ERR_STATE, "engine 0 has no tensor parallelism");
   if (engine == 1 && persist_max_blocks_per_sm() < 1)
     return fail(c, QWEN_ERR_STATE, "persistent kernel does not fit on this device");
   c->engine = engine;
@@ -758,6 +864,7 @@ int qwen_decode_step(qwen_ctx* c, const int* tok, int batch, float* logits_out, 
   if (batch != 1) return fail(c, QWEN_ERR_ARG, "batch must be 1");
   if (!tok) return fail(c, QWEN_ERR_ARG, "tok is null");
   if (tok[0] < 0 || tok[0] >= VOCAB) return fail(c, QWEN_ERR_ARG, "token %d outside [0, %d)", tok[0], VOCAB);
+  if ((rc = check_tp(c))) return rc;
   if (c->T + 1 > c->max_ctx || c->pos + 1 >= c->max_rope)
     return fail(c, QWEN_ERR_STATE, "context full (T=%d, max_ctx=%d)", c->T, c->max_ctx);
   if ((rc = ensure_seq_room(c, 1))) return rc;
@@ -786,6 +893,7 @@ int qwen_generate(qwen_ctx* c, const int* prompt, int n_prompt, int n_new, int* 
   int rc;
   if ((rc = check_ctx(c))) return rc;
   if (!prompt || n_prompt < 1 || n_new < 0) return fail(c, QWEN_ERR_ARG, "need n_prompt >= 1, n_new >= 0");
+  if ((rc = check_tp(c))) return rc;
   if (n_new > 0 && !out_ids) return fail(c, QWEN_ERR_ARG, "out_ids is null");
   const int total = n_prompt + n_new;
   if (total > c->max_steps) return fail(c, QWEN_ERR_ARG, "n_prompt + n_new > %d", c->max_steps);

@@ -1,0 +1,139 @@
+"""Tensor-parallel decode on 2 (and 4, 8 where present) GPUs through the C ABI
+(qwen_create_tp / qwen_tp_export / qwen_tp_connect), one process per GPU.
+
+Bar: the same as one GPU -- greedy ids identical to the reference golden's,
+fp32 logits (the ranks' vocab slices gathered) within 1e-4 of the golden's
+relative to its max |logit| -- and every rank returns the same ids.
+
+The ranks are spawned processes (gloo on 127.0.0.1 carries the set-up
+handles and the logit slices); the per-token exchanges run inside the decode
+kernel over NVLink.  Skipped with fewer GPUs than ranks.
+"""
+
+import multiprocessing as mp
+import os
+import socket
+
+import pytest
+
+from golden_util import LOGIT_RTOL, fixture
+
+pytestmark = pytest.mark.gpu
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _gpus():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, blob_path, job, q):
+    import sys
+    sys.path.insert(0, REPO)
+    sys.path.insert(0, os.path.join(REPO, "tests"))
+    res = {"rank": rank}
+    try:
+        from datetime import timedelta
+
+        import numpy as np
+        import torch
+        import torch.distributed as dist
+
+        from golden_util import logits_close, fixture as fx_load
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                world_size=world, timeout=timedelta(seconds=120))
+        torch.cuda.set_device(rank)
+        from qwen_fpga_b200.tp import TPDecoder
+        d = TPDecoder(blob_path, device=rank, max_ctx=256)
+        fx = fx_load("config0.npz")
+        if job == "config0":
+            d.reset()
+            ids, sec = d.generate(fx["prompt"].tolist(), 64)
+            res["ids"] = ids
+            d.reset()
+            feed = fx["prompt"].tolist() + fx["generated"].tolist()
+            ams, errs = [], {}
+            for i, t in enumerate(feed):
+                want = i in (0, 15, 79)
+                am, lg = d.decode_step(t, want_logits=want)
+                ams.append(am)
+                if want:
+                    errs[i] = logits_close(lg, fx, f"step{i}")
+            res["argmax"] = ams
+            res["errs"] = errs
+        elif job == "stop":
+            # rank world-1 leaves between steps; the others' next step must fail
+            # within the device wait bound and report it
+            d.reset()
+            d.generate(fx["prompt"].tolist()[:4], 2)
+            dist.barrier()
+            if rank != world - 1:
+                from qwen_fpga_b200.api import QwenError
+                try:
+                    d.decode_step(int(fx["prompt"][4]), want_logits=False, sync=False)
+                    res["raised"] = None
+                except QwenError as e:
+                    res["raised"] = (e.code, str(e))
+            dist.barrier()
+        d.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent, which fails the test
+        import traceback
+        res["error"] = traceback.format_exc()
+    q.put(res)
+
+
+def _run(world, job, blob_path, timeout=900):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker, args=(r, world, port, blob_path, job, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    out = []
+    try:
+        for _ in range(world):
+            out.append(q.get(timeout=timeout))
+    finally:
+        for p in ps:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()   # this test's own child
+    out.sort(key=lambda r: r["rank"])
+    for r in out:
+        assert "error" not in r, r["error"]
+    return out
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_config0_matches_golden(world, blob_path):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    fx = fixture("config0.npz")
+    res = _run(world, "config0", blob_path)
+    for r in res:
+        assert r["ids"] == fx["generated"].tolist(), f"rank {r['rank']}"
+        assert r["argmax"] == [int(v) for v in fx["argmax"]], f"rank {r['rank']}"
+        assert max(r["errs"].values()) < LOGIT_RTOL, r["errs"]
+
+
+def test_tp_rank_that_stops_is_reported(blob_path):
+    """A rank that stops calling (between steps) makes the other rank's next
+    step end with QWEN_ERR_DEVICE after the device wait bound, not hang."""
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = _run(2, "stop", blob_path)
+    raised = res[0]["raised"]
+    assert raised is not None and raised[0] == 4, raised
+    assert "wait ran out" in raised[1]
