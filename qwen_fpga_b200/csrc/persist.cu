@@ -307,6 +307,12 @@ __host__ __device__ __forceinline__ unsigned kwin_of(int sub, unsigned kw_out, u
 __device__ __forceinline__ unsigned kwin(const PersistArgs& A, int sub) {
   return kwin_of(sub, (unsigned)A.ok0 | (unsigned)A.ok1 << 16, (unsigned)A.dk0 | (unsigned)A.dk1 << 16);
 }
+// The same in a kernel instance: TP = false compiles the whole-input windows in.
+template <bool TP>
+__device__ __forceinline__ unsigned kwin_t(const PersistArgs& A, int sub) {
+  if constexpr (TP) return kwin(A, sub);
+  else return kwin_of(sub, (unsigned)VDIM << 16, (unsigned)FFN << 16);
+}
 
 // Source and size of chunk k: one K-slice of a layer panel (slice n covers
 // K [k0 + 1024 n, min(k0 + 1024 (n + 1), k1)) of the phase's window), one
@@ -798,6 +804,7 @@ __device__ bool load_residual(PCtx& c, int p) {
 // ACT_INT8 (amax null; whole inputs only): their digit image for the whole
 // CTA as well (encode_lin); W8A32: max|x| folded into *amax instead, for
 // encode_fixed.  false on abort.
+template <bool TP>
 __device__ bool prologue(PCtx& c, int p, unsigned* amax, int& k0, int& k1) {
   float* xf = (float*)(c.sm + OFF_XF);
   const PersistArgs& A = *c.A;
@@ -813,7 +820,7 @@ __device__ bool prologue(PCtx& c, int p, unsigned* amax, int& k0, int& k1) {
   // element i = k0 + tid + 512 j, and k0 is a multiple of LV
   const float gw = gated ? __ldg(L.gnorm_w + (threadIdx.x % LV)) : 0.0f;
   const unsigned long long* src = sub == 4 ? A.tv_act : (L.linear ? A.tv_o : A.tv_attn);
-  const unsigned kw = kwin(A, sub);
+  const unsigned kw = kwin_t<TP>(A, sub);
   k0 = (int)(kw & 0xffffu);
   k1 = (int)(kw >> 16);
   if (!wait_tagged_max(c, src + k0, k1 - k0, tag_of(c, p - 1), xf + k0, gated ? nullptr : amax, false,
@@ -883,6 +890,7 @@ __device__ unsigned long long tp_argmax(PCtx& c, unsigned long long b) {
 
 // Block argmax of the head, then the last CTA reduces every block's maximum,
 // records the step's argmax and advances the step scalars for the next launch.
+template <bool TP>
 __device__ void head_finish(PCtx& c, unsigned long long best) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
@@ -909,7 +917,7 @@ __device__ void head_finish(PCtx& c, unsigned long long best) {
     consumer_sync();
     if (threadIdx.x == 0) {
       for (int w = 0; w < NCW; ++w) b = umax64(b, ms->wbest[w]);
-      if (A.tp_world > 1) b = tp_argmax(c, b);
+      if constexpr (TP) b = tp_argmax(c, b);
       const int step = ms->step;
       if (step < A.max_steps) A.ids[step] = am_index(b);
       else atomicCAS(A.err, 0, ERR_CTX);
@@ -1002,6 +1010,7 @@ __device__ int tile_mma(PCtx& c, int i0, int i1, unsigned tmem, int T0) {
 // slabs (possibly none: the argmax merge still needs every CTA).  Input: the
 // residual stream after the last layer, final-normed, encoded once into the B
 // tile.
+template <bool TP>
 __device__ bool phase_head(PCtx& c, int p, int i0, int i1) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
@@ -1064,7 +1073,7 @@ __device__ bool phase_head(PCtx& c, int p, int i0, int i1) {
   }
   if (!consumer_and(good)) return false;
   if (threadIdx.x == 0) { ms->ntile = T0 + ntiles; ms->hs_tag = 0; }
-  head_finish(c, best);
+  head_finish<TP>(c, best);
   return true;
 }
 
@@ -1164,7 +1173,7 @@ __host__ __device__ __forceinline__ int chunk_tasks(const Chunk& k, unsigned kw)
 struct TaskMap {
   int nq, tb, pv, start, pan, ntask, npan;
 };
-__device__ __forceinline__ TaskMap task_map(const PCtx& c, int sub, int i0, int nj) {
+__device__ __forceinline__ TaskMap task_map(const PCtx& c, unsigned kw, int i0, int nj) {
   const int lane = threadIdx.x & 31;
   TaskMap m;
   m.nq = 0;
@@ -1172,7 +1181,7 @@ __device__ __forceinline__ TaskMap task_map(const PCtx& c, int sub, int i0, int 
   m.pan = 0;
   if (lane < nj) {
     const Chunk k = c.ch[i0 + lane];
-    m.nq = chunk_tasks(k, kwin(*c.A, sub));
+    m.nq = chunk_tasks(k, kw);
     if (k.seg & CHUNK_PANEL) {
       m.pan = 1;
       m.start = 1;
@@ -1221,34 +1230,29 @@ __device__ __forceinline__ const float* row_scale(const LayerW& L, int sub, int 
 
 // Row-parallel OUT / DOWN under tensor parallelism: the residual rows of this
 // CTA's panels once every rank's partial of them is in this rank's exchange
-// buffer, h = r + ((y_0 + y_1) + ...) in rank order (bit-identical on every
-// rank), written as tagged words.  Per warp (the panels it finished), bounded
-// wait; false on abort.
-__device__ bool tp_reduce_rows(PCtx& c, int sub, int i0, const TaskMap& m, bool own, int pr, unsigned tag) {
-  const PersistArgs& A = *c.A;
-  const float* hs = (const float*)(c.sm + OFF_HS);
+// buffer xb ([TP_MAX][HID] of the phase kind), h = r + ((y_0 + y_1) + ...) in
+// rank order (bit-identical on every rank), written as tagged words to tv_h.
+// Per warp: its panels are rows[v] (lane = row pr, own lanes), v = wid, wid +
+// NCW, ... < npan.  Bounded wait; false on abort.  Not inlined, plain
+// arguments: only tensor-parallel runs execute it.
+__device__ __noinline__ bool tp_reduce_rows(const unsigned long long* xb, unsigned long long* tv_h, const float* hs,
+                                            const int* rows, int npan, int P, bool own, int pr, unsigned tag,
+                                            Misc* ms, int* err, int* abort_flag, int sub) {
   const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const unsigned long long* xb = A.xbuf[A.tp_rank] + XB_PART + (size_t)(sub == 4) * TP_MAX * HID;
-  const int P = A.tp_world;
   int good = 1;
-  for (int v = wid; v < m.npan && good; v += NCW) {
-    const int r = (int)c.ch[i0 + panel_chunk(m, v)].row0 * PANEL + pr;
+  for (int v = wid; v < npan && good; v += NCW) {
+    const int r = rows[v] * PANEL + pr;
     const unsigned long long t0 = gtime();
     int it = 0;
     float sum = 0.0f;
     bool done = !own;
     for (;;) {
       if (!done) {
-        unsigned long long w[TP_MAX];
         bool all = true;
-#pragma unroll
-        for (int rr = 0; rr < TP_MAX; ++rr)
-          if (rr < P) { w[rr] = ld_tv_sys(xb + (size_t)rr * HID + r); all = all && tag_ok(w[rr], tag); }
+        for (int rr = 0; rr < P && all; ++rr) all = tag_ok(ld_tv_sys(xb + (size_t)rr * HID + r), tag);
         if (all) {
-          sum = tv_val(w[0]);
-#pragma unroll
-          for (int rr = 1; rr < TP_MAX; ++rr)
-            if (rr < P) sum = __fadd_rn(sum, tv_val(w[rr]));
+          sum = tv_val(ld_tv_sys(xb + r));
+          for (int rr = 1; rr < P; ++rr) sum = __fadd_rn(sum, tv_val(ld_tv_sys(xb + (size_t)rr * HID + r)));
           done = true;
         }
       }
@@ -1256,13 +1260,17 @@ __device__ bool tp_reduce_rows(PCtx& c, int sub, int i0, const TaskMap& m, bool 
       if (((++it) & 63) == 0) {
         int bad = 0;
         if (lane == 0) {
-          if (aborted(c)) bad = 1;
-          else if (gtime() - t0 > WAIT_NS) { raise_abort(c, 23, sub); bad = 1; }
+          if (*(volatile int*)&ms->abort || ld_flag(abort_flag)) {
+            bad = 1;
+          } else if (gtime() - t0 > WAIT_NS) {
+            record_error(err, abort_flag, ms, ERR_WAIT, 23, sub);
+            bad = 1;
+          }
         }
         if (__shfl_sync(0xffffffffu, bad, 0)) { good = 0; break; }
       }
     }
-    if (good && own) st_tv(A.tv_h + r, __fadd_rn(hs[r], sum), tag);
+    if (good && own) st_tv(tv_h + r, __fadd_rn(hs[r], sum), tag);
   }
   return good != 0;
 }
@@ -1283,6 +1291,7 @@ __device__ bool tp_reduce_rows(PCtx& c, int sub, int i0, const TaskMap& m, bool 
 // (GATEUP, golden/model.py:236), or h + y (OUT, DOWN); the fp32 in_proj_b /
 // in_proj_a rows of a DeltaNet IN (golden/model.py:146-147) are dotted with x
 // by their tasks.
+template <bool TP>
 __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
@@ -1301,7 +1310,7 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
     if (threadIdx.x == 0) check_fail(c, 8, nj);
     good = 0;
   }
-  const TaskMap m = task_map(c, sub, i0, good ? nj : 0);
+  const TaskMap m = task_map(c, kwin_t<TP>(A, sub), i0, good ? nj : 0);
   // W8A32 normed inputs: warp 0 computes 1/rms, so tasks start at warp 1
   const int off = (normed && !i8) ? 1 : 0;
   const int t_first = (wid + NCW - off) % NCW;
@@ -1387,7 +1396,7 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
       trace_warp(c, p, 8);
     }
   } else {
-    if (!prologue(c, p, amax, k0, k1)) return false;
+    if (!prologue<TP>(c, p, amax, k0, k1)) return false;
     trace_mark(c, p, 1);
     if (!i8) xs = encode_fixed(c.sm, xf, k0, k1, *amax, false, g2);
   }
@@ -1439,7 +1448,8 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
     }
     const int kb = k0 + (int)k.nrows * PANEL_KB + TASK_KB * q;   // the task's first K position
     const unsigned sa = smem_u32(slot) + 512u * (TASK_KB / 32) * q;
-    const int kl = k1 - kb < TASK_KB ? k1 - kb : TASK_KB;         // a multiple of 128
+    // task length: a multiple of 128; whole inputs (every K a multiple of TASK_KB) always TASK_KB
+    const int kl = !TP ? TASK_KB : (k1 - kb < TASK_KB ? k1 - kb : TASK_KB);
     int d3[3];
     panel_mma(sa, fr, kb >> 5, kl >> 5, nd, d3);
     const int vp = chunk_panel(m, j);
@@ -1491,7 +1501,7 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
           else { out = A.tv_kvn + KVPROJ; o = r - QPROJ - KVPROJ; }
         }
         st_tv(out + o, y, tag);
-      } else if (A.tp_world == 1) {
+      } else if constexpr (!TP) {
         st_tv(A.tv_h + r, __fadd_rn(hs[r], y), tag);
       } else {
         // row-parallel: this rank's partial row into every rank's exchange buffer
@@ -1500,7 +1510,18 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
       }
     }
   }
-  if ((sub == 2 || sub == 4) && A.tp_world > 1 && !tp_reduce_rows(c, sub, i0, m, own, pr, tag)) return false;
+  if (TP && (sub == 2 || sub == 4)) {
+    // this warp's panels (in the fp32 row-dot scratch, which OUT and DOWN do not use)
+    int* rows = (int*)(c.sm + OFF_PARTF);
+    for (int v = wid; v < m.npan; v += NCW) {
+      const int q = (int)c.ch[i0 + panel_chunk(m, v)].row0;
+      if (lane == 0) rows[v] = q;
+    }
+    __syncwarp();
+    if (!tp_reduce_rows(A.xbuf[A.tp_rank] + XB_PART + (size_t)(sub == 4) * TP_MAX * HID, A.tv_h, hs, rows,
+                        m.npan, A.tp_world, own, pr, tag, ms, A.err, A.abort_flag, sub))
+      return false;
+  }
   // the fp32 rows (W8A32: times 1/rms)
   for (int t = wid; t < m.ntask; t += NCW) {
     int q;
@@ -1890,6 +1911,9 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
 
 // ---------------------------------------------------------------- the kernel
 
+// TP: the tensor-parallel instance (launched when tp_world > 1); the other
+// instance compiles every exchange out.
+template <bool TP>
 __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = smem_raw;
@@ -1975,16 +1999,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
         const LayerW& L = c.lay[p / 5];
         if (L.linear) {
           // this rank's heads [dn_h0, dn_h1): one CTA per (head, value slice)
-          if ((int)blockIdx.x < (A.dn_h1 - A.dn_h0) * NDSLICE) ok = delta_item(c, p, A.dn_h0 * NDSLICE + blockIdx.x);
+          const int h0 = TP ? A.dn_h0 : 0, nh = TP ? A.dn_h1 - A.dn_h0 : LH;
+          if ((int)blockIdx.x < nh * NDSLICE) ok = delta_item(c, p, h0 * NDSLICE + blockIdx.x);
         } else {
           const int Tn = ms->T + 1;
           int nch = (Tn + ATT_MINLEN - 1) / ATT_MINLEN;
           nch = nch < 1 ? 1 : (nch > ATT_MAXCH ? ATT_MAXCH : nch);
           const int cl = (Tn + nch - 1) / nch;
           if (cl > ATT_MAXLEN) { if (threadIdx.x == 0) raise_abort(c, 21, p); ok = false; break; }
-          const int ng = A.kv_g1 - A.kv_g0;   // this rank's KV groups
+          const int g0 = TP ? A.kv_g0 : 0, ng = TP ? A.kv_g1 - A.kv_g0 : NKV;   // this rank's KV groups
           for (int it = blockIdx.x; it < ng * nch && ok; it += gridDim.x)
-            ok = attn_item(c, p, A.kv_g0 + it % ng, it / ng, nch, cl);
+            ok = attn_item(c, p, g0 + it % ng, it / ng, nch, cl);
         }
         trace_mark(c, p, 3);
         continue;
@@ -1992,12 +2017,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
       // this phase's chunks, [i0, i1) of the CTA's list (counted loops only)
       const int i0 = ms->pf[p], i1 = ms->pf[p + 1];
       if (p == PH_HEAD) {
-        ok = phase_head(c, p, i0, i1);           // every CTA joins the argmax merge
+        ok = phase_head<TP>(c, p, i0, i1);       // every CTA joins the argmax merge
       } else if (i0 == i1) {                     // no rows of this phase on this CTA
         trace_mark(c, p, 3);
         continue;
       } else {
-        ok = phase_panels(c, p, i0, i1);
+        ok = phase_panels<TP>(c, p, i0, i1);
       }
       // the warps leave a GEMV phase independently; line them up again (and
       // make a failure in any warp the whole CTA's)
@@ -2147,12 +2172,12 @@ bool build_schedule(const ModelW& M, int G, const TpPlan& tp, std::vector<Chunk>
         for (int blk = 0; blk < 4; ++blk)
           for (int h = tp.dn_h0; h < tp.dn_h1; ++h)
             for (int j = 0; j < LK / PANEL; ++j) pans.push_back(blk * (KDIM / PANEL) + h * (LK / PANEL) + j);
-      } else {        // the KV groups' query heads ([q | gate] rows), k and v rows
-        for (int g = tp.kv_g0; g < tp.kv_g1; ++g) {
+      } else {        // the KV groups' query heads ([q | gate] rows), then their k rows, then v rows
+        for (int g = tp.kv_g0; g < tp.kv_g1; ++g)
           for (int j = 0; j < QPROJ / NKV / PANEL; ++j) pans.push_back(g * (QPROJ / NKV / PANEL) + j);
-          for (int kv = 0; kv < 2; ++kv)
+        for (int kv = 0; kv < 2; ++kv)
+          for (int g = tp.kv_g0; g < tp.kv_g1; ++g)
             for (int j = 0; j < HD / PANEL; ++j) pans.push_back((QPROJ + kv * KVPROJ + g * HD) / PANEL + j);
-        }
       }
     } else if (sub == 3) {
       for (int q = tp.dk0 / PAIR_ROWS; q < tp.dk1 / PAIR_ROWS; ++q) pans.push_back(q);
@@ -2268,21 +2293,26 @@ cudaError_t repack_panels(const int8_t* const* rowptr, int8_t* out, int nrows, i
 cudaError_t launch_persistent(const PersistArgs& args, int G, cudaStream_t st) {
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_decode_persistent,
+    cudaError_t e = cudaFuncSetAttribute(k_decode_persistent<false>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(k_decode_persistent<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
   void* kargs[] = {(void*)&args};
-  return cudaLaunchCooperativeKernel((const void*)k_decode_persistent, dim3(G), dim3(NTHREADS), kargs,
-                                     SMEM_BYTES, st);
+  const void* fn = args.tp_world > 1 ? (const void*)k_decode_persistent<true> : (const void*)k_decode_persistent<false>;
+  return cudaLaunchCooperativeKernel(fn, dim3(G), dim3(NTHREADS), kargs, SMEM_BYTES, st);
 }
 
+// Resident CTAs per SM of the persistent kernel (the smaller of its two instances).
 int persist_max_blocks_per_sm() {
-  int n = 0;
-  cudaFuncSetAttribute(k_decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_decode_persistent, NTHREADS, SMEM_BYTES);
-  return n;
+  int n0 = 0, n1 = 0;
+  cudaFuncSetAttribute(k_decode_persistent<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  cudaFuncSetAttribute(k_decode_persistent<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n0, k_decode_persistent<false>, NTHREADS, SMEM_BYTES);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n1, k_decode_persistent<true>, NTHREADS, SMEM_BYTES);
+  return n0 < n1 ? n0 : n1;
 }
 
 }  // namespace qb
