@@ -73,6 +73,19 @@ int qwen_tp_connect(qwen_ctx* ctx, const void* handles);
 int qwen_tp_vocab_range(qwen_ctx* ctx, int* lo, int* hi);
 int qwen_tp_plan(int tp_rank, int tp_world, int* out);
 
+/* Pack a Hugging Face safetensors snapshot of the Qwen3.5 text decoder into
+ * the blob qwen_create loads (replaces scripts/pack_weights.py:50-101 with its
+ * loader golden/loader.py:36-78 and quantiser golden/quant.py:43-49).  Reads
+ * snapshot_dir/config.json (text_config) and every *.safetensors file in
+ * snapshot_dir (BF16, F16, F32, I32 or I64; "model.language_model." prefixes
+ * dropped, vision and MTP tensors skipped); writes out_blob (tensors in
+ * decode read order, 4 KiB aligned, int8 rows + fp32 row scales for the GEMV
+ * weights, fp32 otherwise) and, beside it, <stem>.manifest.json and
+ * <stem>.idx.  Host only, no GPU.  QWEN_ERR_IO (message in
+ * qwen_last_error(NULL)) when a tensor is missing or extra for the config's
+ * layer_types, or a file cannot be read or written. */
+int qwen_pack_blob(const char* snapshot_dir, const char* out_blob);
+
 /* Free every device and host resource of the context. */
 int qwen_destroy(qwen_ctx* ctx);
 

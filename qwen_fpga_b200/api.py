@@ -70,6 +70,7 @@ def load() -> C.CDLL:
     L.qwen_tp_connect.argtypes = [_vp, _vp]
     L.qwen_tp_vocab_range.argtypes = [_vp, _ip, _ip]
     L.qwen_tp_plan.argtypes = [C.c_int, C.c_int, _ip]
+    L.qwen_pack_blob.argtypes = [C.c_char_p, C.c_char_p]
     L.qwen_destroy.argtypes = [_vp]
     L.qwen_reset.argtypes = [_vp, C.c_int]
     L.qwen_state_import.argtypes = [_vp, C.c_int, _fp, _fp, _fp, _fp, C.c_int, C.c_int]
@@ -100,6 +101,14 @@ def _fptr(a):
 
 
 TP_HANDLE_BYTES = 64
+
+
+def pack_blob(snapshot_dir: str, out_blob: str) -> str:
+    """Pack a safetensors snapshot of the Qwen3.5 text decoder into the blob
+    Decoder loads (scripts/pack_weights.py's layout, in C++; host only).
+    Writes out_blob, <stem>.manifest.json and <stem>.idx; returns the index path."""
+    _check(load().qwen_pack_blob(snapshot_dir.encode(), out_blob.encode()))
+    return os.path.splitext(out_blob)[0] + ".idx"
 
 
 def tp_plan(rank: int, world: int) -> dict:

@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libqwenb200.so")
 SOURCES = ["csrc/runtime.cu", "csrc/decode.cu", "csrc/gemv.cu", "csrc/persist.cu", "csrc/persist_tp.cu",
-           "csrc/noalloc.cu"]
+           "csrc/noalloc.cu", "csrc/pack.cpp"]
 HEADERS = ["csrc/common.cuh", "csrc/decode.cuh", "csrc/gemv.cuh", "csrc/persist.cuh", "csrc/noalloc.cuh",
            "../include/qwen_b200.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

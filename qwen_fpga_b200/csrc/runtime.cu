@@ -29,6 +29,15 @@ namespace {
 
 thread_local std::string g_last_error;
 
+}  // namespace
+
+namespace qb {
+// For the library's host-only entry points in other files (pack.cpp).
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace qb
+
+namespace {
+
 struct TensorEnt {
   uint64_t off = 0, nbytes = 0, soff = 0, snbytes = 0;
   int dtype = 0;  // 1 int8, 0 fp32
