@@ -81,15 +81,28 @@ class ClockSampler:
                "-lms", "200"]
         if self.gpu_id is not None:
             cmd += ["-i", str(self.gpu_id)]
+        self.cmd = cmd
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(cmd, stdout=self.fh, stderr=subprocess.DEVNULL)
+            # the timed region starts once the sampler is producing rows
+            t0 = time.time()
+            while os.path.getsize(self.path) == 0 and time.time() - t0 < 3.0:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
 
     def __exit__(self, *a):
         if self.proc is not None:
+            # one more sample at the end of the region (a short region may fall
+            # between the 200 ms ticks)
+            try:
+                one = [c for c in self.cmd if c not in ("-lms", "200")]
+                self.fh.flush()
+                subprocess.run(one, stdout=self.fh, stderr=subprocess.DEVNULL, timeout=10)
+            except Exception:
+                pass
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -446,7 +459,8 @@ def main():
                      "frac": achieved / peak, "peak_source": peak_src,
                      "algorithmic_bytes_per_step": bstep,
                      "state_bytes_per_step": STATE_RW,
-                     "traffic": traffic.get("bytes_per_step") if traffic else None},
+                     # the ncu capture is of the single-GPU kernel
+                     "traffic": traffic.get("bytes_per_step") if traffic and not tp else None},
         "clocks": clocks,
     }
     if world == 1 and not args.no_cpu:
