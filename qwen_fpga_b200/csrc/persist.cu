@@ -803,14 +803,17 @@ __device__ bool prologue(PCtx& c, int p, unsigned* amax, int& k0, int& k1) {
   const unsigned kw = kwin_t<TP>(A, sub);
   k0 = (int)(kw & 0xffffu);
   k1 = (int)(kw >> 16);
+  // silu(z) of the gated norm, parked in the digit region: IN(l) wrote it
+  // before the delta rule ran, so it is read before waiting for o, off the
+  // critical path
+  float* zb = (float*)(c.sm + OFF_DIG);
+  if (gated && !wait_tagged(c, A.tv_z + k0, k1 - k0, tag_of(c, p - 2), zb + k0)) return false;
   if (!wait_tagged_max(c, src + k0, k1 - k0, tag_of(c, p - 1), xf + k0, gated ? nullptr : amax, false,
                        make_float2(0.0f, 0.0f)))
     return false;
   if (gated) {
     // gated RMSNorm of the delta-rule output (golden/model.py:183-189) over the
-    // window's heads, z from IN(l) parked in the digit region
-    float* zb = (float*)(c.sm + OFF_DIG);
-    if (!wait_tagged(c, A.tv_z + k0, k1 - k0, tag_of(c, p - 2), zb + k0)) return false;
+    // window's heads
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     for (int h = k0 / LV + wid; h < k1 / LV; h += NCW) {
       float ss = 0.0f;
@@ -823,7 +826,7 @@ __device__ bool prologue(PCtx& c, int p, unsigned* amax, int& k0, int& k1) {
     float vmax = 0.0f;
     for (int i = k0 + threadIdx.x; i < k1; i += PT) {
       const float v = __fmul_rn(__fmul_rn(xf[i], ms->inv_h[i / LV]), gw);
-      xf[i] = __fmul_rn(v, silu_f(zb[i]));
+      xf[i] = __fmul_rn(v, zb[i]);
       vmax = fmaxf(vmax, fabsf(xf[i]));
     }
     if (amax) {
@@ -1474,7 +1477,7 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
         int o;
         if (L.linear) {
           if (r < CONVD) { out = A.tv_qkv; o = r; }
-          else { out = A.tv_z; o = r - CONVD; }
+          else { out = A.tv_z; o = r - CONVD; y = silu_f(y); }   // the gated norm of OUT takes silu(z)
         } else {
           if (r < QPROJ) { out = A.tv_qg; o = r; }
           else if (r < QPROJ + KVPROJ) { out = A.tv_kvn; o = r - QPROJ; }
