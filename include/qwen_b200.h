@@ -56,7 +56,9 @@ int qwen_create(const char* blob_path, const char* index_path, int n_gpus,
  * and passes the array to qwen_tp_connect.  Every rank then makes the same
  * decode calls in the same order (like collectives); a rank that stops makes
  * the others' next step fail after the 2 s device wait bound with
- * QWEN_ERR_DEVICE.  ACT_INT8 and engine 0 are not available under TP.
+ * QWEN_ERR_DEVICE.  Under ACT_INT8 the ranks also exchange the maxima of the
+ * row-parallel inputs, so each is quantised with the max over the whole
+ * vector as on one GPU.  Engine 0 is not available under TP.
  * Logits: each rank fills only its vocab slice [lo, hi) of logits_out
  * (qwen_tp_vocab_range).  State import/export move the full arrays; a rank
  * uses and updates only its heads' parts.

@@ -756,6 +756,70 @@ __device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2
   sx_out = r.y;
 }
 
+// W8A8 under tensor parallelism: the golden per-vector quantiser
+// (golden/model.py:37-45) of the OUT / DOWN input, of which this rank holds the
+// window [k0, k1) in xf.  The window's max|x| goes to every rank's exchange
+// buffer; the max over all ranks' gives s_x = max / 127 as on one GPU, and the
+// window is quantised with it into digit plane 0 (x itself fake-quantised in
+// xf).  Collective; bounded wait; false on abort.
+__device__ bool tp_encode_i8(PCtx& c, int p, int k0, int k1) {
+  const PersistArgs& A = *c.A;
+  Misc* ms = c.ms;
+  float* xf = (float*)(c.sm + OFF_XF);
+  int8_t* dg = (int8_t*)(c.sm + OFF_DIG);
+  float m = 0.0f;
+  for (int i = k0 + threadIdx.x; i < k1; i += PT) m = fmaxf(m, fabsf(xf[i]));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) ms->red[threadIdx.x >> 5] = m;
+  consumer_sync();
+  int bad = 0;
+  if (threadIdx.x == 0) {
+    float lm = 0.0f;
+    for (int w = 0; w < NCW; ++w) lm = fmaxf(lm, ms->red[w]);
+    const unsigned tag = tag_of(c, p);
+    const size_t slot = XB_AMAX + (size_t)(p % 5 == 4) * TP_MAX;
+    for (int rr = 0; rr < A.tp_world; ++rr) st_tv_sys(A.xbuf[rr] + slot + A.tp_rank, lm, tag);
+    const unsigned long long* xb = A.xbuf[A.tp_rank] + slot;
+    const unsigned long long t0 = gtime();
+    int it = 0;
+    for (;;) {
+      float g = 0.0f;
+      bool all = true;
+      for (int rr = 0; rr < A.tp_world && all; ++rr) {
+        const unsigned long long w = ld_tv_sys(xb + rr);
+        all = tag_ok(w, tag);
+        g = fmaxf(g, tv_val(w));
+      }
+      if (all) { ms->red[NCW] = g; break; }
+      if (((++it) & 63) == 0) {
+        if (aborted(c)) { bad = 1; break; }
+        if (gtime() - t0 > WAIT_NS) { raise_abort(c, 25, p); bad = 1; break; }
+      }
+    }
+  }
+  if (!consumer_and(!bad)) return false;
+  const float amax = ms->red[NCW];
+  const float s = amax > 0.0f ? __fdiv_rn(amax, 127.0f) : 1.0f;
+  for (int i4 = (k0 >> 2) + threadIdx.x; i4 < (k1 >> 2); i4 += PT) {
+    unsigned w0 = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = 4 * i4 + e;
+      int qi = 0;
+      if (amax > 0.0f) {
+        const float q = fminf(fmaxf(rintf(__fdiv_rn(xf[i], s)), -127.0f), 127.0f);
+        xf[i] = __fmul_rn(q, s);
+        qi = (int)q;
+      }
+      w0 |= ((unsigned)qi & 0xffu) << (8 * e);
+    }
+    *reinterpret_cast<unsigned*>(dg + dig_off(0, 4 * i4)) = w0;
+  }
+  if (threadIdx.x == 0) { ms->scale = (double)s; ms->ndig = 1; }
+  consumer_sync();
+  return true;
+}
+
 // The residual stream that an OUT or DOWN phase adds its projection to
 // (golden/model.py:259,263): h after the previous residual add (tagged), or for
 // layer 0's OUT the dequantised embedding row (golden/model.py:246).  Into hs,
@@ -836,7 +900,10 @@ __device__ bool prologue(PCtx& c, int p, unsigned* amax, int& k0, int& k1) {
     }
     consumer_sync();
   }
-  if (!amax) encode_lin(c, k1, i8);
+  if (!amax) {
+    if constexpr (TP) { if (!tp_encode_i8(c, p, k0, k1)) return false; }
+    else encode_lin(c, k1, i8);
+  }
   return true;
 }
 

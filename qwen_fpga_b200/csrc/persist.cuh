@@ -62,7 +62,8 @@ cudaError_t repack_head_tiles(const int8_t* emb_q, int8_t* tiles, cudaStream_t s
 //   head tiles [t0, t1) (vocab slice).
 // An OUT or DOWN phase adds its partial rows across ranks (P2P stores into
 // every rank's exchange buffer, then a fixed-order sum: bit-identical on all
-// ranks); the head exchanges each rank's (max, index).
+// ranks); the head exchanges each rank's (max, index); under W8A8 the OUT and
+// DOWN inputs' maxima are exchanged before they are quantised.
 constexpr int TP_MAX = 8;
 struct TpPlan {
   int rank = 0, world = 1;
@@ -75,10 +76,13 @@ struct TpPlan {
 // The shard of `rank` among `world` (1, 2, 4 or 8); false (with err) otherwise.
 bool tp_plan(int rank, int world, TpPlan& out, std::string& err);
 // Exchange buffer of one rank (tagged words): [2 (OUT, DOWN)][TP_MAX source
-// ranks][HID] partial rows, then [TP_MAX source ranks][2] head (max, index) words.
+// ranks][HID] partial rows, then [TP_MAX source ranks][2] head (max, index)
+// words, then [2 (OUT, DOWN)][TP_MAX source ranks] input maxima (W8A8: the
+// golden quantiser's max over the whole input vector).
 constexpr size_t XB_PART = 0;
 constexpr size_t XB_HEAD = 2 * (size_t)TP_MAX * HID;
-constexpr size_t XB_WORDS = XB_HEAD + 2 * TP_MAX;
+constexpr size_t XB_AMAX = XB_HEAD + 2 * TP_MAX;
+constexpr size_t XB_WORDS = XB_AMAX + 2 * TP_MAX;
 
 // Everything the persistent kernel reads; tv_* are tagged {value, tag} words.
 struct PersistArgs {

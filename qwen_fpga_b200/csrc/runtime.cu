@@ -770,9 +770,6 @@ int qwen_reset(qwen_ctx* c, int seq) {
 int qwen_set_act_int8(qwen_ctx* c, int on) {
   int rc;
   if ((rc = check_ctx(c))) return rc;
-  // the golden W8A8 quantiser needs the max over a whole input vector, which a
-  // row-parallel rank does not hold
-  if (on && c->tp.world > 1) return fail(c, QWEN_ERR_STATE, "ACT_INT8 is not available with tensor parallelism");
   c->act_int8 = on ? 1 : 0;
   return QWEN_OK;
 }

@@ -71,6 +71,21 @@ def _worker(rank, world, port, blob_path, job, q):
                     errs[i] = logits_close(lg, fx, f"step{i}")
             res["argmax"] = ams
             res["errs"] = errs
+        elif job == "w8a8":
+            # ACT_INT8 teacher-forced on the golden's token stream (the bar of
+            # the one-GPU test: agreement within the golden's own spread)
+            fw = fx_load("config0_w8a8.npz")
+            d.reset()
+            d.dec.set_act_int8(True)
+            feed = fw["prompt"].tolist() + fw["generated"].tolist()
+            agree, errs = 0, {}
+            for i, t in enumerate(feed):
+                am, lg = d.decode_step(t, want_logits=(i == 0))
+                agree += int(am == int(fw["argmax"][i]))
+                if i == 0:
+                    errs[0] = logits_close(lg, fw, "step0")
+            res["agree"], res["errs"] = agree, errs
+            res["floor"] = int(fw["self_agreement"].min()) - 2
         elif job == "stop":
             # rank world-1 leaves between steps; the others' next step must fail
             # within the device wait bound and report it
@@ -126,6 +141,20 @@ def test_tp_config0_matches_golden(world, blob_path):
         assert r["ids"] == fx["generated"].tolist(), f"rank {r['rank']}"
         assert r["argmax"] == [int(v) for v in fx["argmax"]], f"rank {r['rank']}"
         assert max(r["errs"].values()) < LOGIT_RTOL, r["errs"]
+
+
+def test_tp_w8a8_teacher_forced_matches_golden(blob_path):
+    """W8A8 (ACT_INT8) on 2 ranks: the row-parallel inputs are quantised with
+    the max exchanged across ranks, so the bar is the one-GPU test's: argmax
+    agreement within the golden's own perturbation spread, step-0 logits
+    within 0.1, and both ranks identical."""
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = _run(2, "w8a8", blob_path)
+    assert res[0]["agree"] == res[1]["agree"]
+    for r in res:
+        assert r["agree"] >= r["floor"], r
+        assert r["errs"][0] < 0.1, r
 
 
 def test_tp_rank_that_stops_is_reported(blob_path):
