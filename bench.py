@@ -3,13 +3,19 @@
 
     python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference]
 
-Workload (config 0 of the build): random-init Qwen3.5-0.8B (seed 1234), a
-16-token prompt (default_rng(0)) prefilled one token at a time (untimed), then
-64 greedy decode steps (timed), repeated as "episodes" until K decode steps
-have been timed.  A step is one decode_step: embed, 24 layers, tied head,
-argmax.  Algorithmic bytes of a step attending T positions:
+Headline workload (config 0 of the build): random-init Qwen3.5-0.8B (seed
+1234), a 16-token prompt (default_rng(0)) prefilled one token at a time
+(untimed), then greedy decode steps (timed) in episodes of at most 64, until
+exactly K decode steps have been timed.  A step is one decode_step: embed, 24
+layers, tied head, argmax.  Algorithmic bytes of a step attending T positions:
 B(T) = 758,248,704 + 24,576 * T (int8 weights + row scales + fp32 small
 tensors, plus fp32 K/V reads of the 6 attention layers).
+
+The same JSON line carries the other configs as sub-objects (each a stated
+sample of its workload): "gemv" (config 1: every int8 GEMV microbench shape,
+GB/s against the HBM peak, int32 accumulators checked exactly), "config2"
+(W8A8 warm start, 4096 cached positions, 256 greedy steps) and "config3"
+(W8A32, 32768 cached positions, 512 greedy steps).
 
 Under torchrun (N > 1) the N ranks decode ONE sequence with tensor
 parallelism (qwen_fpga_b200.tp: heads, FFN columns and the vocab split across
@@ -18,10 +24,13 @@ decode kernel over NVLink); the throughput is that sequence's tokens/s
 (strong scaling).  --replicas instead runs N independent sequences, one per
 GPU, and sums their throughput (weak scaling).
 
---impl reference times the reference's own CPU decoder (the HLS C++ qwen_top
-compiled from the reference sources into oracle/_ref, single thread) on a
-bounded sample of the same workload; without that build it times the oracle
-port (numpy restatement of golden/model.py) instead.
+--impl reference times the reference's CPU decode path on the host cores, on
+a bounded sample of the same workload: the numpy decode step of
+golden/model.py (through its restatement oracle/golden_port.py, pinned to the
+golden's own outputs; the reference's Python cannot travel to the GPU box)
+with every BLAS thread, and beside it the reference's HLS C++ decoder
+(qwen_top, compiled from the reference sources into oracle/_ref), which is
+single-threaded by construction.
 """
 
 from __future__ import annotations
@@ -198,23 +207,26 @@ def run_profile(args):
 
 
 def run_reference(args, rank):
+    """The reference arm: rank 0 alone times the reference's CPU decode path on a
+    bounded sample of config 0 (see the module docstring); other ranks exit."""
     if rank != 0:
         return 0
     from qwen_fpga_b200 import synth
     blob_path = synth.ensure_blob(1234)
     from oracle import native
     n = max(1, min(args.steps, 32))
+    cb = cpu_baseline_port(blob_path, n)
+    hls = None
     if native.have_ref():
-        cb = cpu_reference_hls(blob_path, n)
-    else:
-        cb = cpu_baseline_port(blob_path, n)
+        hls = cpu_reference_hls(blob_path, max(1, min(args.steps, 16)))
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT,
             "n_gpus": args.gpus, "steps": n, "warmup": 0, "ms_per_step": 1e3 / cb["value"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32 (int8 weights dequantised on the fly)", "data": "synthetic",
-            "config": {"workload": "config0 (random-init Qwen3.5-0.8B, 16-token prompt, greedy)",
-                       "batch": 1},
+            "dtype": "f32 (int8 weights dequantised, golden fake-quant)", "data": "synthetic",
+            "config": {"workload": "config0 (random-init Qwen3.5-0.8B, 16-token prompt prefill "
+                                   "untimed, greedy decode steps timed)", "batch": 1},
             "cpu_baseline": cb,
+            "hls_reference": hls,
             "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -225,21 +237,20 @@ GEMV_SHAPES = [(6144, 1024), (2048, 1024), (7168, 1024), (1024, 3584), (1024, 20
                (248320, 1024)]
 
 
-def run_gemv(args):
+def gemv_rows(warmup=3, only_n=0):
     """Config 1 (GEMV microbench): qwen_gemv_i8_i8 on every shape, W int8
     rng.integers(-127, 128), scales U[1e-3, 1e-2], x int8 U[-127, 127] with s_x
     U[1e-3, 1e-2], seed 0 per shape.  Bytes per call = N*K + 4N + K + 4 + 4N
     (+ 4N for the int32 accumulators also written).  Each timed call reads a
     different copy of the weights, enough copies that a pass reads more than
     L2, so the weights come from HBM.  The int32 accumulators of one call per
-    shape are checked against numpy exactly.  One JSON line."""
+    shape are checked against numpy exactly."""
     import torch
     from qwen_fpga_b200 import api
-    torch.cuda.set_device(0)
-    peak, src = peaks()
+    peak, _ = peaks()
     rows = []
     for N, K in GEMV_SHAPES:
-        if args.gemv_n and N != args.gemv_n:
+        if only_n and N != only_n:
             continue
         rng = np.random.default_rng(0)
         w = rng.integers(-127, 128, (N, K), dtype=np.int8)
@@ -260,7 +271,7 @@ def run_gemv(args):
         st = torch.cuda.Stream()
         n = max(8, ncopy)
         with torch.cuda.stream(st):
-            for i in range(max(args.warmup, 3)):
+            for i in range(max(warmup, 3)):
                 api.gemv_i8_i8(ws[i % ncopy], dsw, dxq, sx, acc=acc, y=y, stream=st)
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
@@ -284,22 +295,74 @@ def run_gemv(args):
         gbs = nbytes / (us * 1e-6) / 1e9
         rows.append({"N": N, "K": K, "us": round(us, 3), "bytes": nbytes, "GB_s": round(gbs, 1),
                      "frac": round(gbs / peak, 4), "acc_exact": exact, "weight_copies": ncopy})
-        del ws
+        del ws, g
         torch.cuda.empty_cache()
+    return rows
+
+
+def run_gemv(args):
+    """--gemv: the config-1 rows alone, one JSON line."""
+    import torch
+    torch.cuda.set_device(0)
+    peak, src = peaks()
+    rows = gemv_rows(args.warmup, args.gemv_n)
     print(json.dumps({"metric": "config-1 int8 GEMV achieved HBM GB/s", "unit": "GB/s", "peak": peak,
                       "peak_source": src, "kernel": "k_gemv (qwen_gemv_i8_i8)", "shapes": rows}))
     return 0
 
 
+def timed_decode(dec, prompt, steps, tp=False, dist=None):
+    """Exactly `steps` greedy decode steps timed on the device (CUDA events in
+    qwen_generate), in episodes of the prompt prefill (untimed) + at most
+    EPISODE decode steps.  Returns (device seconds, tokens of the first episode)."""
+    sec_total, done, ids0 = 0.0, 0, None
+    while done < steps:
+        n = min(EPISODE, steps - done)
+        dec.reset()
+        if tp:
+            dist.barrier()
+        ids, sec = dec.generate(prompt, n)
+        sec_total += sec
+        if ids0 is None:
+            ids0 = ids
+        elif ids != ids0[:len(ids)]:
+            raise RuntimeError("episodes produced different tokens")
+        done += n
+    return sec_total, ids0
+
+
+def warm_config(dec, T0, seed, n_steps, act_int8, tp=False, dist=None):
+    """Configs 2 and 3: import the warm start (synth.warm_state_arrays: rec
+    N(0, 0.1), T0 cached positions N(0, 1), the fixtures' recipe), feed the
+    first token (default_rng(0), untimed), then time n_steps greedy steps."""
+    from qwen_fpga_b200 import synth
+    st = synth.warm_state_arrays(T0, seed)
+    first = int(np.random.default_rng(0).integers(0, VOCAB))
+    dec.reset()
+    dec.set_act_int8(act_int8)
+    try:
+        dec.import_state(st)
+        del st
+        if tp:
+            dist.barrier()
+        ids, sec = dec.generate([first], n_steps)
+    finally:
+        dec.set_act_int8(False)
+    t_mean = T0 + 1 + (n_steps - 1) / 2.0
+    return sec, ids, t_mean
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64 * 64, help="timed decode steps (multiple of 64)")
+    ap.add_argument("--steps", type=int, default=64 * 64, help="timed decode steps (exactly)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--e2e-episodes", type=int, default=8)
+    ap.add_argument("--e2e-episodes", type=int, default=4)
     ap.add_argument("--cpu-steps", type=int, default=24)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--configs", default="1,2,3",
+                    help="extra configs measured into the same line (comma list of 1, 2, 3; '' = none)")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent sequences per GPU instead of tensor parallelism")
     ap.add_argument("--engine", type=int, default=1,
@@ -335,15 +398,17 @@ def main():
         dist.barrier()
     blob_path = synth.ensure_blob(1234)
 
-    episodes = max(1, args.steps // EPISODE)
-    K = episodes * EPISODE
+    K = max(1, args.steps)
+    W = max(args.warmup, 3)
+    configs = {c.strip() for c in args.configs.split(",") if c.strip()}
     tp = world > 1 and not args.replicas
+    max_ctx = 32768 + 512 + 64 if "3" in configs else 4096 + 256 + 64
     if tp:
         from qwen_fpga_b200.tp import TPDecoder
-        tpd = TPDecoder(blob_path, device=local, max_ctx=PROMPT_LEN + EPISODE + 64)
+        tpd = TPDecoder(blob_path, device=local, max_ctx=max_ctx)
         dec = tpd.dec
     else:
-        dec = api.Decoder(blob_path, device=local, max_ctx=PROMPT_LEN + EPISODE + 64)
+        dec = api.Decoder(blob_path, device=local, max_ctx=max_ctx)
         dec.set_engine(args.engine)
     engine = dec.engine
     seqs = 1 if tp else world   # sequences decoded by the whole job
@@ -356,25 +421,14 @@ def main():
     dec.reset()
     if world > 1:
         dist.barrier()
-    dec.generate(prompt[:1], max(args.warmup, 3))
+    dec.generate(prompt[:1], W)
 
-    # timed: K decode steps in episodes of (16-token prefill untimed, 64 decode timed)
+    # timed: exactly K decode steps (episodes of 16-token prefill untimed + <= 64 decode timed)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    dev_sec = 0.0
-    ids0 = None
-    with ClockSampler(local if world == 1 else local) as clk:
-        for e in range(episodes):
-            dec.reset()
-            if tp:
-                dist.barrier()
-            ids, sec = dec.generate(prompt, EPISODE)
-            dev_sec += sec
-            if ids0 is None:
-                ids0 = ids
-            elif ids != ids0:
-                raise RuntimeError("episodes produced different tokens")
+    with ClockSampler(local) as clk:
+        dev_sec, ids0 = timed_decode(dec, prompt, K, tp, dist)
     torch.cuda.synchronize()
     if world > 1:
         t = torch.tensor([dev_sec], dtype=torch.float64, device="cuda")
@@ -384,40 +438,70 @@ def main():
     ms_per_step = dev_sec / K * 1e3
     value = seqs * K / dev_sec
 
-    # end to end through the C ABI: host token in, host argmax out, every step
-    e2e_sec = 0.0
-    e2e_steps = 0
-    for e in range(max(1, args.e2e_episodes)):
-        dec.reset()
-        if tp:
-            dist.barrier()
-        am = 0
-        for t in prompt:
-            am, _ = dec.decode_step(int(t), want_logits=False)
-        t0 = time.perf_counter()
-        for _ in range(EPISODE):
-            am, _ = dec.decode_step(am, want_logits=False)
-        e2e_sec += time.perf_counter() - t0
-        e2e_steps += EPISODE
-    # with the fp32 logits returned to host memory each step (what golden decode_step returns;
-    # under TP each rank returns its vocab slice)
-    dec.reset()
-    if tp:
-        dist.barrier()
-    am = 0
-    for t in prompt:
-        am, _ = dec.decode_step(int(t), want_logits=False)
-    t0 = time.perf_counter()
-    for _ in range(EPISODE):
-        am, lg = dec.decode_step(am, want_logits=True)
-    lg_sec = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([e2e_sec, lg_sec], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_sec, lg_sec = (float(v) for v in t.tolist())
+    # end to end through the C ABI, host token in and the step's result out
+    # every step: with the fp32 logits (what golden decode_step returns; pinned
+    # host buffer; under TP each rank returns its vocab slice), and argmax only
+    lg_buf = torch.empty(VOCAB, dtype=torch.float32, pin_memory=True).numpy()
+    e2e = {}
+    for mode in ("logits", "argmax"):
+        sec, nsteps = 0.0, 0
+        for e in range(max(1, args.e2e_episodes)):
+            dec.reset()
+            if tp:
+                dist.barrier()
+            am = 0
+            for t in prompt:
+                am, _ = dec.decode_step(int(t), want_logits=False)
+            t0 = time.perf_counter()
+            for _ in range(EPISODE):
+                if mode == "logits":
+                    am, _ = dec.decode_step(am, out=lg_buf)
+                else:
+                    am, _ = dec.decode_step(am, want_logits=False)
+            sec += time.perf_counter() - t0
+            nsteps += EPISODE
+        if world > 1:
+            t = torch.tensor([sec], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            sec = float(t.item())
+        e2e[mode] = seqs * nsteps / sec
+
+    peak, peak_src = peaks()
+    peak_n = peak * world if tp else peak   # TP: one step's bytes are spread over every rank's HBM
+    extra = {}
+    # config 2: W8A8 warm start at 4096 positions, 256 greedy steps
+    if "2" in configs:
+        sec, ids, tm = warm_config(dec, 4096, 2, 256, True, tp, dist)
+        if world > 1:
+            t = torch.tensor([sec], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            sec = float(t.item())
+        ach = bytes_per_step(tm) * 256 / sec / 1e9
+        extra["config2"] = {"workload": "W8A8 (ACT_INT8), warm start: rec N(0,0.1), 4096 cached positions "
+                                        "N(0,1); 256 greedy decode steps timed", "steps": 256,
+                            "value": seqs * 256 / sec, "unit": UNIT, "ms_per_step": sec / 256 * 1e3,
+                            "bytes_per_step": bytes_per_step(tm), "achieved_GB_s": ach,
+                            "frac": ach / peak_n, "first_ids": ids[:8]}
+    # config 3: W8A32 at 32768 cached positions, 512 greedy steps
+    if "3" in configs:
+        sec, ids, tm = warm_config(dec, 32768, 3, 512, False, tp, dist)
+        if world > 1:
+            t = torch.tensor([sec], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            sec = float(t.item())
+        ach = bytes_per_step(tm) * 512 / sec / 1e9
+        extra["config3"] = {"workload": "W8A32, warm start: rec N(0,0.1), 32768 cached positions N(0,1); "
+                                        "512 greedy decode steps timed", "steps": 512,
+                            "value": seqs * 512 / sec, "unit": UNIT, "ms_per_step": sec / 512 * 1e3,
+                            "bytes_per_step": bytes_per_step(tm), "achieved_GB_s": ach,
+                            "frac": ach / peak_n, "first_ids": ids[:8]}
     if world > 1:
         dist.barrier()   # every rank's last step is done before any context goes away
     dec.close()
+    if "1" in configs and rank == 0 and world == 1:
+        extra["gemv"] = {"workload": "config1: int8 x int8 GEMV microbench, every shape, weights from "
+                                     "HBM (rotated copies > L2)", "kernel": "k_gemv (qwen_gemv_i8_i8)",
+                         "shapes": gemv_rows(W)}
 
     clocks = clk.summary()
     if rank != 0:
@@ -426,43 +510,45 @@ def main():
             dist.destroy_process_group()
         return 0
 
-    peak, peak_src = peaks()
-    t_mean = PROMPT_LEN + 1 + (EPISODE - 1) / 2.0
-    bstep = bytes_per_step(t_mean)
+    # mean attended positions over the timed steps (episodes restart at T = 17)
+    ts = [PROMPT_LEN + 1 + (i % EPISODE) for i in range(K)]
+    bstep = bytes_per_step(float(np.mean(ts)))
     achieved = bstep / (ms_per_step * 1e-3) / 1e9
     if tp:
-        peak = peak * world   # one step's bytes are spread over every rank's HBM
         peak_src = f"{peak_src} x {world} GPUs (aggregate)"
     traffic = load_traffic()
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
-        "warmup": max(args.warmup, 3), "ms_per_step": ms_per_step, "higher_is_better": True,
+        "warmup": W, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "strong" if tp else "weak", "vs_baseline": None,
         "dtype": "int8 weights x fp32 activations -> int32 digit accumulators",
         "data": "synthetic (random-init Qwen3.5-0.8B, seed 1234)",
-        "config": {"workload": "config0: 16-token prompt prefill (untimed) + 64 greedy decode "
-                               "steps (timed), repeated", "model": "Qwen3.5-0.8B (random init)",
-                   "batch": 1, "global_batch": seqs, "episodes": episodes,
-                   "T_ctx": f"{PROMPT_LEN + 1}..{PROMPT_LEN + EPISODE}",
+        "config": {"workload": "config0: 16-token prompt prefill (untimed) + greedy decode steps "
+                               "(timed) in episodes of <= 64", "model": "Qwen3.5-0.8B (random init)",
+                   "batch": 1, "global_batch": seqs, "episodes": -(-K // EPISODE),
+                   "T_ctx": f"{PROMPT_LEN + 1}..{PROMPT_LEN + min(K, EPISODE)}",
                    "l2": "no flush: 758 MB of weights per step > 126 MB L2",
                    "parallelism": ("1 GPU" if world == 1 else
                                    f"tp{world} (tensor parallel, one sequence)" if tp else
                                    f"{world} independent replicas")},
-        "e2e": {"value": seqs * e2e_steps / e2e_sec, "unit": UNIT, "h2d_bytes_per_step": 44,
-                "d2h_bytes_per_step": 20,
-                "with_logits": {"value": seqs * EPISODE / lg_sec, "unit": UNIT,
-                                "d2h_bytes_per_step": 20 + 4 * VOCAB}},
+        "e2e": {"value": e2e["logits"], "unit": UNIT, "h2d_bytes_per_step": 4 + 40,
+                "d2h_bytes_per_step": 4 * VOCAB + 20,
+                "what": "qwen_decode_step per token: host token in, fp32 logits [248320] + argmax "
+                        "out to pinned host memory (golden decode_step's return value)",
+                "argmax_only": {"value": e2e["argmax"], "unit": UNIT, "d2h_bytes_per_step": 20}},
         "gpu_launches": K * launches_per_step,
         "engine": "persistent" if engine == 1 else "graph",
         "roofline": {"bound": "hbm", "kernel": kernel_name,
-                     "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_source": peak_src,
+                     "achieved": achieved, "peak": peak_n, "unit": "GB/s",
+                     "frac": achieved / peak_n, "peak_source": peak_src,
                      "algorithmic_bytes_per_step": bstep,
                      "state_bytes_per_step": STATE_RW,
                      # the ncu capture is of the single-GPU kernel
                      "traffic": traffic.get("bytes_per_step") if traffic and not tp else None},
         "clocks": clocks,
+        "first_ids": ids0[:8],
     }
+    line.update(extra)
     if world == 1 and not args.no_cpu:
         try:
             line["cpu_baseline"] = cpu_baseline_port(blob_path, args.cpu_steps)

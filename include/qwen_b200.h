@@ -184,9 +184,14 @@ int qwen_gemv_i8_i8(int32_t* acc, float* y, const int8_t* w, const float* sw,
  *     larger N is rejected with QWEN_ERR_ARG.  K, w alignment as for
  *     qwen_gemv_i8_f32.  y may be NULL; argmax (one int) may not.
  *   - The first call on each device resolves the array's address
- *     (cudaGetSymbolAddress); make that first call before any stream capture.
- *   - The arrival counter must be zero when a call starts: it is zero when the
- *     library loads and every call leaves it zero.
+ *     (cudaGetSymbolAddress) and keeps it for the life of the process; make
+ *     that first call before any stream capture.  Resetting the device
+ *     (cudaDeviceReset) after that first call is not supported: the kept
+ *     address would be stale.
+ *   - Each call clears the array's arrival counter on its stream (an 8-byte
+ *     memset) before its kernel starts, so a call whose launch failed
+ *     part-way does not disturb the next one.  The per-block maxima need no
+ *     clearing: every block writes its slot before it arrives.
  *   - Calls on the same device share the array: two calls whose kernels run at
  *     the same time (different streams, overlapping launches) race and return
  *     wrong argmax values.  Order them (one stream, or events). */

@@ -226,11 +226,18 @@ class Decoder:
     def reset(self):
         _check(load().qwen_reset(self.h, 0), self.h)
 
-    def decode_step(self, tok: int, want_logits: bool = True):
-        """Returns (argmax, logits or None)."""
+    def decode_step(self, tok: int, want_logits: bool = True, out=None):
+        """Returns (argmax, logits or None).  `out` (optional): a float32 array of
+        VOCAB elements the logits are written into (e.g. pinned host memory);
+        it is returned as the logits."""
         t = (C.c_int * 1)(int(tok))
         am = (C.c_int * 1)()
-        lg = np.empty(VOCAB, np.float32) if want_logits else None
+        if out is not None:
+            if out.dtype != np.float32 or out.size != VOCAB or not out.flags["C_CONTIGUOUS"]:
+                raise ValueError("out must be a contiguous float32 array of VOCAB elements")
+            lg = out
+        else:
+            lg = np.empty(VOCAB, np.float32) if want_logits else None
         rc = load().qwen_decode_step(self.h, t, 1, lg.ctypes.data if lg is not None else None, am)
         _check(rc, self.h)
         return int(am[0]), lg
@@ -308,12 +315,38 @@ def _stream(stream):
     return C.c_void_p(s.cuda_stream)
 
 
+def _need(name, t, dtype, shape, device):
+    """t must be a contiguous CUDA tensor of `dtype` and `shape` on `device`."""
+    if t is None:
+        raise ValueError(f"{name} is required")
+    if not t.is_cuda or t.device != device:
+        raise ValueError(f"{name} must be a CUDA tensor on {device} (got {t.device})")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype} (got {t.dtype})")
+    if tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} must have shape {tuple(shape)} (got {tuple(t.shape)})")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _gemv_shape(w):
+    import torch
+    if w is None or w.dim() != 2:
+        raise ValueError("w must be a 2-D [N, K] tensor")
+    _need("w", w, torch.int8, tuple(w.shape), w.device)
+    return w.shape
+
+
 def gemv_i8_f32(w, s, x, y=None, stream=None):
     """y = s * (w @ x) for torch CUDA tensors w int8 [N,K], s fp32 [N], x fp32 [K]."""
     import torch
-    N, K = w.shape
+    N, K = _gemv_shape(w)
     y = y if y is not None else torch.empty(N, dtype=torch.float32, device=w.device)
-    rc = load().qwen_gemv_i8_f32(_ptr(y), _ptr(w), _ptr(s), _ptr(x), N, K, _stream(stream))
+    _need("s", s, torch.float32, (N,), w.device)
+    _need("x", x, torch.float32, (K,), w.device)
+    _need("y", y, torch.float32, (N,), w.device)
+    with torch.cuda.device(w.device):
+        rc = load().qwen_gemv_i8_f32(_ptr(y), _ptr(w), _ptr(s), _ptr(x), N, K, _stream(stream))
     _check(rc)
     return y
 
@@ -321,13 +354,20 @@ def gemv_i8_f32(w, s, x, y=None, stream=None):
 def gemv_i8_i8(w, sw, xq, sx, acc=None, y=None, stream=None, want_acc=True, want_y=True):
     """acc = w @ xq (int32, exact), y = acc * sx * sw for torch CUDA tensors."""
     import torch
-    N, K = w.shape
+    N, K = _gemv_shape(w)
     if want_acc and acc is None:
         acc = torch.empty(N, dtype=torch.int32, device=w.device)
     if want_y and y is None:
         y = torch.empty(N, dtype=torch.float32, device=w.device)
-    rc = load().qwen_gemv_i8_i8(_ptr(acc if want_acc else None), _ptr(y if want_y else None),
-                                _ptr(w), _ptr(sw), _ptr(xq), float(sx), N, K, _stream(stream))
+    _need("xq", xq, torch.int8, (K,), w.device)
+    if want_acc:
+        _need("acc", acc, torch.int32, (N,), w.device)
+    if want_y:
+        _need("y", y, torch.float32, (N,), w.device)
+        _need("sw", sw, torch.float32, (N,), w.device)
+    with torch.cuda.device(w.device):
+        rc = load().qwen_gemv_i8_i8(_ptr(acc if want_acc else None), _ptr(y if want_y else None),
+                                    _ptr(w), _ptr(sw), _ptr(xq), float(sx), N, K, _stream(stream))
     _check(rc)
     return acc, y
 
@@ -335,10 +375,18 @@ def gemv_i8_i8(w, sw, xq, sx, acc=None, y=None, stream=None, want_acc=True, want
 def gemv_i8_f32_argmax_noalloc(w, s, x, argmax, y=None, stream=None):
     """y = s * (w @ x) (when y is given) and argmax[0] = first index of its maximum,
     through the allocation-free entry point; argmax is a caller-owned int32 CUDA
-    tensor of one element, y an optional fp32 [N] CUDA tensor."""
-    N, K = w.shape
-    rc = load().qwen_gemv_i8_f32_argmax_noalloc(_ptr(y), _ptr(argmax), _ptr(w), _ptr(s), _ptr(x), N, K,
-                                                _stream(stream))
+    tensor of one element, y an optional fp32 [N] CUDA tensor.  Every tensor must
+    be contiguous and on w's device; the call runs with that device current."""
+    import torch
+    N, K = _gemv_shape(w)
+    _need("s", s, torch.float32, (N,), w.device)
+    _need("x", x, torch.float32, (K,), w.device)
+    _need("argmax", argmax, torch.int32, (1,), w.device)
+    if y is not None:
+        _need("y", y, torch.float32, (N,), w.device)
+    with torch.cuda.device(w.device):
+        rc = load().qwen_gemv_i8_f32_argmax_noalloc(_ptr(y), _ptr(argmax), _ptr(w), _ptr(s), _ptr(x), N,
+                                                    K, _stream(stream))
     _check(rc)
     return y, argmax
 

@@ -198,9 +198,14 @@ __device__ __forceinline__ float softplus_f(float x) {
 
 // Total order on (logit, index): larger logit first, then the smaller index
 // (np.argmax and the strict '>' of hls/src/qwen_synth.hpp:86 keep the first).
+// -0.0 and +0.0 are one value (np.argmax compares them equal, so the first
+// index wins); NaN ranks above every number, so the first NaN wins, as with
+// np.argmax.
 __device__ __forceinline__ unsigned long long am_pack(float v, int idx) {
   unsigned u = __float_as_uint(v);
-  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  if ((u << 1) == 0u) u = 0u;                          // -0.0 -> +0.0
+  u = ((u & 0x7fffffffu) > 0x7f800000u) ? 0xffffffffu  // NaN
+      : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
   return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (unsigned)idx);
 }
 __device__ __forceinline__ int am_index(unsigned long long p) {

@@ -15,9 +15,10 @@ namespace qb {
 
 // [0, NA_MAX_BLOCKS): one packed (value, index) maximum per block, written by
 // the block before it arrives (no initial value needed).
-// [NA_MAX_BLOCKS]: arrival counter.  It must be zero when a call starts: device
-// memory of a static symbol is zero when the module loads, and the last block
-// of every call resets it to zero before the call ends.
+// [NA_MAX_BLOCKS]: arrival counter.  It must be zero when a call's kernel
+// starts: every call clears it on its stream just before the launch (a memset
+// of 8 bytes, no allocation), so a launch that failed part-way cannot leave a
+// stale count for the next call; the last block also resets it.
 static __device__ __align__(256) unsigned long long g_argmax_scratch[NA_MAX_BLOCKS + 1];
 
 // Block b owns rows [b * NA_ROWS_PER_BLOCK, ...); its 8 warps take 4-row units.
@@ -109,6 +110,8 @@ cudaError_t enqueue_gemv_argmax_noalloc(float* y, int* argmax, const int8_t* w, 
   cudaError_t e = scratch_for_current_device(&scratch);
   if (e != cudaSuccess) return e;
   const int blocks = (N + NA_ROWS_PER_BLOCK - 1) / NA_ROWS_PER_BLOCK;
+  e = cudaMemsetAsync(scratch + NA_MAX_BLOCKS, 0, sizeof(unsigned long long), st);
+  if (e != cudaSuccess) return e;
   k_gemv_argmax<<<blocks, 256, 0, st>>>(y, argmax, w, s, xf, N, K, scratch);
   return cudaGetLastError();
 }

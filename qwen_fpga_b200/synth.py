@@ -295,3 +295,23 @@ class Blob:
         for i in range(0, len(self.mm), step):
             h.update(self.mm[i:i + step])
         return h.hexdigest()
+
+
+def warm_state_arrays(T: int, seed: int, rec_std: float = 0.1, kv_std: float = 1.0, n_lin: int = 18,
+                      n_full: int = 6, lh: int = 16, lk: int = 128, lv: int = 128, convd: int = 6144,
+                      conv_k: int = 4, nkv: int = 2, hd: int = 256):
+    """Warm-start decode state of the W8A8 and long-context configs: DeltaNet
+    states N(0, rec_std), conv history zero, T cached positions of K (after
+    RoPE) and V drawn N(0, kv_std), pos = T.  Drawn from default_rng(seed) in
+    the order rec, then per attention layer K then V (the order the parity
+    fixtures were generated with).  Returns a simple namespace with conv, rec,
+    kc, vc (lists of [T, nkv, hd]) and pos, as Decoder.import_state takes."""
+    from types import SimpleNamespace
+    f32 = np.float32
+    rng = np.random.default_rng(seed)
+    rec = rng.standard_normal((n_lin, lh, lk, lv), f32) * f32(rec_std)
+    kc, vc = [], []
+    for _ in range(n_full):
+        kc.append(rng.standard_normal((T, nkv, hd), f32) * f32(kv_std))
+        vc.append(rng.standard_normal((T, nkv, hd), f32) * f32(kv_std))
+    return SimpleNamespace(conv=np.zeros((n_lin, convd, conv_k), f32), rec=rec, kc=kc, vc=vc, pos=T)

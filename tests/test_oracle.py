@@ -170,3 +170,16 @@ def test_hls_reference_matches_golden_first_steps(blob_path):
             assert np.abs(lg[SAMPLE_IDX] - fx["step0_sample"]).max() < 5e-2
             assert logits_close(lg, fx, "step0") < 1e-4
     ref.close()
+
+
+def test_synth_warm_state_matches_port_recipe(cfg):
+    """bench.py draws the config 2/3 warm starts with synth.warm_state_arrays
+    (the product side may not import the oracle); it must be the recipe the
+    parity fixtures were generated with (oracle golden_port.warm_state)."""
+    from qwen_fpga_b200 import synth
+    a = synth.warm_state_arrays(7, seed=2)
+    b = P.warm_state(cfg, 7, seed=2)
+    assert a.pos == b.pos == 7
+    assert np.array_equal(a.rec, b.rec) and np.array_equal(a.conv, b.conv)
+    for f in range(6):
+        assert np.array_equal(a.kc[f], b.kc[f]) and np.array_equal(a.vc[f], b.vc[f])
