@@ -126,12 +126,13 @@ int qwen_get_engine(qwen_ctx* ctx);
  * step records, per CTA and per phase, %globaltimer stamps [entry, inputs
  * arrived, outputs written, exit] (ns; 0 where a phase has no such point),
  * n_ctas * n_phases * 4 words;
- * then, for CTA 0, per phase and per warp (16), 16 SM-clock stamps of a GEMV
- * phase [entry, input in, input encoded, first chunk landed, own tasks done,
- * CTA barrier passed, outputs written, slots released, encoder: statistics,
- * their barrier, digits written, 5 unused] (0 = not reached), n_phases * 16 *
- * 16 words; this second part is filled only by a library built with
- * QB_WARP_TRACE defined (its stamps cost instructions on the hot path).
+ * then, for the first CTA that runs GEMV panels, per phase and per warp (16),
+ * 16 SM-clock stamps of a GEMV phase [entry, inputs in, input encoded, first
+ * chunk landed, own tasks done, a task's MMA done, a panel's outputs written,
+ * unused, W8A8 encoder: statistics, their barrier, digits written, 5 unused]
+ * (0 = not reached), n_phases * 16 * 16 words; this second part is filled
+ * only by a library built with QB_WARP_TRACE defined (its stamps cost
+ * instructions on the hot path).
  * qwen_trace_read copies the last step's record to host memory; max_words
  * must cover both parts. */
 int qwen_trace_enable(qwen_ctx* ctx, int on);

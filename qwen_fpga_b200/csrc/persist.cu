@@ -66,13 +66,12 @@ constexpr int OFF_DIG = OFF_RING + NSLOT * SLOT;
 constexpr int OFF_XF = OFF_DIG + DIG_BYTES;               // float [KMAX]
 constexpr int OFF_HS = OFF_XF + 4 * KMAX;                 // float [HID]
 constexpr int MAXPAN = NSLOT;                             // panels of one phase on one CTA (at most)
-constexpr int MAXTASK = NSLOT * (PANEL_KB / TASK_KB);     // tasks of one phase on one CTA (at most)
-constexpr int OFF_PART = OFF_HS + 4 * HID;                // int [MAXPAN][3][PANEL]: exact digit sums
-constexpr int OFF_PARTF = OFF_PART + 4 * MAXPAN * 3 * PANEL;  // float [MAXTASK][PANEL]: fp32 row dots
-constexpr int OFF_LAY = OFF_PARTF + 4 * MAXTASK * PANEL;  // LayerW [NLAYER]
+constexpr int OFF_PART = OFF_HS + 4 * HID;                // int [MAXPAN][4][PANEL]: exact digit sums
+constexpr int OFF_PSC = OFF_PART + 4 * MAXPAN * 4 * PANEL;   // float [MAXPAN][PANEL]: the panels' row scales
+constexpr int OFF_LAY = OFF_PSC + 4 * MAXPAN * PANEL;     // LayerW [NLAYER]
 constexpr int OFF_CH = OFF_LAY + ((int)sizeof(LayerW) * NLAYER + 15) / 16 * 16;  // Chunk [MAXCH]
 constexpr int OFF_BAR = OFF_CH + 8 * MAXCH;               // u64 mbarriers, see bar_* below
-constexpr int NBAR = 3 * NSLOT + 5;                       // full, empty, mma per slot; acc_full[2], acc_empty[2], fin
+constexpr int NBAR = 3 * NSLOT + 5;                       // full, (spare), mma per slot; acc_full[2], acc_empty[2], fin
 constexpr int OFF_MISC = OFF_BAR + 8 * NBAR;              // small scalars
 // tensor-core phases: the x digits as the B operand (16 rows x HID, canonical
 // K-major layout: rows 0-2 the digit planes, 3-15 zero; 8-row groups BT_SBO
@@ -80,7 +79,8 @@ constexpr int OFF_MISC = OFF_BAR + 8 * NBAR;              // small scalars
 constexpr int BT_SBO = (HID / 16) * 128;
 constexpr int OFF_BT = OFF_DIG;
 static_assert(OFF_BT % 128 == 0 && OFF_BT + 2 * BT_SBO <= OFF_HS, "head B tile");
-constexpr int SMEM_BYTES = OFF_MISC + 1024;
+constexpr int MISC_BYTES = 1152;
+constexpr int SMEM_BYTES = OFF_MISC + MISC_BYTES;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 static_assert(OFF_DIG % 16 == 0 && OFF_XF % 16 == 0 && OFF_HS % 16 == 0 && SLOT % 16 == 0, "alignment");
 static_assert(OFF_BAR % 8 == 0 && OFF_MISC % 8 == 0, "alignment");
@@ -106,10 +106,14 @@ struct Misc {
   unsigned long long wbest[NCW];
   float inv_h[LH];
   float gate_g, gate_beta;
+  float abv[2];            // DeltaNet head CTA: the head's in_proj_b, in_proj_a outputs
+  float ssw[NCW];          // per-warp sums of squares of a normed GEMV input
+  int pcnt[NSLOT];         // GEMV phase: tasks finished per panel (the last one finishes the panel)
+  int rfq[NCW][2];         // per warp: ring slots to refill at the next phase (first | count << 16)
   float xinv;              // 1/rms of the current normed GEMV input (W8A32 path)
   unsigned amax[2];        // bits of max|v| of the GEMV input of phases p with p & 1 = index
 };
-static_assert(sizeof(Misc) <= 1024, "misc");
+static_assert(sizeof(Misc) <= MISC_BYTES, "misc");
 static_assert(OFF_MISC % 16 == 0, "tcgen05.alloc destination alignment");
 
 // ---------------------------------------------------------------- PTX helpers
@@ -183,6 +187,20 @@ __device__ __forceinline__ bool mbar_try(unsigned bar, unsigned parity) {
                : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
   return ok != 0;
 }
+// Non-blocking probe of an mbarrier phase.
+__device__ __forceinline__ bool mbar_test(unsigned bar, unsigned parity) {
+  unsigned ok;
+  asm volatile("{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Shared-memory counter with acquire / release semantics at CTA scope.
+__device__ __forceinline__ int atom_add_acq_rel_cta(int* p, int v) {
+  int r;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.s32 %0, [%1], %2;"
+               : "=r"(r) : "r"((unsigned)__cvta_generic_to_shared(p)), "r"(v) : "memory");
+  return r;
+}
 __device__ __forceinline__ void mbar_arrive(unsigned bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
 }
@@ -207,9 +225,6 @@ struct PCtx {
 };
 
 __device__ __forceinline__ unsigned full_bar(const PCtx& c, int slot) { return smem_u32(c.sm + OFF_BAR + 8 * slot); }
-__device__ __forceinline__ unsigned empty_bar(const PCtx& c, int slot) {
-  return smem_u32(c.sm + OFF_BAR + 8 * (NSLOT + slot));
-}
 
 // tcgen05 completion of the MMAs that read slot s (head phase)
 __device__ __forceinline__ unsigned mma_bar(const PCtx& c, int slot) {
@@ -260,13 +275,18 @@ __device__ __forceinline__ void trace_mark(const PCtx& c, int p, int k) {
   if (c.A->trace && threadIdx.x == 0)
     c.A->trace[((size_t)blockIdx.x * NPHASE + p) * TRACE_STAMPS + k] = gtime();
 }
-// per-warp stamps of CTA 0 (after the per-phase block): [phase][warp][TRACE_WARP_STAMPS]
+// The same stamp from any thread, keeping the latest (the record is zeroed
+// before a traced step).
+__device__ __forceinline__ void trace_latest(const PCtx& c, int p, int k) {
+  if (c.A->trace) atomicMax(c.A->trace + ((size_t)blockIdx.x * NPHASE + p) * TRACE_STAMPS + k, gtime());
+}
+// per-warp stamps of the first GEMV CTA (after the per-phase block): [phase][warp][TRACE_WARP_STAMPS]
 // SM clock cycles (clock64), finer than the global timer.  Compiled in only
 // with QB_WARP_TRACE defined (every call site costs instructions on the hot
 // path, traced or not); otherwise that part of the record stays zero.
 __device__ __forceinline__ void trace_warp(const PCtx& c, int p, int k) {
 #ifdef QB_WARP_TRACE
-  if (c.A->trace && blockIdx.x == 0 && (threadIdx.x & 31) == 0)
+  if (c.A->trace && (int)blockIdx.x == c.A->dn_h1 - c.A->dn_h0 && (threadIdx.x & 31) == 0)
     c.A->trace[(size_t)gridDim.x * NPHASE * TRACE_STAMPS +
                ((size_t)p * NCW + (threadIdx.x >> 5)) * TRACE_WARP_STAMPS + k] = clock64();
 #else
@@ -314,9 +334,8 @@ __device__ __forceinline__ unsigned kwin_t(const PersistArgs& A, int sub) {
 }
 
 // Source and size of chunk k: one K-slice of a layer panel (slice n covers
-// K [k0 + 1024 n, min(k0 + 1024 (n + 1), k1)) of the phase's window), one
-// K-slab of a head tile, or (DeltaNet IN) nrows fp32 rows of in_proj_b (seg 2)
-// or in_proj_a (seg 3).  src = null for a chunk outside its matrix.
+// K [k0 + 1024 n, min(k0 + 1024 (n + 1), k1)) of the phase's window), or one
+// K-slab of a head tile.  src = null for a chunk outside its matrix.
 __device__ __forceinline__ void chunk_src(const LayerW* lay, const int8_t* head_tiles, const Chunk& k,
                                           unsigned kw_out, unsigned kw_down, const char*& src,
                                           unsigned& bytes) {
@@ -349,9 +368,6 @@ __device__ __forceinline__ void chunk_src(const LayerW* lay, const int8_t* head_
     bytes = (unsigned)(kl * PANEL);
     return;
   }
-  if (sub != 0 || !L.linear || k.seg < 2 || k.seg > 3 || row0 + n > LH || n * HID * 4 > SLOTW) return;
-  src = (const char*)((k.seg == 2 ? L.b_w : L.a_w) + (size_t)row0 * HID);
-  bytes = (unsigned)(n * HID * 4);
 }
 
 // Issue the bulk copy of chunk i into its slot (one lane).  One copy in the
@@ -397,7 +413,7 @@ __device__ bool wait_bar1(const PCtx& c, unsigned bar, unsigned parity, int site
 // result in every lane.
 __device__ __forceinline__ bool wait_bar_warp(PCtx& c, unsigned bar, unsigned parity, int site, int value) {
   int good = 1;
-  if (!mbar_try(bar, parity)) {
+  if (!mbar_test(bar, parity)) {
     const unsigned long long t0 = gtime();
     int it = 0;
     while (!mbar_try(bar, parity)) {
@@ -424,11 +440,15 @@ __device__ __forceinline__ bool wait_full(PCtx& c, int i) {
 // max|v| of the values into it (red.shared.max on the bits of a non-negative
 // float orders like the floats), v = the value, or value * (1 + g) with the
 // thread's norm gains g (gain, for n = 2 * PT: one pair per thread).  The
-// barrier that ends the wait publishes it.
+// barrier that ends the wait publishes it.  With ssw (may be null), every
+// warp writes the sum of v^2 over its values (the raw values) to ssw[warp]
+// after the wait; the caller's next CTA barrier publishes them.
 __device__ __noinline__ bool wait_tagged_words(Misc* ms, int* err, int* abort_flag,
                                                const unsigned long long* src, int n, unsigned tag,
-                                               float* dst, unsigned* amax, bool gain, float2 g2) {
+                                               float* dst, unsigned* amax, bool gain, float2 g2,
+                                               float* ssw) {
   const unsigned long long t0 = gtime();
+  float ss = 0.0f;
   const int npair = n >> 1;
   unsigned pend = 0;
 #pragma unroll
@@ -452,6 +472,7 @@ __device__ __noinline__ bool wait_tagged_words(Misc* ms, int* err, int* abort_fl
         if (gain) vmax = fmaxf(vmax, fmaxf(fabsf(__fmul_rn(v0, __fadd_rn(1.0f, g2.x))),
                                            fabsf(__fmul_rn(v1, __fadd_rn(1.0f, g2.y)))));
         else vmax = fmaxf(vmax, fmaxf(fabsf(v0), fabsf(v1)));
+        ss = fmaf(v1, v1, fmaf(v0, v0, ss));
         pend &= ~(1u << j);
       }
     }
@@ -463,7 +484,13 @@ __device__ __noinline__ bool wait_tagged_words(Misc* ms, int* err, int* abort_fl
       if ((threadIdx.x & 31) == 0 && wm)
         asm volatile("red.shared.max.u32 [%0], %1;" :: "r"(smem_u32(amax)), "r"(wm) : "memory");
     }
-    if (consumer_and(pend == 0)) return true;
+    if (consumer_and(pend == 0)) {
+      if (ssw) {   // published by the caller's next barrier
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) ssw[threadIdx.x >> 5] = ss;
+      }
+      return true;
+    }
     if (((++it) & 15) == 0) {
       int bad = 0;
       if (threadIdx.x == 0) {
@@ -481,12 +508,98 @@ __device__ __noinline__ bool wait_tagged_words(Misc* ms, int* err, int* abort_fl
 __device__ __forceinline__ bool wait_tagged(PCtx& c, const unsigned long long* src, int n, unsigned tag,
                                             float* dst) {
   return wait_tagged_words(c.ms, c.A->err, c.A->abort_flag, src, n, tag, dst, nullptr, false,
-                           make_float2(0.0f, 0.0f));
+                           make_float2(0.0f, 0.0f), nullptr);
 }
-// The same, folding max|v| into *amax (see above).
-__device__ __forceinline__ bool wait_tagged_max(PCtx& c, const unsigned long long* src, int n, unsigned tag,
-                                                float* dst, unsigned* amax, bool gain, float2 g2) {
-  return wait_tagged_words(c.ms, c.A->err, c.A->abort_flag, src, n, tag, dst, amax, gain, g2);
+
+// One run of tagged words a GEMV phase waits for: np pairs from src into dst
+// (shared memory), all carrying `tag`.
+struct WSeg {
+  const unsigned long long* src;
+  float* dst;
+  int np;
+  unsigned tag;
+};
+constexpr int MAXW = 5;   // pairs per thread over a GEMV phase's segments (DeltaNet OUT: o, z, residual)
+
+// The input wait of a GEMV phase: the words of up to three segments polled
+// together (all of a thread's pending loads issued before any is checked)
+// until every one carries its segment's tag; values into the segments' dst.
+// Pair q = tid + PT j of the concatenated segments.  Segment 0 is the
+// projection input: with amax, max|v| over its values folds into *amax (v =
+// value * (1 + g) with the thread's norm gains g2 when `gain`: a normed input
+// is segment 0 alone, HID values, thread t = pair t), and with ssw each warp
+// writes the sum of value^2 over its segment-0 values to ssw[warp] (the
+// caller's next barrier publishes it).  Collective; false on abort.  Inlined
+// into the GEMV phase (one call site), so the task registers loaded before
+// it are not saved across a call.
+__device__ __forceinline__ bool wait_inputs(Misc* ms, int* err, int* abort_flag, const WSeg& s0, const WSeg& s1,
+                                            const WSeg& s2, unsigned* amax, bool gain, float2 g2, float* ssw) {
+  const unsigned long long t0 = gtime();
+  const int n01 = s0.np + s1.np, ntot = n01 + s2.np;
+  unsigned pend = 0;
+#pragma unroll
+  for (int j = 0; j < MAXW; ++j)
+    if ((int)threadIdx.x + PT * j < ntot) pend |= 1u << j;
+  float vmax = 0.0f, ss = 0.0f;
+  bool folded = false;
+  int it = 0;
+  for (;;) {
+    unsigned long long a[MAXW], b[MAXW];
+#pragma unroll
+    for (int j = 0; j < MAXW; ++j) {
+      if (!(pend >> j & 1)) continue;
+      const int q = (int)threadIdx.x + PT * j;
+      const unsigned long long* sp = q < s0.np ? s0.src + 2 * q
+                                   : (q < n01 ? s1.src + 2 * (q - s0.np) : s2.src + 2 * (q - n01));
+      ld_tv2(sp, a[j], b[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < MAXW; ++j) {
+      if (!(pend >> j & 1)) continue;
+      const int q = (int)threadIdx.x + PT * j;
+      const int sg = q < s0.np ? 0 : (q < n01 ? 1 : 2);
+      const unsigned tag = sg == 0 ? s0.tag : (sg == 1 ? s1.tag : s2.tag);
+      if (!tag_ok(a[j], tag) || !tag_ok(b[j], tag)) continue;
+      float* d = sg == 0 ? s0.dst + 2 * q : (sg == 1 ? s1.dst + 2 * (q - s0.np) : s2.dst + 2 * (q - n01));
+      const float v0 = tv_val(a[j]), v1 = tv_val(b[j]);
+      d[0] = v0;
+      d[1] = v1;
+      if (sg == 0) {
+        if (gain) vmax = fmaxf(vmax, fmaxf(fabsf(__fmul_rn(v0, __fadd_rn(1.0f, g2.x))),
+                                           fabsf(__fmul_rn(v1, __fadd_rn(1.0f, g2.y)))));
+        else vmax = fmaxf(vmax, fmaxf(fabsf(v0), fabsf(v1)));
+        ss = fmaf(v1, v1, fmaf(v0, v0, ss));
+      }
+      pend &= ~(1u << j);
+    }
+    if (amax) {
+      // lanes whose values all arrived fold their max once: one shared atomic per warp
+      const bool nw = pend == 0 && !folded;
+      const unsigned wm = __reduce_max_sync(0xffffffffu, nw ? __float_as_uint(vmax) : 0u);
+      if (nw) folded = true;
+      if ((threadIdx.x & 31) == 0 && wm)
+        asm volatile("red.shared.max.u32 [%0], %1;" :: "r"(smem_u32(amax)), "r"(wm) : "memory");
+    }
+    if (consumer_and(pend == 0)) {
+      if (ssw) {
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) ssw[threadIdx.x >> 5] = ss;
+      }
+      return true;
+    }
+    if (((++it) & 15) == 0) {
+      int bad = 0;
+      if (threadIdx.x == 0) {
+        if (*(volatile int*)&ms->abort || ld_flag(abort_flag)) {
+          bad = 1;
+        } else if (gtime() - t0 > WAIT_NS) {
+          record_error(err, abort_flag, ms, ERR_WAIT, 12, (int)(s0.tag & 127u));
+          bad = 1;
+        }
+      }
+      if (!consumer_and(!bad)) return false;
+    }
+  }
 }
 
 // ---------------------------------------------------------------- prologues
@@ -502,41 +615,43 @@ __device__ __forceinline__ int dig_off(int d, int k) {
   return (k >> 5) * 96 + (d * 4 + ((k >> 2) & 3)) * 8 + ((k >> 4) & 1) * 4;
 }
 
-// W8A32 digit image of v = src[k0 .. k1) (positions of the image; a normed
-// input: v = src * (1 + g), [0, 2 PT), the thread's gains g2) into the CTA's image, shift from the exact
-// max|v| whose bits the input wait folded into amax: |X| <= 2^22 (the rule of
-// the other encoders), three int8 digits per position; an input whose max is
-// below 2^-104 encodes as zero (its share of any output is below 2^-104 * 127 *
-// K of the row scale).  Thread = position pairs tid + PT j.  Returns 2^-shift
-// (0: all zero).  Ends with a CTA barrier.  One copy (not inlined), shared by
-// the four GEMV phases.
-__device__ __noinline__ float encode_fixed(unsigned char* sm, const float* src, int k0, int k1, unsigned amax,
-                                           bool gain, float2 g2) {
-  int8_t* dg = (int8_t*)(sm + OFF_DIG);
+// W8A32 digit image of v = src[k0 .. k1) (a normed input: v = src * (1 + g),
+// gains g from `gains`; may be null) into the CTA's image, as three UNSIGNED
+// int8 digits: X = rint(v * 2^sh) with |X| <= 2^22 from the exact max|v|
+// whose bits the input wait folded into amax, held as U = X + 2^22 in
+// [0, 2^23].  v * 2^sh + 1.5 * 2^23 rounds once to an integer in [2^23, 2^24]
+// whose float bits carry U in bytes 0-2 (U = 2^23 at the top end shows as
+// byte 2 = 0x80): those bytes are the digits D0, D1, D2 (U = D0 + 256 D1 +
+// 65536 D2), gathered with byte permutes.  The panel MMA multiplies them as
+// unsigned against the signed weights and removes the 2^22 offset with the
+// rows' weight sums (a column of ones).  Thread = groups of 4 positions
+// (4 tid + 4 PT j); one 32-bit store per digit plane.  Returns 2^-sh (0: all
+// zero).  Ends with a CTA barrier.
+__device__ __forceinline__ float encode_u8(unsigned char* sm, const float* src, int k0, int k1, unsigned amax,
+                                           const float* gains) {
+  unsigned char* dg = sm + OFF_DIG;
   const int sh = 22 - ((int)((amax >> 23) & 0xffu) - 126);   // max in [2^(ex-1), 2^ex)
   const bool live = amax != 0u && sh <= 126;
   const float p2 = live ? pow2f(sh) : 0.0f;
-  for (int q = (k0 >> 1) + threadIdx.x; 2 * q < k1; q += PT) {
-    float v0 = src[2 * q], v1 = src[2 * q + 1];
-    if (gain) {
-      v0 = __fmul_rn(v0, __fadd_rn(1.0f, g2.x));
-      v1 = __fmul_rn(v1, __fadd_rn(1.0f, g2.y));
+  for (int g = (k0 >> 2) + threadIdx.x; g < (k1 >> 2); g += PT) {
+    float4 x = *reinterpret_cast<const float4*>(src + 4 * g);
+    if (gains) {
+      const float4 w = __ldg(reinterpret_cast<const float4*>(gains) + g);
+      x.x = __fmul_rn(x.x, __fadd_rn(1.0f, w.x));
+      x.y = __fmul_rn(x.y, __fadd_rn(1.0f, w.y));
+      x.z = __fmul_rn(x.z, __fadd_rn(1.0f, w.z));
+      x.w = __fmul_rn(x.w, __fadd_rn(1.0f, w.w));
     }
-    const int X[2] = {__float2int_rn(v0 * p2), __float2int_rn(v1 * p2)};   // exact products
-    unsigned w_[3] = {0u, 0u, 0u};
+    const unsigned f0 = __float_as_uint(__fmaf_rn(x.x, p2, 12582912.0f));
+    const unsigned f1 = __float_as_uint(__fmaf_rn(x.y, p2, 12582912.0f));
+    const unsigned f2 = __float_as_uint(__fmaf_rn(x.z, p2, 12582912.0f));
+    const unsigned f3 = __float_as_uint(__fmaf_rn(x.w, p2, 12582912.0f));
 #pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int a0 = (X[e] << 24) >> 24;
-      const int X1 = (X[e] - a0) >> 8;
-      const int a1 = (X1 << 24) >> 24;
-      const int a2 = (X1 - a1) >> 8;
-      w_[0] |= ((unsigned)a0 & 0xffu) << (8 * e);
-      w_[1] |= ((unsigned)a1 & 0xffu) << (8 * e);
-      w_[2] |= ((unsigned)a2 & 0xffu) << (8 * e);
+    for (int d = 0; d < 3; ++d) {
+      const unsigned sel = (unsigned)(d | (4 + d) << 4);
+      *reinterpret_cast<unsigned*>(dg + dig_off(d, 4 * g)) =
+          __byte_perm(__byte_perm(f0, f1, sel), __byte_perm(f2, f3, sel), 0x5410u);
     }
-#pragma unroll
-    for (int d = 0; d < 3; ++d)
-      *reinterpret_cast<unsigned short*>(dg + dig_off(d, (2 * q) & ~3) + ((2 * q) & 2)) = (unsigned short)w_[d];
   }
   consumer_sync();
   return live ? pow2f(-sh) : 0.0f;
@@ -747,7 +862,7 @@ __device__ __forceinline__ void cta_encode_1024(PCtx& c, const float* hs, float2
                                                 int tp = -1) {
   unsigned long long* tw = nullptr;
 #ifdef QB_WARP_TRACE
-  if (tp >= 0 && c.A->trace && blockIdx.x == 0 && (threadIdx.x & 31) == 0)
+  if (tp >= 0 && c.A->trace && (int)blockIdx.x == c.A->dn_h1 - c.A->dn_h0 && (threadIdx.x & 31) == 0)
     tw = c.A->trace + (size_t)gridDim.x * NPHASE * TRACE_STAMPS +
          ((size_t)tp * NCW + (threadIdx.x >> 5)) * TRACE_WARP_STAMPS;
 #endif
@@ -817,93 +932,6 @@ __device__ bool tp_encode_i8(PCtx& c, int p, int k0, int k1) {
   }
   if (threadIdx.x == 0) { ms->scale = (double)s; ms->ndig = 1; }
   consumer_sync();
-  return true;
-}
-
-// The residual stream that an OUT or DOWN phase adds its projection to
-// (golden/model.py:259,263): h after the previous residual add (tagged), or for
-// layer 0's OUT the dequantised embedding row (golden/model.py:246).  Into hs,
-// unless hs holds it already.
-__device__ bool load_residual(PCtx& c, int p) {
-  const PersistArgs& A = *c.A;
-  float* hs = (float*)(c.sm + OFF_HS);
-  const unsigned need = tag_of(c, p == 2 ? -1 : (p % 5 == 4 ? p - 2 : p - 3));
-  if (c.ms->hs_tag == need) return true;   // the previous phase of this CTA left it in hs
-  if (p == 2) {
-    const int tok = c.ms->tok;
-    const float sc = __ldg(A.emb_s + tok);
-    const int8_t* row = A.emb_q + (size_t)tok * HID;
-    for (int i = threadIdx.x; i < HID; i += PT) hs[i] = __fmul_rn((float)row[i], sc);
-    consumer_sync();
-  } else if (!wait_tagged(c, A.tv_h, HID, need, hs)) {
-    return false;
-  }
-  if (threadIdx.x == 0) c.ms->hs_tag = need;
-  return true;
-}
-
-// Prologue of the OUT (sub 2) and DOWN (sub 4) phases: the residual rows and
-// the inputs of the phase's K window [k0, k1) (kwin: all of them, or the
-// rank's columns under tensor parallelism) into xf at their positions.
-// ACT_INT8 (amax null; whole inputs only): their digit image for the whole
-// CTA as well (encode_lin); W8A32: max|x| folded into *amax instead, for
-// encode_fixed.  false on abort.
-template <bool TP>
-__device__ bool prologue(PCtx& c, int p, unsigned* amax, int& k0, int& k1) {
-  float* xf = (float*)(c.sm + OFF_XF);
-  const PersistArgs& A = *c.A;
-  Misc* ms = c.ms;
-  const bool i8 = ms->act_int8 != 0;
-  const int l = p / 5, sub = p % 5;
-  const LayerW& L = c.lay[l];
-  if (!load_residual(c, p)) return false;
-  // the projection's input: the delta-rule output o (DeltaNet OUT, gated
-  // below), the gated attention output o * sigmoid(gate) written by the merge
-  // (attention OUT), or silu(gate) * up (DOWN)
-  const bool gated = sub == 2 && L.linear;
-  // element i = k0 + tid + 512 j, and k0 is a multiple of LV
-  const float gw = gated ? __ldg(L.gnorm_w + (threadIdx.x % LV)) : 0.0f;
-  const unsigned long long* src = sub == 4 ? A.tv_act : (L.linear ? A.tv_o : A.tv_attn);
-  const unsigned kw = kwin_t<TP>(A, sub);
-  k0 = (int)(kw & 0xffffu);
-  k1 = (int)(kw >> 16);
-  // silu(z) of the gated norm, parked in the digit region: IN(l) wrote it
-  // before the delta rule ran, so it is read before waiting for o, off the
-  // critical path
-  float* zb = (float*)(c.sm + OFF_DIG);
-  if (gated && !wait_tagged(c, A.tv_z + k0, k1 - k0, tag_of(c, p - 2), zb + k0)) return false;
-  if (!wait_tagged_max(c, src + k0, k1 - k0, tag_of(c, p - 1), xf + k0, gated ? nullptr : amax, false,
-                       make_float2(0.0f, 0.0f)))
-    return false;
-  if (gated) {
-    // gated RMSNorm of the delta-rule output (golden/model.py:183-189) over the
-    // window's heads
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    for (int h = k0 / LV + wid; h < k1 / LV; h += NCW) {
-      float ss = 0.0f;
-      for (int i = lane; i < LV; i += 32) ss = fmaf(xf[h * LV + i], xf[h * LV + i], ss);
-      ss = warp_sum(ss);
-      // (ss / LV: LV is a power of two, so the product by 1/LV is the same number)
-      if (lane == 0) ms->inv_h[h] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / LV), EPS)));
-    }
-    consumer_sync();
-    float vmax = 0.0f;
-    for (int i = k0 + threadIdx.x; i < k1; i += PT) {
-      const float v = __fmul_rn(__fmul_rn(xf[i], ms->inv_h[i / LV]), gw);
-      xf[i] = __fmul_rn(v, zb[i]);
-      vmax = fmaxf(vmax, fabsf(xf[i]));
-    }
-    if (amax) {
-      const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(vmax));
-      if ((threadIdx.x & 31) == 0 && wm)
-        asm volatile("red.shared.max.u32 [%0], %1;" :: "r"(smem_u32(amax)), "r"(wm) : "memory");
-    }
-    consumer_sync();
-  }
-  if (!amax) {
-    if constexpr (TP) { if (!tp_encode_i8(c, p, k0, k1)) return false; }
-    else encode_lin(c, k1, i8);
-  }
   return true;
 }
 
@@ -995,9 +1023,6 @@ __device__ void head_finish(PCtx& c, unsigned long long best) {
 //                      digit sums recombined and scaled exactly as the CUDA-core
 //                      GEMVs do (finish_f32), logits stored, argmax kept.
 
-__device__ __forceinline__ void mbar_arrive_cnt(unsigned bar, unsigned cnt) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(cnt) : "memory");
-}
 
 // Refiller (one thread) over the phase's slabs [i0, i1): wait for the MMAs of
 // slab q (per-slot commit parity in *mpar), release its slot on the empty
@@ -1190,23 +1215,6 @@ __device__ __forceinline__ void panel_mma(unsigned a, const unsigned char* fr, i
   d3[2] = u == 0 ? x : c[2];
 }
 
-// A warp is done with chunk i (every task on it finished before the last CTA
-// barrier): complete the slot's empty phase for every warp at once and refill
-// the slot itself.
-__device__ __forceinline__ void release_panel_chunk(PCtx& c, int i) {
-  const int s = i % NSLOT;
-  if ((threadIdx.x & 31) == 0) {
-    mbar_arrive_cnt(empty_bar(c, s), NCW);
-    const int nx = i + NSLOT;
-    if (nx < c.nch && wait_bar1(c, empty_bar(c, s), (unsigned)((i / NSLOT) & 1), 10, i) &&
-        !*(volatile int*)&c.ms->abort) {
-      issue_chunk(c, nx);
-      c.ms->slot_last[s] = nx;
-    }
-  }
-  __syncwarp();
-}
-
 // Tasks of chunk k of a GEMV phase with K window kw (kwin_of): a panel
 // slice's K in pieces of at most TASK_KB (multiples of 128).
 __host__ __device__ __forceinline__ int chunk_tasks(const Chunk& k, unsigned kw) {
@@ -1278,267 +1286,358 @@ __device__ __forceinline__ const float* row_scale(const LayerW& L, int sub, int 
   return (sub == 2 ? (L.linear ? L.out_s : L.o_s) : L.down_s) + r;
 }
 
-// Row-parallel OUT / DOWN under tensor parallelism: the residual rows of this
-// CTA's panels once every rank's partial of them is in this rank's exchange
-// buffer xb ([TP_MAX][HID] of the phase kind), h = r + ((y_0 + y_1) + ...) in
-// rank order (bit-identical on every rank), written as tagged words to tv_h.
-// Per warp: its panels are rows[v] (lane = row pr, own lanes), v = wid, wid +
-// NCW, ... < npan.  Bounded wait; false on abort.  Not inlined, plain
-// arguments: only tensor-parallel runs execute it.
-__device__ __noinline__ bool tp_reduce_rows(const unsigned long long* xb, unsigned long long* tv_h, const float* hs,
-                                            const int* rows, int npan, int P, bool own, int pr, unsigned tag,
-                                            Misc* ms, int* err, int* abort_flag, int sub) {
-  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int good = 1;
-  for (int v = wid; v < npan && good; v += NCW) {
-    const int r = rows[v] * PANEL + pr;
-    const unsigned long long t0 = gtime();
-    int it = 0;
-    float sum = 0.0f;
-    bool done = !own;
-    for (;;) {
-      if (!done) {
-        bool all = true;
-        for (int rr = 0; rr < P && all; ++rr) all = tag_ok(ld_tv_sys(xb + (size_t)rr * HID + r), tag);
-        if (all) {
-          sum = tv_val(ld_tv_sys(xb + r));
-          for (int rr = 1; rr < P; ++rr) sum = __fadd_rn(sum, tv_val(ld_tv_sys(xb + (size_t)rr * HID + r)));
-          done = true;
-        }
-      }
-      if (__all_sync(0xffffffffu, done)) break;
-      if (((++it) & 63) == 0) {
-        int bad = 0;
-        if (lane == 0) {
-          if (*(volatile int*)&ms->abort || ld_flag(abort_flag)) {
-            bad = 1;
-          } else if (gtime() - t0 > WAIT_NS) {
-            record_error(err, abort_flag, ms, ERR_WAIT, 23, sub);
-            bad = 1;
-          }
-        }
-        if (__shfl_sync(0xffffffffu, bad, 0)) { good = 0; break; }
+// Row-parallel OUT / DOWN under tensor parallelism: the 16 residual rows of
+// panel q (lane = row pr, own lanes; hres = the lane's residual value) once
+// every rank's partial of them is in this rank's exchange buffer xb
+// ([TP_MAX][HID] of the phase kind), h = r + ((y_0 + y_1) + ...) in rank
+// order (bit-identical on every rank),
+// written as tagged words to tv_h.  One warp.  Bounded wait; false on abort.
+// Not inlined, plain arguments: only tensor-parallel runs execute it.
+__device__ __noinline__ bool tp_reduce_panel(const unsigned long long* xb, unsigned long long* tv_h, float hres,
+                                             int q, int P, bool own, int pr, unsigned tag, Misc* ms, int* err,
+                                             int* abort_flag, int sub) {
+  const int lane = threadIdx.x & 31;
+  const int r = q * PANEL + pr;
+  const unsigned long long t0 = gtime();
+  int it = 0;
+  float sum = 0.0f;
+  bool done = !own;
+  for (;;) {
+    if (!done) {
+      bool all = true;
+      for (int rr = 0; rr < P && all; ++rr) all = tag_ok(ld_tv_sys(xb + (size_t)rr * HID + r), tag);
+      if (all) {
+        sum = tv_val(ld_tv_sys(xb + r));
+        for (int rr = 1; rr < P; ++rr) sum = __fadd_rn(sum, tv_val(ld_tv_sys(xb + (size_t)rr * HID + r)));
+        done = true;
       }
     }
-    if (good && own) st_tv(tv_h + r, __fadd_rn(hs[r], sum), tag);
+    if (__all_sync(0xffffffffu, done)) break;
+    if (((++it) & 63) == 0) {
+      int bad = 0;
+      if (lane == 0) {
+        if (*(volatile int*)&ms->abort || ld_flag(abort_flag)) {
+          bad = 1;
+        } else if (gtime() - t0 > WAIT_NS) {
+          record_error(err, abort_flag, ms, ERR_WAIT, 23, sub);
+          bad = 1;
+        }
+      }
+      if (__shfl_sync(0xffffffffu, bad, 0)) return false;
+    }
   }
-  return good != 0;
+  if (own) st_tv(tv_h + r, __fadd_rn(hres, sum), tag);
+  return true;
 }
 
-// A GEMV phase over panels (IN, OUT, GATEUP, DOWN).  The input vector is
-// encoded once into the CTA's digit image:
-//   W8A32 (default): the input wait folds max|v| of the values as they arrive
-//     (v = z = h * (1 + w) for the normed input of IN / GATEUP, else x), so one
-//     barrier after the wait (encode_fixed) completes the image.  The 1/rms of
-//     a normed input (sum of squares in numpy's pairwise order,
-//     golden/model.py:74) is computed by warp 0 while the other warps run the
-//     tasks, and applied with 2^-shift when the panel finishes.
-//   ACT_INT8: the golden per-vector quantiser of x itself (cta_encode_1024,
+// mma.m16n8k32 with signed int8 A (weights) and unsigned int8 B (digits).
+__device__ __forceinline__ void mma_s8u8(int (&d)[4], const unsigned (&a)[4], uint2 b) {
+  asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+               "{%0,%1,%2,%3};"
+               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
+}
+// Sums of the 16 rows of a panel over ns K-steps (a multiple of 4) of a
+// slice: A at shared address a (K-step s at a + 512 s), B = the slice's three
+// unsigned digit planes (columns 0-2, from the image fr in the B-fragment
+// order of dig_off) and a column of ones (column 3: the rows' weight sums);
+// four independent accumulator chains.  Lane u = 0 returns row g's S0, S1,
+// S2, Sw (g = lane / 4), lane u = 1 row g + 8's; lanes u = 2, 3 nothing.
+__device__ __forceinline__ void slice_mma(unsigned a, const unsigned char* fr, int ns, int (&d4)[4]) {
+  const int lane = threadIdx.x & 31;
+  int c[4][4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) c[u][0] = c[u][1] = c[u][2] = c[u][3] = 0;
+  a += 16u * lane;
+  const unsigned char* fb = fr + 8 * lane;
+  const bool dig = lane < 12;
+  const uint2 ones = lane < 16 ? make_uint2(0x01010101u, 0x01010101u) : make_uint2(0u, 0u);
+#pragma unroll 1
+  for (int s = 0; s < ns; s += 4) {
+    unsigned w[4][4];
+    uint2 b[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      ldsm_x4(a + 512u * (s + u), w[u]);
+      b[u] = dig ? *reinterpret_cast<const uint2*>(fb + 96 * (s + u)) : ones;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) mma_s8u8(c[u], w[u], b[u]);
+  }
+  int r[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) r[e] = (c[0][e] + c[1][e]) + (c[2][e] + c[3][e]);
+  const int u = lane & 3;
+  const int x = __shfl_xor_sync(0xffffffffu, u == 0 ? r[2] : r[0], 1);
+  const int y = __shfl_xor_sync(0xffffffffu, u == 0 ? r[3] : r[1], 1);
+  d4[0] = u == 0 ? r[0] : x;
+  d4[1] = u == 0 ? r[1] : y;
+  d4[2] = u == 0 ? x : r[2];
+  d4[3] = u == 0 ? y : r[3];
+}
+
+// Ring slots a warp refills at the top of the next phase: up to two runs of
+// chunks were fully read (Misc::rfq[warp]: first | count << 16); chunk + NSLOT
+// goes into each one's slot.
+__device__ __forceinline__ void note_refill(Misc* ms, int a, int n) {
+  int* q = ms->rfq[threadIdx.x >> 5];
+  if ((threadIdx.x & 31) == 0) q[q[0] != 0] = a | n << 16;
+  __syncwarp();
+}
+__device__ __forceinline__ void do_refills(PCtx& c) {
+  const int lane = threadIdx.x & 31;
+  int* q = c.ms->rfq[threadIdx.x >> 5];
+  for (int r = 0; r < 2; ++r) {
+    const int a = q[r] & 0xffff, n = q[r] >> 16;
+    if (lane < n) {
+      const int ii = a + lane, nx = ii + NSLOT;
+      if (nx < c.nch && !*(volatile int*)&c.ms->abort) {
+        issue_chunk(c, nx);
+        c.ms->slot_last[ii % NSLOT] = nx;
+      }
+    }
+  }
+  __syncwarp();
+  if (lane == 0) q[0] = q[1] = 0;
+  __syncwarp();
+}
+
+// A GEMV phase over panels (IN, OUT, GATEUP, DOWN).
+//   Before the input arrives, warp v < npan stages panel v's row scales in
+//   shared memory and every warp waits for its first task's chunk.
+//   The input vector is then encoded once into the CTA's digit image:
+//     W8A32 (default): the input wait folds max|v| of the values as they
+//     arrive (v = z = h * (1 + w) for the normed input of IN / GATEUP, else x)
+//     and, for a normed input, each warp's sum of h^2; one barrier after the
+//     wait (encode_fixed) completes the image.  The 1/rms
+//     (golden/model.py:63-75) is applied with 2^-shift when a panel finishes.
+//     ACT_INT8: the golden per-vector quantiser of x itself (cta_encode_1024,
 //     encode_lin).
-// Every warp runs its own tasks; a task adds exact int32 digit sums into its
-// panel's accumulators.  After a CTA barrier, warp v % NCW finishes the v-th
-// panel of the CTA's phase: the projection rows (IN), silu(gate) * up
-// (GATEUP, golden/model.py:236), or h + y (OUT, DOWN); the fp32 in_proj_b /
-// in_proj_a rows of a DeltaNet IN (golden/model.py:146-147) are dotted with x
-// by their tasks.
-template <bool TP>
+//   Task t runs on warp t % NCW and adds exact int32 digit sums into its
+//   panel's accumulators.  The warp that completes a panel's last task
+//   finishes the panel -- the projection rows (IN), silu(gate) * up (GATEUP,
+//   golden/model.py:236), or h + y (OUT, DOWN; under TP the partial rows are
+//   exchanged first) -- and refills the panel's ring slots.  No CTA barrier
+//   between tasks and outputs.
+// Every piece of the phase's code appears once (one wait, one encode), so a
+// GEMV CTA's instruction working set stays small.  (The fp32 in_proj_b /
+// in_proj_a rows of a DeltaNet IN are dotted by the heads' own CTAs,
+// gate_inputs.)
+template <bool TP, bool I8, bool NORMED>
 __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
   float* hs = (float*)(c.sm + OFF_HS);
-  const float* xf = (const float*)(c.sm + OFF_XF);
+  float* xf = (float*)(c.sm + OFF_XF);
+  float* zb = (float*)(c.sm + OFF_DIG);   // silu(z) of the gated norm, parked in the digit region
   const int l = p / 5, sub = p % 5;
   const LayerW& L = c.lay[l];
-  const bool i8 = ms->act_int8 != 0;
-  const bool normed = sub == 0 || sub == 3;
-  const float* gw = sub == 0 ? L.in_norm : L.post_norm;
+  constexpr bool normed = NORMED;   // IN, GATEUP (else OUT, DOWN)
+  const bool gated = sub == 2 && L.linear;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int nj = i1 - i0;
   trace_warp(c, p, 0);
   int good = 1;
-  if (nj > NSLOT) {   // the schedule keeps a phase within the ring (MAXPAN panels, MAXTASK tasks)
+  if (nj > NSLOT) {   // the schedule keeps a phase within the ring (MAXPAN panels)
     if (threadIdx.x == 0) check_fail(c, 8, nj);
     good = 0;
   }
-  const TaskMap m = task_map(c, kwin_t<TP>(A, sub), i0, good ? nj : 0);
-  // W8A32 normed inputs: warp 0 computes 1/rms, so tasks start at warp 1
-  const int off = (normed && !i8) ? 1 : 0;
-  const int t_first = (wid + NCW - off) % NCW;
+  const unsigned kw = kwin_t<TP>(A, sub);
+  const TaskMap m = task_map(c, kw, i0, good ? nj : 0);
+  const int tpp = m.npan > 0 ? m.ntask / m.npan : 1;      // tasks per panel (same window for all)
+  const int cpp = m.npan > 0 ? nj / m.npan : 1;           // chunks per panel
   // panel row of this lane in the finishing step (lanes with lane & 2 hold none)
   const bool own = (lane & 2) == 0;
   const int pr = (lane >> 2) + 8 * (lane & 1);
-  // before the input wait, so that their latency hides behind it: the row
-  // scales of the (at most two) panels this warp finishes, the norm gains of
-  // its first task's positions, and its first chunk (requested in an earlier
-  // phase, so waiting for it here cannot hold anything up)
-  float sp[2] = {0.0f, 0.0f};
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int v = wid + NCW * u;
-    if (v < m.npan) {
-      const float* sc = row_scale(L, sub, (int)c.ch[i0 + panel_chunk(m, v)].row0, pr);
-      if (own) sp[u] = __ldg(sc);
-    }
+  float* psc = (float*)(c.sm + OFF_PSC);
+  if (wid < m.npan) {
+    const int fc = panel_chunk(m, wid);   // (a warp collective: every lane)
+    if (lane < PANEL) psc[wid * PANEL + lane] = __ldg(row_scale(L, sub, (int)c.ch[i0 + fc].row0, lane));
   }
-  const float2 g2 = normed ? __ldg(reinterpret_cast<const float2*>(gw) + threadIdx.x) : make_float2(0.f, 0.f);
+  const float2 g2 = normed ? __ldg(reinterpret_cast<const float2*>(sub == 0 ? L.in_norm : L.post_norm) + threadIdx.x)
+                           : make_float2(0.f, 0.f);
+  const float gwn = gated ? __ldg(L.gnorm_w + (threadIdx.x % LV)) : 0.0f;
+  // the first task's chunk (requested in an earlier phase, so waiting for it
+  // here cannot hold anything up)
   bool first_in = false;
-  if (good && t_first < m.ntask) {
+  if (good && wid < m.ntask) {
     int q;
-    first_in = wait_full(c, i0 + task_chunk(m, t_first, q));
+    first_in = wait_full(c, i0 + task_chunk(m, wid, q));
     if (!first_in) good = 0;
     trace_warp(c, p, 3);
   }
-  // the input vector (W8A32: its max folded into amax by the wait)
-  float sx = 0.0f, xs = 0.0f;
-  unsigned* amax = i8 ? nullptr : &ms->amax[p & 1];
-  int k0 = 0, k1 = HID;   // the input window (positions of the digit image)
-  if (normed) {
-    if (sub == 0 && l == 0) {
-      // residual stream starts at the dequantised embedding row (golden/model.py:246)
-      const int tok = ms->tok;
-      const float sc = __ldg(A.emb_s + tok);
-      const int8_t* row = A.emb_q + (size_t)tok * HID;
-      const float h0 = __fmul_rn((float)row[2 * threadIdx.x], sc), h1 = __fmul_rn((float)row[2 * threadIdx.x + 1], sc);
-      hs[2 * threadIdx.x] = h0;
-      hs[2 * threadIdx.x + 1] = h1;
-      if (amax) {
-        const float vm = fmaxf(fabsf(__fmul_rn(h0, __fadd_rn(1.0f, g2.x))), fabsf(__fmul_rn(h1, __fadd_rn(1.0f, g2.y))));
-        const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(vm));
-        if (lane == 0 && wm) asm volatile("red.shared.max.u32 [%0], %1;" :: "r"(smem_u32(amax)), "r"(wm) : "memory");
-      }
-      consumer_sync();
-    } else if (!wait_tagged_max(c, A.tv_h, HID, tag_of(c, p - 1), hs, amax, true, g2)) {
+  // The inputs, polled together.  Normed (IN, GATEUP): the residual stream h
+  // (golden/model.py:142,262) into hs.  OUT (sub 2) and DOWN (sub 4): the
+  // projection's input -- the delta-rule output o (DeltaNet OUT, gated
+  // below), the gated attention output o * sigmoid(gate) written by the merge
+  // (attention OUT), or silu(gate) * up (DOWN) -- over the phase's K window
+  // [k0, k1) (kwin: all of it, or the rank's columns under tensor
+  // parallelism) into xf at its positions; for the gated norm silu(z) of the
+  // window (IN(l) wrote it); and the residual stream the projection is added
+  // to (golden/model.py:259,263), unless hs holds it already.  Layer 0 starts
+  // from the dequantised embedding row (golden/model.py:246).
+  unsigned* amax = I8 ? nullptr : &ms->amax[p & 1];
+  const int k0 = normed ? 0 : (int)(kw & 0xffffu), k1 = normed ? HID : (int)(kw >> 16);
+  const unsigned need = tag_of(c, normed ? p - 1 : (p == 2 ? -1 : (sub == 4 ? p - 2 : p - 3)));
+  const bool embed = need == tag_of(c, -1) && ms->hs_tag != need;   // layer 0: the embedding row into hs
+  if (embed) {
+    const int tok = ms->tok;
+    const float sc = __ldg(A.emb_s + tok);
+    const int8_t* row = A.emb_q + (size_t)tok * HID;
+    for (int i = threadIdx.x; i < HID; i += PT) hs[i] = __fmul_rn((float)row[i], sc);
+  }
+  const bool need_h = !embed && ms->hs_tag != need;
+  if constexpr (NORMED) {
+    const WSeg sh{A.tv_h, hs, need_h ? HID / 2 : 0, need}, none{A.tv_h, hs, 0, 0u};
+    if (!wait_inputs(ms, A.err, A.abort_flag, sh, none, none, amax, true, g2, I8 ? nullptr : ms->ssw))
       return false;
+  } else {
+    const unsigned long long* src = sub == 4 ? A.tv_act : (L.linear ? A.tv_o : A.tv_attn);
+    const WSeg sx_{src + k0, xf + k0, (k1 - k0) / 2, tag_of(c, p - 1)};
+    const WSeg sz{A.tv_z + k0, zb + k0, gated ? (k1 - k0) / 2 : 0, tag_of(c, p - 2)};
+    const WSeg sr{A.tv_h, hs, need_h ? HID / 2 : 0, need};
+    if (!wait_inputs(ms, A.err, A.abort_flag, sx_, sz, sr, gated ? nullptr : amax, false, make_float2(0.f, 0.f),
+                     nullptr))
+      return false;
+  }
+  if (embed && normed && amax) {
+    // (the embedding row did not pass through the wait: fold it here)
+    const float h0 = hs[2 * threadIdx.x], h1 = hs[2 * threadIdx.x + 1];
+    const float vm = fmaxf(fabsf(__fmul_rn(h0, __fadd_rn(1.0f, g2.x))), fabsf(__fmul_rn(h1, __fadd_rn(1.0f, g2.y))));
+    const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(vm));
+    if (lane == 0 && wm) asm volatile("red.shared.max.u32 [%0], %1;" :: "r"(smem_u32(amax)), "r"(wm) : "memory");
+    const float ss = warp_sum(fmaf(h1, h1, __fmul_rn(h0, h0)));
+    if (lane == 0) ms->ssw[wid] = ss;
+    consumer_sync();
+  }
+  if (threadIdx.x == 0) ms->hs_tag = need;
+  trace_warp(c, p, 1);
+  if (gated) {
+    // gated RMSNorm of the delta-rule output (golden/model.py:183-189) over the
+    // window's heads
+    for (int h = k0 / LV + wid; h < k1 / LV; h += NCW) {
+      float ss = 0.0f;
+      for (int i = lane; i < LV; i += 32) ss = fmaf(xf[h * LV + i], xf[h * LV + i], ss);
+      ss = warp_sum(ss);
+      // (ss / LV: LV is a power of two, so the product by 1/LV is the same number)
+      if (lane == 0) ms->inv_h[h] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(ss, 1.0f / LV), EPS)));
     }
-    trace_mark(c, p, 1);
-    trace_warp(c, p, 1);
-    if (threadIdx.x == 0) ms->hs_tag = tag_of(c, p - 1);   // layer 0: the embedding (tag of "phase -1")
-    if (i8) {
+    consumer_sync();
+    float vmax = 0.0f;
+    for (int i = k0 + threadIdx.x; i < k1; i += PT) {
+      const float v = __fmul_rn(__fmul_rn(xf[i], ms->inv_h[i / LV]), gwn);
+      xf[i] = __fmul_rn(v, zb[i]);
+      vmax = fmaxf(vmax, fabsf(xf[i]));
+    }
+    if (amax) {
+      const unsigned wm = __reduce_max_sync(0xffffffffu, __float_as_uint(vmax));
+      if (lane == 0 && wm) asm volatile("red.shared.max.u32 [%0], %1;" :: "r"(smem_u32(amax)), "r"(wm) : "memory");
+    }
+    consumer_sync();
+  }
+  trace_mark(c, p, 1);
+  // the digit image
+  float sx = 0.0f, xs = 0.0f;
+  if constexpr (I8) {
+    if (normed) {
       float inv;
       cta_encode_1024(c, hs, g2, true, inv, sx, false, p);
+    } else if constexpr (TP) {
+      if (!tp_encode_i8(c, p, k0, k1)) return false;
     } else {
-      xs = encode_fixed(c.sm, hs, 0, HID, *amax, true, g2);
-    }
-    if (!i8 && wid == 0) {
-      // sum of squares in numpy's pairwise order: chain ch = block ch / 8,
-      // accumulator ch % 8 (lane = chains lane, lane + 32: blocks 0-3, 4-7),
-      // ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)) in a block, then the
-      // blocks pairwise; the two halves summed last
-      float r[2];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int ch = lane + 32 * u;
-        const float* a = hs + 128 * (ch >> 3) + (ch & 7);
-        float acc = __fmul_rn(a[0], a[0]);
-#pragma unroll
-        for (int i = 1; i < 16; ++i) acc = __fadd_rn(acc, __fmul_rn(a[8 * i], a[8 * i]));
-        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
-        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
-        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
-        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
-        acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 16));
-        r[u] = acc;
-      }
-      const float tot = __fadd_rn(r[0], r[1]);
-      // tot / HID as the product by 1/HID (HID a power of two: the same
-      // number); 1/sqrt through the correctly rounded reciprocal
-      if (lane == 0) ms->xinv = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(tot, 1.0f / HID), EPS)));
-      trace_warp(c, p, 8);
+      encode_lin(c, k1, true);
     }
   } else {
-    if (!prologue<TP>(c, p, amax, k0, k1)) return false;
-    trace_mark(c, p, 1);
-    if (!i8) xs = encode_fixed(c.sm, xf, k0, k1, *amax, false, g2);
+    if constexpr (NORMED) xs = encode_u8(c.sm, hs, 0, HID, *amax, sub == 0 ? L.in_norm : L.post_norm);
+    else xs = encode_u8(c.sm, xf, k0, k1, *amax, nullptr);
+    // every thread has read amax: re-arm it for phase p + 2
+    if (threadIdx.x == 0) *amax = 0u;
   }
   trace_warp(c, p, 2);
+  // x scale of the digit sums: ACT_INT8 the quantiser's s_x; W8A32 2^-shift,
+  // times 1/rms for a normed input (exact: a power of two times a float), the
+  // rms from the warps' sums of h^2 (golden/model.py:74: mean over HID)
+  float xsc = xs;
+  if constexpr (I8) {
+    xsc = (float)ms->scale;
+  } else if (normed) {
+    float tot = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) tot = __fadd_rn(tot, ms->ssw[w]);
+    // tot / HID as the product by 1/HID (HID a power of two: the same number);
+    // 1/sqrt through the correctly rounded reciprocal
+    xsc = __fmul_rn(xs, __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(tot, 1.0f / HID), EPS))));
+  }
   const unsigned char* fr = c.sm + OFF_DIG;                   // the CTA's digit image
-  float* part_f = (float*)(c.sm + OFF_PARTF);
   const unsigned part = smem_u32(c.sm + OFF_PART);
-  const int nd = i8 ? ms->ndig : 3;
+  const int nd = I8 ? ms->ndig : 3;   // (W8A32: three unsigned digits and the weight sums)
   const unsigned tag = tag_of(c, p);
-  for (int t = t_first; good && t < m.ntask; t += NCW) {
+  for (int t = wid; good && t < m.ntask; t += NCW) {
     int q;
     const int j = task_chunk(m, t, q);
     const int i = i0 + j;
     const Chunk k = c.ch[i];
-    const bool pan = (k.seg & CHUNK_PANEL) != 0;
-    if (!pan && !(sub == 0 && L.linear && k.seg >= 2)) {
+    if (!(k.seg & CHUNK_PANEL)) {
       if (lane == 0) check_fail(c, 9, i);
       good = 0;
       break;
     }
-    if (!(t == t_first && first_in) && !wait_full(c, i)) { good = 0; break; }
-    const unsigned char* slot = c.sm + OFF_RING + (i % NSLOT) * SLOT;
-    if (!pan) {
-      // row q of the chunk, dotted with x: under ACT_INT8 the encoder's x in
-      // xf; else z = h (1 + w), its 1/rms applied when the phase finishes
-      const float* row = (const float*)slot + q * HID;
-      float a = 0.0f;
-#pragma unroll 1
-      for (int u = 0; u < HID / 128; ++u) {
-        const int pos = 4 * (lane + 32 * u);
-        const float4 w4 = *reinterpret_cast<const float4*>(row + pos);
-        float4 x4;
-        if (i8) {
-          x4 = *reinterpret_cast<const float4*>(xf + pos);
-        } else {
-          const float4 h4 = *reinterpret_cast<const float4*>(hs + pos);
-          const float4 g4 = __ldg(reinterpret_cast<const float4*>(gw + pos));
-          x4 = make_float4(__fmul_rn(h4.x, __fadd_rn(1.0f, g4.x)), __fmul_rn(h4.y, __fadd_rn(1.0f, g4.y)),
-                           __fmul_rn(h4.z, __fadd_rn(1.0f, g4.z)), __fmul_rn(h4.w, __fadd_rn(1.0f, g4.w)));
-        }
-        a = fmaf(w4.x, x4.x, a);
-        a = fmaf(w4.y, x4.y, a);
-        a = fmaf(w4.z, x4.z, a);
-        a = fmaf(w4.w, x4.w, a);
-      }
-      a = warp_sum(a);
-      if (lane == 0) part_f[t * PANEL] = a;
-      continue;
-    }
+    if (!(t == wid && first_in) && !wait_full(c, i)) { good = 0; break; }
     const int kb = k0 + (int)k.nrows * PANEL_KB + TASK_KB * q;   // the task's first K position
-    const unsigned sa = smem_u32(slot) + 512u * (TASK_KB / 32) * q;
+    const unsigned sa = smem_u32(c.sm + OFF_RING + (i % NSLOT) * SLOT) + 512u * (TASK_KB / 32) * q;
     // task length: a multiple of 128; whole inputs (every K a multiple of TASK_KB) always TASK_KB
     const int kl = !TP ? TASK_KB : (k1 - kb < TASK_KB ? k1 - kb : TASK_KB);
-    int d3[3];
-    panel_mma(sa, fr, kb >> 5, kl >> 5, nd, d3);
+    int d4[4];
+    if constexpr (I8) {
+      int d3[3];
+      panel_mma(sa, fr, kb >> 5, kl >> 5, nd, d3);
+      d4[0] = d3[0];
+    } else {
+      slice_mma(sa, fr + 96 * (kb >> 5), kl >> 5, d4);
+    }
+    trace_warp(c, p, 5);
     const int vp = chunk_panel(m, j);
     if (own) {
-      const unsigned pv = part + 4u * (unsigned)(vp * 3 * PANEL + pr);
-      red_add_s32(pv, d3[0]);
-      if (nd == 3) {
-        red_add_s32(pv + 4u * PANEL, d3[1]);
-        red_add_s32(pv + 8u * PANEL, d3[2]);
+      const unsigned pv = part + 4u * (unsigned)(vp * 4 * PANEL + pr);
+      red_add_s32(pv, d4[0]);
+      if constexpr (!I8) {
+        red_add_s32(pv + 4u * PANEL, d4[1]);
+        red_add_s32(pv + 8u * PANEL, d4[2]);
+        red_add_s32(pv + 12u * PANEL, d4[3]);
       }
     }
-  }
-  trace_warp(c, p, 4);
-  if (!consumer_and(good)) return false;
-  trace_warp(c, p, 5);
-  // x scale of the digit sums: ACT_INT8 the quantiser's s_x; W8A32 2^-shift,
-  // times 1/rms for a normed input (exact: a power of two times a float)
-  const float xinv = (normed && !i8) ? ms->xinv : 1.0f;
-  const float xsc = i8 ? (float)ms->scale : __fmul_rn(xs, xinv);
-  if (threadIdx.x == 0 && amax) *amax = 0u;   // read by every thread before the task barrier
-  for (int v = wid; v < m.npan; v += NCW) {
-    const int q = (int)c.ch[i0 + panel_chunk(m, v)].row0;
+    // the last of the panel's tasks finishes it
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atom_add_acq_rel_cta(&ms->pcnt[vp], 1) == tpp - 1;
+    if (!__shfl_sync(0xffffffffu, last, 0)) continue;
+    const int fc = panel_chunk(m, vp);    // the panel's first chunk (a warp collective)
+    const int pq = (int)c.ch[i0 + fc].row0;
     float y = 0.0f;
     if (own) {
-      const float s_row = v < NCW ? sp[0] : (v < 2 * NCW ? sp[1] : __ldg(row_scale(L, sub, q, pr)));
       // the panel's exact sums, and the accumulators zeroed for the next phase
-      int* pv = (int*)(c.sm + OFF_PART) + v * 3 * PANEL + pr;
-      const int a0 = pv[0], a1 = pv[PANEL], a2 = pv[2 * PANEL];
-      pv[0] = 0;
-      pv[PANEL] = 0;
-      pv[2 * PANEL] = 0;
-      y = finish_f32(a0, a1, a2, nd, xsc * s_row);
+      int* pvp = (int*)(c.sm + OFF_PART) + vp * 4 * PANEL + pr;
+      if constexpr (I8) {
+        y = finish_f32(pvp[0], 0, 0, 1, xsc * psc[vp * PANEL + pr]);
+        pvp[0] = 0;
+      } else {
+        // the row's exact sum of w * X: sum of w * U minus 2^22 times the weight sum
+        const double xsum = fma((double)pvp[2 * PANEL], 65536.0, fma((double)pvp[PANEL], 256.0, (double)pvp[0])) -
+                            4194304.0 * (double)pvp[3 * PANEL];
+        y = (float)(xsum * (double)(xsc * psc[vp * PANEL + pr]));
+        pvp[0] = 0;
+        pvp[PANEL] = 0;
+        pvp[2 * PANEL] = 0;
+        pvp[3 * PANEL] = 0;
+      }
     }
+    if (lane == 0) ms->pcnt[vp] = 0;
     if (sub == 3) {
       // pair panel: lane pr = g holds gate row 8q + g, its neighbour the up row
       const float up = __shfl_xor_sync(0xffffffffu, y, 1);
-      if (own && (lane & 1) == 0) st_tv(A.tv_act + q * PAIR_ROWS + pr, __fmul_rn(silu_f(y), up), tag);
+      if (own && (lane & 1) == 0) st_tv(A.tv_act + pq * PAIR_ROWS + pr, __fmul_rn(silu_f(y), up), tag);
     } else if (own) {
-      const int r = q * PANEL + pr;
+      const int r = pq * PANEL + pr;
       if (sub == 0) {
         unsigned long long* out;
         int o;
@@ -1559,69 +1658,113 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
         for (int rr = 0; rr < A.tp_world; ++rr) st_tv_sys(A.xbuf[rr] + off, y, tag);
       }
     }
-  }
-  if (TP && (sub == 2 || sub == 4)) {
-    // this warp's panels (in the fp32 row-dot scratch, which OUT and DOWN do not use)
-    int* rows = (int*)(c.sm + OFF_PARTF);
-    for (int v = wid; v < m.npan; v += NCW) {
-      const int q = (int)c.ch[i0 + panel_chunk(m, v)].row0;
-      if (lane == 0) rows[v] = q;
+    if constexpr (TP) {
+      if (sub == 2 || sub == 4) {
+        if (!tp_reduce_panel(A.xbuf[A.tp_rank] + XB_PART + (size_t)(sub == 4) * TP_MAX * HID, A.tv_h, hs[pq * PANEL + pr], pq,
+                             A.tp_world, own, pr, tag, ms, A.err, A.abort_flag, sub)) {
+          good = 0;
+          break;
+        }
+      }
     }
-    __syncwarp();
-    if (!tp_reduce_rows(A.xbuf[A.tp_rank] + XB_PART + (size_t)(sub == 4) * TP_MAX * HID, A.tv_h, hs, rows,
-                        m.npan, A.tp_world, own, pr, tag, ms, A.err, A.abort_flag, sub))
-      return false;
+    // the panel's outputs are out: its slots can be refilled (every task that
+    // read them has finished).  The refill is left to the top of the next
+    // phase (the bulk-copy issue can wait for the copy engine), so that this
+    // warp reaches the phase's end at once.
+    trace_warp(c, p, 6);
+    if (lane == 0) trace_latest(c, p, 2);
+    note_refill(ms, i0 + fc, cpp);
   }
-  // the fp32 rows (W8A32: times 1/rms)
-  for (int t = wid; t < m.ntask; t += NCW) {
-    int q;
-    const Chunk k = c.ch[i0 + task_chunk(m, t, q)];
-    if (k.seg & CHUNK_PANEL) continue;
-    if (lane == 0) st_tv(A.tv_ab + (k.seg == 2 ? 0 : LH) + (int)k.row0 + q, __fmul_rn(part_f[t * PANEL], xinv), tag);
-  }
-  trace_mark(c, p, 2);
-  trace_warp(c, p, 6);
-  // the outputs are out: now give the slots back and refill them (off the
-  // phase's critical path)
-  for (int j = wid; j < nj; j += NCW) release_panel_chunk(c, i0 + j);
-  trace_warp(c, p, 7);
-  return true;
+  trace_warp(c, p, 4);
+  return good != 0;
 }
 
-// ---------------------------------------------------------------- DeltaNet item
+// ---------------------------------------------------------------- DeltaNet heads
+//
+// Every DeltaNet head has its own CTA (CTA h - h0 for the rank's heads
+// [h0, h1)), which runs no GEMV panel: during IN it computes the head's gate
+// inputs, during MIX the head's conv, gates, l2norm and delta rule.
 
-// (head h, value slice j) of linear layer l: conv+SiLU of the head's q/k and the
-// slice's v channels, gates, l2norm, delta rule on S[h][:, slice], raw o out.
-// golden/model.py:149-178.  512 threads: 0..127 q channels, 128..255 k channels,
-// 256..271 the slice's v channels, 272 the b/a gate inputs; the delta rule maps
-// thread t to column t & 15 and rows 4*(t >> 4) .. +3.  Uses the digit region
-// of smem as scratch.
-__device__ bool delta_item(PCtx& c, int p, int item) {
+// IN phase of linear layer l on head h's CTA: b = in_proj_b[h] . x and
+// a = in_proj_a[h] . x (fp32 rows, golden/model.py:146-147) with x the normed
+// layer input (golden/model.py:142; under ACT_INT8 its golden fake-quant,
+// golden/model.py:37-45, 143), kept in shared memory for the head's delta
+// rule in the MIX phase.  The rows are read before the input wait.
+__device__ bool gate_inputs(PCtx& c, int p, int h) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
   const LayerW& L = c.lay[p / 5];
-  const int h = item / NDSLICE, j = item % NDSLICE;
+  float* hs = (float*)(c.sm + OFF_HS);
+  const int t = threadIdx.x;
+  const bool i8 = ms->act_int8 != 0;
+  const float2 g2 = __ldg(reinterpret_cast<const float2*>(L.in_norm) + t);
+  const float2 wb = __ldg(reinterpret_cast<const float2*>(L.b_w + (size_t)h * HID) + t);
+  const float2 wa = __ldg(reinterpret_cast<const float2*>(L.a_w + (size_t)h * HID) + t);
+  if (p == 0) {
+    // the residual stream starts at the dequantised embedding row (golden/model.py:246)
+    const int tok = ms->tok;
+    const float sc = __ldg(A.emb_s + tok);
+    const int8_t* row = A.emb_q + (size_t)tok * HID;
+    hs[2 * t] = __fmul_rn((float)row[2 * t], sc);
+    hs[2 * t + 1] = __fmul_rn((float)row[2 * t + 1], sc);
+    consumer_sync();
+  } else if (!wait_tagged(c, A.tv_h, HID, tag_of(c, p - 1), hs)) {
+    return false;
+  }
+  trace_mark(c, p, 1);
+  float inv, sx;
+  cta_encode_1024(c, hs, g2, i8, inv, sx);   // x (W8A8: fake-quantised) into xf[2t], xf[2t + 1]
+  const float2 x = *reinterpret_cast<const float2*>(c.sm + OFF_XF + 8 * t);
+  float pb = fmaf(wb.y, x.y, __fmul_rn(wb.x, x.x));
+  float pa = fmaf(wa.y, x.y, __fmul_rn(wa.x, x.x));
+  pb = warp_sum(pb);
+  pa = warp_sum(pa);
+  if ((t & 31) == 0) {
+    ms->red[t >> 5] = pb;
+    ms->red[NCW + (t >> 5)] = pa;
+  }
+  consumer_sync();
+  if (t == 0) {
+    float b = 0.0f, a = 0.0f;
+    for (int w = 0; w < NCW; ++w) { b += ms->red[w]; a += ms->red[NCW + w]; }
+    ms->abv[0] = b;
+    ms->abv[1] = a;
+  }
+  trace_mark(c, p, 2);
+  return true;
+}
+
+// MIX phase of linear layer l on head h's CTA: conv+SiLU of the head's q/k/v
+// channels, gates (from gate_inputs), l2norm, the delta rule on S[h] and the
+// raw o out (golden/model.py:149-178).  512 threads: 0..127 q channels,
+// 128..255 k channels, 256..383 v channels, 384 the gates; the delta rule
+// maps thread t to value column t % 128 and state rows 32 (t / 128) .. +31.
+// Uses the digit region of smem as scratch.
+__device__ bool delta_head(PCtx& c, int p, int h) {
+  const PersistArgs& A = *c.A;
+  Misc* ms = c.ms;
+  const LayerW& L = c.lay[p / 5];
   const int t = threadIdx.x;
   const int lin = L.lin_idx;
   const int base = ms->conv_base;
+  constexpr int NG = PT / LV;                                      // 4 row groups
+  constexpr int KPG = LK / NG;                                     // 32 rows each
   float* qs = (float*)(c.sm + OFF_DIG);
   float* ks = qs + LK;
   float* vs = ks + LK;
-  float* wsq = vs + 32;                                           // [16] per-warp sums
-  float (*part)[DSLICE + 1] = reinterpret_cast<float (*)[DSLICE + 1]>(wsq + 16);  // [32][17]
+  float* wsq = vs + LV;                                            // [16] per-warp sums
+  float (*part)[LV] = reinterpret_cast<float (*)[LV]>(wsq + 16);  // [4][128]
   float* cs = A.conv + (size_t)lin * CONVD * CONVK;
   float* Sh = A.rec + ((size_t)lin * LH + h) * LK * LV;
-  const int v0 = j * DSLICE;
-  const int vi = t & 15, kg = t >> 4;                              // 32 groups of 4 rows
-  constexpr int KPG = LK / 32;
-  // prefetch the state slice, conv history and taps (previous launches wrote them)
+  const int vi = t & (LV - 1), kg = t / LV;
+  // prefetch the state, conv history and taps (previous launches wrote them)
   float sv[KPG];
 #pragma unroll
-  for (int kk = 0; kk < KPG; ++kk) sv[kk] = Sh[(size_t)(kg * KPG + kk) * LV + v0 + vi];
-  const int role = (t < 2 * LK) ? 0 : (t < 2 * LK + DSLICE ? 1 : (t == 2 * LK + DSLICE ? 2 : 3));
+  for (int kk = 0; kk < KPG; ++kk) sv[kk] = Sh[(size_t)(kg * KPG + kk) * LV + vi];
+  const int role = (t < 2 * LK) ? 0 : (t < 2 * LK + LV ? 1 : (t == 2 * LK + LV ? 2 : 3));
   int ch = 0;
   if (role == 0) ch = (t < LK) ? (h * LK + t) : (KDIM + h * LK + (t - LK));
-  else if (role == 1) ch = 2 * KDIM + h * LV + v0 + (t - 2 * LK);
+  else if (role == 1) ch = 2 * KDIM + h * LV + (t - 2 * LK);
   float s1 = 0.f, s2 = 0.f, s3 = 0.f;
   float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
   if (role <= 1) {
@@ -1630,20 +1773,17 @@ __device__ bool delta_item(PCtx& c, int p, int item) {
     w4 = *reinterpret_cast<const float4*>(L.conv_w + (size_t)ch * CONVK);
   }
   const float alog = __ldg(L.A_log + h), dtb = __ldg(L.dt_bias + h);
-  // wait for this token's projections (tagged, from IN)
+  // wait for this token's q/k/v projections of the head (tagged, from IN)
   const unsigned tin = tag_of(c, p - 1);
   const unsigned long long t0 = gtime();
-  float nv = 0.f, bb = 0.f, aa = 0.f;
-  bool have = (role == 3);
+  float nv = 0.f;
+  bool have = (role >= 2);
   int it = 0;
   if (t == 0) ms->pend_min = 0x7fffffff;
   for (;;) {
-    unsigned long long w = 0, w2 = 0;
     if (!have) {
-      if (role <= 1) w = ld_tv(A.tv_qkv + ch);
-      else { w = ld_tv(A.tv_ab + h); w2 = ld_tv(A.tv_ab + LH + h); }
-      if (role <= 1 && tag_ok(w, tin)) { nv = tv_val(w); have = true; }
-      if (role == 2 && tag_ok(w, tin) && tag_ok(w2, tin)) { bb = tv_val(w); aa = tv_val(w2); have = true; }
+      const unsigned long long w = ld_tv(A.tv_qkv + ch);
+      if (tag_ok(w, tin)) { nv = tv_val(w); have = true; }
     }
     if (consumer_and(have)) break;
     if (((++it) & 15) == 0) {
@@ -1654,12 +1794,11 @@ __device__ bool delta_item(PCtx& c, int p, int item) {
       }
       if (!consumer_and(st == 0)) {
         if (!consumer_and(!(t == 0 && st == 2))) {
-          // report what is missing: q/k, v, gate words, and the lowest missing channel
-          if (!have && role <= 1) atomicMin(&ms->pend_min, ch);
+          // report what is missing: q/k, v, and the lowest missing channel
+          if (!have) atomicMin(&ms->pend_min, ch);
           const int pq = consumer_or(!have && role == 0), pv = consumer_or(!have && role == 1);
-          const int pg = consumer_or(!have && role == 2);
           const int lo = (pq | pv) ? (ms->pend_min & 0x7ffff) : 0;   // a channel < CONVD
-          if (t == 0) raise_abort(c, 18, p | pq << 8 | pv << 9 | pg << 10 | lo << 12);
+          if (t == 0) raise_abort(c, 18, p | pq << 8 | pv << 9 | lo << 12);
         }
         return false;
       }
@@ -1672,12 +1811,11 @@ __device__ bool delta_item(PCtx& c, int p, int item) {
     acc = __fadd_rn(acc, __fmul_rn(s3, w4.z));
     acc = __fadd_rn(acc, __fmul_rn(nv, w4.w));
     x = silu_f(acc);
-    // the dead oldest column takes the newest value (q/k channels: slice 0 only)
-    if (role == 1 || j == 0) cs[(size_t)ch * CONVK + (base & 3)] = nv;
+    cs[(size_t)ch * CONVK + (base & 3)] = nv;   // the dead oldest column takes the newest value
     if (role == 1) vs[t - 2 * LK] = x;
   } else if (role == 2) {
-    ms->gate_beta = sigmoid_f(bb);
-    ms->gate_g = __fmul_rn(-expf(alog), softplus_f(__fadd_rn(aa, dtb)));
+    ms->gate_beta = sigmoid_f(ms->abv[0]);
+    ms->gate_g = __fmul_rn(-expf(alog), softplus_f(__fadd_rn(ms->abv[1], dtb)));
   }
   // l2norm of q (warps 0-3) and k (warps 4-7)
   const float ss = warp_sum(role == 0 ? x * x : 0.0f);
@@ -1691,7 +1829,8 @@ __device__ bool delta_item(PCtx& c, int p, int item) {
     else ks[t - LK] = __fmul_rn(x, inv);
   }
   consumer_sync();
-  // delta rule on the prefetched slice (same arithmetic as delta_slice in decode.cu)
+  // delta rule on the prefetched state: S *= exp(g); kv = k^T S; d = (v - kv) beta;
+  // S += k (x) d; o = q^T S (after the update)
   const float gexp = expf(ms->gate_g);
   float pkv = 0.0f;
 #pragma unroll
@@ -1703,7 +1842,7 @@ __device__ bool delta_item(PCtx& c, int p, int item) {
   consumer_sync();
   float kvv = 0.0f;
 #pragma unroll
-  for (int g = 0; g < 32; ++g) kvv += part[g][vi];
+  for (int g = 0; g < NG; ++g) kvv += part[g][vi];
   const float delta = __fmul_rn(__fsub_rn(vs[vi], kvv), ms->gate_beta);
   consumer_sync();
   float po = 0.0f;
@@ -1711,16 +1850,16 @@ __device__ bool delta_item(PCtx& c, int p, int item) {
   for (int kk = 0; kk < KPG; ++kk) {
     const int k = kg * KPG + kk;
     const float s2v = __fadd_rn(sv[kk], __fmul_rn(ks[k], delta));
-    Sh[(size_t)k * LV + v0 + vi] = s2v;
+    Sh[(size_t)k * LV + vi] = s2v;
     po = fmaf(s2v, qs[k], po);
   }
   part[kg][vi] = po;
   consumer_sync();
-  if (t < DSLICE) {
+  if (t < LV) {
     float o = 0.0f;
 #pragma unroll
-    for (int g = 0; g < 32; ++g) o += part[g][t];
-    st_tv(A.tv_o + h * LV + v0 + t, o, tag_of(c, p));
+    for (int g = 0; g < NG; ++g) o += part[g][t];
+    st_tv(A.tv_o + h * LV + t, o, tag_of(c, p));
   }
   consumer_sync();
   return true;
@@ -1961,9 +2100,10 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
 
 // ---------------------------------------------------------------- the kernel
 
-// TP: the tensor-parallel instance (launched when tp_world > 1); the other
-// instance compiles every exchange out.
-template <bool TP>
+// TP: the tensor-parallel instances (launched when tp_world > 1); the others
+// compile every exchange out.  I8: the ACT_INT8 (W8A8) instances; the W8A32
+// ones compile the int8 activation quantisers out of their GEMV phases.
+template <bool TP, bool I8>
 __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* sm = smem_raw;
@@ -1983,7 +2123,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
     ((int*)c.lay)[i] = ((const int*)A.layers)[i];
   for (int i = threadIdx.x; i < c.nch; i += NTHREADS) chs[i] = A.chunks[(size_t)blockIdx.x * MAXCH + i];
   for (int i = threadIdx.x; i <= NPHASE; i += NTHREADS) ms->pf[i] = A.phase_first[(size_t)blockIdx.x * (NPHASE + 1) + i];
-  for (int i = threadIdx.x; i < MAXPAN * 3 * PANEL; i += NTHREADS) ((int*)(sm + OFF_PART))[i] = 0;
+  for (int i = threadIdx.x; i < MAXPAN * 4 * PANEL; i += NTHREADS) ((int*)(sm + OFF_PART))[i] = 0;
+  if (threadIdx.x < 2 * NCW) ms->rfq[threadIdx.x >> 1][threadIdx.x & 1] = 0;
   if (threadIdx.x == 0) {
     ms->amax[0] = 0u;
     ms->amax[1] = 0u;
@@ -2001,9 +2142,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
     ms->tok = tok;
     for (int s = 0; s < NSLOT; ++s) {
       mbar_init(full_bar(c, s), 1);
-      mbar_init(empty_bar(c, s), NCW);
       mbar_init(mma_bar(c, s), 1);
       ms->slot_last[s] = -1;
+    ms->pcnt[s] = 0;
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf_bar(c, b), 1);
@@ -2045,12 +2186,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
     for (int p = 0; p < NPHASE && ok; ++p) {
       const int sub = p % 5;
       trace_mark(c, p, 0);
+      if (ms->rfq[threadIdx.x >> 5][0]) do_refills(c);   // the slots this warp's finished panels released
       if (p != PH_HEAD && sub == 1) {
         const LayerW& L = c.lay[p / 5];
         if (L.linear) {
-          // this rank's heads [dn_h0, dn_h1): one CTA per (head, value slice)
+          // this rank's heads [dn_h0, dn_h1): CTA j runs head dn_h0 + j
           const int h0 = TP ? A.dn_h0 : 0, nh = TP ? A.dn_h1 - A.dn_h0 : LH;
-          if ((int)blockIdx.x < nh * NDSLICE) ok = delta_item(c, p, h0 * NDSLICE + blockIdx.x);
+          if ((int)blockIdx.x < nh) ok = delta_head(c, p, h0 + blockIdx.x);
         } else {
           const int Tn = ms->T + 1;
           int nch = (Tn + ATT_MINLEN - 1) / ATT_MINLEN;
@@ -2066,13 +2208,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
       }
       // this phase's chunks, [i0, i1) of the CTA's list (counted loops only)
       const int i0 = ms->pf[p], i1 = ms->pf[p + 1];
+      const int nhead = TP ? A.dn_h1 - A.dn_h0 : LH;
+      if (p != PH_HEAD && sub == 0 && c.lay[p / 5].linear && (int)blockIdx.x < nhead) {
+        // a DeltaNet head's CTA: the head's gate inputs (it holds no panels)
+        ok = consumer_and(gate_inputs(c, p, (TP ? A.dn_h0 : 0) + blockIdx.x)) != 0;
+        trace_mark(c, p, 3);
+        continue;
+      }
       if (p == PH_HEAD) {
         ok = phase_head<TP>(c, p, i0, i1);       // every CTA joins the argmax merge
       } else if (i0 == i1) {                     // no rows of this phase on this CTA
         trace_mark(c, p, 3);
         continue;
       } else {
-        ok = phase_panels<TP>(c, p, i0, i1);
+        ok = (sub == 0 || sub == 3) ? phase_panels<TP, I8, true>(c, p, i0, i1)
+                                     : phase_panels<TP, I8, false>(c, p, i0, i1);
       }
       // the warps leave a GEMV phase independently; line them up again (and
       // make a failure in any warp the whole CTA's)
@@ -2121,27 +2271,38 @@ static_assert(OFF_DIG + (4 * HD + 2 * HD + 4 * ATT_MAXLEN) * 4 <= OFF_HS,
 // launcher, so the single-GPU kernel's code here is laid out without any of
 // the exchange paths (measured: 8 us per step when both shared one module).
 
-#ifdef QB_PERSIST_TP
-cudaError_t launch_persistent_tp(const PersistArgs& args, int G, cudaStream_t st) {
+// Launch one instance (cooperative: every CTA resident, one per SM).
+template <bool TP, bool I8>
+cudaError_t launch_instance(const PersistArgs& args, int G, cudaStream_t st) {
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_decode_persistent<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(k_decode_persistent<TP, I8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
   void* kargs[] = {(void*)&args};
-  return cudaLaunchCooperativeKernel((const void*)k_decode_persistent<true>, dim3(G), dim3(NTHREADS), kargs,
+  return cudaLaunchCooperativeKernel((const void*)k_decode_persistent<TP, I8>, dim3(G), dim3(NTHREADS), kargs,
                                      SMEM_BYTES, st);
 }
-int persist_tp_max_blocks_per_sm() {
-  int n = 0;
-  cudaFuncSetAttribute(k_decode_persistent<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_decode_persistent<true>, NTHREADS, SMEM_BYTES);
-  return n;
+// Resident CTAs per SM of the smaller of an instance pair.
+template <bool TP>
+int blocks_per_sm() {
+  int n0 = 0, n1 = 0;
+  cudaFuncSetAttribute(k_decode_persistent<TP, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  cudaFuncSetAttribute(k_decode_persistent<TP, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n0, k_decode_persistent<TP, false>, NTHREADS, SMEM_BYTES);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n1, k_decode_persistent<TP, true>, NTHREADS, SMEM_BYTES);
+  return n0 < n1 ? n0 : n1;
 }
+
+#ifdef QB_PERSIST_TP
+cudaError_t launch_persistent_tp(const PersistArgs& args, int G, cudaStream_t st, bool i8) {
+  return i8 ? launch_instance<true, true>(args, G, st) : launch_instance<true, false>(args, G, st);
+}
+int persist_tp_max_blocks_per_sm() { return blocks_per_sm<true>(); }
 #else
-cudaError_t launch_persistent_tp(const PersistArgs& args, int G, cudaStream_t st);   // persist_tp.cu
+cudaError_t launch_persistent_tp(const PersistArgs& args, int G, cudaStream_t st, bool i8);   // persist_tp.cu
 int persist_tp_max_blocks_per_sm();
 
 int persist_smem_bytes() { return SMEM_BYTES; }
@@ -2157,9 +2318,10 @@ size_t persist_trace_words(int G) {
 //     one CTA).  Each panel goes to the CTA with the fewest 4 KB tasks so far
 //     in the phase, then the fewest bytes so far in the step, then the lowest
 //     index, among the CTAs whose ring still holds the panel's chunks with the
-//     phase's others; the fp32 in_proj_a/b rows of a DeltaNet IN follow, 4 rows
-//     per chunk, by the same rule.
-//   HEAD: contiguous, balanced ranges of the 1940 tiles.
+//     phase's others.  The first nh CTAs (nh = the rank's DeltaNet heads) hold
+//     no panels: CTA j runs DeltaNet head dn_h0 + j (gate inputs in IN, the
+//     delta rule in MIX).
+//   HEAD: contiguous, balanced ranges of the 1940 tiles over every CTA.
 bool tp_plan(int rank, int world, TpPlan& out, std::string& err) {
   if (world != 1 && world != 2 && world != 4 && world != TP_MAX) { err = "tp world must be 1, 2, 4 or 8"; return false; }
   if (rank < 0 || rank >= world) { err = "tp rank outside [0, world)"; return false; }
@@ -2216,6 +2378,8 @@ bool build_schedule(const ModelW& M, int G, const TpPlan& tp, std::vector<Chunk>
   constexpr double T_ROUND = 0.2 + 0.5 * TASK_KB / 512.0;   // one task per warp
   constexpr double T_DELTA = 2.4, T_ATTN = 4.0;
   constexpr int ATT_CTAS = 20;   // CTAs running attention items at short contexts
+  const int nhead = tp.dn_h1 - tp.dn_h0;   // CTAs [0, nhead): the DeltaNet heads, no panels
+  if (G <= nhead) { err = "fewer CTAs than DeltaNet heads"; return false; }
   std::vector<double> freeb(G, 0.0);
   double ready = 0.0;            // when the current phase's input reaches an idle CTA
   for (int p = 0; p < NPHASE; ++p) {
@@ -2237,7 +2401,7 @@ bool build_schedule(const ModelW& M, int G, const TpPlan& tp, std::vector<Chunk>
     if (sub == 1) {
       double last = ready;
       for (int b = 0; b < G; ++b)
-        if (linear ? b < (tp.dn_h1 - tp.dn_h0) * NDSLICE : b < ATT_CTAS) {
+        if (linear ? b < nhead : b < ATT_CTAS) {
           freeb[b] = std::max(freeb[b], ready) + (linear ? T_DELTA : T_ATTN);
           last = std::max(last, freeb[b]);
         }
@@ -2283,7 +2447,7 @@ bool build_schedule(const ModelW& M, int G, const TpPlan& tp, std::vector<Chunk>
     auto least_fit = [&](int need, int add) {
       int best = -1;
       double fb = 0.0;
-      for (int b = 0; b < G; ++b) {
+      for (int b = nhead; b < G; ++b) {
         if (inph[b] + need > NSLOT) continue;
         const double f = fin_of(b, tasks[b] + add);
         if (best < 0 || f < fb - 1e-9 ||
@@ -2301,19 +2465,6 @@ bool build_schedule(const ModelW& M, int G, const TpPlan& tp, std::vector<Chunk>
       tasks[b] += ptasks;
       for (int j = 0; j < nslice; ++j)
         if (!push(b, p, CHUNK_PANEL, j, q, sl_bytes[j])) return false;
-    }
-    if (sub == 0 && linear) {
-      // in_proj_b (seg 2) and in_proj_a (seg 3): fp32 rows, 4 per chunk, one task per row
-      constexpr int per = SLOTW / (HID * 4);
-      for (int seg = 2; seg <= 3; ++seg)
-        for (int r = tp.dn_h0; r < tp.dn_h1; r += per) {
-          const int n = std::min(per, tp.dn_h1 - r);
-          const int b = least_fit(1, n);
-          if (b < 0) { err = "phase does not fit the rings"; return false; }
-          inph[b] += 1;
-          tasks[b] += n;
-          if (!push(b, p, seg, n, r, n * HID * 4)) return false;
-        }
     }
     double last = ready;
     for (int b = 0; b < G; ++b)
@@ -2370,25 +2521,14 @@ cudaError_t repack_panels(const int8_t* const* rowptr, int8_t* out, int nrows, i
   return cudaGetLastError();
 }
 
-cudaError_t launch_persistent(const PersistArgs& args, int G, cudaStream_t st) {
-  if (args.tp_world > 1) return launch_persistent_tp(args, G, st);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(k_decode_persistent<false>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
-  void* kargs[] = {(void*)&args};
-  return cudaLaunchCooperativeKernel((const void*)k_decode_persistent<false>, dim3(G), dim3(NTHREADS), kargs,
-                                     SMEM_BYTES, st);
+cudaError_t launch_persistent(const PersistArgs& args, int G, cudaStream_t st, bool i8) {
+  if (args.tp_world > 1) return launch_persistent_tp(args, G, st, i8);
+  return i8 ? launch_instance<false, true>(args, G, st) : launch_instance<false, false>(args, G, st);
 }
 
-// Resident CTAs per SM of the persistent kernel (the smaller of its two instances).
+// Resident CTAs per SM of the persistent kernel (the smallest of its instances).
 int persist_max_blocks_per_sm() {
-  int n = 0;
-  cudaFuncSetAttribute(k_decode_persistent<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_decode_persistent<false>, NTHREADS, SMEM_BYTES);
+  const int n = blocks_per_sm<false>();
   const int n1 = persist_tp_max_blocks_per_sm();
   return n < n1 ? n : n1;
 }

@@ -26,13 +26,14 @@ constexpr unsigned char CHUNK_MMA = 0x80;
 constexpr int PERSIST_NPHASE = NLAYER * 5 + 1;
 
 // Trace record layout: per CTA and phase, %globaltimer stamps at phase entry,
-// inputs arrived (the input wait done), outputs written (a GEMV phase; the
-// head: its first slab landed), phase exit; then,
-// for CTA 0 only, per phase and warp, clock64 stamps of a GEMV phase: 0 entry,
-// 1 input vector in, 2 digit image encoded, 3 first task's chunk landed, 4 own
-// tasks done, 5 CTA barrier passed, 6 panels finished, 7 slots released, and
-// inside the encoder of a normed input 8 norm statistics, 9 their barrier
-// passed, 10 digits written (0 = not reached).
+// inputs arrived (the input wait done), outputs written (a GEMV phase: its
+// last panel's; the head: its first slab landed), phase exit; then, for the
+// first GEMV CTA (the one after the DeltaNet heads' CTAs) only, per phase and
+// warp, clock64 stamps of a GEMV phase: 0 entry, 1 inputs in, 2 digit image
+// encoded, 3 first task's chunk landed, 4 own tasks done, 5 a task's MMA done,
+// 6 a panel's outputs written by this warp, and inside the W8A8 encoder of a
+// normed input 8 norm statistics, 9 their barrier passed, 10 digits written
+// (0 = not reached).
 constexpr int TRACE_STAMPS = 4;
 constexpr int TRACE_WARP_STAMPS = 16;
 
@@ -92,7 +93,7 @@ struct PersistArgs {
   const Chunk* chunks;         // [G][MAXCH]
   const unsigned short* phase_first;  // [G][PERSIST_NPHASE + 1]: a phase's chunks are
                                       // [first[p], first[p + 1]) of the CTA's list
-  unsigned long long *tv_h, *tv_qkv, *tv_z, *tv_ab, *tv_o, *tv_qg, *tv_kvn, *tv_attn, *tv_act;
+  unsigned long long *tv_h, *tv_qkv, *tv_z, *tv_o, *tv_qg, *tv_kvn, *tv_attn, *tv_act;
   float* conv; float* rec; float* kcache; float* vcache;
   float* att_part; int* att_cnt;   // att_cnt: [NFULL][NKV]
   int* head_cnt;
@@ -139,6 +140,7 @@ size_t persist_trace_words(int G);   // words of the trace record for G CTAs
 int persist_max_blocks_per_sm();
 bool build_schedule(const ModelW& M, int G, const TpPlan& tp, std::vector<Chunk>& chunks,
                     std::vector<unsigned short>& phase_first, std::string& err);
-cudaError_t launch_persistent(const PersistArgs& args, int G, cudaStream_t st);
+// i8: the ACT_INT8 instance (must match the step's StepDyn::act_int8).
+cudaError_t launch_persistent(const PersistArgs& args, int G, cudaStream_t st, bool i8);
 
 }  // namespace qb

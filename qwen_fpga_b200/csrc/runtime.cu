@@ -393,7 +393,7 @@ int launch_step(qwen_ctx* c) {
   if (c->engine == 1) {
     // a traced step starts from a cleared record (0 = stamp not reached)
     if (c->P.trace) QCUDA(c, cudaMemsetAsync(c->P.trace, 0, persist_trace_words(c->sm_count) * 8, c->st));
-    cudaError_t e = launch_persistent(c->P, c->sm_count, c->st);
+    cudaError_t e = launch_persistent(c->P, c->sm_count, c->st, c->act_int8 != 0);
     if (e != cudaSuccess) return fail(c, QWEN_ERR_CUDA, "persistent launch: %s", cudaGetErrorString(e));
   } else {
     QCUDA(c, cudaGraphLaunch(c->graph, c->st));
@@ -558,7 +558,7 @@ int create_impl(const char* blob_path, const char* index_path, int dev, int tp_r
   if ((rc = build_graph(c))) return bail(rc);
   {
     // persistent engine: tagged activation words, counters, per-CTA schedule
-    const size_t words = HID + CONVD + VDIM + 2 * LH + VDIM + QPROJ + 2 * KVPROJ + NH * HD + FFN;
+    const size_t words = HID + CONVD + VDIM + VDIM + QPROJ + 2 * KVPROJ + NH * HD + FFN;
     if ((rc = dalloc(c, &c->tv_base, words * 8))) return bail(rc);
     c->tv_words = words;
     PersistArgs& P = c->P;
@@ -566,7 +566,6 @@ int create_impl(const char* blob_path, const char* index_path, int dev, int tp_r
     P.tv_h = w; w += HID;
     P.tv_qkv = w; w += CONVD;
     P.tv_z = w; w += VDIM;
-    P.tv_ab = w; w += 2 * LH;
     P.tv_o = w; w += VDIM;
     P.tv_qg = w; w += QPROJ;
     P.tv_kvn = w; w += 2 * KVPROJ;
