@@ -1804,6 +1804,7 @@ __device__ bool delta_head(PCtx& c, int p, int h) {
       }
     }
   }
+  trace_mark(c, p, 1);
   float x = 0.0f;
   if (role <= 1) {
     float acc = __fmul_rn(s1, w4.x);
@@ -1861,6 +1862,7 @@ __device__ bool delta_head(PCtx& c, int p, int h) {
     for (int g = 0; g < NG; ++g) o += part[g][t];
     st_tv(A.tv_o + h * LV + t, o, tag_of(c, p));
   }
+  trace_mark(c, p, 2);
   consumer_sync();
   return true;
 }
@@ -1887,8 +1889,19 @@ __device__ __forceinline__ void warp_norm_rope_v(const float* v_in, const float 
   for (int q = 0; q < 8; ++q) dst[lane + 32 * q] = v[q];
 }
 
-// Split-KV item (kv group g, chunk cc) of attention layer l; the last item of a
-// group merges the partials and writes o * sigmoid(gate) (golden/model.py:194-229).
+// Split-KV item (kv group g, chunk cc of nch, positions [cc cl, min(cc cl + cl, T + 1)))
+// of attention layer l (golden/model.py:194-229).  The chunk's cached K / V
+// rows are read in blocks of ASB = 16 positions, the first block before this
+// token's projections can arrive and every next block while the current one
+// is used; scores, softmax and P V run as an online (flash-decoding) softmax
+// over the blocks: per head a running max m and sum l, and the unnormalised
+// output o.  Layouts of a block: K with warp = position, lane = 8 dims; V with
+// thread = (dim d, half h) holding positions 8 h .. 8 h + 7.  One chunk
+// (nch = 1): o / l * sigmoid(gate) goes straight to tv_attn.  Otherwise the
+// chunk's (m, l, o) of its four heads go out as tagged words (att_tv) and
+// chunk 0's CTA merges the group: M = max m_c, w_c = exp(m_c - M),
+// O = sum w_c o_c / sum w_c l_c, times sigmoid(gate) (golden/model.py:227-229).
+constexpr int ASB = 16;
 __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
@@ -1896,14 +1909,36 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
   const int T = ms->T, pos = ms->pos, Tn = T + 1;
   const int fi = L.full_idx;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int t0 = cc * cl, t1 = min(Tn, t0 + cl), n = t1 - t0;
+  const int t0 = cc * cl, t1 = min(Tn, t0 + cl);
+  const int tc = min(t1, T);                // positions [t0, tc) come from the cache
   float* qn = (float*)(c.sm + OFF_DIG);    // [4][256] normed + roped queries
   float* kn = qn + 4 * HD;                  // [256] new key
   float* vn = kn + HD;                      // [256] new value
   float* raw = vn + HD;                     // [6][256] projections as read (q x4, k, v)
-  float* sc = raw;                          // [4][ATT_MAXLEN] scores, after raw is consumed
-  const unsigned tin = tag_of(c, p - 1);
-  // prefetch this warp's norm gains and RoPE cos/sin before waiting
+  float* sp = raw;                          // [4][ASB] scores, then probabilities (after raw is consumed)
+  float* st = sp + 4 * ASB;                 // [4] running max, [4] running sum, [4] rescale
+  float* ox = st + 12;                      // [4][256] the second half's o
+  const unsigned tin = tag_of(c, p - 1), tout = tag_of(c, p);
+  const float* kc = A.kcache + (size_t)fi * A.max_ctx * KVPROJ + g * HD;
+  const float* vc = A.vcache + (size_t)fi * A.max_ctx * KVPROJ + g * HD;
+  const int d = threadIdx.x & (HD - 1), half = threadIdx.x >> 8;
+  // block registers: K (this warp's position, dims 8 lane ..) and V (dim d, 8 positions)
+  float kr[8], vr[8];
+  auto load_block = [&](int s0) {
+    const int tk = s0 + wid;
+    if (tk < tc) {
+      const float4 a = *reinterpret_cast<const float4*>(kc + (size_t)tk * KVPROJ + 8 * lane);
+      const float4 b = *reinterpret_cast<const float4*>(kc + (size_t)tk * KVPROJ + 8 * lane + 4);
+      kr[0] = a.x; kr[1] = a.y; kr[2] = a.z; kr[3] = a.w; kr[4] = b.x; kr[5] = b.y; kr[6] = b.z; kr[7] = b.w;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int tv = s0 + 8 * half + j;
+      vr[j] = tv < tc ? vc[(size_t)tv * KVPROJ + d] : 0.0f;
+    }
+  };
+  load_block(t0);
+  // this warp's norm gains and RoPE cos/sin, before waiting
   float nw[8];
   const float* wsrc = (wid < 4) ? L.qn_w : L.kn_w;
 #pragma unroll
@@ -1952,150 +1987,158 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
       }
     }
   }
+  trace_mark(c, p, 1);
   if (wid < 5) warp_norm_rope_v(raw + wid * HD, nw, rco, rsi, wid < 4 ? qn + wid * HD : kn);   // kn follows qn
-  else if (wid == 5) for (int d = lane; d < HD; d += 32) vn[d] = raw[5 * HD + d];
+  else if (wid == 5) for (int e = lane; e < HD; e += 32) vn[e] = raw[5 * HD + e];
   consumer_sync();
-  float* kc = A.kcache + (size_t)fi * A.max_ctx * KVPROJ;
-  float* vc = A.vcache + (size_t)fi * A.max_ctx * KVPROJ;
+  if (threadIdx.x < 4) { st[threadIdx.x] = -INFINITY; st[4 + threadIdx.x] = 0.0f; }
   if (cc == 0 && threadIdx.x < HD) {   // roped K and raw V into slot T (golden/model.py:216-217)
-    kc[(size_t)T * KVPROJ + g * HD + threadIdx.x] = kn[threadIdx.x];
-    vc[(size_t)T * KVPROJ + g * HD + threadIdx.x] = vn[threadIdx.x];
+    A.kcache[((size_t)fi * A.max_ctx + T) * KVPROJ + g * HD + threadIdx.x] = kn[threadIdx.x];
+    A.vcache[((size_t)fi * A.max_ctx + T) * KVPROJ + g * HD + threadIdx.x] = vn[threadIdx.x];
   }
-  // scores of this chunk's positions: warp = position (cached K, or the new
-  // key for position T), lane = 8 of the 256 dims, 4 query heads
-  for (int i = wid; i < n; i += NCW) {
-    const int tt = t0 + i;
-    const float* kp = tt < T ? kc + (size_t)tt * KVPROJ + g * HD : kn;
-    const float4 k0 = *reinterpret_cast<const float4*>(kp + 4 * lane);
-    const float4 k1 = *reinterpret_cast<const float4*>(kp + 128 + 4 * lane);
-#pragma unroll
-    for (int hq = 0; hq < 4; ++hq) {
-      const float4 q0 = *reinterpret_cast<const float4*>(qn + hq * HD + 4 * lane);
-      const float4 q1 = *reinterpret_cast<const float4*>(qn + hq * HD + 128 + 4 * lane);
-      float d = q0.x * k0.x + q0.y * k0.y + q0.z * k0.z + q0.w * k0.w;
-      d += q1.x * k1.x + q1.y * k1.y + q1.z * k1.z + q1.w * k1.w;
-      d = warp_sum(d);
-      if (lane == 0) sc[hq * ATT_MAXLEN + i] = d * 0.0625f;   // 256^-0.5, exact
-    }
-  }
-  consumer_sync();
-  float* mh = ms->red;       // [4] maxima, [4..8) sums
-  if (wid < 4) {
-    float m = -INFINITY;
-    for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[wid * ATT_MAXLEN + i]);
-    m = warp_max(m);
-    float lsum = 0.0f;
-    for (int i = lane; i < n; i += 32) {
-      const float pe = expf(sc[wid * ATT_MAXLEN + i] - m);
-      sc[wid * ATT_MAXLEN + i] = pe;
-      lsum += pe;
-    }
-    lsum = warp_sum(lsum);
-    if (lane == 0) { mh[wid] = m; mh[4 + wid] = lsum; }
-  }
-  consumer_sync();
-  // P V: thread = one dim d of one half of the positions (all V loads of a
-  // thread independent, four in flight); halves summed through shared memory
-  const int d = threadIdx.x & (HD - 1), half = threadIdx.x >> 8;
   float o[4] = {0.f, 0.f, 0.f, 0.f};
-  {
-    const int ncache = min(n, T - t0);     // positions with a cached V
-#pragma unroll 4
-    for (int i = half; i < ncache; i += 2) {
-      const float v = vc[(size_t)(t0 + i) * KVPROJ + g * HD + d];
+  for (int s0 = t0; s0 < t1; s0 += ASB) {
+    const int nb = min(ASB, t1 - s0);
+    // scores of the block (256^-0.5, exact): warp = position
+    if (wid < nb) {
+      const int tp = s0 + wid;
+      float kk[8];
 #pragma unroll
-      for (int hq = 0; hq < 4; ++hq) o[hq] = fmaf(sc[hq * ATT_MAXLEN + i], v, o[hq]);
-    }
-    if (t1 == Tn && ((n - 1) & 1) == half) {   // the new position T
+      for (int i = 0; i < 8; ++i) kk[i] = tp < T ? kr[i] : kn[8 * lane + i];
 #pragma unroll
-      for (int hq = 0; hq < 4; ++hq) o[hq] = fmaf(sc[hq * ATT_MAXLEN + n - 1], vn[d], o[hq]);
+      for (int hq = 0; hq < 4; ++hq) {
+        const float4 q0 = *reinterpret_cast<const float4*>(qn + hq * HD + 8 * lane);
+        const float4 q1 = *reinterpret_cast<const float4*>(qn + hq * HD + 8 * lane + 4);
+        float dt = q0.x * kk[0] + q0.y * kk[1] + q0.z * kk[2] + q0.w * kk[3];
+        dt += q1.x * kk[4] + q1.y * kk[5] + q1.z * kk[6] + q1.w * kk[7];
+        dt = warp_sum(dt);
+        if (lane == 0) sp[hq * ASB + wid] = dt * 0.0625f;
+      }
     }
+    // the block's V stays in registers; the next block's K can be requested now
+    float vb[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) vb[j] = vr[j];
+    if (s0 + ASB < t1) load_block(s0 + ASB);
+    consumer_sync();
+    // online softmax: warp hq < 4 updates head hq
+    if (wid < 4) {
+      const float sv = lane < nb ? sp[wid * ASB + lane] : -INFINITY;
+      const float mold = st[wid];
+      const float mnew = fmaxf(mold, warp_max(sv));
+      const float pe = lane < nb ? expf(sv - mnew) : 0.0f;
+      const float ls = warp_sum(pe);
+      if (lane < ASB) sp[wid * ASB + lane] = pe;
+      if (lane == 0) {
+        const float sc = mold == -INFINITY ? 0.0f : expf(mold - mnew);
+        st[8 + wid] = sc;
+        st[4 + wid] = fmaf(st[4 + wid], sc, ls);
+        st[wid] = mnew;
+      }
+    }
+    consumer_sync();
+    // P V over this thread's 8 positions of the block
+#pragma unroll
+    for (int hq = 0; hq < 4; ++hq) o[hq] = __fmul_rn(o[hq], st[8 + hq]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int tv = s0 + 8 * half + j;
+      if (tv < t1) {
+        const float vv = tv < T ? vb[j] : vn[d];
+#pragma unroll
+        for (int hq = 0; hq < 4; ++hq) o[hq] = fmaf(sp[hq * ASB + 8 * half + j], vv, o[hq]);
+      }
+    }
+    consumer_sync();   // sp is rewritten by the next block
   }
-  float* ox = qn;                       // [4][256], the queries are consumed
+  // the two halves' o
   if (half == 1) {
 #pragma unroll
     for (int hq = 0; hq < 4; ++hq) ox[hq * HD + d] = o[hq];
   }
   consumer_sync();
-  float* part = A.att_part + ((size_t)(g * ATT_MAXCH + cc) * 4) * (2 + HD);
+  if (half == 0) {
+#pragma unroll
+    for (int hq = 0; hq < 4; ++hq) o[hq] = __fadd_rn(o[hq], ox[hq * HD + d]);
+  }
+  // the output gates (in q_proj's [q | gate] rows, written by IN with q): head 4g + hq, dim e
+  auto gate = [&](int hq, int e, int& bad) -> float {
+    const unsigned long long* gp = A.tv_qg + (size_t)(4 * g + hq) * 2 * HD + HD + e;
+    unsigned long long w = ld_tv(gp);
+    const unsigned long long tw = gtime();
+    int it = 0;
+    while (!bad && !tag_ok(w, tin)) {
+      if (((++it) & 63) == 0) {
+        if (aborted(c)) bad = 1;
+        else if (gtime() - tw > WAIT_NS) { raise_abort(c, 20, p); bad = 1; }
+      }
+      w = ld_tv(gp);
+    }
+    return tv_val(w);
+  };
+  int bad = 0;
+  if (nch == 1) {
+    // the whole group in this chunk: o / l * sigmoid(gate)
+    if (half == 0) {
+#pragma unroll
+      for (int hq = 0; hq < 4; ++hq) {
+        const float gt = gate(hq, d, bad);
+        st_tv(A.tv_attn + (4 * g + hq) * HD + d, __fmul_rn(__fdiv_rn(o[hq], st[4 + hq]), sigmoid_f(gt)), tout);
+      }
+    }
+    trace_mark(c, p, 2);
+    return consumer_and(!bad) != 0;
+  }
+  // this chunk's (m, l, o) of the four heads as tagged words
+  unsigned long long* part = A.att_tv + ((size_t)(g * ATT_MAXCH + cc) * 4) * (2 + HD);
   if (half == 0) {
 #pragma unroll
     for (int hq = 0; hq < 4; ++hq) {
-      part[hq * (2 + HD) + 2 + d] = __fadd_rn(o[hq], ox[hq * HD + d]);
-      if (d == 0) { part[hq * (2 + HD)] = mh[hq]; part[hq * (2 + HD) + 1] = mh[4 + hq]; }
-    }
-  }
-  __threadfence();
-  consumer_sync();
-  int* cnt = A.att_cnt + (L.full_idx * NKV + g);
-  if (threadIdx.x == 0) ms->last = (atomicAdd(cnt, 1) == nch - 1);
-  consumer_sync();
-  if (!ms->last) return true;
-  __threadfence();
-  if (threadIdx.x == 0) *cnt = 0;
-  // merge of the group's chunks (this CTA holds the last one): every chunk's
-  // maxima and sums staged in shared memory, the overall max and the weights
-  // exp(m_q - M) once per (head, chunk), then thread = (head, two dims) with
-  // the partial outputs of all chunks read independently
-  float* mq = sc;                       // [4][nch]: chunk maxima, then weights
-  float* lq = sc + 4 * ATT_MAXCH;       // [4][nch]: chunk sums
-  float* Mh = sc + 8 * ATT_MAXCH;       // [4] overall maxima, [4..8) total sums
-  for (int i = threadIdx.x; i < 4 * nch; i += PT) {
-    const int hq = i / nch, q = i % nch;
-    const float* pb = A.att_part + ((size_t)(g * ATT_MAXCH + q) * 4 + hq) * (2 + HD);
-    mq[i] = __ldcg(pb);
-    lq[i] = __ldcg(pb + 1);
-  }
-  consumer_sync();
-  if (threadIdx.x < 4) {
-    float M = -INFINITY;
-    for (int q = 0; q < nch; ++q) M = fmaxf(M, mq[threadIdx.x * nch + q]);
-    Mh[threadIdx.x] = M;
-  }
-  consumer_sync();
-  for (int i = threadIdx.x; i < 4 * nch; i += PT) mq[i] = expf(mq[i] - Mh[i / nch]);
-  consumer_sync();
-  if (threadIdx.x < 4) {
-    float Ls = 0.0f;
-    for (int q = 0; q < nch; ++q) Ls = fmaf(lq[threadIdx.x * nch + q], mq[threadIdx.x * nch + q], Ls);
-    Mh[4 + threadIdx.x] = Ls;
-  }
-  consumer_sync();
-  const int hq = threadIdx.x >> 7, d2 = 2 * (threadIdx.x & 127);
-  // the gates of head 4g + hq at dims d2, d2 + 1 (tagged, from IN), polled
-  // while the partial outputs load
-  const unsigned long long* gsrc = A.tv_qg + (size_t)(4 * g + hq) * 2 * HD + HD + d2;
-  unsigned long long ga, gb;
-  ld_tv2(gsrc, ga, gb);
-  float O0 = 0.0f, O1 = 0.0f;
-  {
-    const float* pb = A.att_part + ((size_t)(g * ATT_MAXCH) * 4 + hq) * (2 + HD) + 2 + d2;
-    const size_t stride = 4 * (2 + HD);
-#pragma unroll 4
-    for (int q = 0; q < nch; ++q) {
-      const float2 ov = __ldcg(reinterpret_cast<const float2*>(pb + q * stride));
-      const float f = mq[hq * nch + q];
-      O0 = fmaf(ov.x, f, O0);
-      O1 = fmaf(ov.y, f, O1);
-    }
-  }
-  {
-    const unsigned long long tg0 = gtime();
-    int it = 0;
-    while (!(tag_ok(ga, tin) && tag_ok(gb, tin))) {
-      if (((++it) & 63) == 0) {
-        if (aborted(c)) break;
-        if (gtime() - tg0 > WAIT_NS) { raise_abort(c, 20, p); break; }
+      st_tv(part + hq * (2 + HD) + 2 + d, o[hq], tout);
+      if (d == 0) {
+        st_tv(part + hq * (2 + HD), st[hq], tout);
+        st_tv(part + hq * (2 + HD) + 1, st[4 + hq], tout);
       }
-      ld_tv2(gsrc, ga, gb);
     }
   }
-  const unsigned tout = tag_of(c, p);
-  const float Ls = Mh[4 + hq];
-  st_tv(A.tv_attn + (4 * g + hq) * HD + d2, __fmul_rn(__fdiv_rn(O0, Ls), sigmoid_f(tv_val(ga))), tout);
-  st_tv(A.tv_attn + (4 * g + hq) * HD + d2 + 1, __fmul_rn(__fdiv_rn(O1, Ls), sigmoid_f(tv_val(gb))), tout);
-  consumer_sync();
-  return true;
+  trace_mark(c, p, 2);
+  if (cc != 0) return consumer_and(1) != 0;
+  // chunk 0's CTA merges the group: thread = (head hq, dims 2 d2, 2 d2 + 1),
+  // chunks in order (online: running max M, sum Ls, output O)
+  const int hq = threadIdx.x >> 7, d2 = 2 * (threadIdx.x & 127);
+  const unsigned long long* pb = A.att_tv + ((size_t)(g * ATT_MAXCH) * 4 + hq) * (2 + HD);
+  const size_t stride = 4 * (2 + HD);
+  float M = -INFINITY, Ls = 0.0f, O0 = 0.0f, O1 = 0.0f;
+  for (int q = 0; q < nch && !bad; ++q) {
+    const unsigned long long* pq_ = pb + q * stride;
+    unsigned long long wm, wl, w0, w1;
+    const unsigned long long tw = gtime();
+    int it = 0;
+    for (;;) {
+      wm = ld_tv(pq_);
+      wl = ld_tv(pq_ + 1);
+      ld_tv2(pq_ + 2 + d2, w0, w1);
+      if (tag_ok(wm, tout) && tag_ok(wl, tout) && tag_ok(w0, tout) && tag_ok(w1, tout)) break;
+      if (((++it) & 63) == 0) {
+        if (aborted(c)) { bad = 1; break; }
+        if (gtime() - tw > WAIT_NS) { raise_abort(c, 22, p); bad = 1; break; }
+      }
+    }
+    if (bad) break;
+    const float mq = tv_val(wm), lq = tv_val(wl);
+    const float Mn = fmaxf(M, mq);
+    const float a = M == -INFINITY ? 0.0f : expf(M - Mn), b = expf(mq - Mn);
+    Ls = fmaf(lq, b, __fmul_rn(Ls, a));
+    O0 = fmaf(tv_val(w0), b, __fmul_rn(O0, a));
+    O1 = fmaf(tv_val(w1), b, __fmul_rn(O1, a));
+    M = Mn;
+  }
+  if (!bad) {
+    const float ga = gate(hq, d2, bad), gb = gate(hq, d2 + 1, bad);
+    st_tv(A.tv_attn + (4 * g + hq) * HD + d2, __fmul_rn(__fdiv_rn(O0, Ls), sigmoid_f(ga)), tout);
+    st_tv(A.tv_attn + (4 * g + hq) * HD + d2 + 1, __fmul_rn(__fdiv_rn(O1, Ls), sigmoid_f(gb)), tout);
+  }
+  return consumer_and(!bad) != 0;
 }
 
 // ---------------------------------------------------------------- the kernel
@@ -2194,12 +2237,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
           const int h0 = TP ? A.dn_h0 : 0, nh = TP ? A.dn_h1 - A.dn_h0 : LH;
           if ((int)blockIdx.x < nh) ok = delta_head(c, p, h0 + blockIdx.x);
         } else {
-          const int Tn = ms->T + 1;
-          int nch = (Tn + ATT_MINLEN - 1) / ATT_MINLEN;
-          nch = nch < 1 ? 1 : (nch > ATT_MAXCH ? ATT_MAXCH : nch);
-          const int cl = (Tn + nch - 1) / nch;
-          if (cl > ATT_MAXLEN) { if (threadIdx.x == 0) raise_abort(c, 21, p); ok = false; break; }
+          // chunks of ASB positions (at most ATT_MAXCH, and one item per CTA)
           const int g0 = TP ? A.kv_g0 : 0, ng = TP ? A.kv_g1 - A.kv_g0 : NKV;   // this rank's KV groups
+          const int Tn = ms->T + 1;
+          int nch = (Tn + ASB - 1) / ASB;
+          const int cap = min(ATT_MAXCH, (int)gridDim.x / ng);
+          nch = nch < 1 ? 1 : (nch > cap ? cap : nch);
+          const int cl = (Tn + nch - 1) / nch;
           for (int it = blockIdx.x; it < ng * nch && ok; it += gridDim.x)
             ok = attn_item(c, p, g0 + it % ng, it / ng, nch, cl);
         }
@@ -2259,7 +2303,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
   }
 }
 
-static_assert(OFF_DIG + (4 * HD + 2 * HD + 4 * ATT_MAXLEN) * 4 <= OFF_HS,
+static_assert(OFF_DIG + (4 * HD + 2 * HD + 6 * HD) * 4 <= OFF_HS && 4 * ASB + 12 + 4 * HD <= 6 * HD,
               "attention scratch must fit in the digit/xf region");
 
 }  // namespace

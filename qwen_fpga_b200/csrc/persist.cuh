@@ -95,7 +95,7 @@ struct PersistArgs {
                                       // [first[p], first[p + 1]) of the CTA's list
   unsigned long long *tv_h, *tv_qkv, *tv_z, *tv_o, *tv_qg, *tv_kvn, *tv_attn, *tv_act;
   float* conv; float* rec; float* kcache; float* vcache;
-  float* att_part; int* att_cnt;   // att_cnt: [NFULL][NKV]
+  unsigned long long* att_tv;      // [NKV][ATT_MAXCH][4][2 + HD] tagged split-KV partials (m, l, o)
   int* head_cnt;
   unsigned long long* am_part;     // [G]
   const float* rope;

@@ -409,7 +409,6 @@ int check_device(qwen_ctx* c) {
     QCUDA(c, cudaMemset(c->S.err, 0, 4 * sizeof(int)));
     QCUDA(c, cudaMemset(c->P.abort_flag, 0, sizeof(int)));
     QCUDA(c, cudaMemset(c->P.head_cnt, 0, sizeof(int)));
-    QCUDA(c, cudaMemset(c->P.att_cnt, 0, NFULL * NKV * sizeof(int)));
     if (code == ERR_TOKEN) return fail(c, QWEN_ERR_ARG, "token id outside [0, %d)", VOCAB);
     if (code == ERR_CTX) return fail(c, QWEN_ERR_STATE, "context or step capacity exceeded on device");
     if (code == ERR_WAIT)
@@ -582,7 +581,7 @@ int create_impl(const char* blob_path, const char* index_path, int dev, int tp_r
     unsigned short* dfirst = nullptr;
     if ((rc = dalloc(c, &dch, chunks.size() * sizeof(Chunk))) ||
         (rc = dalloc(c, &dfirst, first.size() * sizeof(unsigned short))) ||
-        (rc = dalloc(c, &P.att_cnt, NFULL * NKV * sizeof(int))) ||
+        (rc = dalloc(c, &P.att_tv, (size_t)NKV * ATT_MAXCH * 4 * (2 + HD) * 8)) ||
         (rc = dalloc(c, &P.head_cnt, 64)) || (rc = dalloc(c, &P.abort_flag, 64)))
       return bail(rc);
     if (cudaMemcpy(dch, chunks.data(), chunks.size() * sizeof(Chunk), cudaMemcpyHostToDevice) != cudaSuccess ||
@@ -651,7 +650,6 @@ int create_impl(const char* blob_path, const char* index_path, int dev, int tp_r
     }
     P.final_norm = c->Mh.final_norm;
     P.conv = S.conv; P.rec = S.rec; P.kcache = S.kcache; P.vcache = S.vcache;
-    P.att_part = S.att_part;
     P.am_part = S.am_part;
     P.rope = S.rope;
     P.logits = S.logits;
