@@ -198,7 +198,6 @@ def run_profile(args):
     """Target for ncu: build the context, then exactly args.profile decode steps."""
     from qwen_fpga_b200 import api, synth
     dec = api.Decoder(synth.ensure_blob(1234), max_ctx=PROMPT_LEN + args.profile + 8)
-    dec.set_engine(args.engine)
     for t in prompt_ids()[:args.profile]:
         dec.decode_step(int(t), want_logits=False)
     dec.close()
@@ -365,8 +364,6 @@ def main():
                     help="extra configs measured into the same line (comma list of 1, 2, 3; '' = none)")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent sequences per GPU instead of tensor parallelism")
-    ap.add_argument("--engine", type=int, default=1,
-                    help="1 = persistent weight-streaming kernel, 0 = graph of phase kernels")
     ap.add_argument("--gemv", action="store_true", help="config-1 GEMV microbench (one JSON line)")
     ap.add_argument("--gemv-n", type=int, default=0, help="with --gemv: only the shape with this N")
     ap.add_argument("--profile", type=int, default=0,
@@ -409,12 +406,9 @@ def main():
         dec = tpd.dec
     else:
         dec = api.Decoder(blob_path, device=local, max_ctx=max_ctx)
-        dec.set_engine(args.engine)
-    engine = dec.engine
     seqs = 1 if tp else world   # sequences decoded by the whole job
-    launches_per_step = 1 if engine == 1 else 24 * 5 + 2
-    kernel_name = ("k_decode_persistent (one cooperative launch per step)" if engine == 1
-                   else "whole decode step (CUDA graph of 122 kernels)")
+    launches_per_step = 1
+    kernel_name = "k_decode_persistent (one cooperative launch per step)"
     prompt = prompt_ids()
 
     # warm-up: W untimed steps
@@ -537,7 +531,6 @@ def main():
                         "out to pinned host memory (golden decode_step's return value)",
                 "argmax_only": {"value": e2e["argmax"], "unit": UNIT, "d2h_bytes_per_step": 20}},
         "gpu_launches": K * launches_per_step,
-        "engine": "persistent" if engine == 1 else "graph",
         "roofline": {"bound": "hbm", "kernel": kernel_name,
                      "achieved": achieved, "peak": peak_n, "unit": "GB/s",
                      "frac": achieved / peak_n, "peak_source": peak_src,

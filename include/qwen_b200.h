@@ -58,7 +58,7 @@ int qwen_create(const char* blob_path, const char* index_path, int n_gpus,
  * the others' next step fail after the 2 s device wait bound with
  * QWEN_ERR_DEVICE.  Under ACT_INT8 the ranks also exchange the maxima of the
  * row-parallel inputs, so each is quantised with the max over the whole
- * vector as on one GPU.  Engine 0 is not available under TP.
+ * vector as on one GPU.
  * Logits: each rank fills only its vocab slice [lo, hi) of logits_out
  * (qwen_tp_vocab_range).  State import/export move the full arrays; a rank
  * uses and updates only its heads' parts.
@@ -112,16 +112,7 @@ int qwen_state_export(qwen_ctx* ctx, int seq, float* conv, float* rec, float* kc
  * activations (W8A32).  The tied head always takes fp32 activations. */
 int qwen_set_act_int8(qwen_ctx* ctx, int on);
 
-/* Select the decode engine of the context (no counterpart in the reference,
- * which has one sequencer): 1 = one persistent cooperative kernel per step
- * that streams the weights through a shared-memory ring (default), 0 = a CUDA
- * graph of per-phase kernels.  Both compute the same arithmetic.  The
- * environment variable QWEN_B200_ENGINE=0 selects 0 at qwen_create.
- * qwen_get_engine returns the current engine (-1 for a NULL context). */
-int qwen_set_engine(qwen_ctx* ctx, int engine);
-int qwen_get_engine(qwen_ctx* ctx);
-
-/* Per-phase tracing of the persistent engine (no counterpart in the reference,
+/* Per-phase tracing of the decode kernel (no counterpart in the reference,
  * which times steps with perf_counter at run_prompt.py:80-98): when on, every
  * step records, per CTA and per phase, %globaltimer stamps [entry, inputs
  * arrived, outputs written, exit] (ns; 0 where a phase has no such point),
@@ -138,6 +129,22 @@ int qwen_get_engine(qwen_ctx* ctx);
 int qwen_trace_enable(qwen_ctx* ctx, int on);
 int qwen_trace_read(qwen_ctx* ctx, unsigned long long* out, int max_words, int* n_ctas,
                     int* n_phases);
+
+/* W8A8 arithmetic capture, a test hook (no counterpart in the reference):
+ * qwen_capture_phase arms GEMV phase `phase` (5 l + 0 IN, + 2 OUT, + 3 GATEUP,
+ * + 4 DOWN of layer l; -1 disarms) of every following ACT_INT8 step on the
+ * decode kernel of a single-GPU context.  The step then records, into
+ * QWEN_CAPTURE_FLOATS floats that qwen_capture_read copies out: [0, 4096) the
+ * phase's fp32 input as the kernel quantises it (IN / GATEUP: the residual
+ * stream h before the RMSNorm), [4096, 8192) its int8 activations (golden
+ * _qa, golden/model.py:37-45), [8192] s_x, [8193] K, [8194] 1 when captured,
+ * and from [8200] the int32 accumulators of the phase's rows as bit patterns
+ * (IN: [qkv | z] or [q | k | v] rows; GATEUP: 3584 gate rows then 3584 up
+ * rows; OUT / DOWN: 1024 rows) -- the exact integer products of
+ * scripts/export_gemv_tv.py:49 that a test recomputes. */
+#define QWEN_CAPTURE_FLOATS 16392
+int qwen_capture_phase(qwen_ctx* ctx, int phase);
+int qwen_capture_read(qwen_ctx* ctx, float* out, int max_floats);
 
 /* One decode step for each of `batch` (must be 1) tokens: embed, 24 layers,
  * final norm, tied head, argmax (first index on ties).  Mirrors

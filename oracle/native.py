@@ -26,12 +26,25 @@ def _p(a, t):
     return a.ctypes.data_as(t) if a is not None else None
 
 
+def reference_checkout() -> str | None:
+    """The reference checkout: $QWEN_REF, else the reference_path that
+    BASELINE.json at the repository root records (None if neither exists)."""
+    ref = os.environ.get("QWEN_REF")
+    if not ref:
+        import json
+        bj = os.path.join(os.path.dirname(HERE), "BASELINE.json")
+        if os.path.exists(bj):
+            with open(bj) as f:
+                ref = json.load(f).get("reference_path")
+    return ref if ref and os.path.isdir(ref) else None
+
+
 def build(ref: str | None = None) -> None:
     """Compile the C port, and the reference shim when the reference checkout exists."""
     import subprocess
     subprocess.run(["make", "-s", "-C", HERE, "port"], check=True)
-    ref = ref or os.environ.get("QWEN_REF", "/root/reference")
-    if os.path.isdir(os.path.join(ref, "hls", "src")):
+    ref = ref or reference_checkout()
+    if ref and os.path.isdir(os.path.join(ref, "hls", "src")):
         subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref}"], check=True)
 
 

@@ -76,8 +76,6 @@ def load() -> C.CDLL:
     L.qwen_state_import.argtypes = [_vp, C.c_int, _fp, _fp, _fp, _fp, C.c_int, C.c_int]
     L.qwen_state_export.argtypes = [_vp, C.c_int, _fp, _fp, _fp, _fp, _ip, _ip]
     L.qwen_set_act_int8.argtypes = [_vp, C.c_int]
-    L.qwen_set_engine.argtypes = [_vp, C.c_int]
-    L.qwen_get_engine.argtypes = [_vp]
     L.qwen_trace_enable.argtypes = [_vp, C.c_int]
     L.qwen_trace_read.argtypes = [_vp, C.POINTER(C.c_ulonglong), C.c_int, _ip, _ip]
     L.qwen_decode_step.argtypes = [_vp, _ip, C.c_int, _vp, _ip]
@@ -86,6 +84,8 @@ def load() -> C.CDLL:
     L.qwen_gemv_i8_i8.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_float, C.c_int, C.c_int, _vp]
     L.qwen_delta_rule_layer.argtypes = [_vp] * 7 + [_vp]
     L.qwen_gemv_i8_f32_argmax_noalloc.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]
+    L.qwen_capture_phase.argtypes = [_vp, C.c_int]
+    L.qwen_capture_read.argtypes = [_vp, _fp, C.c_int]
     _lib = L
     return L
 
@@ -199,14 +199,6 @@ class Decoder:
         _check(load().qwen_set_act_int8(self.h, 1 if on else 0), self.h)
         self.act_int8 = bool(on)
 
-    def set_engine(self, engine: int):
-        """1 = persistent weight-streaming kernel (default), 0 = graph of phase kernels."""
-        _check(load().qwen_set_engine(self.h, int(engine)), self.h)
-
-    @property
-    def engine(self) -> int:
-        return int(load().qwen_get_engine(self.h))
-
     def trace_enable(self, on: bool = True):
         _check(load().qwen_trace_enable(self.h, 1 if on else 0), self.h)
 
@@ -225,6 +217,21 @@ class Decoder:
 
     def reset(self):
         _check(load().qwen_reset(self.h, 0), self.h)
+
+    CAPTURE_FLOATS = 16392
+
+    def capture_phase(self, phase: int):
+        """Arm (phase >= 0) or disarm (-1) the W8A8 capture of one GEMV phase."""
+        _check(load().qwen_capture_phase(self.h, int(phase)), self.h)
+
+    def capture_read(self) -> dict:
+        """The last armed step's capture: x (fp32 input), xq (int8), sx, K, acc (int32 rows)."""
+        buf = np.zeros(self.CAPTURE_FLOATS, np.float32)
+        _check(load().qwen_capture_read(self.h, buf.ctypes.data_as(_fp), buf.size), self.h)
+        K = int(buf[8193])
+        return {"captured": bool(buf[8194] != 0), "K": K, "x": buf[:K].copy(),
+                "xq": buf[4096:4096 + K].astype(np.int8), "sx": np.float32(buf[8192]),
+                "acc": buf[8200:].view(np.int32).copy()}
 
     def decode_step(self, tok: int, want_logits: bool = True, out=None):
         """Returns (argmax, logits or None).  `out` (optional): a float32 array of

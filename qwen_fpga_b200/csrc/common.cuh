@@ -47,14 +47,13 @@ constexpr int ROT = 64;         // rotated dims (head_dim * 0.25)
 constexpr int KMAX = FFN;       // largest GEMV reduction length in the model
 constexpr float EPS = 1e-6f;
 
-// DeltaNet work split: each head's 128 value columns in slices of DSLICE.
+// The standalone delta-rule operator: each head's 128 value columns in slices of DSLICE.
 constexpr int DSLICE = 16;
 constexpr int NDSLICE = LV / DSLICE;      // 8
-// attention split-KV bounds
-constexpr int ATT_MAXCH = 64;            // chunks per kv head
-constexpr int ATT_MINLEN = 8;            // positions per chunk (at least)
-constexpr int ATT_MAXLEN = 1024;         // positions per chunk (at most, smem bound)
-constexpr int AM_PARTS = 4096;           // argmax partial slots (>= head grid)
+// attention split-KV: at most ATT_MAXCH chunks per kv head; cached positions per attention layer
+constexpr int ATT_MAXCH = 64;
+constexpr int MAX_CTX = 65536;
+constexpr int AM_PARTS = 4096;           // argmax partial slots (>= the grid)
 
 // ---- device view of one layer's tensors inside the uploaded blob
 struct LayerW {
@@ -95,8 +94,8 @@ struct ModelW {
   LayerW L[NLAYER];
 };
 
-// ---- per-step values that change every token; live in device memory so one
-// captured graph serves every step.
+// ---- per-step values that change every token; they live in device memory,
+// read by each launch of the decode kernel.
 struct StepDyn {
   int pos;        // RoPE position of the token being decoded
   int T;          // cached positions per attention layer before this token
@@ -108,23 +107,12 @@ struct StepDyn {
   int seq;        // launch sequence number (tags of the persistent kernel)
 };
 
-// ---- device decode state + scratch of one sequence
+// ---- device decode state of one sequence
 struct StateW {
-  float* h;          // [1024] residual stream
-  float* qkv;        // [6144] DeltaNet in_proj_qkv output (pre-conv)
-  float* z;          // [2048] in_proj_z output
-  float* ab;         // [32]   in_proj_b (0..15), in_proj_a (16..31)
-  float* o;          // [2048] delta-rule output (before the gated norm)
-  float* qg;         // [4096] attention q_proj output
-  float* kvn;        // [1024] attention k_proj (0..511), v_proj (512..1023)
-  float* attn_o;     // [2048] attention output before the sigmoid gate
-  float* act;        // [3584] silu(gate) * up
   float* conv;       // [18][6144][4] conv history ring
   float* rec;        // [18][16][128][128] DeltaNet state
   float* kcache;     // [6][max_ctx][512] post-RoPE K
   float* vcache;     // [6][max_ctx][512] V
-  float* att_part;   // [2][ATT_MAXCH][4][2+256] split-KV partials
-  int* att_cnt;      // [2] arrival counters of the split-KV combine
   const float* rope; // [max_ctx][64]: cos[32] | sin[32] (angles pos * inv_freq)
   float* logits;     // [248320]
   unsigned long long* am_part;  // [AM_PARTS] packed (logit, index) maxima
@@ -162,8 +150,7 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // Block-wide sum / max; `red` is >= 32 floats of shared scratch.  All threads
 // of the block must call; returns the result to every thread.  The sum adds
-// the per-warp partials in warp order, the same order as the persistent
-// kernel, so both engines round identically.
+// the per-warp partials in warp order.
 __device__ __forceinline__ float block_sum(float v, float* red) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
   v = warp_sum(v);

@@ -1536,6 +1536,17 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
     consumer_sync();
   }
   trace_mark(c, p, 1);
+  // W8A8 capture: the first CTA to reach the phase records its input
+  bool dbg_cta = false;
+  if constexpr (I8 && !TP) {
+    if (p == A.dbg_phase) {
+      if (threadIdx.x == 0) ms->last = atomicCAS((int*)(A.dbg + DBG_FLAG), 0, 1) == 0;
+      consumer_sync();
+      dbg_cta = ms->last != 0;
+      if (dbg_cta)
+        for (int e = threadIdx.x; e < k1; e += PT) A.dbg[DBG_X + e] = normed ? hs[e] : xf[e];
+    }
+  }
   // the digit image
   float sx = 0.0f, xs = 0.0f;
   if constexpr (I8) {
@@ -1554,6 +1565,11 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
     if (threadIdx.x == 0) *amax = 0u;
   }
   trace_warp(c, p, 2);
+  if (dbg_cta) {
+    const int8_t* dg = (const int8_t*)(c.sm + OFF_DIG);
+    for (int e = threadIdx.x; e < k1; e += PT) A.dbg[DBG_XQ + e] = (float)dg[dig_off(0, e & ~3) + (e & 3)];
+    if (threadIdx.x == 0) { A.dbg[DBG_SX] = (float)ms->scale; A.dbg[DBG_K] = (float)k1; }
+  }
   // x scale of the digit sums: ACT_INT8 the quantiser's s_x; W8A32 2^-shift,
   // times 1/rms for a normed input (exact: a power of two times a float), the
   // rms from the warps' sums of h^2 (golden/model.py:74: mean over HID)
@@ -1619,6 +1635,13 @@ __device__ bool phase_panels(PCtx& c, int p, int i0, int i1) {
       int* pvp = (int*)(c.sm + OFF_PART) + vp * 4 * PANEL + pr;
       if constexpr (I8) {
         y = finish_f32(pvp[0], 0, 0, 1, xsc * psc[vp * PANEL + pr]);
+        if constexpr (!TP) {
+          if (p == A.dbg_phase) {   // the row's accumulator (GATEUP: gate rows, then up rows)
+            const int rr = sub == 3 ? (pr < PAIR_ROWS ? pq * PAIR_ROWS + pr : FFN + pq * PAIR_ROWS + pr - PAIR_ROWS)
+                                    : pq * PANEL + pr;
+            reinterpret_cast<int*>(A.dbg)[DBG_ACC + rr] = pvp[0];
+          }
+        }
         pvp[0] = 0;
       } else {
         // the row's exact sum of w * X: sum of w * U minus 2^22 times the weight sum

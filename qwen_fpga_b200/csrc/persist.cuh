@@ -103,6 +103,11 @@ struct PersistArgs {
   int* io; int* ids; int* err; int* abort_flag;
   StepDyn* dyn;
   unsigned long long* trace;       // nullable: the trace record (layout above persist_trace_words)
+  // W8A8 capture (qwen_capture_phase): phase dbg_phase (-1: off) of the next
+  // step writes its input, int8 image, s_x and int32 accumulators to dbg
+  // (layout DBG_*); single-GPU ACT_INT8 instance only.
+  int dbg_phase;
+  float* dbg;
   int max_ctx, max_rope, max_steps;
   // tensor parallelism (tp_world = 1: none; see TpPlan)
   int tp_rank, tp_world;
@@ -132,6 +137,15 @@ static_assert(KDIM == VDIM && LK == LV && LH % TP_MAX == 0 && NH % TP_MAX == 0, 
 // Re-lay nrows rows (row r read from rowptr[r], K bytes each) as 16-row panels
 // (for GATEUP the caller orders the rows 8 gate, 8 up per panel).
 cudaError_t repack_panels(const int8_t* const* rowptr, int8_t* out, int nrows, int K, cudaStream_t st);
+
+// Capture buffer layout (floats): the phase's fp32 input as the kernel
+// quantises it (a normed input: the residual h before the norm) at DBG_X, the
+// int8 image (as floats, natural order) at DBG_XQ, s_x at DBG_SX, K at DBG_K,
+// a claim word at DBG_FLAG, and the int32 accumulators (bit patterns) of the
+// phase's rows at DBG_ACC: IN rows in panel order ([qkv | z] or [q | k | v]),
+// GATEUP gate rows then up rows, OUT / DOWN the 1024 hidden rows.
+constexpr int DBG_X = 0, DBG_XQ = 4096, DBG_SX = 8192, DBG_K = 8193, DBG_FLAG = 8194, DBG_ACC = 8200;
+constexpr int DBG_FLOATS = DBG_ACC + 8192;
 
 int persist_smem_bytes();
 int persist_num_phases();

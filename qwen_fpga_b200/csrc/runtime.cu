@@ -1,8 +1,10 @@
 // Host runtime and C ABI of libqwenb200 (declared in include/qwen_b200.h).
 //
-// A context owns one GPU's copy of the packed weight blob, one batch-1 decode
-// state, and a CUDA graph of the whole decode step.  Per call the host only
-// writes a small control block (position, token source) and replays the graph.
+// A context owns one GPU's copy of the packed weight blob (plus the panel and
+// head-tile copies the persistent kernel streams), one batch-1 decode state,
+// and the kernel's per-CTA schedule.  Per call the host only writes a small
+// control block (position, token source) and launches the persistent kernel
+// once per step.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -18,12 +20,14 @@
 
 #include "../../include/qwen_b200.h"
 #include "common.cuh"
-#include "decode.cuh"
+#include "delta.cuh"
 #include "gemv.cuh"
 #include "noalloc.cuh"
 #include "persist.cuh"
 
 using namespace qb;
+
+static_assert(DBG_FLOATS == QWEN_CAPTURE_FLOATS, "capture layout");
 
 namespace {
 
@@ -205,7 +209,6 @@ struct qwen_ctx {
   int pos = 0, T = 0, conv_base = 0;
   unsigned seq = 1;           // launch sequence number (tag base of the persistent kernel)
   int act_int8 = 0;
-  int engine = 1;             // 1 = persistent weight-streaming kernel, 0 = graph of phase kernels
   PersistArgs P{};
   TpPlan tp{};                // tensor-parallel shard of this context (world 1: everything)
   unsigned long long* xbuf = nullptr;   // this rank's exchange buffer (IPC-exported)
@@ -213,7 +216,6 @@ struct qwen_ctx {
   bool tp_ready = true;                 // world 1, or qwen_tp_connect done
   unsigned long long* tv_base = nullptr;
   size_t tv_words = 0;
-  cudaGraphExec_t graph = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
 };
 
@@ -388,15 +390,14 @@ int ensure_seq_room(qwen_ctx* c, int launches) {
   return QWEN_OK;
 }
 
-// One decode step on the context stream with the selected engine.
+// One decode step on the context stream: one persistent-kernel launch.
 int launch_step(qwen_ctx* c) {
-  if (c->engine == 1) {
+  {
     // a traced step starts from a cleared record (0 = stamp not reached)
     if (c->P.trace) QCUDA(c, cudaMemsetAsync(c->P.trace, 0, persist_trace_words(c->sm_count) * 8, c->st));
+    if (c->P.dbg_phase >= 0) QCUDA(c, cudaMemsetAsync(c->P.dbg, 0, DBG_FLOATS * sizeof(float), c->st));
     cudaError_t e = launch_persistent(c->P, c->sm_count, c->st, c->act_int8 != 0);
     if (e != cudaSuccess) return fail(c, QWEN_ERR_CUDA, "persistent launch: %s", cudaGetErrorString(e));
-  } else {
-    QCUDA(c, cudaGraphLaunch(c->graph, c->st));
   }
   return QWEN_OK;
 }
@@ -418,19 +419,6 @@ int check_device(qwen_ctx* c) {
       return fail(c, QWEN_ERR_DEVICE, "device bounds check failed (site %d, value %d)", c->h_err[1], c->h_err[2]);
     return fail(c, QWEN_ERR_DEVICE, "device reported error %d", code);
   }
-  return QWEN_OK;
-}
-
-int build_graph(qwen_ctx* c) {
-  cudaGraph_t g = nullptr;
-  QCUDA(c, cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
-  cudaError_t e = enqueue_step(c->Mh, c->Md, c->S, c->sm_count, c->st);
-  cudaError_t e2 = cudaStreamEndCapture(c->st, &g);
-  if (e != cudaSuccess) return fail(c, QWEN_ERR_CUDA, "capture of the decode step: %s", cudaGetErrorString(e));
-  if (e2 != cudaSuccess) return fail(c, QWEN_ERR_CUDA, "end capture: %s", cudaGetErrorString(e2));
-  e = cudaGraphInstantiate(&c->graph, g, 0);
-  cudaGraphDestroy(g);
-  if (e != cudaSuccess) return fail(c, QWEN_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
   return QWEN_OK;
 }
 
@@ -456,7 +444,6 @@ int qwen_destroy(qwen_ctx* c) {
   if (!c) return QWEN_OK;
   cudaSetDevice(c->dev);
   if (c->st) cudaStreamSynchronize(c->st);
-  if (c->graph) cudaGraphExecDestroy(c->graph);
   for (void* p : c->ipc_open) cudaIpcCloseMemHandle(p);
   for (void* p : c->allocs) cudaFree(p);
   if (c->h_ctl) cudaFreeHost(c->h_ctl);
@@ -479,8 +466,7 @@ int create_impl(const char* blob_path, const char* index_path, int dev, int tp_r
   *out = nullptr;
   if (!blob_path || !index_path) return fail(nullptr, QWEN_ERR_ARG, "blob_path / index_path is null");
   if (max_batch != 1) return fail(nullptr, QWEN_ERR_ARG, "max_batch must be 1");
-  if (max_ctx < 1 || max_ctx > ATT_MAXCH * ATT_MAXLEN)
-    return fail(nullptr, QWEN_ERR_ARG, "max_ctx must be in [1, %d]", ATT_MAXCH * ATT_MAXLEN);
+  if (max_ctx < 1 || max_ctx > MAX_CTX) return fail(nullptr, QWEN_ERR_ARG, "max_ctx must be in [1, %d]", MAX_CTX);
   TpPlan plan;
   {
     std::string perr;
@@ -516,17 +502,11 @@ int create_impl(const char* blob_path, const char* index_path, int dev, int tp_r
   S.max_ctx = c->max_ctx;
   S.max_rope = c->max_rope;
   S.max_steps = c->max_steps;
-  if ((rc = dalloc(c, &S.h, HID * 4)) || (rc = dalloc(c, &S.qkv, CONVD * 4)) ||
-      (rc = dalloc(c, &S.z, VDIM * 4)) || (rc = dalloc(c, &S.ab, 2 * LH * 4)) ||
-      (rc = dalloc(c, &S.o, VDIM * 4)) || (rc = dalloc(c, &S.qg, QPROJ * 4)) ||
-      (rc = dalloc(c, &S.kvn, 2 * KVPROJ * 4)) || (rc = dalloc(c, &S.attn_o, NH * HD * 4)) ||
-      (rc = dalloc(c, &S.act, FFN * 4)) ||
-      (rc = dalloc(c, &S.conv, (size_t)NLIN * CONVD * CONVK * 4)) ||
+  if ((rc = dalloc(c, &S.conv, (size_t)NLIN * CONVD * CONVK * 4)) ||
       (rc = dalloc(c, &S.rec, (size_t)NLIN * LH * LK * LV * 4)) ||
       (rc = dalloc(c, &S.kcache, (size_t)NFULL * max_ctx * KVPROJ * 4)) ||
       (rc = dalloc(c, &S.vcache, (size_t)NFULL * max_ctx * KVPROJ * 4)) ||
-      (rc = dalloc(c, &S.att_part, (size_t)NKV * ATT_MAXCH * 4 * (2 + HD) * 4)) ||
-      (rc = dalloc(c, &S.att_cnt, 64)) || (rc = dalloc(c, &S.logits, (size_t)VOCAB * 4)) ||
+      (rc = dalloc(c, &S.logits, (size_t)VOCAB * 4)) ||
       (rc = dalloc(c, &S.am_part, AM_PARTS * 8)) ||
       (rc = dalloc(c, &S.err, 16 + (size_t)c->max_steps * 4)) ||
       (rc = dalloc(c, &c->d_ctl, ctl_bytes(c->max_steps))) ||
@@ -553,8 +533,7 @@ int create_impl(const char* blob_path, const char* index_path, int dev, int tp_r
     memset(c->h_ctl, 0, ctl_bytes(c->max_steps));
     c->h_ids = c->h_err + 4;
   }
-  if (head_grid_size(c->sm_count) > AM_PARTS) { fail(c, QWEN_ERR_STATE, "too many SMs"); return bail(QWEN_ERR_STATE); }
-  if ((rc = build_graph(c))) return bail(rc);
+  if (c->sm_count > AM_PARTS) { fail(c, QWEN_ERR_STATE, "too many SMs"); return bail(QWEN_ERR_STATE); }
   {
     // persistent engine: tagged activation words, counters, per-CTA schedule
     const size_t words = HID + CONVD + VDIM + VDIM + QPROJ + 2 * KVPROJ + NH * HD + FFN;
@@ -596,7 +575,7 @@ int create_impl(const char* blob_path, const char* index_path, int dev, int tp_r
     P.emb_s = c->Mh.emb_s;
     {
       // the head's weights re-tiled once for the tensor cores (a second copy:
-      // the row-major table still serves the embedding lookup and engine 0)
+      // the row-major table still serves the embedding lookup)
       int8_t* tiles = nullptr;
       if ((rc = dalloc(c, &tiles, HEAD_TILE_BYTES))) return bail(rc);
       cudaError_t e = repack_head_tiles(c->Mh.emb_q, tiles, c->st);
@@ -605,7 +584,7 @@ int create_impl(const char* blob_path, const char* index_path, int dev, int tp_r
     }
     {
       // every layer projection re-laid as 16-row panels for the persistent
-      // engine (second copies; the row-major tensors still serve engine 0)
+      // engine (second copies)
       struct Job { std::vector<const int8_t*> rows; int K; const int8_t** slot; };
       std::vector<Job> jobs;
       for (int l = 0; l < NLAYER; ++l) {
@@ -661,17 +640,14 @@ int create_impl(const char* blob_path, const char* index_path, int dev, int tp_r
     P.kv_g0 = c->tp.kv_g0; P.kv_g1 = c->tp.kv_g1;
     P.ok0 = c->tp.ok0; P.ok1 = c->tp.ok1;
     P.dk0 = c->tp.dk0; P.dk1 = c->tp.dk1;
+    P.dbg_phase = -1;
+    P.dbg = nullptr;
     if (c->tp.world > 1) {
       // the exchange buffer peers store into (its own allocation: IPC maps whole allocations)
       if ((rc = dalloc(c, &c->xbuf, XB_WORDS * 8))) return bail(rc);
       P.xbuf[c->tp.rank] = c->xbuf;
     }
-    const char* env = getenv("QWEN_B200_ENGINE");
-    c->engine = (env && env[0] == '0' && c->tp.world == 1) ? 0 : 1;
-    if (c->engine == 1 && persist_max_blocks_per_sm() < 1) {
-      if (c->tp.world > 1) { fail(c, QWEN_ERR_STATE, "persistent kernel does not fit"); return bail(QWEN_ERR_STATE); }
-      c->engine = 0;
-    }
+    if (persist_max_blocks_per_sm() < 1) { fail(c, QWEN_ERR_STATE, "persistent kernel does not fit"); return bail(QWEN_ERR_STATE); }
   }
   {
     cudaError_t e = cudaDeviceSynchronize();
@@ -771,18 +747,6 @@ int qwen_set_act_int8(qwen_ctx* c, int on) {
   return QWEN_OK;
 }
 
-int qwen_set_engine(qwen_ctx* c, int engine) {
-  int rc;
-  if ((rc = check_ctx(c))) return rc;
-  if (engine != 0 && engine != 1) return fail(c, QWEN_ERR_ARG, "engine must be 0 or 1");
-  if (engine == 0 && c->tp.world > 1) return fail(c, QWEN_ERR_STATE, "engine 0 has no tensor parallelism");
-  if (engine == 1 && persist_max_blocks_per_sm() < 1)
-    return fail(c, QWEN_ERR_STATE, "persistent kernel does not fit on this device");
-  c->engine = engine;
-  return QWEN_OK;
-}
-
-int qwen_get_engine(qwen_ctx* c) { return c ? c->engine : -1; }
 
 int qwen_trace_enable(qwen_ctx* c, int on) {
   int rc;
@@ -807,6 +771,31 @@ int qwen_trace_read(qwen_ctx* c, unsigned long long* out, int max_words, int* n_
   QCUDA(c, cudaMemcpy(out, c->P.trace, words * 8, cudaMemcpyDeviceToHost));
   if (n_ctas) *n_ctas = c->sm_count;
   if (n_phases) *n_phases = persist_num_phases();
+  return QWEN_OK;
+}
+
+int qwen_capture_phase(qwen_ctx* c, int phase) {
+  int rc;
+  if ((rc = check_ctx(c))) return rc;
+  if (phase < 0) {
+    c->P.dbg_phase = -1;
+    return QWEN_OK;
+  }
+  if (phase >= persist_num_phases() - 1 || phase % 5 == 1)
+    return fail(c, QWEN_ERR_ARG, "phase %d is not a GEMV phase (IN, OUT, GATEUP or DOWN of a layer)", phase);
+  if (c->tp.world > 1) return fail(c, QWEN_ERR_STATE, "capture is single-GPU only");
+  if (!c->P.dbg && (rc = dalloc(c, &c->P.dbg, DBG_FLOATS * sizeof(float)))) return rc;
+  c->P.dbg_phase = phase;
+  return QWEN_OK;
+}
+
+int qwen_capture_read(qwen_ctx* c, float* out, int max_floats) {
+  int rc;
+  if ((rc = check_ctx(c))) return rc;
+  if (!c->P.dbg) return fail(c, QWEN_ERR_STATE, "no capture armed (qwen_capture_phase)");
+  if (!out || max_floats < DBG_FLOATS) return fail(c, QWEN_ERR_ARG, "need %d floats", DBG_FLOATS);
+  QCUDA(c, cudaStreamSynchronize(c->st));
+  QCUDA(c, cudaMemcpy(out, c->P.dbg, DBG_FLOATS * sizeof(float), cudaMemcpyDeviceToHost));
   return QWEN_OK;
 }
 

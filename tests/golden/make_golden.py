@@ -5,7 +5,7 @@ Runs in the build container only (it imports ``golden/model.py`` and
 read-only reference checkout).  The GPU box never runs this; it only reads
 the ``.npz`` files written here.
 
-    python tests/golden/make_golden.py [--ref PATH]
+    python tests/golden/make_golden.py --ref PATH   (or QWEN_REF=PATH)
 
 Fixtures (all small; logits are stored as fixed-index samples + top-k):
 
@@ -16,7 +16,7 @@ Fixtures (all small; logits are stored as fixed-index samples + top-k):
   state, plus the golden's own logit movement under a 1e-7 perturbation.
 * ``config2.npz``  -- ACT_INT8 (W8A8) warm start: rec N(0,0.1), 4096 cached
   positions N(0,1), first token ``default_rng(0).integers(vocab)``; 6 greedy steps.
-* ``config3.npz``  -- W8A32 warm start with 32768 cached positions; 2 steps.
+* ``config3.npz``  -- W8A32 warm start with 32768 cached positions; 8 greedy steps.
 * ``deltanet_trace.npz`` -- delta-rule inputs/outputs of linear layer 0 on a
   warm state (5 prompt tokens, then the 6th traced), the capture pattern of
   scripts/export_testvectors.py:31-40; full q,k,v,g,beta,o and S for heads 0 and 9.
@@ -77,9 +77,12 @@ def gemv_inputs(N, K, seed=0):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("QWEN_REF"),
+                    help="the reference checkout (or set QWEN_REF)")
     ap.add_argument("--only", default="")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("pass --ref or set QWEN_REF to the reference checkout")
     sys.path.insert(0, os.path.join(args.ref, "golden"))
     sys.path.insert(0, os.path.join(args.ref, "scripts"))
     import model as G  # the reference golden, unmodified
@@ -275,7 +278,7 @@ def main():
         tok = int(np.random.default_rng(0).integers(0, VOCAB))
         out = {"first_token": np.int64(tok), "T0": np.int64(32768)}
         argmax = []
-        for j in range(2):
+        for j in range(8):
             logits = G.decode_step(W, cfg, tok, st)
             tok = int(np.argmax(logits))
             argmax.append(tok)

@@ -7,7 +7,7 @@ points its snapshot lookup at the generated snapshot and runs its main().
 The test (tests/test_pack.py) compares libqwenb200's qwen_pack_blob with the
 digests stored here.
 
-    python tests/golden/make_pack_golden.py [--ref PATH]
+    python tests/golden/make_pack_golden.py --ref PATH   (or QWEN_REF=PATH)
 
 Writes tests/golden/pack_tiny.json: the blob's sha256 and size, and the
 manifest's config and tensor entries.
@@ -31,7 +31,8 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))  # the repository (qw
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("QWEN_REF"),
+                    help="the reference checkout (or set QWEN_REF)")
     args = ap.parse_args()
     from pack_util import make_tiny_snapshot
 

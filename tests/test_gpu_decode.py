@@ -17,14 +17,11 @@ pytestmark = pytest.mark.gpu
 MAX_CTX = 32768 + 64
 
 
-@pytest.fixture(scope="module", params=[1, 0], ids=["persistent", "graph"])
-def dec(request, blob_path):
-    """One context per engine: 1 = persistent weight-streaming kernel, 0 = graph
-    of per-phase kernels.  Every test runs against both."""
+@pytest.fixture(scope="module")
+def dec(blob_path):
+    """One context (the persistent decode kernel) shared by the tests."""
     from qwen_fpga_b200 import api
     d = api.Decoder(blob_path, max_ctx=MAX_CTX)
-    d.set_engine(request.param)
-    assert d.engine == request.param
     yield d
     d.close()
 
@@ -104,26 +101,35 @@ def test_config0_w8a8_teacher_forced_matches_golden(dec):
 
 
 def test_config2_w8a8_warm_step_matches_golden(dec, cfg):
-    """ACT_INT8 warm start (rec N(0,0.1), 4096 cached positions N(0,1)).
+    """ACT_INT8 warm start (rec N(0,0.1), 4096 cached positions N(0,1)), six
+    greedy steps fed back as the golden feeds them.
 
     This start is chaotic: the golden's own step-0 logits move by 1.75e-2
     (relative to max |logit|) when its warm state is perturbed by 3e-7 relative
-    (fixture key step0_sens_3e-07).  Bar: identical step-0 argmax and step-0
-    logits within 0.1."""
+    (fixture key step0_sens_3e-07).  Bar: all six argmaxes identical to the
+    golden's, and the step-0 and step-5 logits within 0.1 (measured on B200:
+    4.9e-2 and 5.8e-2).  The integer arithmetic under this chaos is pinned
+    bit-exactly by tests/test_gpu_w8a8_capture.py."""
     fx = fixture("config2.npz")
     assert float(fx["step0_sens_3e-07"]) > 1e-3
     st = P.warm_state(cfg, int(fx["T0"]), seed=2)
     dec.reset()
     dec.set_act_int8(True)
+    errs = {}
     try:
         dec.import_state(st)
-        am, lg = dec.decode_step(int(fx["first_token"]), want_logits=True)
+        tok = int(fx["first_token"])
+        for j in range(len(fx["argmax"])):
+            am, lg = dec.decode_step(tok, want_logits=True)
+            assert am == int(fx["argmax"][j]), f"step {j}"
+            if f"step{j}_sample" in fx.files:
+                errs[j] = logits_close(lg, fx, f"step{j}")
+            tok = am
     finally:
         dec.set_act_int8(False)
-    err = logits_close(lg, fx, "step0")
-    print(f"W8A8 warm step-0 logits rel err {err:.3e}")
-    assert am == int(fx["argmax"][0])
-    assert err < 0.1
+    print(f"W8A8 warm logits rel err {errs}")
+    assert sorted(errs) == [0, 5]
+    assert max(errs.values()) < 0.1
 
 
 def test_config3_long_context_matches_golden(dec, cfg):
@@ -183,27 +189,6 @@ def test_matches_reference_hls_decoder(dec, blob_path):
     ref.close()
 
 
-def test_engines_agree(blob_path):
-    """The persistent weight-streaming kernel and the graph of per-phase kernels
-    share the exact-integer GEMVs and differ only in fp32 reduction order (the
-    rmsnorm sums, the delta rule's column sums, the order GEMV partials are
-    combined): same argmax and logits within 3e-5 of each other (W8A32),
-    three times tighter than the golden bar.  Measured on B200: 6e-6 .. 1.1e-5
-    over these 12 steps."""
-    from qwen_fpga_b200 import api
-    fx = fixture("config0.npz")
-    toks = fx["prompt"].tolist()[:12]
-    out = {}
-    for eng in (1, 0):
-        d = api.Decoder(blob_path, max_ctx=64)
-        d.set_engine(eng)
-        out[eng] = [d.decode_step(t, want_logits=True) for t in toks]
-        d.close()
-    for (a1, l1), (a0, l0) in zip(out[1], out[0]):
-        assert a1 == a0
-        assert np.abs(l1 - l0).max() <= 3e-5 * np.abs(l0).max()
-
-
 def test_errors_are_reported(dec):
     from qwen_fpga_b200 import api
     with pytest.raises(api.QwenError) as e:
@@ -212,7 +197,6 @@ def test_errors_are_reported(dec):
     with pytest.raises(api.QwenError):
         dec.decode_step(-1)
     small = api.Decoder(dec_blob_path(dec), max_ctx=4)
-    small.set_engine(dec.engine)
     try:
         for t in range(4):
             small.decode_step(t, want_logits=False)
