@@ -30,18 +30,22 @@ typedef struct CUstream_st* qwen_stream_t; /* same handle as cudaStream_t */
 
 /* Load a packed int8 blob (scripts/pack_weights.py:28-101 layout) and its
  * index (either the flat weights.idx of scripts/emit_weight_index.py:1-22 or
- * the *.manifest.json of pack_weights.py:93-101) onto the GPU and create one
- * batch-1 decode state with room for max_ctx cached positions per attention
- * layer.  Replaces the blob mmap + DecodeState set-up of
- * hls/tb/run_hls.cpp:27-52 and golden/model.py:97-107.  n_gpus must be 1;
- * device_ids may be NULL (device 0).  max_batch must be 1. */
+ * the *.manifest.json of pack_weights.py:93-101) onto the GPU and create
+ * max_batch decode states (golden/model.py:86-107 DecodeState, one per
+ * sequence) with room for max_ctx cached positions per attention layer each.
+ * Replaces the blob mmap + DecodeState set-up of hls/tb/run_hls.cpp:27-52 and
+ * golden/model.py:97-107.  n_gpus must be 1; device_ids may be NULL (device
+ * 0).  max_batch in [1, 64]: 1 = the batch-1 persistent decode kernel; > 1 =
+ * the batched engine (sequences 0 .. max_batch-1, each with its own DeltaNet
+ * state, conv history and KV cache; projections as tcgen05 int8 GEMMs over
+ * the batch's tokens). */
 int qwen_create(const char* blob_path, const char* index_path, int n_gpus,
                 const int* device_ids, int max_ctx, int max_batch, qwen_ctx** out);
 
 /* Tensor parallelism over tp_world (1, 2, 4 or 8) GPUs of one node, one
  * process and one context per GPU: the weight sharding of a multi-device
- * decode step (the reference runs one device; BASELINE north_star names the
- * split).  Rank tp_rank of the job keeps the full weights on device
+ * decode step (the reference runs one device; the split follows the
+ * weights' natural shards).  Rank tp_rank of the job keeps the full weights on device
  * device_id and computes its shard: DeltaNet heads, attention KV groups (all
  * four query heads of each), gate/up rows and down columns in 128-column
  * blocks, out/o columns by head, and a vocab slice of the head.  Row-parallel
@@ -146,13 +150,22 @@ int qwen_trace_read(qwen_ctx* ctx, unsigned long long* out, int max_words, int* 
 int qwen_capture_phase(qwen_ctx* ctx, int phase);
 int qwen_capture_read(qwen_ctx* ctx, float* out, int max_floats);
 
-/* One decode step for each of `batch` (must be 1) tokens: embed, 24 layers,
- * final norm, tied head, argmax (first index on ties).  Mirrors
- * golden/model.py:243-267 decode_step and hls/src/qwen_synth.hpp:39-92
- * qwen_top.  tok and argmax_out are host pointers; logits_out (nullable) may be
- * a host or device pointer of vocab (248320) floats. */
+/* One decode step for each of `batch` tokens: embed, 24 layers, final norm,
+ * tied head, argmax (first index on ties).  Mirrors golden/model.py:243-267
+ * decode_step and hls/src/qwen_synth.hpp:39-92 qwen_top.  A max_batch 1
+ * context takes batch 1; a batched context steps sequences 0 .. batch-1
+ * (batch <= max_batch) together, tok[b] feeding sequence b.  tok and
+ * argmax_out (batch ints) are host pointers; logits_out (nullable) may be a
+ * host or device pointer of batch x vocab (248320) floats, sequence-major.
+ * On a batched context tok may be NULL: every sequence then takes its own
+ * previous argmax (greedy continuation). */
 int qwen_decode_step(qwen_ctx* ctx, const int* tok, int batch, float* logits_out,
                      int* argmax_out);
+
+/* Batched context only: `steps` greedy steps of sequences 0 .. batch-1 (each
+ * fed its previous argmax), timed on the device (decode steps only, as
+ * run_prompt.py:80-98 times them); seconds receives the device time. */
+int qwen_decode_timed(qwen_ctx* ctx, int batch, int steps, double* seconds);
 
 /* Prefill n_prompt tokens one at a time, then n_new greedy steps; out_ids gets
  * the n_new generated ids (golden/model.py:270-280, run_prompt.py:80-98).
@@ -179,6 +192,17 @@ int qwen_gemv_i8_f32(float* y, const int8_t* w, const float* s, const float* x, 
  * alignment rules as above. */
 int qwen_gemv_i8_i8(int32_t* acc, float* y, const int8_t* w, const float* sw,
                     const int8_t* xq, float sx, int N, int K, qwen_stream_t stream);
+
+/* The same operator over a batch of B activation vectors (the projection
+ * datapath of a batched context), on device pointers: acc[b*N + o] =
+ * sum_i w[o,i]*xq[b*K + i] exactly in int32 on the tensor cores
+ * (tcgen05.mma kind::i8, 128 weight rows x B tokens per tile) and
+ * y[b*N + o] = acc * (sx[b] * sw[o]) in fp32.  acc and y are each nullable
+ * (not both).  N a multiple of 128, K of 128 in [128, 4096], B in [1, 64];
+ * w and xq 16-byte aligned.  Allocates its scratch (the weights re-laid as
+ * tiles) on the stream and returns after the stream has drained. */
+int qwen_gemm_i8_i8(int32_t* acc, float* y, const int8_t* w, const float* sw,
+                    const int8_t* xq, const float* sx, int N, int K, int B, qwen_stream_t stream);
 
 /* Allocation-free GEMV + argmax on device pointers (no counterpart in the
  * reference): y = s .* (W x) exactly as qwen_gemv_i8_f32 computes it, and

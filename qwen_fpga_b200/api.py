@@ -82,6 +82,8 @@ def load() -> C.CDLL:
     L.qwen_generate.argtypes = [_vp, _ip, C.c_int, C.c_int, _ip, C.POINTER(C.c_double)]
     L.qwen_gemv_i8_f32.argtypes = [_vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]
     L.qwen_gemv_i8_i8.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_float, C.c_int, C.c_int, _vp]
+    L.qwen_gemm_i8_i8.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp]
+    L.qwen_decode_timed.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(C.c_double)]
     L.qwen_delta_rule_layer.argtypes = [_vp] * 7 + [_vp]
     L.qwen_gemv_i8_f32_argmax_noalloc.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]
     L.qwen_capture_phase.argtypes = [_vp, C.c_int]
@@ -290,6 +292,105 @@ class Decoder:
         return DecodeStateView(conv, rec, list(kc), list(vc), pos.value)
 
 
+class BatchDecoder:
+    """One GPU context holding max_batch sequences, each with its own decode
+    state (golden/model.py:86-107), stepped together (golden/model.py:243-267
+    per sequence) by the batched engine: int8 projections on tcgen05 over the
+    batch's tokens."""
+
+    def __init__(self, blob_path: str, max_batch: int, index_path: str | None = None, device: int = 0,
+                 max_ctx: int = 4096, act_int8: bool = True):
+        L = load()
+        if index_path is None:
+            index_path = os.path.splitext(blob_path)[0] + ".idx"
+        self.max_ctx, self.max_batch = int(max_ctx), int(max_batch)
+        h = _vp()
+        dev = (C.c_int * 1)(device)
+        _check(L.qwen_create(blob_path.encode(), index_path.encode(), 1, dev, self.max_ctx, self.max_batch,
+                             C.byref(h)))
+        self.h = h
+        self.set_act_int8(act_int8)
+
+    def close(self):
+        if getattr(self, "h", None):
+            load().qwen_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_act_int8(self, on: bool):
+        _check(load().qwen_set_act_int8(self.h, 1 if on else 0), self.h)
+        self.act_int8 = bool(on)
+
+    def reset(self, seq: int = -1):
+        """Zero sequence seq's state (-1: every sequence)."""
+        _check(load().qwen_reset(self.h, int(seq)), self.h)
+
+    def import_state(self, seq: int, st):
+        """st: a golden DecodeState (conv, rec, kc / vc lists of [T,2,256], pos) for sequence seq."""
+        conv = np.ascontiguousarray(st.conv, np.float32)
+        rec = np.ascontiguousarray(st.rec, np.float32)
+        T = int(st.kc[0].shape[0]) if len(st.kc) else 0
+        kc = np.ascontiguousarray(np.stack([np.asarray(k, np.float32) for k in st.kc])) if T else None
+        vc = np.ascontiguousarray(np.stack([np.asarray(v, np.float32) for v in st.vc])) if T else None
+        _check(load().qwen_state_import(self.h, int(seq), _fptr(conv), _fptr(rec), _fptr(kc), _fptr(vc), T,
+                                        int(st.pos)), self.h)
+
+    def export_state(self, seq: int) -> DecodeStateView:
+        T, pos = C.c_int(), C.c_int()
+        L = load()
+        _check(L.qwen_state_export(self.h, int(seq), None, None, None, None, C.byref(T), C.byref(pos)), self.h)
+        conv = np.empty((18, 6144, 4), np.float32)
+        rec = np.empty((18, 16, 128, 128), np.float32)
+        kc = np.empty((6, T.value, 2, 256), np.float32)
+        vc = np.empty((6, T.value, 2, 256), np.float32)
+        _check(L.qwen_state_export(self.h, int(seq), _fptr(conv), _fptr(rec), _fptr(kc) if T.value else None,
+                                   _fptr(vc) if T.value else None, C.byref(T), C.byref(pos)), self.h)
+        return DecodeStateView(conv, rec, list(kc), list(vc), pos.value)
+
+    def step(self, toks, want_logits: bool = False, out=None):
+        """One step of sequences 0 .. len(toks)-1, toks[b] feeding sequence b.
+        Returns (argmax list, logits [B, VOCAB] or None); `out` (optional): a
+        float32 array of B * VOCAB elements the logits are written into."""
+        t = np.ascontiguousarray(np.asarray(toks, np.int32))
+        B = int(t.size)
+        am = np.empty(B, np.int32)
+        lg = None
+        if out is not None:
+            if out.dtype != np.float32 or out.size != B * VOCAB or not out.flags["C_CONTIGUOUS"]:
+                raise ValueError("out must be a contiguous float32 array of B * VOCAB elements")
+            lg = out
+        elif want_logits:
+            lg = np.empty((B, VOCAB), np.float32)
+        _check(load().qwen_decode_step(self.h, t.ctypes.data_as(_ip), B, lg.ctypes.data if lg is not None else None,
+                                       am.ctypes.data_as(_ip)), self.h)
+        return [int(v) for v in am], lg
+
+    def step_greedy(self, batch: int, want_logits: bool = False):
+        """One step in which every sequence b < batch takes its previous argmax."""
+        am = np.empty(batch, np.int32)
+        lg = np.empty((batch, VOCAB), np.float32) if want_logits else None
+        _check(load().qwen_decode_step(self.h, None, int(batch), lg.ctypes.data if lg is not None else None,
+                                       am.ctypes.data_as(_ip)), self.h)
+        return [int(v) for v in am], lg
+
+    def timed(self, batch: int, steps: int) -> float:
+        """`steps` greedy steps of sequences 0 .. batch-1; device seconds."""
+        sec = C.c_double()
+        _check(load().qwen_decode_timed(self.h, int(batch), int(steps), C.byref(sec)), self.h)
+        return sec.value
+
+
 # ---------------------------------------------------------------- golden-shaped façade
 
 def decode_step(dec: Decoder, cfg, tok: int, st=None):
@@ -375,6 +476,33 @@ def gemv_i8_i8(w, sw, xq, sx, acc=None, y=None, stream=None, want_acc=True, want
     with torch.cuda.device(w.device):
         rc = load().qwen_gemv_i8_i8(_ptr(acc if want_acc else None), _ptr(y if want_y else None),
                                     _ptr(w), _ptr(sw), _ptr(xq), float(sx), N, K, _stream(stream))
+    _check(rc)
+    return acc, y
+
+
+def gemm_i8_i8(w, sw, xq, sx, acc=None, y=None, stream=None, want_acc=True, want_y=True):
+    """Batched int8 x int8 projection on the tensor cores: acc[b] = w @ xq[b]
+    (int32, exact), y[b] = acc[b] * sx[b] * sw, for torch CUDA tensors w int8
+    [N, K], sw fp32 [N], xq int8 [B, K], sx fp32 [B].  Returns (acc [B, N], y [B, N])."""
+    import torch
+    N, K = _gemv_shape(w)
+    if xq is None or xq.dim() != 2:
+        raise ValueError("xq must be a 2-D [B, K] tensor")
+    B = int(xq.shape[0])
+    _need("xq", xq, torch.int8, (B, K), w.device)
+    _need("sx", sx, torch.float32, (B,), w.device)
+    _need("sw", sw, torch.float32, (N,), w.device)
+    if want_acc and acc is None:
+        acc = torch.empty((B, N), dtype=torch.int32, device=w.device)
+    if want_y and y is None:
+        y = torch.empty((B, N), dtype=torch.float32, device=w.device)
+    if want_acc:
+        _need("acc", acc, torch.int32, (B, N), w.device)
+    if want_y:
+        _need("y", y, torch.float32, (B, N), w.device)
+    with torch.cuda.device(w.device):
+        rc = load().qwen_gemm_i8_i8(_ptr(acc if want_acc else None), _ptr(y if want_y else None), _ptr(w),
+                                    _ptr(sw), _ptr(xq), _ptr(sx), N, K, B, _stream(stream))
     _check(rc)
     return acc, y
 

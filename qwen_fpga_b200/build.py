@@ -15,9 +15,9 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "libqwenb200.so")
-SOURCES = ["csrc/runtime.cu", "csrc/delta.cu", "csrc/gemv.cu", "csrc/persist.cu", "csrc/persist_tp.cu",
+SOURCES = ["csrc/runtime.cu", "csrc/batch.cu", "csrc/delta.cu", "csrc/gemv.cu", "csrc/persist.cu", "csrc/persist_tp.cu",
            "csrc/noalloc.cu", "csrc/pack.cpp"]
-HEADERS = ["csrc/common.cuh", "csrc/delta.cuh", "csrc/gemv.cuh", "csrc/persist.cuh", "csrc/noalloc.cuh",
+HEADERS = ["csrc/common.cuh", "csrc/batch.cuh", "csrc/tc.cuh", "csrc/delta.cuh", "csrc/gemv.cuh", "csrc/persist.cuh", "csrc/noalloc.cuh",
            "../include/qwen_b200.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "../../include/qwen_b200.h"
+#include "batch.cuh"
 #include "common.cuh"
 #include "delta.cuh"
 #include "gemv.cuh"
@@ -217,6 +218,8 @@ struct qwen_ctx {
   unsigned long long* tv_base = nullptr;
   size_t tv_words = 0;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  int max_batch = 1;
+  BatchEngine* be = nullptr;            // max_batch > 1: the batched engine owns the sequences
 };
 
 namespace {
@@ -444,6 +447,7 @@ int qwen_destroy(qwen_ctx* c) {
   if (!c) return QWEN_OK;
   cudaSetDevice(c->dev);
   if (c->st) cudaStreamSynchronize(c->st);
+  batch_destroy(c->be);
   for (void* p : c->ipc_open) cudaIpcCloseMemHandle(p);
   for (void* p : c->allocs) cudaFree(p);
   if (c->h_ctl) cudaFreeHost(c->h_ctl);
@@ -465,7 +469,8 @@ int create_impl(const char* blob_path, const char* index_path, int dev, int tp_r
   if (!out) return fail(nullptr, QWEN_ERR_ARG, "out is null");
   *out = nullptr;
   if (!blob_path || !index_path) return fail(nullptr, QWEN_ERR_ARG, "blob_path / index_path is null");
-  if (max_batch != 1) return fail(nullptr, QWEN_ERR_ARG, "max_batch must be 1");
+  if (max_batch < 1 || max_batch > BATCH_MAX) return fail(nullptr, QWEN_ERR_ARG, "max_batch must be in [1, %d]", BATCH_MAX);
+  if (max_batch > 1 && tp_world != 1) return fail(nullptr, QWEN_ERR_ARG, "a batched context runs on one GPU");
   if (max_ctx < 1 || max_ctx > MAX_CTX) return fail(nullptr, QWEN_ERR_ARG, "max_ctx must be in [1, %d]", MAX_CTX);
   TpPlan plan;
   {
@@ -649,11 +654,23 @@ int create_impl(const char* blob_path, const char* index_path, int dev, int tp_r
     }
     if (persist_max_blocks_per_sm() < 1) { fail(c, QWEN_ERR_STATE, "persistent kernel does not fit"); return bail(QWEN_ERR_STATE); }
   }
+  c->max_batch = max_batch;
+  if (max_batch > 1) {
+    std::string berr;
+    c->be = batch_create(c->Mh, c->P.head_tiles, c->S.rope, c->max_rope, max_batch, max_ctx, c->sm_count, c->st, berr);
+    if (!c->be) { fail(c, QWEN_ERR_CUDA, "batched engine: %s", berr.c_str()); return bail(QWEN_ERR_CUDA); }
+  }
   {
     cudaError_t e = cudaDeviceSynchronize();
     if (e != cudaSuccess) { fail(c, QWEN_ERR_CUDA, "create: %s", cudaGetErrorString(e)); return bail(QWEN_ERR_CUDA); }
   }
   *out = c;
+  return QWEN_OK;
+}
+
+// A batched context's entry points report through the context's error string.
+int batch_rc(qwen_ctx* c, int rc, const std::string& err) {
+  if (rc != QWEN_OK) return fail(c, rc, "%s", err.c_str());
   return QWEN_OK;
 }
 
@@ -732,6 +749,10 @@ int qwen_tp_vocab_range(qwen_ctx* c, int* lo, int* hi) {
 int qwen_reset(qwen_ctx* c, int seq) {
   int rc;
   if ((rc = check_ctx(c))) return rc;
+  if (c->be) {
+    std::string err;
+    return batch_rc(c, batch_reset(c->be, seq, err), err);
+  }
   if (seq != 0) return fail(c, QWEN_ERR_ARG, "seq must be 0 (batch 1)");
   QCUDA(c, cudaMemsetAsync(c->S.conv, 0, (size_t)NLIN * CONVD * CONVK * 4, c->st));
   QCUDA(c, cudaMemsetAsync(c->S.rec, 0, (size_t)NLIN * LH * LK * LV * 4, c->st));
@@ -803,6 +824,10 @@ int qwen_state_import(qwen_ctx* c, int seq, const float* conv, const float* rec,
                       const float* vc, int T, int pos) {
   int rc;
   if ((rc = check_ctx(c))) return rc;
+  if (c->be) {
+    std::string err;
+    return batch_rc(c, batch_import(c->be, seq, conv, rec, kc, vc, T, pos, err), err);
+  }
   if (seq != 0) return fail(c, QWEN_ERR_ARG, "seq must be 0 (batch 1)");
   if (!conv || !rec) return fail(c, QWEN_ERR_ARG, "conv / rec is null");
   if (T < 0 || T > c->max_ctx - 1) return fail(c, QWEN_ERR_ARG, "T=%d outside [0, %d]", T, c->max_ctx - 1);
@@ -828,6 +853,10 @@ int qwen_state_export(qwen_ctx* c, int seq, float* conv, float* rec, float* kc, 
                       int* pos) {
   int rc;
   if ((rc = check_ctx(c))) return rc;
+  if (c->be) {
+    std::string err;
+    return batch_rc(c, batch_export(c->be, seq, conv, rec, kc, vc, T, pos, err), err);
+  }
   if (seq != 0) return fail(c, QWEN_ERR_ARG, "seq must be 0 (batch 1)");
   QCUDA(c, cudaStreamSynchronize(c->st));
   if (conv) {
@@ -853,7 +882,11 @@ int qwen_state_export(qwen_ctx* c, int seq, float* conv, float* rec, float* kc, 
 int qwen_decode_step(qwen_ctx* c, const int* tok, int batch, float* logits_out, int* argmax_out) {
   int rc;
   if ((rc = check_ctx(c))) return rc;
-  if (batch != 1) return fail(c, QWEN_ERR_ARG, "batch must be 1");
+  if (c->be) {
+    std::string err;
+    return batch_rc(c, batch_step(c->be, tok, batch, c->act_int8 != 0, logits_out, argmax_out, err), err);
+  }
+  if (batch != 1) return fail(c, QWEN_ERR_ARG, "batch must be 1 (a context created with max_batch 1)");
   if (!tok) return fail(c, QWEN_ERR_ARG, "tok is null");
   if (tok[0] < 0 || tok[0] >= VOCAB) return fail(c, QWEN_ERR_ARG, "token %d outside [0, %d)", tok[0], VOCAB);
   if ((rc = check_tp(c))) return rc;
@@ -884,6 +917,7 @@ int qwen_generate(qwen_ctx* c, const int* prompt, int n_prompt, int n_new, int* 
                   double* decode_seconds) {
   int rc;
   if ((rc = check_ctx(c))) return rc;
+  if (c->be) return fail(c, QWEN_ERR_STATE, "qwen_generate runs batch-1 contexts; a batched context steps with qwen_decode_step");
   if (!prompt || n_prompt < 1 || n_new < 0) return fail(c, QWEN_ERR_ARG, "need n_prompt >= 1, n_new >= 0");
   if ((rc = check_tp(c))) return rc;
   if (n_new > 0 && !out_ids) return fail(c, QWEN_ERR_ARG, "out_ids is null");
@@ -921,6 +955,14 @@ int qwen_generate(qwen_ctx* c, const int* prompt, int n_prompt, int n_new, int* 
   return QWEN_OK;
 }
 
+int qwen_decode_timed(qwen_ctx* c, int batch, int steps, double* seconds) {
+  int rc;
+  if ((rc = check_ctx(c))) return rc;
+  if (!c->be) return fail(c, QWEN_ERR_STATE, "qwen_decode_timed needs a context created with max_batch > 1");
+  std::string err;
+  return batch_rc(c, batch_timed_steps(c->be, batch, c->act_int8 != 0, steps, seconds, err), err);
+}
+
 // ------------------------------------------------------------------ operators
 
 static int sm_count_current() {
@@ -956,6 +998,24 @@ int qwen_gemv_i8_i8(int32_t* acc, float* y, const int8_t* w, const float* sw, co
   cudaError_t e = enqueue_gemv(y, acc, w, sw, nullptr, xq, sx, N, K, sm_count_current(),
                                reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(nullptr, QWEN_ERR_CUDA, "gemv_i8_i8 launch: %s", cudaGetErrorString(e));
+  return QWEN_OK;
+}
+
+int qwen_gemm_i8_i8(int32_t* acc, float* y, const int8_t* w, const float* sw, const int8_t* xq,
+                    const float* sx, int N, int K, int B, qwen_stream_t stream) {
+  if (!w || !xq || !sx || !sw || (!acc && !y)) return fail(nullptr, QWEN_ERR_ARG, "null pointer");
+  if (N < GT_M || N % GT_M) return fail(nullptr, QWEN_ERR_ARG, "N must be a positive multiple of %d", GT_M);
+  if (K < GT_KS || K % GT_KS || K > 4096) return fail(nullptr, QWEN_ERR_ARG, "K must be a multiple of %d in [%d, 4096]", GT_KS, GT_KS);
+  if (B < 1 || B > BATCH_MAX) return fail(nullptr, QWEN_ERR_ARG, "B must be in [1, %d]", BATCH_MAX);
+  if (reinterpret_cast<uintptr_t>(w) % 16 || reinterpret_cast<uintptr_t>(xq) % 16)
+    return fail(nullptr, QWEN_ERR_ARG, "w and xq must be 16-byte aligned");
+  float* yy = y;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (!yy && cudaMallocAsync((void**)&yy, (size_t)N * B * 4, st) != cudaSuccess)
+    return fail(nullptr, QWEN_ERR_CUDA, "gemm_i8_i8: scratch");
+  cudaError_t e = gemm_i8_i8_batched(acc, yy, w, sw, xq, sx, N, K, B, st);
+  if (!y) cudaFreeAsync(yy, st);
+  if (e != cudaSuccess) return fail(nullptr, QWEN_ERR_CUDA, "gemm_i8_i8: %s", cudaGetErrorString(e));
   return QWEN_OK;
 }
 

@@ -17,6 +17,13 @@ Fixtures (all small; logits are stored as fixed-index samples + top-k):
 * ``config2.npz``  -- ACT_INT8 (W8A8) warm start: rec N(0,0.1), 4096 cached
   positions N(0,1), first token ``default_rng(0).integers(vocab)``; 6 greedy steps.
 * ``config3.npz``  -- W8A32 warm start with 32768 cached positions; 8 greedy steps.
+* ``config4.npz``  -- batched decode: four sampled sequences of a 64-sequence
+  batch (batch slots CONFIG4_SLOTS), each its own golden DecodeState with a
+  2048-position warm start (warm_state seed 40 + i) and first token
+  ``default_rng(100 + i).integers(vocab)``; 6 greedy steps each under ACT_INT8
+  (W8A8) and under W8A32, logit digests and top-2 margins of every step, and
+  the golden's own W8A8 agreement with itself when the warm DeltaNet state
+  moves by 3e-7 relative.
 * ``deltanet_trace.npz`` -- delta-rule inputs/outputs of linear layer 0 on a
   warm state (5 prompt tokens, then the 6th traced), the capture pattern of
   scripts/export_testvectors.py:31-40; full q,k,v,g,beta,o and S for heads 0 and 9.
@@ -49,6 +56,7 @@ from oracle.golden_port import warm_state  # noqa: E402
 
 VOCAB = 248320
 SAMPLE_IDX = np.sort(np.random.default_rng(7).choice(VOCAB, 4096, replace=False))
+CONFIG4_SLOTS = [0, 21, 42, 63]
 GEMV_SHAPES = [(6144, 1024), (2048, 1024), (7168, 1024), (1024, 3584), (1024, 2048),
                (4096, 1024), (248320, 1024)]
 
@@ -286,6 +294,52 @@ def main():
         out["argmax"] = np.array(argmax, np.int64)
         np.savez_compressed(os.path.join(HERE, "config3.npz"), **out)
         print(f"config3: {time.time() - t0:.1f}s argmax={argmax}")
+
+    if only is None or "config4" in only:
+        # batched decode: four sampled sequences of the 64-sequence batch, each
+        # its own DecodeState with a 2048-position warm start
+        t0 = time.time()
+        out = {"slots": np.array(CONFIG4_SLOTS, np.int64), "T0": np.int64(2048)}
+        firsts = [int(np.random.default_rng(100 + i).integers(0, VOCAB)) for i in range(len(CONFIG4_SLOTS))]
+        out["first_token"] = np.array(firsts, np.int64)
+        for mode, i8 in (("w8a8", True), ("w8a32", False)):
+            G.ACT_INT8 = i8
+            argmaxes, margins = [], []
+            for i in range(len(CONFIG4_SLOTS)):
+                st = golden_state_from(warm_state(cfg, 2048, seed=40 + i))
+                tok = firsts[i]
+                am, mg = [], []
+                for j in range(6):
+                    logits = G.decode_step(W, cfg, tok, st)
+                    top2 = np.partition(logits, -2)[-2:]
+                    mg.append(float((top2[1] - top2[0]) / np.abs(logits).max()))
+                    tok = int(np.argmax(logits))
+                    am.append(tok)
+                    put(out, f"{mode}_seq{i}_step{j}", logit_digest(logits))
+                argmaxes.append(am)
+                margins.append(mg)
+                print(f"config4 {mode} seq {i}: argmax={am} margins={np.round(mg, 5).tolist()}", flush=True)
+            out[f"{mode}_argmax"] = np.array(argmaxes, np.int64)
+            out[f"{mode}_margin"] = np.array(margins, np.float32)
+        # the golden's own W8A8 spread: the same runs teacher-forced on the
+        # tokens above with the warm DeltaNet state perturbed by 3e-7 relative
+        G.ACT_INT8 = True
+        agree = []
+        for i in range(len(CONFIG4_SLOTS)):
+            pst = warm_state(cfg, 2048, seed=40 + i)
+            pert = np.random.default_rng(77 + i).standard_normal(pst.rec.shape).astype(np.float32)
+            pst.rec *= (1 + np.float32(3e-7) * pert).astype(np.float32)
+            st = golden_state_from(pst)
+            feed = [firsts[i]] + out["w8a8_argmax"][i][:-1].tolist()
+            n = 0
+            for j, tok in enumerate(feed):
+                n += int(int(np.argmax(G.decode_step(W, cfg, tok, st))) == int(out["w8a8_argmax"][i][j]))
+            agree.append(n)
+        out["w8a8_self_agreement_3e-07"] = np.array(agree, np.int64)
+        print(f"config4 golden W8A8 self-agreement under 3e-7: {agree}")
+        np.savez_compressed(os.path.join(HERE, "config4.npz"), **out)
+        G.ACT_INT8 = False
+        print(f"config4: {time.time() - t0:.1f}s")
 
     if only is None or "gemv" in only:
         import export_gemv_tv as TV   # reference quantiser q_i8_vec

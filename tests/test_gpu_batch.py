@@ -1,0 +1,254 @@
+"""GPU parity of the batched engine (contexts created with max_batch > 1):
+sequences 0 .. B-1 each own a golden DecodeState (golden/model.py:86-107) and
+step together through golden/model.py:243-267 decode_step.
+
+* the tensor-core GEMM operator: int32 accumulators bit-exact against numpy's
+  int64 product, y = acc * (sx[b] * sw[o]) bit-exact in fp32;
+* W8A32: every sequence's greedy ids equal to the golden's (config 0 stream)
+  and to the batch-1 persistent kernel's on other streams, logits within
+  1e-4 relative;
+* config 4: four sampled sequences of a 64-sequence batch, each with a
+  2048-position warm start: six greedy W8A32 ids equal to the golden's (logits
+  within 1e-4), and W8A8 agreement within the golden's own spread;
+* slot independence, greedy feedback, state round trips and error codes.
+"""
+
+import numpy as np
+import pytest
+
+from golden_util import LOGIT_RTOL, VOCAB, fixture, logits_close
+from oracle import golden_port as P
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def api():
+    from qwen_fpga_b200 import api as A
+    return A
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("N,K,B", [(256, 1024, 64), (384, 3584, 7), (128, 128, 1), (1024, 2048, 64),
+                                   (7168, 1024, 33)])
+def test_gemm_i8_i8_bit_exact(N, K, B):
+    rng = np.random.default_rng(N + K + B)
+    w = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    sw = rng.uniform(1e-3, 1e-2, N).astype(np.float32)
+    xq = rng.integers(-127, 128, (B, K), dtype=np.int8)
+    sx = rng.uniform(1e-3, 1e-2, B).astype(np.float32)
+    acc, y = api().gemm_i8_i8(dev(w), dev(sw), dev(xq), dev(sx))
+    torch.cuda.synchronize()
+    ref = (xq.astype(np.int64) @ w.T.astype(np.int64))
+    assert np.abs(ref).max() < 2 ** 31
+    ref = ref.astype(np.int32)
+    assert np.array_equal(acc.cpu().numpy(), ref)
+    y_ref = ref.astype(np.float32) * (sx[:, None] * sw[None, :])
+    assert np.array_equal(y.cpu().numpy(), y_ref)
+
+
+def test_gemm_i8_i8_rejects_bad_shapes():
+    A = api()
+    w = torch.zeros((100, 128), dtype=torch.int8, device="cuda")
+    with pytest.raises(ValueError):
+        A.gemm_i8_i8(w, torch.zeros(100, device="cuda"), torch.zeros((2, 64), dtype=torch.int8, device="cuda"),
+                     torch.zeros(2, device="cuda"))
+    with pytest.raises(A.QwenError) as e:
+        A.gemm_i8_i8(w, torch.zeros(100, device="cuda"), torch.zeros((2, 128), dtype=torch.int8, device="cuda"),
+                     torch.zeros(2, device="cuda"))
+    assert e.value.code == A.QWEN_ERR_ARG
+
+
+def _streams(B, n, first):
+    """Token streams: stream 0 = `first`, the others seeded uniform ids."""
+    out = [list(first[:n])]
+    for b in range(1, B):
+        out.append(np.random.default_rng(500 + b).integers(0, VOCAB, n).tolist())
+    return out
+
+
+def test_batch_w8a32_matches_golden_and_batch1(blob_path):
+    """Five sequences, 24 teacher-forced steps: stream 0 is config 0's token
+    stream (checked against the golden's argmax at every step and its logits at
+    steps 0 and 15), streams 1-4 are checked against the batch-1 persistent
+    kernel on the same tokens (ids at every step, logits at steps 0, 15, 23)."""
+    fx = fixture("config0.npz")
+    feed0 = fx["prompt"].tolist() + fx["generated"].tolist()
+    B, n, want = 5, 24, (0, 15, 23)
+    streams = _streams(B, n, feed0)
+    A = api()
+    bd = A.BatchDecoder(blob_path, max_batch=8, max_ctx=64, act_int8=False)
+    got_ids = np.zeros((B, n), np.int64)
+    got_lg = {}
+    try:
+        for i in range(n):
+            am, lg = bd.step([s[i] for s in streams], want_logits=i in want)
+            got_ids[:, i] = am
+            if lg is not None:
+                got_lg[i] = lg.copy()
+    finally:
+        bd.close()
+    assert got_ids[0].tolist() == fx["argmax"][:n].tolist()
+    for i in (0, 15):
+        assert logits_close(got_lg[i][0], fx, f"step{i}") < LOGIT_RTOL
+    ref = A.Decoder(blob_path, max_ctx=64)
+    try:
+        for b in range(1, B):
+            ref.reset()
+            for i in range(n):
+                am, lg = ref.decode_step(streams[b][i], want_logits=i in want)
+                assert am == got_ids[b, i], f"seq {b} step {i}"
+                if lg is not None:
+                    err = np.abs(got_lg[i][b] - lg).max() / np.abs(lg).max()
+                    assert err < LOGIT_RTOL, (b, i, err)
+    finally:
+        ref.close()
+
+
+def _config4_batch(blob_path, cfg, fx, act_int8):
+    """A 64-sequence batched context: slots CONFIG4_SLOTS carry the golden's
+    2048-position warm starts, the others cold states fed seeded tokens."""
+    slots = fx["slots"].tolist()
+    T0 = int(fx["T0"])
+    bd = api().BatchDecoder(blob_path, max_batch=64, max_ctx=T0 + 16, act_int8=act_int8)
+    for i, slot in enumerate(slots):
+        bd.import_state(slot, P.warm_state(cfg, T0, seed=40 + i))
+    toks = np.random.default_rng(9).integers(0, VOCAB, 64)
+    for i, slot in enumerate(slots):
+        toks[slot] = int(fx["first_token"][i])
+    return bd, slots, toks
+
+
+def test_config4_w8a32_sampled_sequences_match_golden(blob_path, cfg):
+    """Config 4 shape under W8A32: the four sampled sequences' six greedy ids
+    (each fed back) identical to the golden's, logits within 1e-4 at every step."""
+    fx = fixture("config4.npz")
+    bd, slots, toks = _config4_batch(blob_path, cfg, fx, act_int8=False)
+    errs = {}
+    try:
+        for j in range(6):
+            am, lg = bd.step(toks.tolist(), want_logits=True)
+            for i, slot in enumerate(slots):
+                assert am[slot] == int(fx["w8a32_argmax"][i][j]), f"seq {i} (slot {slot}) step {j}"
+                errs[(i, j)] = logits_close(lg[slot], fx, f"w8a32_seq{i}_step{j}")
+            toks = np.asarray(am)
+    finally:
+        bd.close()
+    print(f"config4 W8A32 logits rel err max {max(errs.values()):.2e}")
+    assert max(errs.values()) < LOGIT_RTOL
+
+
+def test_config4_w8a8_sampled_sequences_match_golden(blob_path, cfg):
+    """Config 4 under ACT_INT8 (W8A8), the four sampled sequences fed the
+    golden's own tokens.  W8A8 re-quantises every projection input with rint,
+    so an ulp anywhere can flip an int8 code and the flip persists in the
+    state: the golden itself, with its warm DeltaNet state moved by 3e-7
+    relative, agrees with itself on fx['w8a8_self_agreement_3e-07'] of the six
+    ids per sequence (the top-2 margins of the flipping steps are ~1e-2).
+    Bar: per sequence at least that agreement minus one, every step-0 id
+    identical, and step-0 logits within 0.1 of the golden's."""
+    fx = fixture("config4.npz")
+    bd, slots, toks = _config4_batch(blob_path, cfg, fx, act_int8=True)
+    golden = fx["w8a8_argmax"]
+    agree = [0] * len(slots)
+    errs = {}
+    try:
+        for j in range(6):
+            am, lg = bd.step(toks.tolist(), want_logits=True)
+            for i, slot in enumerate(slots):
+                agree[i] += int(am[slot] == int(golden[i][j]))
+                errs[(i, j)] = logits_close(lg[slot], fx, f"w8a8_seq{i}_step{j}")
+                if j == 0:
+                    assert am[slot] == int(golden[i][0]), f"seq {i} step 0"
+            toks = np.asarray(am)
+            for i, slot in enumerate(slots):
+                toks[slot] = int(golden[i][j])
+    finally:
+        bd.close()
+    self_agree = fx["w8a8_self_agreement_3e-07"].tolist()
+    print(f"config4 W8A8 agreement {agree} (golden self-agreement {self_agree}), logits rel err "
+          f"{ {k: round(v, 4) for k, v in errs.items()} }")
+    for i in range(len(slots)):
+        assert agree[i] >= self_agree[i] - 1, (i, agree, self_agree)
+    assert max(errs[(i, 0)] for i in range(len(slots))) < 0.1
+
+
+def test_batch_slots_are_independent_and_feedback_matches(blob_path, cfg):
+    """A state imported into two slots and fed the same token gives
+    bit-identical logits in both (the batch's other columns do not leak into a
+    sequence); import -> export is the identity; greedy feedback on the device
+    (tok = NULL) continues exactly like feeding the argmax back from the host."""
+    A = api()
+    st = P.warm_state(cfg, 40, seed=11)
+    st.conv[...] = np.random.default_rng(12).standard_normal(st.conv.shape).astype(np.float32)
+    bd = A.BatchDecoder(blob_path, max_batch=6, max_ctx=64, act_int8=True)
+    try:
+        bd.import_state(1, st)
+        bd.import_state(4, st)
+        ex = bd.export_state(4)
+        assert np.array_equal(ex.conv, st.conv) and np.array_equal(ex.rec, st.rec)
+        assert ex.pos == st.pos and np.array_equal(np.stack(ex.kc), np.stack(st.kc))
+        toks = [7, 100, 2000, 30000, 100, 248319]
+        am, lg = bd.step(toks, want_logits=True)
+        assert np.array_equal(lg[1], lg[4]) and am[1] == am[4]
+        ex = bd.export_state(1)
+        assert ex.pos == st.pos + 1 and ex.kc[0].shape[0] == 41
+        # host feedback
+        bd.reset()
+        bd.import_state(0, st)
+        a1, _ = bd.step([100])
+        a2, lg2 = bd.step([a1[0]], want_logits=True)
+        # device feedback from the same start
+        bd.reset()
+        bd.import_state(0, st)
+        b1, _ = bd.step([100])
+        b2, lg3 = bd.step_greedy(1, want_logits=True)
+        assert a1 == b1 and a2 == b2 and np.array_equal(lg2, lg3)
+    finally:
+        bd.close()
+
+
+def test_batch_timed_steps_advance_the_state(blob_path):
+    A = api()
+    bd = A.BatchDecoder(blob_path, max_batch=4, max_ctx=32, act_int8=True)
+    try:
+        bd.step([1, 2, 3, 4])
+        sec = bd.timed(4, 5)
+        assert sec > 0
+        assert bd.export_state(3).pos == 6 and bd.export_state(0).kc[0].shape[0] == 6
+    finally:
+        bd.close()
+
+
+def test_batch_errors(blob_path):
+    A = api()
+    bd = A.BatchDecoder(blob_path, max_batch=4, max_ctx=4, act_int8=True)
+    try:
+        with pytest.raises(A.QwenError) as e:
+            bd.step([1, 2, 3, 4, 5])
+        assert e.value.code == A.QWEN_ERR_ARG
+        with pytest.raises(A.QwenError) as e:
+            bd.step([1, VOCAB])
+        assert e.value.code == A.QWEN_ERR_ARG
+        with pytest.raises(A.QwenError) as e:
+            bd.reset(4)
+        assert e.value.code == A.QWEN_ERR_ARG
+        for _ in range(4):
+            bd.step([1, 2])
+        with pytest.raises(A.QwenError) as e:
+            bd.step([1, 2])              # sequences 0 and 1 hold max_ctx positions
+        assert e.value.code == A.QWEN_ERR_STATE
+        bd.reset(0)
+        bd.reset(1)
+        bd.step([5, 6, 7])              # a reset sequence starts again; sequence 2 has its own position
+        assert bd.export_state(1).pos == 1 and bd.export_state(2).pos == 1
+        h = A.load()
+        rc = h.qwen_generate(bd.h, (A.C.c_int * 1)(1), 1, 1, (A.C.c_int * 1)(), None)
+        assert rc == A.QWEN_ERR_STATE
+    finally:
+        bd.close()
+    with pytest.raises(A.QwenError):
+        A.BatchDecoder(blob_path, max_batch=65, max_ctx=8)
