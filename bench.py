@@ -14,8 +14,11 @@ tensors, plus fp32 K/V reads of the 6 attention layers).
 The same JSON line carries the other configs as sub-objects (each a stated
 sample of its workload): "gemv" (config 1: every int8 GEMV microbench shape,
 GB/s against the HBM peak, int32 accumulators checked exactly), "config2"
-(W8A8 warm start, 4096 cached positions, 256 greedy steps) and "config3"
-(W8A32, 32768 cached positions, 512 greedy steps).
+(W8A8 warm start, 4096 cached positions, 256 greedy steps), "config3"
+(W8A32, 32768 cached positions, 512 greedy steps) and "config4" (batched
+decode: 64 sequences, each with its own 2048-position warm start and DeltaNet
+state, W8A8 projections on the tcgen05 tensor cores; a stated sample of the
+128 greedy steps).
 
 Under torchrun (N > 1) the N ranks decode ONE sequence with tensor
 parallelism (qwen_fpga_b200.tp: heads, FFN columns and the vocab split across
@@ -186,6 +189,17 @@ def cpu_reference_hls(blob_path, n_steps):
                       f"config0 prompt prefill untimed + {n_steps} greedy decode steps timed"}
 
 
+def load_tensor_pipe():
+    """Tensor-pipe utilisation of the batched GEMMs from the committed ncu
+    summary (profiles/k_bt_gemm_config4.json), or None."""
+    p = os.path.join(REPO, "profiles", "k_bt_gemm_config4.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return None
+
+
 def load_traffic():
     p = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(p):
@@ -330,6 +344,51 @@ def timed_decode(dec, prompt, steps, tp=False, dist=None):
     return sec_total, ids0
 
 
+# config 4 (batched decode): per step, every sequence reads its KV (T positions
+# x 6 layers x K and V x 2 heads x 256 fp32) and reads + writes its DeltaNet
+# state (18 x 16 x 128 x 128 fp32 + conv history); the weights are read once
+# for the whole batch
+C4_BATCH, C4_T0 = 64, 2048
+C4_STATE = 2 * (18 * 16 * 128 * 128 * 4) + 2 * (18 * 6144 * 4)
+
+
+def c4_bytes_per_step(B, T):
+    return B_WEIGHTS + B * (KV_PER_POS * T + C4_STATE)
+
+
+def config4(blob_path, device, steps, warmup, B=C4_BATCH, T0=C4_T0):
+    """Config 4: B sequences with 2048-position warm starts (four distinct
+    synth.warm_state_arrays draws, seeds 40-43, each imported into B/4 slots),
+    first tokens default_rng(100 + b); one untimed step, `warmup` untimed
+    greedy steps, then `steps` greedy steps timed on the device
+    (qwen_decode_timed: tokens fed back on the device), then the same number
+    end to end through qwen_decode_step (host tokens in, host argmax out)."""
+    from qwen_fpga_b200 import api, synth
+    n_e2e = steps
+    bd = api.BatchDecoder(blob_path, max_batch=B, device=device,
+                          max_ctx=T0 + 1 + warmup + steps + n_e2e + 8, act_int8=True)
+    try:
+        for i in range(4):
+            st = synth.warm_state_arrays(T0, 40 + i)
+            for b in range(i, B, 4):
+                bd.import_state(b, st)
+            del st
+        first = [int(np.random.default_rng(100 + b).integers(0, VOCAB)) for b in range(B)]
+        am, _ = bd.step(first)
+        bd.timed(B, warmup)
+        t_mean = T0 + 1 + warmup + (steps - 1) / 2.0
+        sec = bd.timed(B, steps)
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            am, _ = bd.step(am)
+        e2e_sec = time.perf_counter() - t0
+    finally:
+        bd.close()
+    bstep = c4_bytes_per_step(B, t_mean)
+    return {"sec": sec, "steps": steps, "bytes_per_step": bstep, "e2e_sec": e2e_sec, "e2e_steps": n_e2e,
+            "t_mean": t_mean, "B": B}
+
+
 def warm_config(dec, T0, seed, n_steps, act_int8, tp=False, dist=None):
     """Configs 2 and 3: import the warm start (synth.warm_state_arrays: rec
     N(0, 0.1), T0 cached positions N(0, 1), the fixtures' recipe), feed the
@@ -360,8 +419,9 @@ def main():
     ap.add_argument("--e2e-episodes", type=int, default=4)
     ap.add_argument("--cpu-steps", type=int, default=24)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--configs", default="1,2,3",
-                    help="extra configs measured into the same line (comma list of 1, 2, 3; '' = none)")
+    ap.add_argument("--configs", default="1,2,3,4",
+                    help="extra configs measured into the same line (comma list of 1, 2, 3, 4; '' = none)")
+    ap.add_argument("--c4-steps", type=int, default=32, help="config 4: timed steps (a sample of its 128)")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent sequences per GPU instead of tensor parallelism")
     ap.add_argument("--gemv", action="store_true", help="config-1 GEMV microbench (one JSON line)")
@@ -492,6 +552,29 @@ def main():
     if world > 1:
         dist.barrier()   # every rank's last step is done before any context goes away
     dec.close()
+    # config 4: batched decode, every rank its own batch of 64 sequences (data parallel)
+    if "4" in configs:
+        r4 = config4(blob_path, local, max(1, args.c4_steps), W)
+        sec4, e2e4 = r4["sec"], r4["e2e_sec"]
+        if world > 1:
+            t = torch.tensor([sec4, e2e4], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            sec4, e2e4 = float(t[0].item()), float(t[1].item())
+        st4 = r4["steps"]
+        ach4 = r4["bytes_per_step"] * st4 / sec4 / 1e9
+        extra["config4"] = {
+            "workload": f"batched decode: {r4['B']} sequences per GPU, each its own 2048-position warm start "
+                        "(rec N(0,0.1), K/V N(0,1)); W8A8 (ACT_INT8) projections as tcgen05 int8 GEMMs; "
+                        f"{st4} of the 128 greedy steps timed (device-fed tokens), then {r4['e2e_steps']} more "
+                        "end to end", "batch_per_gpu": r4["B"], "n_gpus": world,
+            "parallelism": "1 GPU" if world == 1 else f"{world} GPUs, one batch each (data parallel)",
+            "value": world * r4["B"] * st4 / sec4, "unit": UNIT, "ms_per_step": sec4 / st4 * 1e3,
+            "bytes_per_step": r4["bytes_per_step"], "achieved_GB_s": ach4, "frac": ach4 / peak,
+            "mean_T": r4["t_mean"],
+            "e2e": {"value": world * r4["B"] * r4["e2e_steps"] / e2e4, "unit": UNIT,
+                    "h2d_bytes_per_step": 4 * r4["B"] + 800, "d2h_bytes_per_step": 4 * r4["B"] + 16,
+                    "what": "qwen_decode_step(batch 64): host tokens in, host argmax out"},
+            "tensor_pipe": load_tensor_pipe()}
     if "1" in configs and rank == 0 and world == 1:
         extra["gemv"] = {"workload": "config1: int8 x int8 GEMV microbench, every shape, weights from "
                                      "HBM (rotated copies > L2)", "kernel": "k_gemv (qwen_gemv_i8_i8)",

@@ -175,8 +175,6 @@ struct BtCtl {
 
 constexpr int AT_CL = 256;   // positions per attention chunk
 constexpr int BT_HEAD_TILES = VOCAB / GT_M;            // tied head tiles (1940)
-constexpr int BT_MAXTILES = (CONVD + VDIM) / GT_M;   // most tiles of one layer projection (64)
-static_assert(2 * FFN / GT_M <= BT_MAXTILES && (QPROJ + 2 * KVPROJ) / GT_M <= BT_MAXTILES, "split-K scratch");
 
 // ---------------------------------------------------------------- repack
 
@@ -213,13 +211,11 @@ struct GemmArgs {
   const float* sw;     // per row, tile order
   const int8_t* X;     // image [nslab][64 NPL][128]
   const float* xs;     // per token
-  int nslab, kspl;     // slabs of K; slabs per CTA (grid.y = ceil(nslab / kspl))
+  int nslab, kspl;     // slabs of K; slabs per CTA (grid.y = ceil(nslab / kspl) <= 8: one cluster per tile)
   int nb;              // live tokens
   int mode;
   float* Y;            // STORE / ADD: Y[b ldy + row]; SWIGLU: Y[b ldy + 64 tile + r]
   int ldy;
-  int32_t* part;       // split-K sums [ntiles][64 NPL][128], zero between uses
-  int* cnt;            // [ntiles] arrival counters, zero between uses
   int32_t* acc_out;    // nullable (NPL 1): acc[b nrows + row]
   int nrows;
   int* err;
@@ -230,15 +226,260 @@ struct GC {
   static constexpr int NR = 64 * NPL;
   static constexpr int BBYTES = NR * GT_KS;
   static constexpr int STAGE = GT_SLAB + BBYTES;
-  static constexpr int NST = 4;
+  // ring depth: W8A8 holds every slab of an unsplit K = 1024 tile in flight
+  // (one CTA per SM)
+  static constexpr int NST = NPL == 1 ? 8 : 5;
   static constexpr int OFF_BAR = NST * STAGE;
-  static constexpr int SMEM = OFF_BAR + 128;   // barriers, TMEM slot, flags
+  // W8A32 split-K epilogue (pull): the parked sums (128 rows x (NR + 4) ints)
+  // and, after them, the SwiGLU exchange (64 tokens x 128 rows floats), inside the ring
+  static constexpr int XCH = ((128 * (NR + 4) * 4 + 1023) / 1024) * 1024;
+  static_assert(XCH + 64 * 128 * 4 <= OFF_BAR, "split-K scratch inside the ring");
+  // barriers (full[NST], empty[NST], accf), the TMEM slot, three flags
+  static constexpr int OFF_SLOT = OFF_BAR + 16 * NST + 8;
+  static constexpr int SMEM = OFF_SLOT + 16;
   static constexpr int TCOLS = NPL == 1 ? 64 : 256;
   static constexpr unsigned IDESC = tc::idesc_i8(GT_M, NR);
 };
+static_assert(GC<1>::SMEM + 1024 <= 227 * 1024 && GC<3>::SMEM + 1024 <= 227 * 1024, "GEMM shared memory");
 
+// W8A8 split-K over a (1, S, 1) cluster (push): tokens are owned in
+// contiguous ranges of TPC; every CTA stores its int32 sums of each 4-token
+// group straight into the owner's receive buffer (slot = source rank; remote
+// 16-byte stores over distributed shared memory, fire and forget), one
+// cluster barrier, then each owner adds its S slots from its own shared
+// memory.  The receive buffer sits at the end of the ring, beyond the stages
+// the CTA's K range uses (checked).
+__host__ __device__ constexpr int push_tpc(int S) { return ((64 + S - 1) / S + 3) & ~3; }
+__host__ __device__ constexpr int push_rsp(int S) {
+  return (push_tpc(S) + 4) % 16 == 0 ? push_tpc(S) + 8 : push_tpc(S) + 4;
+}
+// ring offset of the receive buffer of an S-CTA cluster
+__host__ __device__ constexpr int push_off(int S) { return GC<1>::OFF_BAR - S * 128 * push_rsp(S) * 4; }
+template <int S>
+struct SplitPush {
+  static constexpr int TPC = push_tpc(S);   // tokens per owner
+  static constexpr int RSP = push_rsp(S);   // padded row (ints)
+  static constexpr int OFF = push_off(S);
+  static_assert(OFF > 0, "receive buffer");
+};
+// W8A8 GEMM split: the most slabs a CTA of an S-CTA cluster may stream (its
+// stages must stay clear of the receive buffer)
+__host__ __device__ constexpr int push_max_slabs(int S) { return push_off(S) / GC<1>::STAGE; }
+
+// Dequantised output of one token from its digit sums: W8A8 acc * (s_x s_w);
+// W8A32 the exact digit recombination, scaled once in fp64.
 template <int NPL>
-__global__ void __launch_bounds__(128) k_bt_gemm(const GemmArgs a) {
+__device__ __forceinline__ float dequant(const int (&v)[NPL], float xs, float sw) {
+  if constexpr (NPL == 1) {
+    return (float)v[0] * (xs * sw);
+  } else {
+    const long long X = (long long)v[0] + 256ll * v[1] + 65536ll * v[2];
+    return (float)((double)X * (double)(xs * sw));
+  }
+}
+
+// Split-K epilogue over a (1, S, 1) cluster, one CTA per K range: every CTA
+// parks its int32 sums in its own shared memory (row-major, padded rows),
+// then CTA r finishes the contiguous tokens [r tpc, (r + 1) tpc): it reads the
+// S CTAs' sums of its row over distributed shared memory, 16 bytes at a time,
+// all loads of a chunk in flight before the first add (exact integer adds).
+// Every CTA takes both cluster barriers, whatever happened before.
+template <int NPL, int S, int MODE>
+__device__ __forceinline__ void split_epilogue(const GemmArgs& a, unsigned char* sm, const float* xs_s, unsigned taddr,
+                                               bool ok, int tile, int row, int grow, float sw0) {
+  using C = GC<NPL>;
+  constexpr int RS = C::NR + 4;   // padded row stride (ints): conflict-free 16-byte accesses
+  int* red = reinterpret_cast<int*>(sm);
+  if (ok) {
+    tc::fence_after();
+    for (int c0 = 0; c0 < C::NR; c0 += 16) {
+      unsigned r[16];
+      tc::tmem_ld16(taddr + c0, r);
+      tc::tmem_ld_wait();
+      int4* dst = reinterpret_cast<int4*>(red + row * RS + c0);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dst[e] = make_int4((int)r[4 * e], (int)r[4 * e + 1], (int)r[4 * e + 2], (int)r[4 * e + 3]);
+    }
+  }
+  tc::cluster_sync();
+  const int rank = (int)tc::cluster_ctarank();
+  constexpr int TPC = ((64 + S - 1) / S + 3) & ~3;      // tokens per CTA
+  constexpr int LDN = NPL == 1 ? 16 : 8;                 // 16-byte loads in flight per plane
+  constexpr int G = LDN / S > 0 ? LDN / S : 1;           // 4-token groups per chunk
+  const int bl0 = rank * TPC, bl1 = min(a.nb, bl0 + TPC);
+  const unsigned rbase = tc::smem_u32(red) + 4u * (unsigned)(row * RS);
+  unsigned rq[S];
+#pragma unroll
+  for (int q = 0; q < S; ++q) rq[q] = tc::mapa(rbase, (unsigned)q);
+  float* xch = reinterpret_cast<float*>(sm + C::XCH);   // SWIGLU: [tokens of this CTA][128 rows]
+  float* __restrict__ Yp = a.Y;
+  for (int g0 = bl0; g0 < bl1; g0 += 4 * G) {           // (CTA-uniform bounds)
+    int4 sum[NPL][G];
+#pragma unroll
+    for (int p = 0; p < NPL; ++p) {
+      int4 v[G][S];
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int q = 0; q < S; ++q) {
+          v[g][q] = make_int4(0, 0, 0, 0);
+          if (ok && g0 + 4 * g < bl1) v[g][q] = tc::ld_dsmem_v4(rq[q] + 4u * (unsigned)(64 * p + g0 + 4 * g));
+        }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        sum[p][g] = v[g][0];
+#pragma unroll
+        for (int q = 1; q < S; ++q) {
+          sum[p][g].x += v[g][q].x; sum[p][g].y += v[g][q].y; sum[p][g].z += v[g][q].z; sum[p][g].w += v[g][q].w;
+        }
+      }
+    }
+    float yv[4 * G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int b = g0 + 4 * g + e;
+        int v[NPL];
+#pragma unroll
+        for (int p = 0; p < NPL; ++p)
+          v[p] = e == 0 ? sum[p][g].x : e == 1 ? sum[p][g].y : e == 2 ? sum[p][g].z : sum[p][g].w;
+        yv[4 * g + e] = 0.0f;
+        if (b < bl1) {
+          yv[4 * g + e] = dequant<NPL>(v, xs_s[b], sw0);
+          if (NPL == 1 && a.acc_out && grow < a.nrows && ok) a.acc_out[(size_t)b * a.nrows + grow] = v[0];
+        }
+      }
+    }
+    const int nt = min(4 * G, bl1 - g0);
+    if constexpr (MODE == EPI_SWIGLU) {
+      // gate rows 0-63 and up rows 64-127 of the pair tile meet in shared memory
+#pragma unroll
+      for (int j = 0; j < 4 * G; ++j)
+        if (j < nt) xch[(g0 + j - bl0) * 128 + row] = yv[j];
+      __syncthreads();
+      if (ok && row < 64) {
+#pragma unroll
+        for (int j = 0; j < 4 * G; ++j)
+          if (j < nt)
+            Yp[(size_t)(g0 + j) * a.ldy + 64 * tile + row] =
+                __fmul_rn(silu_f(xch[(g0 + j - bl0) * 128 + row]), xch[(g0 + j - bl0) * 128 + row + 64]);
+      }
+      __syncthreads();
+    } else if (ok) {
+      if constexpr (MODE == EPI_STORE) {
+        if (grow < a.nrows) {
+#pragma unroll
+          for (int j = 0; j < 4 * G; ++j)
+            if (j < nt) Yp[(size_t)(g0 + j) * a.ldy + grow] = yv[j];
+        }
+      } else {
+        float h[4 * G];
+#pragma unroll
+        for (int j = 0; j < 4 * G; ++j) h[j] = j < nt ? Yp[(size_t)(g0 + j) * a.ldy + grow] : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4 * G; ++j)
+          if (j < nt) Yp[(size_t)(g0 + j) * a.ldy + grow] = __fadd_rn(h[j], yv[j]);
+      }
+    }
+  }
+  tc::cluster_sync();   // the other CTAs' sums stay readable until every CTA is done
+}
+
+__device__ __forceinline__ void st_dsmem_v4(unsigned addr, int4 v) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1,%2,%3,%4};" :: "r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Outputs of tokens b0 .. b0 + n - 1 (n <= N) of this thread's row: stored,
+// added to the residual rows (loads first, then the stores), or, for a SwiGLU
+// pair tile, exchanged through xch ([token][128 rows] floats, CTA-uniform
+// call) and combined by all 128 threads.
+template <int MODE, int N>
+__device__ __forceinline__ void emit_rows(const GemmArgs& a, const float (&yv)[N], int b0, int n, int tile, int row,
+                                          int grow, float* xch) {
+  float* __restrict__ Yp = a.Y;
+  if constexpr (MODE == EPI_SWIGLU) {
+#pragma unroll
+    for (int j = 0; j < N; ++j)
+      if (j < n) xch[j * 128 + row] = yv[j];
+    __syncthreads();
+    // thread t: row t % 64 of tokens j = t / 64, t / 64 + 2, ...
+    const int r = row & 63;
+    for (int j = row >> 6; j < n; j += 2)
+      Yp[(size_t)(b0 + j) * a.ldy + 64 * tile + r] = __fmul_rn(silu_f(xch[j * 128 + r]), xch[j * 128 + r + 64]);
+    __syncthreads();
+  } else if constexpr (MODE == EPI_STORE) {
+    if (grow < a.nrows) {
+#pragma unroll
+      for (int j = 0; j < N; ++j)
+        if (j < n) Yp[(size_t)(b0 + j) * a.ldy + grow] = yv[j];
+    }
+  } else {
+    float h[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) h[j] = j < n ? Yp[(size_t)(b0 + j) * a.ldy + grow] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < N; ++j)
+      if (j < n) Yp[(size_t)(b0 + j) * a.ldy + grow] = __fadd_rn(h[j], yv[j]);
+  }
+}
+
+template <int S, int MODE>
+__device__ __forceinline__ void split_push(const GemmArgs& a, unsigned char* sm, const float* xs_s, unsigned taddr,
+                                           bool ok, int ns, int tile, int row, int grow, float sw0) {
+  using P = SplitPush<S>;
+  const int rank = (int)tc::cluster_ctarank();
+  const bool fits = ns * GC<1>::STAGE <= P::OFF;
+  if (!fits && threadIdx.x == 0 && atomicCAS(a.err, 0, ERR_CHECK) == 0) { a.err[1] = 44; a.err[2] = ns; }
+  const bool go = ok && fits;
+  const unsigned recv = tc::smem_u32(sm + P::OFF);
+  if (go) {
+    tc::fence_after();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      unsigned r[16];
+      tc::tmem_ld16(taddr + 16 * c, r);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int tb = 16 * c + 4 * g, ow = tb / P::TPC, tl = tb - ow * P::TPC;
+        const unsigned dst = tc::mapa(recv, (unsigned)ow) + 4u * (unsigned)((rank * 128 + row) * P::RSP + tl);
+        st_dsmem_v4(dst, make_int4((int)r[4 * g], (int)r[4 * g + 1], (int)r[4 * g + 2], (int)r[4 * g + 3]));
+      }
+    }
+  }
+  tc::cluster_sync();   // every CTA's sums have landed with their owners
+  const int bl0 = rank * P::TPC, n = max(0, min(a.nb, bl0 + P::TPC) - bl0);
+  if (!go || n == 0) return;
+  const int* rv = reinterpret_cast<const int*>(sm + P::OFF);
+  float yv[P::TPC];
+#pragma unroll
+  for (int g = 0; g < P::TPC / 4; ++g) {
+    int4 acc = *reinterpret_cast<const int4*>(rv + row * P::RSP + 4 * g);
+#pragma unroll
+    for (int q = 1; q < S; ++q) {
+      const int4 v = *reinterpret_cast<const int4*>(rv + (q * 128 + row) * P::RSP + 4 * g);
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    const int vv[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int j = 4 * g + e, b = bl0 + j;
+      const int v1[1] = {vv[e]};
+      yv[j] = b < a.nb ? dequant<1>(v1, xs_s[b < 64 ? b : 0], sw0) : 0.0f;
+      if (a.acc_out && j < n && grow < a.nrows) a.acc_out[(size_t)b * a.nrows + grow] = vv[e];
+    }
+  }
+  // (the stages are free: the SwiGLU exchange may use the ring's start)
+  emit_rows<MODE, P::TPC>(a, yv, bl0, n, tile, row, grow, reinterpret_cast<float*>(sm));
+}
+
+// One instance per (digit planes, K-split cluster size S, epilogue): each
+// launch runs only its own path (a small kernel: its instructions stay in the
+// SM's instruction cache).
+template <int NPL, int S, int MODE>
+__global__ void __launch_bounds__(128, 1) k_bt_gemm(const GemmArgs a) {
   using C = GC<NPL>;
   extern __shared__ __align__(1024) unsigned char sm[];
   const int t = threadIdx.x, wid = t >> 5, lane = t & 31;
@@ -246,8 +487,8 @@ __global__ void __launch_bounds__(128) k_bt_gemm(const GemmArgs a) {
   const int j0 = blockIdx.y * a.kspl, j1 = min(a.nslab, j0 + a.kspl), ns = j1 - j0;
   const unsigned bar0 = tc::smem_u32(sm + C::OFF_BAR);
   const unsigned accf = bar0 + 16u * C::NST;
-  unsigned* tslot = reinterpret_cast<unsigned*>(sm + C::OFF_BAR + 16 * C::NST + 8);
-  int* flag = reinterpret_cast<int*>(tslot + 1);
+  unsigned* tslot = reinterpret_cast<unsigned*>(sm + C::OFF_SLOT);
+  int* flag = reinterpret_cast<int*>(tslot + 1);   // [0] spare, [1] issued, [2] consumed
   if (t == 0) {
     for (int s = 0; s < C::NST; ++s) {
       tc::mbar_init(bar0 + 8u * s, 1);                 // full
@@ -257,25 +498,46 @@ __global__ void __launch_bounds__(128) k_bt_gemm(const GemmArgs a) {
     tc::mbar_init_fence();
     flag[0] = 0;
   }
+  // The first stages' weight slabs do not depend on the previous kernel: they
+  // are requested before the dependency wait (under programmatic dependent
+  // launch they stream in while the previous kernel drains).
+  // Slab i of this CTA is K slab j0 + (i + tile) % ns: concurrent tiles stream
+  // different offsets of their weights (the int32 sums do not depend on order).
+  const int npre = min(ns, C::NST);
+  auto slab = [&](int i) { const int j = i + tile % max(ns, 1); return j0 + (j >= ns ? j - ns : j); };
+  unsigned long long pw = 0, px = 0;
+  if (t == 0) {
+    pw = tc::policy_evict_first();
+    px = tc::policy_evict_last();
+    for (int i = 0; i < npre; ++i) {
+      const unsigned fb = bar0 + 8u * i;
+      tc::mbar_expect(fb, (unsigned)C::STAGE);
+      tc::bulk_g2s(tc::smem_u32(sm + i * C::STAGE), a.W + ((size_t)tile * a.nslab + slab(i)) * GT_SLAB, GT_SLAB, fb, pw);
+    }
+  }
   tc::grid_wait();
   if (wid == 0) tc::tmem_alloc<C::TCOLS>(tslot);
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
   const unsigned tmem = *tslot;
+  __shared__ float xs_s[64];   // per-token scales, read in the epilogue
+  if (t < 64) xs_s[t] = a.xs[t];
   int issued = 0, consumed = 0;
   if (t == 0) {
     // producer: weights (read once: evict first) and the image slab (shared by every tile)
-    const unsigned long long pw = tc::policy_evict_first(), px = tc::policy_evict_last();
-    for (int i = 0; i < ns; ++i) {
+    for (int i = 0; i < npre; ++i)
+      tc::bulk_g2s(tc::smem_u32(sm + i * C::STAGE) + GT_SLAB, a.X + (size_t)slab(i) * C::BBYTES, C::BBYTES,
+                   bar0 + 8u * i, px);
+    issued = npre;
+    for (int i = npre; i < ns; ++i) {
       const int s = i % C::NST;
-      if (i >= C::NST && !tc::mbar_wait(bar0 + 8u * (C::NST + s), (unsigned)(((i / C::NST) - 1) & 1), a.err, 40, i))
-        break;
+      if (!tc::mbar_wait(bar0 + 8u * (C::NST + s), (unsigned)(((i / C::NST) - 1) & 1), a.err, 40, i)) break;
       const unsigned dst = tc::smem_u32(sm + s * C::STAGE);
       const unsigned fb = bar0 + 8u * s;
       tc::mbar_expect(fb, (unsigned)C::STAGE);
-      tc::bulk_g2s(dst, a.W + ((size_t)tile * a.nslab + j0 + i) * GT_SLAB, GT_SLAB, fb, pw);
-      tc::bulk_g2s(dst + GT_SLAB, a.X + (size_t)(j0 + i) * C::BBYTES, C::BBYTES, fb, px);
+      tc::bulk_g2s(dst, a.W + ((size_t)tile * a.nslab + slab(i)) * GT_SLAB, GT_SLAB, fb, pw);
+      tc::bulk_g2s(dst + GT_SLAB, a.X + (size_t)slab(i) * C::BBYTES, C::BBYTES, fb, px);
       issued = i + 1;
     }
   } else if (t == 32) {
@@ -301,86 +563,34 @@ __global__ void __launch_bounds__(128) k_bt_gemm(const GemmArgs a) {
   const bool ok = __syncthreads_and(got) && flag[2] == ns && flag[1] == ns;
   const int row = 32 * wid + lane;                       // TMEM lane = tile row
   const unsigned taddr = tmem + ((unsigned)(32 * wid) << 16);
-  bool last = true;
-  if (ok && gridDim.y > 1) {
-    // split K: add this CTA's sums into the tile's exact int32 totals; the
-    // last CTA to arrive finishes the tile
+  const int grow = tile * GT_M + row;
+  const float sw0 = a.sw[grow];   // this thread's row scale
+  auto yval = [&](int b, const int (&v)[NPL], float sw) -> float { return dequant<NPL>(v, xs_s[b], sw); };
+  if constexpr (S > 1) {
+    // split K over the cluster's CTAs
+    if constexpr (NPL == 1) split_push<S, MODE>(a, sm, xs_s, taddr, ok, ns, tile, row, grow, sw0);
+    else split_epilogue<NPL, S, MODE>(a, sm, xs_s, taddr, ok, tile, row, grow, sw0);
+  } else if (ok) {
+    // one CTA per tile: the sums straight from TMEM, 16 tokens at a time (all
+    // planes' loads in flight before the wait)
     tc::fence_after();
-    int32_t* P = a.part + (size_t)tile * C::NR * 128;
-    for (int c0 = 0; c0 < C::NR; c0 += 16) {
-      unsigned r[16];
-      tc::tmem_ld16(taddr + c0, r);
-      tc::tmem_ld_wait();
-#pragma unroll
-      for (int e = 0; e < 16; ++e) atomicAdd(P + (size_t)(c0 + e) * 128 + row, (int)r[e]);
-    }
-    __threadfence();
-    __syncthreads();
-    if (t == 0) flag[0] = atomicAdd(a.cnt + tile, 1) == (int)gridDim.y - 1;
-    __syncthreads();
-    last = flag[0] != 0;
-    if (last) __threadfence();
-  }
-  if (ok && last) {
-    tc::fence_after();
-    const bool split = gridDim.y > 1;
-    int32_t* P = a.part + (size_t)tile * C::NR * 128;
-    const int grow = tile * GT_M + row;
-    const float sw = a.sw[grow];
-    float* ub = reinterpret_cast<float*>(sm);   // SWIGLU: up rows [64 tokens][64]
     for (int c0 = 0; c0 < 64; c0 += 16) {
       unsigned r[NPL][16];
 #pragma unroll
-      for (int p = 0; p < NPL; ++p) {
-        if (split) {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            int32_t* q = P + (size_t)(64 * p + c0 + e) * 128 + row;
-            r[p][e] = (unsigned)__ldcg(q);
-            *q = 0;
-          }
-        } else {
-          tc::tmem_ld16(taddr + 64 * p + c0, r[p]);
-        }
-      }
-      if (!split) tc::tmem_ld_wait();
+      for (int p = 0; p < NPL; ++p) tc::tmem_ld16(taddr + 64 * p + c0, r[p]);
+      tc::tmem_ld_wait();
+      float yv[16];
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
-        const int b = c0 + e;
-        float y;
-        if constexpr (NPL == 1) {
-          y = (float)(int)r[0][e] * (a.xs[b] * sw);
-          if (a.acc_out && b < a.nb && grow < a.nrows) a.acc_out[(size_t)b * a.nrows + grow] = (int)r[0][e];
-        } else {
-          const long long X = (long long)(int)r[0][e] + 256ll * (int)r[1][e] + 65536ll * (int)r[2][e];
-          y = (float)((double)X * (double)(a.xs[b] * sw));
-        }
-        if (b >= a.nb) continue;
-        if (a.mode == EPI_STORE) {
-          if (grow < a.nrows) a.Y[(size_t)b * a.ldy + grow] = y;
-        } else if (a.mode == EPI_ADD) {
-          float* h = a.Y + (size_t)b * a.ldy + grow;
-          *h = __fadd_rn(*h, y);
-        } else if (row >= 64) {
-          ub[b * 64 + row - 64] = y;   // up row
-        } else {
-          r[0][e] = __float_as_uint(y);   // gate row, kept for the SwiGLU below
-        }
-      }
-      if (a.mode == EPI_SWIGLU) {
-        __syncthreads();
-        if (row < 64) {
+        int v[NPL];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int b = c0 + e;
-            if (b < a.nb)
-              a.Y[(size_t)b * a.ldy + 64 * tile + row] = __fmul_rn(silu_f(__uint_as_float(r[0][e])), ub[b * 64 + row]);
-          }
-        }
-        __syncthreads();
+        for (int p = 0; p < NPL; ++p) v[p] = (int)r[p][e];
+        yv[e] = yval(c0 + e, v, sw0);
+        if (NPL == 1 && a.acc_out && c0 + e < a.nb && grow < a.nrows)
+          a.acc_out[(size_t)(c0 + e) * a.nrows + grow] = v[0];
       }
+      emit_rows<MODE, 16>(a, yv, c0, max(0, min(16, a.nb - c0)), tile, row, grow, reinterpret_cast<float*>(sm));
     }
-    if (split && t == 0) a.cnt[tile] = 0;
   }
   // teardown: copies that were issued but never consumed (only after a wait
   // ran out) are waited for, with the same bound, before the CTA exits
@@ -394,6 +604,7 @@ __global__ void __launch_bounds__(128) k_bt_gemm(const GemmArgs a) {
     tc::fence_after();
     tc::tmem_free<C::TCOLS>(tmem);
   }
+  tc::grid_launch_dependents();
 }
 
 // ---------------------------------------------------------------- norm + image
@@ -482,6 +693,7 @@ __global__ void __launch_bounds__(NT) k_bt_normq(const NormqArgs a) {
       a.AB[b * 32 + t] = s;
     }
   }
+  tc::grid_launch_dependents();
 }
 
 // Quantiser of a K-vector per token (K a multiple of 4, <= 4096): src[b lds + k].
@@ -508,6 +720,7 @@ __global__ void __launch_bounds__(NT) k_bt_quant(const float* __restrict__ src, 
     const int g = t + NT * j;
     if (4 * g < K) image_store<NPL, 4>(v[j], 4 * g, b, amax, X, xs, nullptr);
   }
+  tc::grid_launch_dependents();
 }
 
 // ---------------------------------------------------------------- DeltaNet mixer
@@ -621,26 +834,27 @@ __global__ void __launch_bounds__(NT) k_bt_delta(const DeltaArgs a) {
     const float v = __fmul_rn(__fmul_rn(ob[t], ginv), a.gnorm_w[t]);
     a.O[(size_t)b * VDIM + h * LV + t] = __fmul_rn(v, z);
   }
+  tc::grid_launch_dependents();
 }
 
 // ---------------------------------------------------------------- attention
 
-constexpr int AT_BLK = 16;                       // positions per staged block
-constexpr int AT_NST = 3;                        // staged blocks in flight
-constexpr int AT_KROW = HD * 4 + 16;             // padded K row in shared memory (bytes)
-constexpr int AT_KB = AT_BLK * AT_KROW;
-constexpr int AT_VB = AT_BLK * HD * 4;
-constexpr int AT_STAGE = AT_KB + AT_VB;
-constexpr int AT_OFF_Q = AT_NST * AT_STAGE;      // qn [4][256]
-constexpr int AT_OFF_KN = AT_OFF_Q + 4 * HD * 4; // kn [256]
-constexpr int AT_OFF_VN = AT_OFF_KN + HD * 4;    // vn [256]
-constexpr int AT_OFF_PART = AT_OFF_VN + HD * 4;  // partial scores [4 quarters][4 heads][16]
-constexpr int AT_OFF_SP = AT_OFF_PART + 4 * 4 * AT_BLK * 4;   // probabilities [4][16]
-constexpr int AT_OFF_ST = AT_OFF_SP + 4 * AT_BLK * 4;         // m[4], l[4], scale[4]
-constexpr int AT_OFF_BAR = AT_OFF_ST + 64;
-constexpr int AT_SMEM = AT_OFF_BAR + 8 * AT_NST;
-constexpr int AT_PROW = 4 + HD;                  // partial row: m, l, 2 pad, o[256]
-static_assert(AT_STAGE % 16 == 0 && AT_KROW % 16 == 0 && AT_OFF_BAR % 8 == 0, "attention smem alignment");
+constexpr int AT_BLK = 32;                        // positions per staged block
+constexpr int AT_NST = 3;                         // staged blocks in flight (one CTA per SM)
+constexpr int AT_CW = 8;                          // compute warps; one more warp loads
+constexpr int AT_U = AT_BLK / AT_CW;              // positions per warp per block
+constexpr int AT_THREADS = 32 * (AT_CW + 1);
+constexpr int AT_KB = AT_BLK * HD * 4;            // K (or V) rows of a block
+constexpr int AT_STAGE = 2 * AT_KB;               // K rows, then V rows
+constexpr int AT_PROW = 4 + HD;                   // partial row: m, l, 2 pad, o[256]
+constexpr int AT_OFF_Q = AT_NST * AT_STAGE;       // qn [4][256]
+constexpr int AT_OFF_KN = AT_OFF_Q + 4 * HD * 4;  // kn [256]
+constexpr int AT_OFF_VN = AT_OFF_KN + HD * 4;     // vn [256]
+constexpr int AT_OFF_MRG = AT_OFF_VN + HD * 4;    // per-warp partials of four warps [4][4][AT_PROW]
+constexpr int AT_OFF_BAR = AT_OFF_MRG + 4 * 4 * AT_PROW * 4;
+constexpr int AT_SMEM = AT_OFF_BAR + 16 * AT_NST;
+static_assert(AT_STAGE % 1024 == 0 && AT_OFF_BAR % 8 == 0, "attention smem alignment");
+static_assert(AT_SMEM <= 227 * 1024, "attention shared memory");
 
 struct AttnArgs {
   const float* Y; int ldy;     // in-proj outputs: [q | gate] per head (4096), k (512), v (512)
@@ -672,156 +886,267 @@ __device__ __forceinline__ void norm_rope_warp(const float* src, const float* w,
   for (int q = 0; q < 8; ++q) dst[lane + 32 * q] = v[q];
 }
 
-// Persistent over items (token b, group g, chunk cc); 256 threads.
-__global__ void __launch_bounds__(256, 2) k_bt_attn(const AttnArgs a) {
+__device__ __forceinline__ void bar_compute() { asm volatile("bar.sync 1, %0;" :: "n"(32 * AT_CW) : "memory"); }
+
+// Item (token b, KV group g, chunk cc) of the persistent attention kernel's
+// stride loop; false if the chunk is empty.
+struct AtItem {
+  int b, g, cc, T, pos, t0, t1, tcache, nblk;
+};
+// The i-th block an item's CTA stages: the chunk's blocks in an order rotated
+// by the CTA index, so that concurrent CTAs stream different offsets of their
+// chunks (the online softmax does not depend on the order).
+__device__ __forceinline__ int at_block(const AtItem& it, int i) {
+  const int r = (int)(blockIdx.x * 7u % (unsigned)it.nblk);
+  const int j = i + r;
+  return j >= it.nblk ? j - it.nblk : j;
+}
+__device__ __forceinline__ bool at_item(const BtCtl& C, int item, int nchm, AtItem& it) {
+  it.cc = item % nchm;
+  it.g = (item / nchm) % NKV;
+  it.b = item / (nchm * NKV);
+  it.T = C.T[it.b];
+  it.pos = C.pos[it.b];
+  it.t0 = it.cc * AT_CL;
+  if (it.t0 >= it.T + 1) return false;
+  it.t1 = min(it.T + 1, it.t0 + AT_CL);
+  it.tcache = min(it.t1, it.T);
+  it.nblk = (it.t1 - it.t0 + AT_BLK - 1) / AT_BLK;
+  return true;
+}
+
+// Split-KV attention (golden/model.py:194-229), persistent over items (token
+// b, KV group g, 256-position chunk cc).  Warp 8 stages the chunk's cached K
+// and V rows, 32 positions per block, into a three-block ring (bulk copies);
+// the eight compute warps each take positions w, w + 8, ... of every block for
+// all four query heads of the group: lane = 8 dims, the four 256-dim scores
+// by butterfly sums, an online softmax per warp and head (running max m, sum
+// l, output o).  At the chunk's end the warps' (m, l, o) merge, four warps at
+// a time through shared memory, in warp order (online: M, L = L a + l_w e,
+// O = O a + o_w e) into the chunk's partial.  The new token's key and value (position T) come
+// from this CTA's own QK-norm + RoPE; the chunk holding T writes them to
+// cache slot T.
+__global__ void __launch_bounds__(AT_THREADS, 1) k_bt_attn(const AttnArgs a) {
   extern __shared__ __align__(1024) unsigned char sm[];
   float* qn = reinterpret_cast<float*>(sm + AT_OFF_Q);
   float* kn = reinterpret_cast<float*>(sm + AT_OFF_KN);
   float* vn = reinterpret_cast<float*>(sm + AT_OFF_VN);
-  float* part = reinterpret_cast<float*>(sm + AT_OFF_PART);
-  float* sp = reinterpret_cast<float*>(sm + AT_OFF_SP);
-  float* st = reinterpret_cast<float*>(sm + AT_OFF_ST);
-  const unsigned bar0 = tc::smem_u32(sm + AT_OFF_BAR);
+  float* mrg = reinterpret_cast<float*>(sm + AT_OFF_MRG);
+  const unsigned bar0 = tc::smem_u32(sm + AT_OFF_BAR);   // full[s]; empty[s] at + 8 (NST + s)
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
   if (t == 0) {
-    for (int s = 0; s < AT_NST; ++s) tc::mbar_init(bar0 + 8u * s, 1);
+    for (int s = 0; s < AT_NST; ++s) {
+      tc::mbar_init(bar0 + 8u * s, 1);
+      tc::mbar_init(bar0 + 8u * (AT_NST + s), AT_CW);
+    }
     tc::mbar_init_fence();
   }
   tc::grid_wait();
   __syncthreads();
   const BtCtl& C = *a.ctl;
   const int nchm = C.nchmax, nitems = C.nb * NKV * nchm;
-  const unsigned long long pol = tc::policy_evict_first();
-  unsigned nblk_done = 0;   // blocks this CTA consumed so far (stage / parity bookkeeping)
-  unsigned nissued = 0, nfail = 0;   // blocks staged so far (warp 0's count); the block whose wait failed
-  bool good = true;
-  for (int item = blockIdx.x; item < nitems && good; item += gridDim.x) {
-    const int cc = item % nchm, g = (item / nchm) % NKV, b = item / (nchm * NKV);
-    const int T = C.T[b], pos = C.pos[b], Tn = T + 1;
-    const int t0 = cc * AT_CL;
-    if (t0 >= Tn) continue;
-    const int t1 = min(Tn, t0 + AT_CL), tcache = min(t1, T);
-    const int nblk = (t1 - t0 + AT_BLK - 1) / AT_BLK;
-    const size_t kvoff = (((size_t)b * NFULL + a.fi) * NKV + g) * (size_t)a.max_ctx * HD;
-    const float* kc = a.kc + kvoff;
-    const float* vc = a.vc + kvoff;
-    // stage the cached rows of block i (warp 0: lane 0 arms the barrier, lanes
-    // 0-15 copy one K row each into the padded layout, lane 16 the V rows)
-    auto issue = [&](int i) {
-      const unsigned n = nblk_done + (unsigned)i, s = n % AT_NST;
-      const int s0 = t0 + i * AT_BLK;
-      const int nbc = max(0, min(AT_BLK, tcache - s0));
-      const unsigned kb = tc::smem_u32(sm + s * AT_STAGE), vb = kb + AT_KB, bar = bar0 + 8u * s;
-      if (lane == 0) tc::mbar_expect(bar, (unsigned)(2 * nbc * HD * 4));
-      __syncwarp();
-      if (lane < nbc) tc::bulk_g2s(kb + lane * AT_KROW, kc + (size_t)(s0 + lane) * HD, HD * 4, bar, pol);
-      if (lane == 16 && nbc > 0) tc::bulk_g2s(vb, vc + (size_t)s0 * HD, (unsigned)(nbc * HD * 4), bar, pol);
-      nissued = n + 1;
-    };
-    if (wid == 0) {
-      tc::fence_async_smem();
-      for (int i = 0; i < AT_NST && i < nblk; ++i) issue(i);
-    }
-    // this token's q (4 heads of group g), k and v: RMSNorm + RoPE (golden/model.py:203-214)
-    const float* y = a.Y + (size_t)b * a.ldy;
-    const float* rope = a.rope + (size_t)pos * ROT;
-    if (wid < 4) norm_rope_warp(y + (4 * g + wid) * 2 * HD, a.qn_w, rope[lane], rope[32 + lane], qn + wid * HD);
-    else if (wid == 4) norm_rope_warp(y + QPROJ + g * HD, a.kn_w, rope[lane], rope[32 + lane], kn);
-    else if (wid == 5) for (int e = lane; e < HD; e += 32) vn[e] = y[QPROJ + KVPROJ + g * HD + e];
-    if (t < 4) { st[t] = -INFINITY; st[4 + t] = 0.0f; }
-    __syncthreads();
-    float o[4] = {0.f, 0.f, 0.f, 0.f};
-    const int p = t & 15, hq = (t >> 4) & 3, qd = t >> 6;
-    for (int i = 0; i < nblk; ++i) {
-      const unsigned n = nblk_done + (unsigned)i, s = n % AT_NST;
-      if (!tc::mbar_wait(bar0 + 8u * s, (n / AT_NST) & 1u, a.err, 50, item)) good = false;
-      if (__syncthreads_or(!good)) {
-        good = false;
-        nfail = n;
-        break;
-      }
-      const int s0 = t0 + i * AT_BLK;
-      const int nbk = min(AT_BLK, t1 - s0), nbc = max(0, min(AT_BLK, tcache - s0));
-      unsigned char* kb = sm + s * AT_STAGE;
-      float* vb = reinterpret_cast<float*>(kb + AT_KB);
-      if (nbk > nbc) {
-        // this block holds the new token (position T) at row nbc
-        reinterpret_cast<float*>(kb + nbc * AT_KROW)[t] = kn[t];
-        vb[nbc * HD + t] = vn[t];
-        __syncthreads();
-      }
-      // scores: thread = (position p, head hq, quarter qd of the 256 dims)
-      if (p < nbk) {
-        const float4* kr = reinterpret_cast<const float4*>(kb + p * AT_KROW) + qd * 16;
-        const float4* qr = reinterpret_cast<const float4*>(qn + hq * HD) + qd * 16;
-        float d = 0.0f;
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float4 kv = kr[j], qv = qr[j];
-          d = fmaf(qv.x, kv.x, d);
-          d = fmaf(qv.y, kv.y, d);
-          d = fmaf(qv.z, kv.z, d);
-          d = fmaf(qv.w, kv.w, d);
-        }
-        part[(qd * 4 + hq) * AT_BLK + p] = d;
-      }
-      __syncthreads();
-      // online softmax: warp hq < 4 updates head hq (scale 256^-0.5 = 1/16, exact)
-      if (wid < 4) {
-        const int h4 = wid;
-        float sv = -INFINITY;
-        if (lane < nbk)
-          sv = __fmul_rn(((part[(0 * 4 + h4) * AT_BLK + lane] + part[(1 * 4 + h4) * AT_BLK + lane]) +
-                          part[(2 * 4 + h4) * AT_BLK + lane]) + part[(3 * 4 + h4) * AT_BLK + lane], 0.0625f);
-        const float mold = st[h4];
-        const float mnew = fmaxf(mold, warp_max(sv));
-        const float pe = lane < nbk ? expf(sv - mnew) : 0.0f;
-        const float ls = warp_sum(pe);
-        if (lane < AT_BLK) sp[h4 * AT_BLK + lane] = pe;
-        if (lane == 0) {
-          const float sc = mold == -INFINITY ? 0.0f : expf(mold - mnew);
-          st[8 + h4] = sc;
-          st[4 + h4] = fmaf(st[4 + h4], sc, ls);
-          st[h4] = mnew;
+  if (wid == AT_CW) {
+    // loader: every block of this CTA's items, in order
+    if (lane == 0) {
+      const unsigned long long pol = tc::policy_evict_first();
+      unsigned n = 0;
+      bool good = true;
+      for (int item = blockIdx.x; item < nitems && good; item += gridDim.x) {
+        AtItem it;
+        if (!at_item(C, item, nchm, it)) continue;
+        const size_t kvoff = (((size_t)it.b * NFULL + a.fi) * NKV + it.g) * (size_t)a.max_ctx * HD;
+        for (int i = 0; i < it.nblk; ++i, ++n) {
+          const unsigned s = n % AT_NST;
+          if (n >= AT_NST && !tc::mbar_wait(bar0 + 8u * (AT_NST + s), ((n / AT_NST) - 1) & 1u, a.err, 52, (int)n)) {
+            good = false;
+            break;
+          }
+          const int s0 = it.t0 + at_block(it, i) * AT_BLK;
+          const int nbc = max(0, min(AT_BLK, it.tcache - s0));
+          const unsigned kb = tc::smem_u32(sm + s * AT_STAGE), fb = bar0 + 8u * s;
+          tc::mbar_expect(fb, (unsigned)(2 * nbc * HD * 4));
+          if (nbc > 0) {
+            tc::bulk_g2s(kb, a.kc + kvoff + (size_t)s0 * HD, (unsigned)(nbc * HD * 4), fb, pol);
+            tc::bulk_g2s(kb + AT_KB, a.vc + kvoff + (size_t)s0 * HD, (unsigned)(nbc * HD * 4), fb, pol);
+          }
         }
       }
-      __syncthreads();
-      // P V: thread = dim t
+      // every staged block is consumed before the CTA ends (the compute warps'
+      // empty arrivals of the last blocks)
+      for (unsigned u = n > AT_NST ? n - AT_NST : 0; u < n && good; ++u)
+        if (!tc::mbar_wait(bar0 + 8u * (AT_NST + u % AT_NST), (u / AT_NST) & 1u, a.err, 53, (int)u)) break;
+    }
+    __syncwarp();
+  } else {
+    unsigned n = 0;
+    bool good = true;
+    for (int item = blockIdx.x; item < nitems && good; item += gridDim.x) {
+      AtItem it;
+      if (!at_item(C, item, nchm, it)) continue;
+      // this token's q (4 heads of group g), k and v: RMSNorm + RoPE (golden/model.py:203-214)
+      const float* y = a.Y + (size_t)it.b * a.ldy;
+      const float* rope = a.rope + (size_t)it.pos * ROT;
+      if (wid < 4) norm_rope_warp(y + (4 * it.g + wid) * 2 * HD, a.qn_w, rope[lane], rope[32 + lane], qn + wid * HD);
+      else if (wid == 4) norm_rope_warp(y + QPROJ + it.g * HD, a.kn_w, rope[lane], rope[32 + lane], kn);
+      else if (wid == 5) for (int e = lane; e < HD; e += 32) vn[e] = y[QPROJ + KVPROJ + it.g * HD + e];
+      bar_compute();
+      float qr[4][8];
 #pragma unroll
-      for (int h4 = 0; h4 < 4; ++h4) o[h4] = __fmul_rn(o[h4], st[8 + h4]);
-      for (int j = 0; j < nbk; ++j) {
-        const float vv = vb[j * HD + t];
-#pragma unroll
-        for (int h4 = 0; h4 < 4; ++h4) o[h4] = fmaf(sp[h4 * AT_BLK + j], vv, o[h4]);
+      for (int h = 0; h < 4; ++h) {
+        const float4 u0 = *reinterpret_cast<const float4*>(qn + h * HD + 8 * lane);
+        const float4 u1 = *reinterpret_cast<const float4*>(qn + h * HD + 8 * lane + 4);
+        qr[h][0] = u0.x; qr[h][1] = u0.y; qr[h][2] = u0.z; qr[h][3] = u0.w;
+        qr[h][4] = u1.x; qr[h][5] = u1.y; qr[h][6] = u1.z; qr[h][7] = u1.w;
       }
-      __syncthreads();   // the stage is free
-      if (wid == 0 && i + AT_NST < nblk) {
-        tc::fence_async_smem();
-        issue(i + AT_NST);
+      // running max / sum of head (lane >> 1) & 3 in every lane; o: every head, this lane's 8 dims
+      float mh = -INFINITY, lh = 0.0f, o[4][8];
+#pragma unroll
+      for (int h = 0; h < 4; ++h)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[h][j] = 0.0f;
+      for (int i = 0; i < it.nblk; ++i, ++n) {
+        const unsigned s = n % AT_NST;
+        if (!tc::mbar_wait(bar0 + 8u * s, (n / AT_NST) & 1u, a.err, 50, item)) { good = false; break; }
+        const int s0 = it.t0 + at_block(it, i) * AT_BLK;
+        const int nbk = min(AT_BLK, it.t1 - s0);
+        const float* kb = reinterpret_cast<const float*>(sm + s * AT_STAGE);
+        const float* vb = kb + AT_BLK * HD;
+        // this warp's two positions of the block
+        float sc[AT_U][4], vv[AT_U][8];
+#pragma unroll
+        for (int u = 0; u < AT_U; ++u) {
+          const int p = wid + AT_CW * u;
+          const bool live = p < nbk;
+          const bool fresh = s0 + p == it.T;   // the new token: k, v from this CTA
+          const float* kr = fresh ? kn : kb + p * HD;
+          const float* vr = fresh ? vn : vb + p * HD;
+          float kk[8];
+          if (live) {
+            const float4 k0 = *reinterpret_cast<const float4*>(kr + 8 * lane);
+            const float4 k1 = *reinterpret_cast<const float4*>(kr + 8 * lane + 4);
+            const float4 v0 = *reinterpret_cast<const float4*>(vr + 8 * lane);
+            const float4 v1 = *reinterpret_cast<const float4*>(vr + 8 * lane + 4);
+            kk[0] = k0.x; kk[1] = k0.y; kk[2] = k0.z; kk[3] = k0.w; kk[4] = k1.x; kk[5] = k1.y; kk[6] = k1.z; kk[7] = k1.w;
+            vv[u][0] = v0.x; vv[u][1] = v0.y; vv[u][2] = v0.z; vv[u][3] = v0.w;
+            vv[u][4] = v1.x; vv[u][5] = v1.y; vv[u][6] = v1.z; vv[u][7] = v1.w;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) { kk[j] = 0.0f; vv[u][j] = 0.0f; }
+          }
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            float d = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) d = fmaf(qr[h][j], kk[j], d);
+            sc[u][h] = d;
+          }
+        }
+        // the 16 dot products (AT_U = 4 positions x 4 heads) summed over the
+        // lanes by a reduce-scatter: at each level a lane keeps half of its
+        // values and adds its partner's; lane 2 i, 2 i + 1 end with sum i
+        // (i = 4 u + h)
+        static_assert(AT_U == 4, "reduce-scatter of 16 sums");
+        float w8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const bool hi = lane & 16;
+          const float mine = hi ? sc[(8 + k) >> 2][(8 + k) & 3] : sc[k >> 2][k & 3];
+          const float oth = hi ? sc[k >> 2][k & 3] : sc[(8 + k) >> 2][(8 + k) & 3];
+          w8[k] = mine + __shfl_xor_sync(0xffffffffu, oth, 16);
+        }
+        float w4[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const bool hi = lane & 8;
+          w4[k] = (hi ? w8[4 + k] : w8[k]) + __shfl_xor_sync(0xffffffffu, hi ? w8[k] : w8[4 + k], 8);
+        }
+        float w2[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const bool hi = lane & 4;
+          w2[k] = (hi ? w4[2 + k] : w4[k]) + __shfl_xor_sync(0xffffffffu, hi ? w4[k] : w4[2 + k], 4);
+        }
+        const bool h2 = lane & 2;
+        float w1 = (h2 ? w2[1] : w2[0]) + __shfl_xor_sync(0xffffffffu, h2 ? w2[0] : w2[1], 2);
+        w1 += __shfl_xor_sync(0xffffffffu, w1, 1);
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(bar0 + 8u * (AT_NST + s));   // (the rows are in registers)
+        // this lane's (position u, head h): score scaled by 256^-0.5 = 1/16
+        // (exact); the head's max over the warp's four positions (lanes ^ 8,
+        // ^ 16), online softmax update of the head's running max / sum
+        const int iu = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
+        const float sv = wid + AT_CW * iu < nbk ? __fmul_rn(w1, 0.0625f) : -INFINITY;
+        float mx = fmaxf(sv, __shfl_xor_sync(0xffffffffu, sv, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float mn = fmaxf(mh, mx);
+        const float al = mh == -INFINITY ? (mn == -INFINITY ? 1.0f : 0.0f) : expf(mh - mn);
+        const float e = sv == -INFINITY ? 0.0f : expf(sv - mn);
+        float es = e + __shfl_xor_sync(0xffffffffu, e, 8);
+        es += __shfl_xor_sync(0xffffffffu, es, 16);
+        lh = fmaf(lh, al, es);
+        mh = mn;
+        // P V: every lane updates its 8 dims of the four heads
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float ah = __shfl_sync(0xffffffffu, al, 2 * h);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[h][j] = __fmul_rn(o[h][j], ah);
+#pragma unroll
+          for (int u = 0; u < AT_U; ++u) {
+            const float pe = __shfl_sync(0xffffffffu, e, 2 * (4 * u + h));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[h][j] = fmaf(pe, vv[u][j], o[h][j]);
+          }
+        }
+      }
+      if (!good) break;
+      if (it.t1 == it.T + 1) {
+        // roped K and raw V into slot T (golden/model.py:216-217)
+        const size_t kvoff = (((size_t)it.b * NFULL + a.fi) * NKV + it.g) * (size_t)a.max_ctx * HD;
+        a.kc[kvoff + (size_t)it.T * HD + t] = kn[t];
+        a.vc[kvoff + (size_t)it.T * HD + t] = vn[t];
+      }
+      // the warps' (m, l, o), four warps per round; thread t = dim t of every head
+      float M[4], Ls[4], O[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) { M[h] = -INFINITY; Ls[h] = 0.0f; O[h] = 0.0f; }
+#pragma unroll
+      for (int rnd = 0; rnd < 2; ++rnd) {
+        if ((wid >> 2) == rnd) {
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            float* mw = mrg + ((wid & 3) * 4 + h) * AT_PROW;
+            const float m_h = __shfl_sync(0xffffffffu, mh, 2 * h), l_h = __shfl_sync(0xffffffffu, lh, 2 * h);
+            if (lane == 0) { mw[0] = m_h; mw[1] = l_h; }
+            *reinterpret_cast<float4*>(mw + 4 + 8 * lane) = make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
+            *reinterpret_cast<float4*>(mw + 8 + 8 * lane) = make_float4(o[h][4], o[h][5], o[h][6], o[h][7]);
+          }
+        }
+        bar_compute();
+#pragma unroll
+        for (int h = 0; h < 4; ++h)
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const float* mw = mrg + (w * 4 + h) * AT_PROW;
+            const float mq = mw[0];
+            if (mq == -INFINITY) continue;   // a warp without positions
+            const float Mn = fmaxf(M[h], mq);
+            const float sa = M[h] == -INFINITY ? 0.0f : expf(M[h] - Mn), sb = expf(mq - Mn);
+            Ls[h] = fmaf(mw[1], sb, __fmul_rn(Ls[h], sa));
+            O[h] = fmaf(mw[4 + t], sb, __fmul_rn(O[h], sa));
+            M[h] = Mn;
+          }
+        if (rnd == 0) bar_compute();   // round 1 rewrites the buffer
+      }
+      float* pr = a.part + ((((size_t)it.b * NKV + it.g) * a.maxch + it.cc) * 4) * AT_PROW;
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        pr[h * AT_PROW + 4 + t] = O[h];
+        if (t == 0) { pr[h * AT_PROW] = M[h]; pr[h * AT_PROW + 1] = Ls[h]; }
       }
     }
-    if (!good) break;
-    nblk_done += (unsigned)nblk;
-    // the chunk's (m, l, o) of its four heads
-    float* pr = a.part + ((((size_t)b * NKV + g) * a.maxch + cc) * 4) * AT_PROW;
-#pragma unroll
-    for (int h4 = 0; h4 < 4; ++h4) pr[h4 * AT_PROW + 4 + t] = o[h4];
-    if (t < 4) {
-      pr[t * AT_PROW] = st[t];
-      pr[t * AT_PROW + 1] = st[4 + t];
-    }
-    if (t1 == Tn) {
-      // roped K and raw V into slot T (golden/model.py:216-217)
-      a.kc[kvoff + (size_t)T * HD + t] = kn[t];
-      a.vc[kvoff + (size_t)T * HD + t] = vn[t];
-    }
-    __syncthreads();
   }
-  // after a wait that ran out: the stages still in flight, waited for with the same bound
-  if (!good && t == 0) {
-    for (unsigned u = nfail; u < nissued; ++u)
-      if (!tc::mbar_wait(bar0 + 8u * (u % AT_NST), (u / AT_NST) & 1u, a.err, 51, (int)u)) break;
-  }
+  tc::grid_launch_dependents();
 }
 
 // Merge the chunks of every head of token b (online, in chunk order), times
@@ -857,6 +1182,7 @@ __global__ void __launch_bounds__(NT) k_bt_merge(const float* __restrict__ Y, in
   x[3] = __fmul_rn(__fdiv_rn(O[3], Ls), sigmoid_f(gt.w));
   const float amax = amax512(fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3]))), red);
   image_store<NPL, 4>(x, hh * HD + d0, b, amax, X, xs, nullptr);
+  tc::grid_launch_dependents();
 }
 
 // ---------------------------------------------------------------- head
@@ -1024,6 +1350,7 @@ __global__ void __launch_bounds__(HB_THREADS, 1) k_bt_head(const HeadArgs a) {
     tc::fence_after();
     tc::tmem_free<512>(tmem);
   }
+  tc::grid_launch_dependents();
 }
 
 // argmax over the head CTAs per token -> ids, and the next step's token
@@ -1039,6 +1366,7 @@ __global__ void k_bt_finish(const unsigned long long* __restrict__ am, int G, in
     ids[b] = id;
     tok[b] = id;
   }
+  tc::grid_launch_dependents();
 }
 
 }  // namespace
@@ -1055,17 +1383,86 @@ cudaError_t repack_tiles(const int8_t* const* rowptr, int8_t* out, int nrows, in
 
 namespace {
 
+// Launch with programmatic dependent launch (the kernel's prologue may start
+// while its predecessor drains; every kernel waits on griddepcontrol.wait
+// before it reads what the predecessor wrote) and, for cluster_y > 0, a
+// (1, cluster_y, 1) thread-block cluster.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                     int cluster_y, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  int n = 0;
+  if (pdl) {
+    at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_y > 0) {
+    at[n].id = cudaLaunchAttributeClusterDimension;
+    at[n].val.clusterDim.x = 1;
+    at[n].val.clusterDim.y = (unsigned)cluster_y;
+    at[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+using GemmKernel = void (*)(const GemmArgs);
+
+template <int NPL, int MODE>
+GemmKernel gemm_kernel_s(int S) {
+  switch (S) {
+    case 1: return k_bt_gemm<NPL, 1, MODE>;
+    case 2: return k_bt_gemm<NPL, 2, MODE>;
+    case 4: return k_bt_gemm<NPL, 4, MODE>;
+    case 8: return k_bt_gemm<NPL, 8, MODE>;
+    default: break;
+  }
+  if constexpr (MODE != EPI_SWIGLU) {
+    switch (S) {
+      case 3: return k_bt_gemm<NPL, 3, MODE>;
+      case 5: return k_bt_gemm<NPL, 5, MODE>;
+      case 6: return k_bt_gemm<NPL, 6, MODE>;
+      case 7: return k_bt_gemm<NPL, 7, MODE>;
+      default: break;
+    }
+  }
+  return nullptr;
+}
+// The instance for `mode` and an S-CTA K split (null when not built).
 template <int NPL>
-cudaError_t launch_gemm(const GemmArgs& a, int ntiles, cudaStream_t st) {
+GemmKernel gemm_kernel(int mode, int S) {
+  if (mode == EPI_STORE) return gemm_kernel_s<NPL, EPI_STORE>(S);
+  if (mode == EPI_ADD) return gemm_kernel_s<NPL, EPI_ADD>(S);
+  if (mode == EPI_SWIGLU) return gemm_kernel_s<NPL, EPI_SWIGLU>(S);
+  return nullptr;
+}
+
+template <int NPL>
+cudaError_t launch_gemm(const GemmArgs& a, int ntiles, cudaStream_t st, bool pdl = false) {
   const int ny = (a.nslab + a.kspl - 1) / a.kspl;
-  k_bt_gemm<NPL><<<dim3(ntiles, ny), 128, GC<NPL>::SMEM, st>>>(a);
-  return cudaGetLastError();
+  if (ny < 1 || ny > 8) return cudaErrorInvalidValue;
+  const GemmKernel k = gemm_kernel<NPL>(a.mode, ny);
+  if (!k) return cudaErrorInvalidValue;
+  return launch_k(k, dim3(ntiles, ny, 1), dim3(128, 1, 1), GC<NPL>::SMEM, st, pdl, ny, a);
 }
 
 cudaError_t set_smem_attrs() {
   cudaError_t e;
-  if ((e = cudaFuncSetAttribute(k_bt_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, GC<1>::SMEM))) return e;
-  if ((e = cudaFuncSetAttribute(k_bt_gemm<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, GC<3>::SMEM))) return e;
+  for (int mode = 0; mode < 3; ++mode)
+    for (int S = 1; S <= 8; ++S) {
+      if (GemmKernel k = gemm_kernel<1>(mode, S))
+        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, GC<1>::SMEM))) return e;
+      if (GemmKernel k = gemm_kernel<3>(mode, S))
+        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, GC<3>::SMEM))) return e;
+    }
   if ((e = cudaFuncSetAttribute(k_bt_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM))) return e;
   if ((e = cudaFuncSetAttribute(k_bt_head, cudaFuncAttributeMaxDynamicSharedMemorySize, HB_SMEM))) return e;
   return cudaSuccess;
@@ -1083,24 +1480,24 @@ cudaError_t gemm_i8_i8_batched(int32_t* acc, float* y, const int8_t* w, const fl
   int8_t* img = nullptr;
   const int8_t** rows = nullptr;
   float* xs = nullptr;
-  int32_t* part = nullptr;
-  int* cnt = nullptr;
   int* err = nullptr;
   std::vector<const int8_t*> hrows(N);
   for (int r = 0; r < N; ++r) hrows[r] = w + (size_t)r * K;
-  const int kspl = nslab >= 8 ? (nslab + 1) / 2 : nslab;   // two K halves for the long shapes (exercises split K)
+  // K split over a cluster: the fewest CTAs (at least two when there are two
+  // slabs) whose K ranges fit the ring beside the receive buffer
+  int kspl = nslab;
+  for (int S = 2; S <= 8 && nslab >= 2; ++S) {
+    const int k = (nslab + S - 1) / S;
+    if (k <= push_max_slabs(S) && (nslab + k - 1) / k == S) { kspl = k; break; }
+  }
   if ((e = cudaMallocAsync((void**)&tiles, (size_t)N * K, st)) ||
       (e = cudaMallocAsync((void**)&img, (size_t)nslab * 64 * GT_KS, st)) ||
       (e = cudaMallocAsync((void**)&rows, N * sizeof(void*), st)) ||
-      (e = cudaMallocAsync((void**)&xs, 64 * 4, st)) ||
-      (e = cudaMallocAsync((void**)&part, (size_t)ntiles * 64 * 128 * 4, st)) ||
-      (e = cudaMallocAsync((void**)&cnt, ntiles * 4 + 16, st)) || (e = cudaMallocAsync((void**)&err, 16, st)))
+      (e = cudaMallocAsync((void**)&xs, 64 * 4, st)) || (e = cudaMallocAsync((void**)&err, 16, st)))
     return e;
   e = cudaMemcpyAsync(rows, hrows.data(), N * sizeof(void*), cudaMemcpyHostToDevice, st);
   if (!e) e = cudaMemsetAsync(xs, 0, 64 * 4, st);
   if (!e) e = cudaMemcpyAsync(xs, sx, B * 4, cudaMemcpyDeviceToDevice, st);
-  if (!e) e = cudaMemsetAsync(part, 0, (size_t)ntiles * 64 * 128 * 4, st);
-  if (!e) e = cudaMemsetAsync(cnt, 0, ntiles * 4 + 16, st);
   if (!e) e = cudaMemsetAsync(err, 0, 16, st);
   if (!e) e = repack_tiles(rows, tiles, N, K, st);
   if (!e) {
@@ -1110,13 +1507,13 @@ cudaError_t gemm_i8_i8_batched(int32_t* acc, float* y, const int8_t* w, const fl
   GemmArgs a{};
   a.W = tiles; a.sw = sw; a.X = img; a.xs = xs;
   a.nslab = nslab; a.kspl = kspl; a.nb = B; a.mode = EPI_STORE;
-  a.Y = y; a.ldy = N; a.part = part; a.cnt = cnt; a.acc_out = acc; a.nrows = N; a.err = err;
+  a.Y = y; a.ldy = N; a.acc_out = acc; a.nrows = N; a.err = err;
   if (!e) e = launch_gemm<1>(a, ntiles, st);
   int herr[4] = {0, 0, 0, 0};
   if (!e) e = cudaMemcpyAsync(herr, err, 16, cudaMemcpyDeviceToHost, st);
   if (!e) e = cudaStreamSynchronize(st);
   cudaFreeAsync(tiles, st); cudaFreeAsync(img, st); cudaFreeAsync(rows, st); cudaFreeAsync(xs, st);
-  cudaFreeAsync(part, st); cudaFreeAsync(cnt, st); cudaFreeAsync(err, st);
+  cudaFreeAsync(err, st);
   if (!e && herr[0]) e = cudaErrorLaunchTimeout;
   return e;
 }
@@ -1149,8 +1546,6 @@ struct BatchEngine {
   float *H = nullptr, *Y = nullptr, *O = nullptr, *AB = nullptr, *xs = nullptr, *hxs = nullptr, *attp = nullptr,
         *logits = nullptr;
   int8_t *X = nullptr, *HX = nullptr;
-  int32_t* part = nullptr;
-  int* cnt = nullptr;
   unsigned long long* am = nullptr;
   int *tok = nullptr, *ids = nullptr, *err = nullptr;
   BtCtl* dctl = nullptr;
@@ -1162,7 +1557,7 @@ struct BatchEngine {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   // slabs per CTA of each projection (K / 128 slabs; fewer slabs per CTA =
   // more CTAs per tile, reduced exactly in int32)
-  int ksplit_in = 4, ksplit_out = 2, ksplit_gu = 4, ksplit_down = 4;
+  int ksplit_in = 8, ksplit_out = 2, ksplit_gu = 8, ksplit_down = 4;
 };
 
 namespace {
@@ -1197,8 +1592,10 @@ cudaError_t enqueue_step(BatchEngine* E, int nb) {
     GemmArgs a{};
     a.W = W; a.sw = sw; a.X = E->X; a.xs = E->xs;
     a.nslab = K / GT_KS; a.kspl = kspl; a.nb = nb; a.mode = mode;
-    a.Y = Y; a.ldy = ldy; a.part = E->part; a.cnt = E->cnt; a.acc_out = nullptr; a.nrows = nrows; a.err = E->err;
-    e = launch_gemm<NPL>(a, nrows / GT_M, st);
+    a.Y = Y; a.ldy = ldy; a.acc_out = nullptr; a.nrows = nrows; a.err = E->err;
+    const int ny = (a.nslab + kspl - 1) / kspl;
+    if (NPL == 1 && ny > 1 && kspl > push_max_slabs(ny)) { e = cudaErrorInvalidValue; return; }
+    e = launch_gemm<NPL>(a, nrows / GT_M, st, true);
   };
   auto normq = [&](int l, bool embed, bool head) {
     if (e != cudaSuccess) return;
@@ -1208,22 +1605,21 @@ cudaError_t enqueue_step(BatchEngine* E, int nb) {
     if (head) {
       a.gain = E->M.final_norm;
       a.X = E->HX; a.xs = E->hxs;
-      k_bt_normq<3><<<nb, NT, 0, st>>>(a);
+      e = launch_k(k_bt_normq<3>, dim3(nb), dim3(NT), 0, st, true, 0, a);
+      return;
     } else {
       const LayerW& Lw = E->M.L[l];
       a.gain = Lw.in_norm;
       if (Lw.linear) { a.a_w = Lw.a_w; a.b_w = Lw.b_w; a.AB = E->AB; }
       a.X = E->X; a.xs = E->xs;
-      k_bt_normq<NPL><<<nb, NT, 0, st>>>(a);
+      e = launch_k(k_bt_normq<NPL>, dim3(nb), dim3(NT), 0, st, true, 0, a);
     }
-    e = cudaGetLastError();
   };
   auto post_normq = [&](int l) {
     if (e != cudaSuccess) return;
     NormqArgs a{};
     a.H = E->H; a.gain = E->M.L[l].post_norm; a.X = E->X; a.xs = E->xs; a.err = E->err;
-    k_bt_normq<NPL><<<nb, NT, 0, st>>>(a);
-    e = cudaGetLastError();
+    e = launch_k(k_bt_normq<NPL>, dim3(nb), dim3(NT), 0, st, true, 0, a);
   };
   constexpr int LDY = 8192;
   normq(0, true, false);
@@ -1237,23 +1633,23 @@ cudaError_t enqueue_step(BatchEngine* E, int nb) {
       d.conv_seq = E->conv_seq; d.rec_seq = E->rec_seq; d.lin = Lw.lin_idx;
       d.conv_w = Lw.conv_w; d.A_log = Lw.A_log; d.dt_bias = Lw.dt_bias; d.gnorm_w = Lw.gnorm_w;
       d.ctl = E->dctl; d.O = E->O;
-      if (e == cudaSuccess) { k_bt_delta<<<dim3(LH, nb), NT, 0, st>>>(d); e = cudaGetLastError(); }
-      if (e == cudaSuccess) { k_bt_quant<NPL><<<nb, NT, 0, st>>>(E->O, VDIM, VDIM, E->X, E->xs); e = cudaGetLastError(); }
+      if (e == cudaSuccess) e = launch_k(k_bt_delta, dim3(LH, nb), dim3(NT), 0, st, true, 0, d);
+      if (e == cudaSuccess) e = launch_k(k_bt_quant<NPL>, dim3(nb), dim3(NT), 0, st, true, 0, (const float*)E->O, (int)VDIM, (int)VDIM, E->X, E->xs);
     } else {
       AttnArgs at{};
       at.Y = E->Y; at.ldy = LDY; at.kc = E->kc; at.vc = E->vc; at.fi = Lw.full_idx; at.max_ctx = E->max_ctx;
       at.qn_w = Lw.qn_w; at.kn_w = Lw.kn_w; at.rope = E->rope; at.ctl = E->dctl; at.part = E->attp;
       at.maxch = E->maxch; at.err = E->err;
-      if (e == cudaSuccess) { k_bt_attn<<<2 * E->sm_count, 256, AT_SMEM, st>>>(at); e = cudaGetLastError(); }
+      if (e == cudaSuccess) e = launch_k(k_bt_attn, dim3(E->sm_count), dim3(AT_THREADS), AT_SMEM, st, true, 0, at);
       if (e == cudaSuccess) {
-        k_bt_merge<NPL><<<nb, NT, 0, st>>>(E->Y, LDY, E->attp, E->maxch, E->dctl, E->X, E->xs);
-        e = cudaGetLastError();
+        e = launch_k(k_bt_merge<NPL>, dim3(nb), dim3(NT), 0, st, true, 0, (const float*)E->Y, (int)LDY,
+                     (const float*)E->attp, E->maxch, (const BtCtl*)E->dctl, E->X, E->xs);
       }
     }
     gemm(T.wout, T.swout, HID, VDIM, E->ksplit_out, EPI_ADD, E->H, HID);
     post_normq(l);
     gemm(T.wgu, T.swgu, 2 * FFN, HID, E->ksplit_gu, EPI_SWIGLU, E->O, FFN);
-    if (e == cudaSuccess) { k_bt_quant<NPL><<<nb, NT, 0, st>>>(E->O, FFN, FFN, E->X, E->xs); e = cudaGetLastError(); }
+    if (e == cudaSuccess) e = launch_k(k_bt_quant<NPL>, dim3(nb), dim3(NT), 0, st, true, 0, (const float*)E->O, (int)FFN, (int)FFN, E->X, E->xs);
     gemm(T.wdown, T.swdown, HID, FFN, E->ksplit_down, EPI_ADD, E->H, HID);
     if (l + 1 < NLAYER) normq(l + 1, false, false);
   }
@@ -1262,12 +1658,11 @@ cudaError_t enqueue_step(BatchEngine* E, int nb) {
     HeadArgs h{};
     h.tiles = E->head_tiles; h.emb_s = E->M.emb_s; h.HX = E->HX; h.hxs = E->hxs; h.ctl = E->dctl;
     h.logits = E->logits; h.am = E->am; h.err = E->err;
-    k_bt_head<<<E->head_grid, HB_THREADS, HB_SMEM, st>>>(h);
-    e = cudaGetLastError();
+    e = launch_k(k_bt_head, dim3(E->head_grid), dim3(HB_THREADS), HB_SMEM, st, true, 0, h);
   }
   if (e == cudaSuccess) {
-    k_bt_finish<<<nb, 32, 0, st>>>(E->am, E->head_grid, E->ids, E->tok);
-    e = cudaGetLastError();
+    e = launch_k(k_bt_finish, dim3(nb), dim3(32), 0, st, true, 0, (const unsigned long long*)E->am, E->head_grid,
+                 E->ids, E->tok);
   }
   return e;
 }
@@ -1382,8 +1777,6 @@ BatchEngine* batch_create(const ModelW& M, const int8_t* head_tiles, const float
       (e = balloc(E, &E->attp, B * NKV * E->maxch * 4 * AT_PROW * 4)) ||
       (e = balloc(E, &E->logits, (size_t)BATCH_MAX * VOCAB * 4)) ||
       (e = balloc(E, &E->X, (size_t)(FFN / GT_KS) * 192 * GT_KS)) || (e = balloc(E, &E->HX, (size_t)HB_IMG)) ||
-      (e = balloc(E, &E->part, (size_t)BT_MAXTILES * 192 * 128 * 4)) ||
-      (e = balloc(E, &E->cnt, (size_t)BT_MAXTILES * 4)) ||
       (e = balloc(E, &E->am, (size_t)E->head_grid * 64 * 8)) || (e = balloc(E, &E->tok, 64 * 4)) ||
       (e = balloc(E, &E->ids, 64 * 4)) || (e = balloc(E, &E->err, 16)) || (e = balloc(E, &E->dctl, sizeof(BtCtl))))
     return bail(std::string("device memory: ") + cudaGetErrorString(e));

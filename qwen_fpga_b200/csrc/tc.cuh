@@ -35,12 +35,20 @@ __device__ __forceinline__ void mbar_arrive(unsigned bar) {
 __device__ __forceinline__ void mbar_expect(unsigned bar, unsigned bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
 }
+// try_wait that may suspend the thread (up to the hint, in ns) until the
+// phase completes: waiting threads take no issue slots from the SM's others
+__device__ __forceinline__ bool mbar_try_sleep(unsigned bar, unsigned parity) {
+  unsigned ok;
+  asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+               : "=r"(ok) : "r"(bar), "r"(parity), "r"(100000u) : "memory");
+  return ok != 0;
+}
 // Bounded wait for phase `parity` (one thread or many).  On time-out the
 // first error wins into err[0..2] = {ERR_WAIT, site, value}; returns false.
 __device__ __forceinline__ bool mbar_wait(unsigned bar, unsigned parity, int* err, int site, int value) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = gtime();
-  while (!mbar_try(bar, parity)) {
+  while (!mbar_try_sleep(bar, parity)) {
     if (gtime() - t0 > WAIT_NS) {
       if (atomicCAS(err, 0, 3) == 0) { err[1] = site; err[2] = value; }
       return false;
@@ -117,6 +125,33 @@ __device__ __forceinline__ void tmem_ld16(unsigned addr, unsigned (&r)[16]) {
                : "r"(addr) : "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---- thread-block clusters (distributed shared memory)
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ unsigned cluster_ctarank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The address of `addr` (this CTA's shared memory) in CTA `rank` of the cluster.
+__device__ __forceinline__ unsigned mapa(unsigned addr, unsigned rank) {
+  unsigned r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ int ld_dsmem(unsigned addr) {
+  int v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ int4 ld_dsmem_v4(unsigned addr) {
+  int4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
 
 // ---- programmatic dependent launch (no-ops for a launch without the attribute)
 __device__ __forceinline__ void grid_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
