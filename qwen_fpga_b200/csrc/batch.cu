@@ -515,6 +515,7 @@ __global__ void __launch_bounds__(128, 1) k_bt_gemm(const GemmArgs a) {
       tc::bulk_g2s(tc::smem_u32(sm + i * C::STAGE), a.W + ((size_t)tile * a.nslab + slab(i)) * GT_SLAB, GT_SLAB, fb, pw);
     }
   }
+  tc::grid_launch_dependents();   // dependents may launch (they wait for this grid before reading)
   tc::grid_wait();
   if (wid == 0) tc::tmem_alloc<C::TCOLS>(tslot);
   tc::fence_before();
@@ -574,11 +575,23 @@ __global__ void __launch_bounds__(128, 1) k_bt_gemm(const GemmArgs a) {
     // one CTA per tile: the sums straight from TMEM, 16 tokens at a time (all
     // planes' loads in flight before the wait)
     tc::fence_after();
+    unsigned rall[NPL == 1 ? 64 : 1];   // W8A8: all 64 sums requested before one wait
+    if constexpr (NPL == 1) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_ld16(taddr + 16 * c, *reinterpret_cast<unsigned(*)[16]>(rall + 16 * c));
+      tc::tmem_ld_wait();
+    }
+#pragma unroll
     for (int c0 = 0; c0 < 64; c0 += 16) {
       unsigned r[NPL][16];
+      if constexpr (NPL == 1) {
 #pragma unroll
-      for (int p = 0; p < NPL; ++p) tc::tmem_ld16(taddr + 64 * p + c0, r[p]);
-      tc::tmem_ld_wait();
+        for (int e = 0; e < 16; ++e) r[0][e] = rall[c0 + e];
+      } else {
+#pragma unroll
+        for (int p = 0; p < NPL; ++p) tc::tmem_ld16(taddr + 64 * p + c0, r[p]);
+        tc::tmem_ld_wait();
+      }
       float yv[16];
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
@@ -604,7 +617,6 @@ __global__ void __launch_bounds__(128, 1) k_bt_gemm(const GemmArgs a) {
     tc::fence_after();
     tc::tmem_free<C::TCOLS>(tmem);
   }
-  tc::grid_launch_dependents();
 }
 
 // ---------------------------------------------------------------- norm + image
@@ -627,6 +639,7 @@ __global__ void __launch_bounds__(NT) k_bt_normq(const NormqArgs a) {
   __shared__ float red[2 * NW];
   __shared__ float rab[32][NW];
   const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  tc::grid_launch_dependents();   // dependents may launch (they wait for this grid before reading)
   tc::grid_wait();
   float* hrow = a.H + (size_t)b * HID;
   float2 h2;
@@ -693,7 +706,6 @@ __global__ void __launch_bounds__(NT) k_bt_normq(const NormqArgs a) {
       a.AB[b * 32 + t] = s;
     }
   }
-  tc::grid_launch_dependents();
 }
 
 // Quantiser of a K-vector per token (K a multiple of 4, <= 4096): src[b lds + k].
@@ -701,6 +713,7 @@ template <int NPL>
 __global__ void __launch_bounds__(NT) k_bt_quant(const float* __restrict__ src, int lds, int K, int8_t* X, float* xs) {
   __shared__ float red[NW];
   const int b = blockIdx.x, t = threadIdx.x;
+  tc::grid_launch_dependents();   // dependents may launch (they wait for this grid before reading)
   tc::grid_wait();
   const float* s = src + (size_t)b * lds;
   float v[2][4];
@@ -720,7 +733,6 @@ __global__ void __launch_bounds__(NT) k_bt_quant(const float* __restrict__ src, 
     const int g = t + NT * j;
     if (4 * g < K) image_store<NPL, 4>(v[j], 4 * g, b, amax, X, xs, nullptr);
   }
-  tc::grid_launch_dependents();
 }
 
 // ---------------------------------------------------------------- DeltaNet mixer
@@ -745,6 +757,7 @@ __global__ void __launch_bounds__(NT) k_bt_delta(const DeltaArgs a) {
   __shared__ float gbeta, gg, ginv;
   const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
   constexpr int KPG = LK / 4;
+  tc::grid_launch_dependents();   // dependents may launch (they wait for this grid before reading)
   tc::grid_wait();
   const float* y = a.Y + (size_t)b * a.ldy;
   float* cs = a.conv + (size_t)b * a.conv_seq + (size_t)a.lin * CONVD * CONVK;
@@ -834,7 +847,6 @@ __global__ void __launch_bounds__(NT) k_bt_delta(const DeltaArgs a) {
     const float v = __fmul_rn(__fmul_rn(ob[t], ginv), a.gnorm_w[t]);
     a.O[(size_t)b * VDIM + h * LV + t] = __fmul_rn(v, z);
   }
-  tc::grid_launch_dependents();
 }
 
 // ---------------------------------------------------------------- attention
@@ -941,6 +953,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_bt_attn(const AttnArgs a) {
     }
     tc::mbar_init_fence();
   }
+  tc::grid_launch_dependents();   // dependents may launch (they wait for this grid before reading)
   tc::grid_wait();
   __syncthreads();
   const BtCtl& C = *a.ctl;
@@ -1146,7 +1159,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_bt_attn(const AttnArgs a) {
       }
     }
   }
-  tc::grid_launch_dependents();
 }
 
 // Merge the chunks of every head of token b (online, in chunk order), times
@@ -1158,6 +1170,7 @@ __global__ void __launch_bounds__(NT) k_bt_merge(const float* __restrict__ Y, in
   __shared__ float red[NW];
   const int b = blockIdx.x, t = threadIdx.x;
   const int hh = t >> 6, d0 = 4 * (t & 63), g = hh >> 2, hq = hh & 3;
+  tc::grid_launch_dependents();   // dependents may launch (they wait for this grid before reading)
   tc::grid_wait();
   const int nch = (ctl->T[b] + 1 + AT_CL - 1) / AT_CL;
   float M = -INFINITY, Ls = 0.0f, O[4] = {0.f, 0.f, 0.f, 0.f};
@@ -1182,7 +1195,6 @@ __global__ void __launch_bounds__(NT) k_bt_merge(const float* __restrict__ Y, in
   x[3] = __fmul_rn(__fdiv_rn(O[3], Ls), sigmoid_f(gt.w));
   const float amax = amax512(fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3]))), red);
   image_store<NPL, 4>(x, hh * HD + d0, b, amax, X, xs, nullptr);
-  tc::grid_launch_dependents();
 }
 
 // ---------------------------------------------------------------- head
@@ -1233,6 +1245,7 @@ __global__ void __launch_bounds__(HB_THREADS, 1) k_bt_head(const HeadArgs a) {
     tc::mbar_init(bimg, 1);
     tc::mbar_init_fence();
   }
+  tc::grid_launch_dependents();   // dependents may launch (they wait for this grid before reading)
   tc::grid_wait();
   if (wid == 0) tc::tmem_alloc<512>(tslot);
   tc::fence_before();
@@ -1350,12 +1363,12 @@ __global__ void __launch_bounds__(HB_THREADS, 1) k_bt_head(const HeadArgs a) {
     tc::fence_after();
     tc::tmem_free<512>(tmem);
   }
-  tc::grid_launch_dependents();
 }
 
 // argmax over the head CTAs per token -> ids, and the next step's token
 __global__ void k_bt_finish(const unsigned long long* __restrict__ am, int G, int* ids, int* tok) {
   const int b = blockIdx.x, lane = threadIdx.x;
+  tc::grid_launch_dependents();   // dependents may launch (they wait for this grid before reading)
   tc::grid_wait();
   unsigned long long m = 0ull;
   for (int c = lane; c < G; c += 32) m = umax64(m, am[(size_t)c * 64 + b]);
@@ -1366,7 +1379,6 @@ __global__ void k_bt_finish(const unsigned long long* __restrict__ am, int G, in
     ids[b] = id;
     tok[b] = id;
   }
-  tc::grid_launch_dependents();
 }
 
 }  // namespace
