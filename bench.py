@@ -219,6 +219,26 @@ def run_profile(args):
     return 0
 
 
+def run_profile_c4(args):
+    """Target for ncu: a config-4 batched context (args.c4_batch sequences,
+    four distinct 2048-position warm starts), one step with host tokens, then
+    args.profile_c4 greedy steps."""
+    from qwen_fpga_b200 import api, synth
+    B = args.c4_batch
+    bd = api.BatchDecoder(synth.ensure_blob(1234), max_batch=B, max_ctx=C4_T0 + args.profile_c4 + 16,
+                          act_int8=True)
+    for i in range(4):
+        st = synth.warm_state_arrays(C4_T0, 40 + i)
+        for b in range(i, B, 4):
+            bd.import_state(b, st)
+    am, _ = bd.step([int(np.random.default_rng(100 + b).integers(0, VOCAB)) for b in range(B)])
+    for _ in range(args.profile_c4):
+        am, _ = bd.step_greedy(B)
+    bd.close()
+    print("profile ok")
+    return 0
+
+
 def run_reference(args, rank):
     """The reference arm: rank 0 alone times the reference's CPU decode path on a
     bounded sample of config 0 (see the module docstring); other ranks exit."""
@@ -428,9 +448,14 @@ def main():
     ap.add_argument("--gemv-n", type=int, default=0, help="with --gemv: only the shape with this N")
     ap.add_argument("--profile", type=int, default=0,
                     help="run N decode steps of the config-0 prompt (no timing, no JSON) for ncu")
+    ap.add_argument("--profile-c4", type=int, default=0,
+                    help="config 4 for ncu: one step, then N greedy steps of a batched context (no timing)")
+    ap.add_argument("--c4-batch", type=int, default=C4_BATCH, help="config 4: sequences per GPU")
     args = ap.parse_args()
     if args.profile:
         return run_profile(args)
+    if args.profile_c4:
+        return run_profile_c4(args)
     if args.gemv:
         return run_gemv(args)
 
@@ -554,7 +579,7 @@ def main():
     dec.close()
     # config 4: batched decode, every rank its own batch of 64 sequences (data parallel)
     if "4" in configs:
-        r4 = config4(blob_path, local, max(1, args.c4_steps), W)
+        r4 = config4(blob_path, local, max(1, args.c4_steps), W, B=args.c4_batch)
         sec4, e2e4 = r4["sec"], r4["e2e_sec"]
         if world > 1:
             t = torch.tensor([sec4, e2e4], dtype=torch.float64, device="cuda")
