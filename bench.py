@@ -593,6 +593,7 @@ def main():
                         f"{st4} of the 128 greedy steps timed (device-fed tokens), then {r4['e2e_steps']} more "
                         "end to end", "batch_per_gpu": r4["B"], "n_gpus": world,
             "parallelism": "1 GPU" if world == 1 else f"{world} GPUs, one batch each (data parallel)",
+            "scaling": "weak",
             "value": world * r4["B"] * st4 / sec4, "unit": UNIT, "ms_per_step": sec4 / st4 * 1e3,
             "bytes_per_step": r4["bytes_per_step"], "achieved_GB_s": ach4, "frac": ach4 / peak,
             "mean_T": r4["t_mean"],
