@@ -1,5 +1,6 @@
-/* qwen_b200.h -- C ABI of libqwenb200.so, the B200 (sm_100a) int8 batch-1
- * decode step of the Qwen3.5-0.8B hybrid text decoder.
+/* qwen_b200.h -- C ABI of libqwenb200.so, the B200 (sm_100a) int8 decode
+ * step of the Qwen3.5-0.8B hybrid text decoder, at batch 1 and batched over up
+ * to 64 independent sequences.
  *
  * Every entry point returns an int status (0 = QWEN_OK); a context keeps the
  * message of its last failure (qwen_last_error).  Plain pointers and sizes
@@ -96,10 +97,13 @@ int qwen_pack_blob(const char* snapshot_dir, const char* out_blob);
 int qwen_destroy(qwen_ctx* ctx);
 
 /* Zero the recurrent state, empty the KV cache, pos = 0
- * (hls/src/state.hpp:24-34, golden/model.py:97-107).  seq must be 0. */
+ * (hls/src/state.hpp:24-34, golden/model.py:97-107) of sequence seq: 0 on a
+ * batch-1 context; 0 .. max_batch-1, or -1 for every sequence, on a batched
+ * context. */
 int qwen_reset(qwen_ctx* ctx, int seq);
 
-/* Load / read back the decode state (golden/model.py:86-95 DecodeState):
+/* Load / read back the decode state of sequence seq (golden/model.py:86-95
+ * DecodeState; seq as for qwen_reset, -1 excluded):
  *   conv [18][6144][4]   rec [18][16][128][128]
  *   kc, vc [6][T][2][256] (K after QK-norm and RoPE, V raw)   pos
  * Host pointers.  Import requires T <= max_ctx - 1.  Export writes T and pos
@@ -161,6 +165,18 @@ int qwen_capture_read(qwen_ctx* ctx, float* out, int max_floats);
  * previous argmax (greedy continuation). */
 int qwen_decode_step(qwen_ctx* ctx, const int* tok, int batch, float* logits_out,
                      int* argmax_out);
+
+/* Prefill (batch-1 single-GPU context): the n prompt tokens run through every
+ * layer at once instead of n decode steps -- the projections as tensor-core
+ * GEMMs over the tokens, the DeltaNet layers by the chunked delta rule
+ * (the recurrence of golden/model.py:168-178 unrolled over a chunk of up to
+ * 32 tokens: one triangular solve and dense products, the state read and
+ * written once per chunk), attention causal over the cache and the prompt.
+ * The decode state afterwards is that of n qwen_decode_step calls (fp32
+ * reassociation aside); logits_out (nullable, host or device, vocab floats)
+ * and argmax_out (nullable) get the last token's.  The reference only loops
+ * the decode step (golden/model.py:1-7, run_prompt.py:82-83). */
+int qwen_prefill(qwen_ctx* ctx, const int* tok, int n, float* logits_out, int* argmax_out);
 
 /* Batched context only: `steps` greedy steps of sequences 0 .. batch-1 (each
  * fed its previous argmax), timed on the device (decode steps only, as

@@ -84,6 +84,7 @@ def load() -> C.CDLL:
     L.qwen_gemv_i8_i8.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_float, C.c_int, C.c_int, _vp]
     L.qwen_gemm_i8_i8.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, C.c_int, _vp]
     L.qwen_decode_timed.argtypes = [_vp, C.c_int, C.c_int, C.POINTER(C.c_double)]
+    L.qwen_prefill.argtypes = [_vp, _ip, C.c_int, _vp, _ip]
     L.qwen_delta_rule_layer.argtypes = [_vp] * 7 + [_vp]
     L.qwen_gemv_i8_f32_argmax_noalloc.argtypes = [_vp, _vp, _vp, _vp, _vp, C.c_int, C.c_int, _vp]
     L.qwen_capture_phase.argtypes = [_vp, C.c_int]
@@ -249,6 +250,17 @@ class Decoder:
             lg = np.empty(VOCAB, np.float32) if want_logits else None
         rc = load().qwen_decode_step(self.h, t, 1, lg.ctypes.data if lg is not None else None, am)
         _check(rc, self.h)
+        return int(am[0]), lg
+
+    def prefill(self, tokens, want_logits: bool = True):
+        """All prompt tokens through the layers at once (qwen_prefill): the
+        state afterwards is that of one decode_step per token.  Returns the
+        last token's (argmax, logits or None)."""
+        t = np.ascontiguousarray(np.asarray(tokens, np.int32))
+        am = (C.c_int * 1)()
+        lg = np.empty(VOCAB, np.float32) if want_logits else None
+        _check(load().qwen_prefill(self.h, t.ctypes.data_as(_ip), int(t.size),
+                                   lg.ctypes.data if lg is not None else None, am), self.h)
         return int(am[0]), lg
 
     def generate(self, prompt, n_new: int):

@@ -1197,6 +1197,326 @@ __global__ void __launch_bounds__(NT) k_bt_merge(const float* __restrict__ Y, in
   image_store<NPL, 4>(x, hh * HD + d0, b, amax, X, xs, nullptr);
 }
 
+// ---------------------------------------------------------------- prefill (one sequence, n tokens)
+//
+// A prompt chunk of n <= PF_MAX tokens of ONE sequence runs through the
+// layers at once: the projections are the batched GEMMs with N = the chunk's
+// tokens; the DeltaNet mixer is the chunked delta rule (below); attention
+// appends the chunk's keys and values to the cache and attends causally.
+
+constexpr int PF_MAX = 32;   // tokens per prefill chunk
+
+struct PfDeltaArgs {
+  const float* Y; int ldy;       // in-proj outputs of the chunk: qkv [0, 6144), z [6144, 8192)
+  const float* AB;               // [n][32]: b rows, then a rows
+  float* conv; float* rec;       // the sequence's conv ring [18][6144][4] and state [18][16][128][128]
+  int lin, base, n;              // linear layer, ring origin before the chunk, tokens
+  const float* conv_w; const float* A_log; const float* dt_bias; const float* gnorm_w;
+  float* O;                      // [n][VDIM] gated-normed outputs
+};
+// dynamic shared memory of k_pf_delta (floats)
+constexpr int PFD_QS = 0, PFD_KS = PFD_QS + PF_MAX * LK, PFD_VS = PFD_KS + PF_MAX * LK, PFD_U = PFD_VS + PF_MAX * LV,
+              PFD_PART = PFD_U + PF_MAX * LV, PFD_A = PFD_PART + 4 * PF_MAX * LV, PFD_QK = PFD_A + PF_MAX * PF_MAX,
+              PFD_G = PFD_QK + PF_MAX * PF_MAX, PFD_BETA = PFD_G + PF_MAX, PFD_GL = PFD_BETA + PF_MAX,
+              PFD_W = PFD_GL + PF_MAX, PFD_WSQ = PFD_W + PF_MAX, PFD_INV = PFD_WSQ + PF_MAX * 8,
+              PFD_GINV = PFD_INV + 2 * PF_MAX, PFD_FLOATS = PFD_GINV + PF_MAX;
+constexpr int PFD_SMEM = PFD_FLOATS * 4;
+
+// Chunked gated delta rule of head blockIdx.x over the chunk's n tokens
+// (golden/model.py:149-189 for each token, restated in the WY form of the
+// recurrence).  With G_t = g_0 + ... + g_t (log decay), Gamma_t = e^{G_t} and
+// S the state before the chunk, the recurrence S_t = e^{g_t} S_{t-1} + k_t d_t^T,
+// d_t = beta_t (v_t - (e^{g_t} S_{t-1})^T k_t), o_t = S_t^T q_t unrolls to
+//   d_t = beta_t (v_t - Gamma_t S^T k_t) - sum_{s<t} beta_t e^{G_t - G_s} (k_t . k_s) d_s
+//   o_t = Gamma_t S^T q_t + sum_{s<=t} e^{G_t - G_s} (q_t . k_s) d_s
+//   S_n = Gamma_{n-1} S + sum_t e^{G_{n-1} - G_t} k_t d_t^T,
+// so the chunk needs one triangular solve for d and a few dense products; the
+// state is read and written once.  512 threads: conv + SiLU (threads 0-383,
+// one channel each, every token), gates (384 + t), l2norm per token as the
+// decode step does it, then the products with thread (v = t % 128, row group
+// t / 128) holding 32 state rows of column v.
+__global__ void __launch_bounds__(NT) k_pf_delta(const PfDeltaArgs a) {
+  extern __shared__ __align__(16) float smf[];
+  float* qs = smf + PFD_QS;      // [t][128]
+  float* ks = smf + PFD_KS;
+  float* vs = smf + PFD_VS;      // v, later o
+  float* U = smf + PFD_U;        // d_t
+  float* part = smf + PFD_PART;  // [4][t][128]
+  float* Am = smf + PFD_A;       // [t][s]
+  float* QK = smf + PFD_QK;      // [t][s]
+  float* G = smf + PFD_G;
+  float* beta = smf + PFD_BETA;
+  float* gl = smf + PFD_GL;
+  float* wt = smf + PFD_W;       // e^{G_{n-1} - G_t}
+  float* wsq = smf + PFD_WSQ;    // [t][8] warp sums of squares
+  float* inv = smf + PFD_INV;    // [2][t]
+  float* ginv = smf + PFD_GINV;  // [t]
+  const int h = blockIdx.x, t = threadIdx.x, n = a.n, lane = t & 31, wid = t >> 5;
+  const int vi = t & (LV - 1), kg = t / LV;
+  constexpr int KPG = LK / 4;
+  tc::grid_launch_dependents();
+  tc::grid_wait();
+  float* Sh = a.rec + ((size_t)a.lin * LH + h) * LK * LV;
+  float sv[KPG];
+#pragma unroll
+  for (int kk = 0; kk < KPG; ++kk) sv[kk] = Sh[(size_t)(kg * KPG + kk) * LV + vi];
+  // conv over [x_{t-3}, x_{t-2}, x_{t-1}, x_t] (history from the ring) + SiLU
+  if (t < 3 * LK) {
+    const int c = t & (LK - 1);
+    const int ch = t < LK ? h * LK + c : (t < 2 * LK ? KDIM + h * LK + c : 2 * KDIM + h * LV + c);
+    float* dst = t < LK ? qs : (t < 2 * LK ? ks : vs);
+    float* st = a.conv + ((size_t)a.lin * CONVD + ch) * CONVK;
+    const int base = a.base;
+    float h1 = st[(base + 1) & 3], h2 = st[(base + 2) & 3], h3 = st[(base + 3) & 3];
+    const float4 w4 = *reinterpret_cast<const float4*>(a.conv_w + (size_t)ch * CONVK);
+    for (int tt = 0; tt < n; ++tt) {
+      const float nv = a.Y[(size_t)tt * a.ldy + ch];
+      float acc = __fmul_rn(h1, w4.x);
+      acc = __fadd_rn(acc, __fmul_rn(h2, w4.y));
+      acc = __fadd_rn(acc, __fmul_rn(h3, w4.z));
+      acc = __fadd_rn(acc, __fmul_rn(nv, w4.w));
+      dst[tt * LK + c] = silu_f(acc);
+      h1 = h2; h2 = h3; h3 = nv;
+    }
+    // the ring as n decode steps leave it: input j in slot (base + j) & 3
+    for (int j = max(0, n - 4); j < n; ++j) st[(base + j) & 3] = a.Y[(size_t)j * a.ldy + ch];
+  } else if (t < 3 * LK + n) {
+    const int tt = t - 3 * LK;
+    beta[tt] = sigmoid_f(a.AB[tt * 32 + h]);
+    gl[tt] = __fmul_rn(-expf(a.A_log[h]), softplus_f(__fadd_rn(a.AB[tt * 32 + 16 + h], a.dt_bias[h])));
+  }
+  __syncthreads();
+  if (t == 0) {
+    float acc = 0.0f;
+    for (int tt = 0; tt < n; ++tt) { acc = __fadd_rn(acc, gl[tt]); G[tt] = acc; }
+  }
+  // l2norm of q (warps 0-3) and k (warps 4-7) per token, as the decode step
+  if (t < 2 * LK) {
+    const float* src = t < LK ? qs : ks;
+    for (int tt = 0; tt < n; ++tt) {
+      const float x = src[tt * LK + (t & (LK - 1))];
+      const float ss = warp_sum(x * x);
+      if (lane == 0) wsq[tt * 8 + wid] = ss;
+    }
+  }
+  __syncthreads();
+  if (t < 2 * PF_MAX) {
+    const int tt = t % PF_MAX, g0 = t < PF_MAX ? 0 : 4;
+    if (tt < n) {
+      const float tot = ((wsq[tt * 8 + g0] + wsq[tt * 8 + g0 + 1]) + wsq[tt * 8 + g0 + 2]) + wsq[tt * 8 + g0 + 3];
+      inv[(t < PF_MAX ? 0 : PF_MAX) + tt] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(tot, EPS)));
+    }
+  }
+  if (t == 64) for (int tt = 0; tt < n; ++tt) wt[tt] = 0.0f;
+  __syncthreads();
+  if (t < 2 * LK) {
+    float* dst = t < LK ? qs : ks;
+    const int c = t & (LK - 1);
+    for (int tt = 0; tt < n; ++tt) {
+      const float x = dst[tt * LK + c];
+      dst[tt * LK + c] = t < LK ? __fmul_rn(__fmul_rn(x, inv[tt]), 0.08838834764831845f)
+                                : __fmul_rn(x, inv[PF_MAX + tt]);
+    }
+  }
+  if (t == 64) {
+    const float Gl = G[n - 1];
+    for (int tt = 0; tt < n; ++tt) wt[tt] = expf(Gl - G[tt]);
+  }
+  __syncthreads();
+  // KK (strictly lower, scaled) and QK (lower with the diagonal): pair (tt, ss)
+  // per thread, dims read from a lane-rotated start (no bank conflicts)
+  for (int pidx = t; pidx < n * n; pidx += NT) {
+    const int tt = pidx / n, ss = pidx - tt * n;
+    float kk = 0.0f, qk = 0.0f;
+    if (ss <= tt) {
+      for (int d0 = 0; d0 < LK; ++d0) {
+        const int d = (d0 + lane) & (LK - 1);
+        const float ksd = ks[ss * LK + d];
+        kk = fmaf(ks[tt * LK + d], ksd, kk);
+        qk = fmaf(qs[tt * LK + d], ksd, qk);
+      }
+    }
+    const float dec = ss <= tt ? expf(G[tt] - G[ss]) : 0.0f;
+    Am[tt * PF_MAX + ss] = ss < tt ? __fmul_rn(__fmul_rn(beta[tt], dec), kk) : 0.0f;
+    QK[tt * PF_MAX + ss] = ss <= tt ? __fmul_rn(dec, qk) : 0.0f;
+  }
+  // S^T k_t partials over this thread's 32 rows
+  for (int tt = 0; tt < n; ++tt) {
+    float p = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < KPG; ++kk) p = fmaf(sv[kk], ks[tt * LK + kg * KPG + kk], p);
+    part[(kg * PF_MAX + tt) * LV + vi] = p;
+  }
+  __syncthreads();
+  // right-hand side beta_t (v_t - Gamma_t S^T k_t)
+  for (int tt = kg; tt < n; tt += 4) {
+    const float kv = ((part[(0 * PF_MAX + tt) * LV + vi] + part[(1 * PF_MAX + tt) * LV + vi]) +
+                      part[(2 * PF_MAX + tt) * LV + vi]) + part[(3 * PF_MAX + tt) * LV + vi];
+    U[tt * LV + vi] = __fmul_rn(beta[tt], __fsub_rn(vs[tt * LV + vi], __fmul_rn(expf(G[tt]), kv)));
+  }
+  __syncthreads();
+  // forward substitution: d_t = r_t - sum_{s<t} A[t][s] d_s (threads 0-127, column vi)
+  if (t < LV) {
+    for (int tt = 1; tt < n; ++tt) {
+      float u = U[tt * LV + vi];
+      for (int ss = 0; ss < tt; ++ss) u = fmaf(-Am[tt * PF_MAX + ss], U[ss * LV + vi], u);
+      U[tt * LV + vi] = u;
+    }
+  }
+  // S^T q_t partials
+  for (int tt = 0; tt < n; ++tt) {
+    float p = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < KPG; ++kk) p = fmaf(sv[kk], qs[tt * LK + kg * KPG + kk], p);
+    part[(kg * PF_MAX + tt) * LV + vi] = p;
+  }
+  __syncthreads();
+  // o_t = Gamma_t S^T q_t + sum_{s<=t} QK[t][s] d_s (into vs)
+  for (int tt = kg; tt < n; tt += 4) {
+    const float sq = ((part[(0 * PF_MAX + tt) * LV + vi] + part[(1 * PF_MAX + tt) * LV + vi]) +
+                      part[(2 * PF_MAX + tt) * LV + vi]) + part[(3 * PF_MAX + tt) * LV + vi];
+    float o = __fmul_rn(expf(G[tt]), sq);
+    for (int ss = 0; ss <= tt; ++ss) o = fmaf(QK[tt * PF_MAX + ss], U[ss * LV + vi], o);
+    vs[tt * LV + vi] = o;
+  }
+  // the state after the chunk
+  {
+    const float gam = expf(G[n - 1]);
+#pragma unroll
+    for (int kk = 0; kk < KPG; ++kk) {
+      const int k = kg * KPG + kk;
+      float sval = __fmul_rn(sv[kk], gam);
+      for (int tt = 0; tt < n; ++tt) sval = fmaf(__fmul_rn(wt[tt], ks[tt * LK + k]), U[tt * LV + vi], sval);
+      Sh[(size_t)k * LV + vi] = sval;
+    }
+  }
+  __syncthreads();
+  // gated RMSNorm per token (golden/model.py:183-189), one warp per token
+  for (int tt = wid; tt < n; tt += NW) {
+    float s = 0.0f;
+    for (int i = lane; i < LV; i += 32) s = fmaf(vs[tt * LV + i], vs[tt * LV + i], s);
+    s = warp_sum(s);
+    if (lane == 0) ginv[tt] = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(s, 1.0f / LV), EPS)));
+  }
+  __syncthreads();
+  for (int tt = kg; tt < n; tt += 4) {
+    const float z = silu_f(a.Y[(size_t)tt * a.ldy + CONVD + h * LV + vi]);
+    const float v = __fmul_rn(__fmul_rn(vs[tt * LV + vi], ginv[tt]), a.gnorm_w[vi]);
+    a.O[(size_t)tt * VDIM + h * LV + vi] = __fmul_rn(v, z);
+  }
+}
+
+struct PfAttnArgs {
+  const float* Y; int ldy;       // in-proj outputs of the chunk: [q | gate] per head, k, v
+  float* kc; float* vc;          // the sequence's cache, [6][max_ctx][512] (K after QK-norm + RoPE)
+  int fi, max_ctx, T0, pos0, n;  // positions before the chunk; the chunk's first RoPE position
+  const float* qn_w; const float* kn_w; const float* rope;
+  float* QN;                     // [n][8][256] normed + roped queries
+  float* O;                      // [n][VDIM]
+};
+
+// QK-norm + RoPE of token blockIdx.x's query heads of group blockIdx.y (warps
+// 0-3) and its key (warp 4), value (warp 5) into cache slot T0 + token.
+__global__ void __launch_bounds__(192) k_pf_kvprep(const PfAttnArgs a) {
+  const int tt = blockIdx.x, g = blockIdx.y, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  tc::grid_launch_dependents();
+  tc::grid_wait();
+  const float* y = a.Y + (size_t)tt * a.ldy;
+  const float* rope = a.rope + (size_t)(a.pos0 + tt) * ROT;
+  const size_t row = ((size_t)a.fi * a.max_ctx + a.T0 + tt) * KVPROJ + (size_t)g * HD;
+  if (wid < 4) norm_rope_warp(y + (4 * g + wid) * 2 * HD, a.qn_w, rope[lane], rope[32 + lane],
+                              a.QN + ((size_t)tt * NH + 4 * g + wid) * HD);
+  else if (wid == 4) norm_rope_warp(y + QPROJ + g * HD, a.kn_w, rope[lane], rope[32 + lane], a.kc + row);
+  else for (int e = lane; e < HD; e += 32) a.vc[row + e] = y[QPROJ + KVPROJ + g * HD + e];
+}
+
+// Causal attention of token blockIdx.x of the chunk over cache positions
+// [0, T0 + token], the four query heads of group blockIdx.y: warp w takes
+// positions w, w + 8, ..., lane = 8 dims, online softmax per warp and head;
+// the warps merge in shared memory (dynamic, 8 x 4 x AT_PROW floats), then
+// o / l * sigmoid(gate) (golden/model.py:219-229).
+__global__ void __launch_bounds__(256) k_pf_attn(const PfAttnArgs a) {
+  extern __shared__ __align__(16) float mrg[];
+  const int tt = blockIdx.x, g = blockIdx.y, t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  tc::grid_launch_dependents();
+  tc::grid_wait();
+  float qr[4][8];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const float* q = a.QN + ((size_t)tt * NH + 4 * g + h) * HD + 8 * lane;
+    const float4 u0 = *reinterpret_cast<const float4*>(q), u1 = *reinterpret_cast<const float4*>(q + 4);
+    qr[h][0] = u0.x; qr[h][1] = u0.y; qr[h][2] = u0.z; qr[h][3] = u0.w;
+    qr[h][4] = u1.x; qr[h][5] = u1.y; qr[h][6] = u1.z; qr[h][7] = u1.w;
+  }
+  float m[4], l[4], o[4][8];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[h][j] = 0.0f;
+  }
+  const int npos = a.T0 + tt + 1;
+  const float* kb = a.kc + (size_t)a.fi * a.max_ctx * KVPROJ + (size_t)g * HD + 8 * lane;
+  const float* vb = a.vc + (size_t)a.fi * a.max_ctx * KVPROJ + (size_t)g * HD + 8 * lane;
+  for (int p = wid; p < npos; p += 8) {
+    const float4 k0 = *reinterpret_cast<const float4*>(kb + (size_t)p * KVPROJ);
+    const float4 k1 = *reinterpret_cast<const float4*>(kb + (size_t)p * KVPROJ + 4);
+    const float4 v0 = *reinterpret_cast<const float4*>(vb + (size_t)p * KVPROJ);
+    const float4 v1 = *reinterpret_cast<const float4*>(vb + (size_t)p * KVPROJ + 4);
+    const float kk[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+    const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    float sc[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      float d = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) d = fmaf(qr[h][j], kk[j], d);
+      sc[h] = d;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int h = 0; h < 4; ++h) sc[h] += __shfl_xor_sync(0xffffffffu, sc[h], off);
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float sv = __fmul_rn(sc[h], 0.0625f);
+      const float mn = fmaxf(m[h], sv);
+      const float al = m[h] == -INFINITY ? 0.0f : expf(m[h] - mn);
+      const float e = expf(sv - mn);
+      l[h] = fmaf(l[h], al, e);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[h][j] = fmaf(e, vv[j], __fmul_rn(o[h][j], al));
+      m[h] = mn;
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    float* mw = mrg + (wid * 4 + h) * AT_PROW;
+    if (lane == 0) { mw[0] = m[h]; mw[1] = l[h]; }
+    *reinterpret_cast<float4*>(mw + 4 + 8 * lane) = make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
+    *reinterpret_cast<float4*>(mw + 8 + 8 * lane) = make_float4(o[h][4], o[h][5], o[h][6], o[h][7]);
+  }
+  __syncthreads();
+  const float* y = a.Y + (size_t)tt * a.ldy;
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    float M = -INFINITY, L = 0.0f, Ov = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const float* mw = mrg + (w * 4 + h) * AT_PROW;
+      if (mw[0] == -INFINITY) continue;
+      const float Mn = fmaxf(M, mw[0]);
+      const float sa = M == -INFINITY ? 0.0f : expf(M - Mn), sb = expf(mw[0] - Mn);
+      L = fmaf(mw[1], sb, __fmul_rn(L, sa));
+      Ov = fmaf(mw[4 + t], sb, __fmul_rn(Ov, sa));
+      M = Mn;
+    }
+    const float gt = y[(4 * g + h) * 2 * HD + HD + t];
+    a.O[(size_t)tt * VDIM + (4 * g + h) * HD + t] = __fmul_rn(__fdiv_rn(Ov, L), sigmoid_f(gt));
+  }
+}
+
 // ---------------------------------------------------------------- head
 
 constexpr int HB_BBYTES = 3 * 64 * GT_KS;             // one K-slab of the head image (192 rows)
@@ -1477,6 +1797,8 @@ cudaError_t set_smem_attrs() {
     }
   if ((e = cudaFuncSetAttribute(k_bt_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM))) return e;
   if ((e = cudaFuncSetAttribute(k_bt_head, cudaFuncAttributeMaxDynamicSharedMemorySize, HB_SMEM))) return e;
+  if ((e = cudaFuncSetAttribute(k_pf_delta, cudaFuncAttributeMaxDynamicSharedMemorySize, PFD_SMEM))) return e;
+  if ((e = cudaFuncSetAttribute(k_pf_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 4 * AT_PROW * 4))) return e;
   return cudaSuccess;
 }
 
@@ -1679,6 +2001,82 @@ cudaError_t enqueue_step(BatchEngine* E, int nb) {
   return e;
 }
 
+// One prefill chunk of n tokens (E->tok) of one sequence whose arrays are
+// conv / rec / kc / vc (the batch-1 layouts); head: the last token's logits,
+// argmax into E->ids[0] (E->dctl: nb = 1).
+template <int NPL>
+cudaError_t enqueue_prefill(BatchEngine* E, float* conv, float* rec, float* kc, float* vc, int max_ctx, int base, int T0,
+                            int pos0, int n, bool head) {
+  cudaStream_t st = E->st;
+  cudaError_t e = cudaSuccess;
+  constexpr int LDY = 8192;
+  auto gemm = [&](const int8_t* W, const float* sw, int nrows, int K, int kspl, int mode, float* Y, int ldy) {
+    if (e != cudaSuccess) return;
+    GemmArgs a{};
+    a.W = W; a.sw = sw; a.X = E->X; a.xs = E->xs;
+    a.nslab = K / GT_KS; a.kspl = kspl; a.nb = n; a.mode = mode;
+    a.Y = Y; a.ldy = ldy; a.acc_out = nullptr; a.nrows = nrows; a.err = E->err;
+    e = launch_gemm<NPL>(a, nrows / GT_M, st, true);
+  };
+  auto normq = [&](int l, bool embed) {
+    if (e != cudaSuccess) return;
+    NormqArgs a{};
+    const LayerW& Lw = E->M.L[l];
+    a.H = E->H; a.tok = embed ? E->tok : nullptr; a.emb_q = E->M.emb_q; a.emb_s = E->M.emb_s; a.err = E->err;
+    a.gain = Lw.in_norm;
+    if (Lw.linear) { a.a_w = Lw.a_w; a.b_w = Lw.b_w; a.AB = E->AB; }
+    a.X = E->X; a.xs = E->xs;
+    e = launch_k(k_bt_normq<NPL>, dim3(n), dim3(NT), 0, st, true, 0, a);
+  };
+  auto quant = [&](const float* src, int K) {
+    if (e == cudaSuccess) e = launch_k(k_bt_quant<NPL>, dim3(n), dim3(NT), 0, st, true, 0, src, K, K, E->X, E->xs);
+  };
+  normq(0, true);
+  for (int l = 0; l < NLAYER && e == cudaSuccess; ++l) {
+    const LayerW& Lw = E->M.L[l];
+    const LayerTiles& T = E->L[l];
+    gemm(T.win, T.swin, T.nin, HID, E->ksplit_in, EPI_STORE, E->Y, LDY);
+    if (Lw.linear) {
+      PfDeltaArgs d{};
+      d.Y = E->Y; d.ldy = LDY; d.AB = E->AB; d.conv = conv; d.rec = rec; d.lin = Lw.lin_idx; d.base = base; d.n = n;
+      d.conv_w = Lw.conv_w; d.A_log = Lw.A_log; d.dt_bias = Lw.dt_bias; d.gnorm_w = Lw.gnorm_w; d.O = E->O;
+      if (e == cudaSuccess) e = launch_k(k_pf_delta, dim3(LH), dim3(NT), PFD_SMEM, st, true, 0, d);
+    } else {
+      PfAttnArgs at{};
+      at.Y = E->Y; at.ldy = LDY; at.kc = kc; at.vc = vc; at.fi = Lw.full_idx; at.max_ctx = max_ctx;
+      at.T0 = T0; at.pos0 = pos0; at.n = n; at.qn_w = Lw.qn_w; at.kn_w = Lw.kn_w; at.rope = E->rope;
+      at.QN = E->attp; at.O = E->O;
+      if (e == cudaSuccess) e = launch_k(k_pf_kvprep, dim3(n, NKV), dim3(192), 0, st, true, 0, at);
+      if (e == cudaSuccess)
+        e = launch_k(k_pf_attn, dim3(n, NKV), dim3(256), (size_t)8 * 4 * AT_PROW * 4, st, true, 0, at);
+    }
+    quant(E->O, VDIM);
+    gemm(T.wout, T.swout, HID, VDIM, E->ksplit_out, EPI_ADD, E->H, HID);
+    if (e == cudaSuccess) {
+      NormqArgs a{};
+      a.H = E->H; a.gain = Lw.post_norm; a.X = E->X; a.xs = E->xs; a.err = E->err;
+      e = launch_k(k_bt_normq<NPL>, dim3(n), dim3(NT), 0, st, true, 0, a);
+    }
+    gemm(T.wgu, T.swgu, 2 * FFN, HID, E->ksplit_gu, EPI_SWIGLU, E->O, FFN);
+    quant(E->O, FFN);
+    gemm(T.wdown, T.swdown, HID, FFN, E->ksplit_down, EPI_ADD, E->H, HID);
+    if (l + 1 < NLAYER) normq(l + 1, false);
+  }
+  if (head && e == cudaSuccess) {
+    NormqArgs a{};
+    a.H = E->H + (size_t)(n - 1) * HID; a.gain = E->M.final_norm; a.X = E->HX; a.xs = E->hxs; a.err = E->err;
+    e = launch_k(k_bt_normq<3>, dim3(1), dim3(NT), 0, st, true, 0, a);
+    HeadArgs h{};
+    h.tiles = E->head_tiles; h.emb_s = E->M.emb_s; h.HX = E->HX; h.hxs = E->hxs; h.ctl = E->dctl;
+    h.logits = E->logits; h.am = E->am; h.err = E->err;
+    if (e == cudaSuccess) e = launch_k(k_bt_head, dim3(E->head_grid), dim3(HB_THREADS), HB_SMEM, st, true, 0, h);
+    if (e == cudaSuccess)
+      e = launch_k(k_bt_finish, dim3(1), dim3(32), 0, st, true, 0, (const unsigned long long*)E->am, E->head_grid,
+                   E->ids, E->tok);
+  }
+  return e;
+}
+
 cudaError_t graph_for(BatchEngine* E, int nb, bool i8, cudaGraphExec_t* out) {
   const int key = nb * 2 + (i8 ? 1 : 0);
   auto it = E->graphs.find(key);
@@ -1786,7 +2184,7 @@ BatchEngine* batch_create(const ModelW& M, const int8_t* head_tiles, const float
       (e = balloc(E, &E->H, (size_t)BATCH_MAX * HID * 4)) || (e = balloc(E, &E->Y, (size_t)BATCH_MAX * 8192 * 4)) ||
       (e = balloc(E, &E->O, (size_t)BATCH_MAX * FFN * 4)) || (e = balloc(E, &E->AB, (size_t)BATCH_MAX * 32 * 4)) ||
       (e = balloc(E, &E->xs, 64 * 4)) || (e = balloc(E, &E->hxs, 64 * 4)) ||
-      (e = balloc(E, &E->attp, B * NKV * E->maxch * 4 * AT_PROW * 4)) ||
+      (e = balloc(E, &E->attp, std::max(B * NKV * E->maxch * 4 * AT_PROW, (size_t)PF_MAX * NH * HD) * 4)) ||
       (e = balloc(E, &E->logits, (size_t)BATCH_MAX * VOCAB * 4)) ||
       (e = balloc(E, &E->X, (size_t)(FFN / GT_KS) * 192 * GT_KS)) || (e = balloc(E, &E->HX, (size_t)HB_IMG)) ||
       (e = balloc(E, &E->am, (size_t)E->head_grid * 64 * 8)) || (e = balloc(E, &E->tok, 64 * 4)) ||
@@ -2008,6 +2406,47 @@ int batch_timed_steps(BatchEngine* E, int nb, bool act_int8, int steps, double* 
   cudaEventElapsedTime(&ms, E->ev0, E->ev1);
   if (seconds) *seconds = ms * 1e-3;
   return read_err(E, err);
+}
+
+}  // namespace qb
+
+namespace qb {
+
+int batch_prefill(BatchEngine* E, float* conv, float* rec, float* kc, float* vc, int max_ctx, int conv_base, int T0,
+                  int pos0, const int* tok, int n, bool act_int8, float* logits_out, int* argmax_out, std::string& err) {
+  if (n < 1 || !tok) {
+    err = "prefill: need n >= 1 tokens";
+    return QWEN_ERR_ARG;
+  }
+  for (int i = 0; i < n; ++i)
+    if (tok[i] < 0 || tok[i] >= VOCAB) {
+      err = "prefill: token id out of range";
+      return QWEN_ERR_ARG;
+    }
+  if (T0 + n > max_ctx || pos0 + n > E->max_rope) {
+    err = "prefill: the context would overflow max_ctx";
+    return QWEN_ERR_STATE;
+  }
+  cudaStream_t st = E->st;
+  memset(E->hctl, 0, sizeof(BtCtl));
+  E->hctl->nb = 1;
+  E->hctl->want_logits = logits_out ? 1 : 0;
+  BCUDA(cudaMemcpyAsync(E->dctl, E->hctl, sizeof(BtCtl), cudaMemcpyHostToDevice, st));
+  for (int c0 = 0; c0 < n; c0 += PF_MAX) {
+    const int nc = std::min(PF_MAX, n - c0);
+    BCUDA(cudaStreamSynchronize(st));   // the pinned token slot is rewritten
+    memcpy(E->hbuf, tok + c0, nc * sizeof(int));
+    BCUDA(cudaMemcpyAsync(E->tok, E->hbuf, nc * sizeof(int), cudaMemcpyHostToDevice, st));
+    const bool last = c0 + nc == n;
+    BCUDA(act_int8 ? enqueue_prefill<1>(E, conv, rec, kc, vc, max_ctx, conv_base + c0, T0 + c0, pos0 + c0, nc, last)
+                   : enqueue_prefill<3>(E, conv, rec, kc, vc, max_ctx, conv_base + c0, T0 + c0, pos0 + c0, nc, last));
+  }
+  int* hid = E->hbuf + BATCH_MAX;
+  BCUDA(cudaMemcpyAsync(hid, E->ids, sizeof(int), cudaMemcpyDeviceToHost, st));
+  if (logits_out) BCUDA(cudaMemcpyAsync(logits_out, E->logits, (size_t)VOCAB * 4, cudaMemcpyDefault, st));
+  if (int rc = read_err(E, err)) return rc;
+  if (argmax_out) *argmax_out = hid[0];
+  return QWEN_OK;
 }
 
 }  // namespace qb

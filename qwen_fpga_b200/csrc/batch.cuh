@@ -67,5 +67,16 @@ int batch_step(BatchEngine* e, const int* tok, int nb, bool act_int8, float* log
 // Device time of the last batch_timed_steps call.
 int batch_timed_steps(BatchEngine* e, int nb, bool act_int8, int steps, double* seconds, std::string& err);
 int batch_max(const BatchEngine* e);
+// Prefill: n prompt tokens of ONE sequence through every layer at once (in
+// chunks of 32), on that sequence's arrays in the batch-1 layouts (conv ring
+// with origin conv_base, rec, kc / vc [6][max_ctx][512] with T0 cached
+// positions, first RoPE position pos0): the state afterwards is that of n
+// decode steps (the DeltaNet layers by the chunked delta rule).  The last
+// token's logits (nullable, host or device) and argmax are returned.  Uses
+// the engine's kernels and work buffers (an engine created with max_batch 1
+// serves a batch-1 context).
+int batch_prefill(BatchEngine* e, float* conv, float* rec, float* kc, float* vc, int max_ctx, int conv_base, int T0,
+                  int pos0, const int* tok, int n, bool act_int8, float* logits_out, int* argmax_out,
+                  std::string& err);
 
 }  // namespace qb

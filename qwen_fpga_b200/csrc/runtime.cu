@@ -220,6 +220,7 @@ struct qwen_ctx {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   int max_batch = 1;
   BatchEngine* be = nullptr;            // max_batch > 1: the batched engine owns the sequences
+  BatchEngine* pf = nullptr;            // batch 1: kernels and buffers of qwen_prefill (made on first use)
 };
 
 namespace {
@@ -448,6 +449,7 @@ int qwen_destroy(qwen_ctx* c) {
   cudaSetDevice(c->dev);
   if (c->st) cudaStreamSynchronize(c->st);
   batch_destroy(c->be);
+  batch_destroy(c->pf);
   for (void* p : c->ipc_open) cudaIpcCloseMemHandle(p);
   for (void* p : c->allocs) cudaFree(p);
   if (c->h_ctl) cudaFreeHost(c->h_ctl);
@@ -952,6 +954,29 @@ int qwen_generate(qwen_ctx* c, const int* prompt, int n_prompt, int n_new, int* 
     if (n_new > 0) QCUDA(c, cudaEventElapsedTime(&ms, c->ev0, c->ev1));
     *decode_seconds = ms * 1e-3;
   }
+  return QWEN_OK;
+}
+
+int qwen_prefill(qwen_ctx* c, const int* tok, int n, float* logits_out, int* argmax_out) {
+  int rc;
+  if ((rc = check_ctx(c))) return rc;
+  if (c->be) return fail(c, QWEN_ERR_STATE, "qwen_prefill runs batch-1 contexts");
+  if (c->tp.world != 1) return fail(c, QWEN_ERR_STATE, "qwen_prefill runs single-GPU contexts");
+  if (!tok || n < 1) return fail(c, QWEN_ERR_ARG, "need n >= 1 tokens");
+  if (c->T + n > c->max_ctx || c->pos + n >= c->max_rope)
+    return fail(c, QWEN_ERR_STATE, "context would overflow (T=%d + %d > %d)", c->T, n, c->max_ctx);
+  std::string err;
+  if (!c->pf) {
+    c->pf = batch_create(c->Mh, c->P.head_tiles, c->S.rope, c->max_rope, 1, 64, c->sm_count, c->st, err);
+    if (!c->pf) return fail(c, QWEN_ERR_CUDA, "prefill engine: %s", err.c_str());
+  }
+  QCUDA(c, cudaStreamSynchronize(c->st));
+  rc = batch_prefill(c->pf, c->S.conv, c->S.rec, c->S.kcache, c->S.vcache, c->max_ctx, c->conv_base, c->T, c->pos,
+                     tok, n, c->act_int8 != 0, logits_out, argmax_out, err);
+  if (rc) return fail(c, rc, "%s", err.c_str());
+  c->pos += n;
+  c->T += n;
+  c->conv_base += n;
   return QWEN_OK;
 }
 
