@@ -548,6 +548,29 @@ def main():
     peak, peak_src = peaks()
     peak_n = peak * world if tp else peak   # TP: one step's bytes are spread over every rank's HBM
     extra = {}
+    # prefill (qwen_prefill, single GPU): the config-0 prompt and a 256-token
+    # prompt at once, against the same tokens one decode step at a time
+    if not tp and world == 1:
+        toks = np.random.default_rng(5).integers(0, VOCAB, 256).tolist()
+        pf = {}
+        for name, ptoks in (("config0_prompt_16", prompt.tolist() if hasattr(prompt, "tolist") else list(prompt)),
+                            ("prompt_256", toks)):
+            best = 1e9
+            for _ in range(3):
+                dec.reset()
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                dec.prefill(ptoks, want_logits=False)
+                best = min(best, time.perf_counter() - t0)
+            dec.reset()
+            t0 = time.perf_counter()
+            for t in ptoks:
+                dec.decode_step(int(t), want_logits=False)
+            stepwise = time.perf_counter() - t0
+            pf[name] = {"tokens": len(ptoks), "prefill_ms": best * 1e3, "prefill_tok_s": len(ptoks) / best,
+                        "stepwise_ms": stepwise * 1e3, "stepwise_tok_s": len(ptoks) / stepwise}
+        extra["prefill"] = {"what": "qwen_prefill (chunked delta rule, tokens through every layer at once, "
+                                    "host wall clock) against one qwen_decode_step per token", **pf}
     # config 2: W8A8 warm start at 4096 positions, 256 greedy steps
     if "2" in configs:
         sec, ids, tm = warm_config(dec, 4096, 2, 256, True, tp, dist)
