@@ -5,10 +5,12 @@
 //                 -- rtl/gemv_i8.sv:13-76 + rtl/dequant.sv:12-29,
 //                    scripts/export_gemv_tv.py:49-50
 //
-// Each CTA stages x (its digit image) in shared memory once, then its warps
-// stream R weight rows at a time with 32-byte-per-lane loads and reduce the
-// dp4a partial sums with warp shuffles into int32 accumulators; the per-row
-// scale is applied in the epilogue.
+// Each CTA owns a contiguous range of rows: it asks L2 for their weights
+// (bulk prefetch) before waiting on the previous kernel, stages x (its digit
+// image) in shared memory once, then its warps stream R weight rows at a time
+// with 32-byte-per-lane loads and reduce the dp4a partial sums with warp
+// shuffles into int32 accumulators; the per-row scale is applied in the
+// epilogue.
 #include "common.cuh"
 #include "gemv.cuh"
 
@@ -22,6 +24,24 @@ __global__ void __launch_bounds__(256) k_gemv(float* __restrict__ y, int32_t* __
                                               const int8_t* xq, float sx, int N, int K) {
   __shared__ __align__(16) XEnc enc;
   __shared__ float red[32];
+  // This CTA's rows are [r_lo, r_hi) (contiguous).  Their weights do not depend
+  // on the previous kernel: ask L2 for them before griddepcontrol.wait, so that
+  // under programmatic dependent launch they stream in while it drains.
+  const int units_all = (N + R - 1) / R;
+  const int upc = (units_all + gridDim.x - 1) / gridDim.x;   // row units per CTA
+  const int r_lo = min(N, (int)blockIdx.x * upc * R), r_hi = min(N, r_lo + upc * R);
+  if (threadIdx.x < 32) {
+    // (at most the first 64 KB: a large GEMV's CTAs together would otherwise
+    // ask for more than L2 holds before they reach it)
+    const size_t lo = (size_t)r_lo * K;   // K % 32 == 0: 32-byte aligned pieces
+    const size_t hi = min((size_t)r_hi * K, lo + (size_t)65536);
+    for (size_t off = lo + (size_t)threadIdx.x * 4096; off < hi; off += 32 * 4096) {
+      const unsigned bytes = (unsigned)min((size_t)4096, hi - off);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(w + off), "r"(bytes) : "memory");
+    }
+  }
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (XINT8) {
     int8_t* d0 = &enc.dig[0][0][0];
     for (int i = threadIdx.x; i < K; i += blockDim.x) d0[dig_off(i)] = xq[i];
@@ -33,10 +53,8 @@ __global__ void __launch_bounds__(256) k_gemv(float* __restrict__ y, int32_t* __
     encode_x(enc, K, false, red);
   }
   const int lane = threadIdx.x & 31;
-  const int nwarps = gridDim.x * (blockDim.x >> 5);
-  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int units = N / R;
-  for (int u = gw; u < units + ((N % R) ? 1 : 0); u += nwarps) {
+  const int wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int u = (int)blockIdx.x * upc + wid; u < min(units_all, ((int)blockIdx.x + 1) * upc); u += nw) {
     const int r0 = u * R;
     const int8_t* rows[R];
 #pragma unroll
@@ -70,17 +88,32 @@ static int grid_for(int N, int R, int sm_count) {
   return g < 1 ? 1 : (g > cap ? cap : g);
 }
 
+// Launched with programmatic dependent launch: a GEMV's weight prefetch and
+// launch overlap the previous kernel in the stream.
+template <int R, bool XINT8>
+static cudaError_t launch_gemv(int grid, float* y, int32_t* acc, const int8_t* w, const float* s, const float* xf,
+                               const int8_t* xq, float sx, int N, int K, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_gemv<R, XINT8>, y, acc, w, s, xf, xq, sx, N, K);
+}
+
 cudaError_t enqueue_gemv(float* y, int32_t* acc, const int8_t* w, const float* s, const float* xf,
                          const int8_t* xq, float sx, int N, int K, int sm_count, cudaStream_t st) {
   const bool big = N >= 8 * 8 * sm_count * 4;   // enough rows to give every warp 4-row units
   if (xq) {
-    if (big) k_gemv<4, true><<<grid_for(N, 4, sm_count), 256, 0, st>>>(y, acc, w, s, xf, xq, sx, N, K);
-    else k_gemv<1, true><<<grid_for(N, 1, sm_count), 256, 0, st>>>(y, acc, w, s, xf, xq, sx, N, K);
-  } else {
-    if (big) k_gemv<4, false><<<grid_for(N, 4, sm_count), 256, 0, st>>>(y, acc, w, s, xf, xq, sx, N, K);
-    else k_gemv<1, false><<<grid_for(N, 1, sm_count), 256, 0, st>>>(y, acc, w, s, xf, xq, sx, N, K);
+    if (big) return launch_gemv<4, true>(grid_for(N, 4, sm_count), y, acc, w, s, xf, xq, sx, N, K, st);
+    return launch_gemv<1, true>(grid_for(N, 1, sm_count), y, acc, w, s, xf, xq, sx, N, K, st);
   }
-  return cudaGetLastError();
+  if (big) return launch_gemv<4, false>(grid_for(N, 4, sm_count), y, acc, w, s, xf, xq, sx, N, K, st);
+  return launch_gemv<1, false>(grid_for(N, 1, sm_count), y, acc, w, s, xf, xq, sx, N, K, st);
 }
 
 }  // namespace qb
