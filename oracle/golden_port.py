@@ -267,6 +267,43 @@ class PortDecoder:
         return out, argmaxes, st
 
 
+def delta_rule_steps(S, q, k, v, g, beta):
+    """The golden's recurrence (golden/model.py:174-178) over n tokens of one
+    head: S [K, V]; q, k [n, K]; v [n, V]; g, beta [n].  Returns (o [n, V],
+    S after the n tokens); float32, S not modified."""
+    S = S.astype(F32).copy()
+    o = np.empty((len(g), S.shape[1]), F32)
+    for t in range(len(g)):
+        S *= np.exp(F32(g[t]))
+        d = (v[t] - k[t] @ S) * F32(beta[t])
+        S += np.outer(k[t], d).astype(F32)
+        o[t] = q[t] @ S
+    return o, S
+
+
+def delta_rule_chunk(S, q, k, v, g, beta):
+    """The same n tokens in the chunked (WY) form the GPU prefill computes.
+    With G_t = g_0 + ... + g_t and Gamma_t = e^{G_t}:
+      d_t = beta_t (v_t - Gamma_t S^T k_t) - sum_{s<t} beta_t e^{G_t-G_s} (k_t.k_s) d_s
+      o_t = Gamma_t S^T q_t + sum_{s<=t} e^{G_t-G_s} (q_t.k_s) d_s
+      S'  = Gamma_{n-1} S + sum_t e^{G_{n-1}-G_t} k_t d_t^T
+    (one triangular solve for d, then dense products).  float32."""
+    n = len(g)
+    G = np.cumsum(np.asarray(g, F32)).astype(F32)
+    dec = np.exp(G[:, None] - G[None, :]).astype(F32)          # e^{G_t - G_s}
+    low = np.tril(np.ones((n, n), bool), -1)
+    A = np.where(low, beta[:, None] * dec * (k @ k.T), 0).astype(F32)
+    R = (beta[:, None] * (v - np.exp(G)[:, None] * (k @ S))).astype(F32)
+    D = np.zeros_like(R)
+    for t in range(n):                                         # (I + A) D = R, forward substitution
+        D[t] = R[t] - A[t, :t] @ D[:t]
+    QK = np.where(np.tril(np.ones((n, n), bool)), dec * (q @ k.T), 0).astype(F32)
+    o = (np.exp(G)[:, None] * (q @ S) + QK @ D).astype(F32)
+    w = np.exp(G[-1] - G).astype(F32)
+    S2 = (np.exp(G[-1]) * S + (k * w[:, None]).T @ D).astype(F32)
+    return o, S2
+
+
 def gemv_int32(w_i8: np.ndarray, x_i8: np.ndarray) -> np.ndarray:
     """Exact int32 accumulators acc[o] = sum_i w[o,i]*x[i] (scripts/export_gemv_tv.py:49)."""
     return (w_i8.astype(np.int32) @ x_i8.astype(np.int32)).astype(np.int32)
