@@ -1924,15 +1924,22 @@ __device__ __forceinline__ void warp_norm_rope_v(const float* v_in, const float 
 // chunk's (m, l, o) of its four heads go out as tagged words (att_tv) and
 // chunk 0's CTA merges the group: M = max m_c, w_c = exp(m_c - M),
 // O = sum w_c o_c / sum w_c l_c, times sigmoid(gate) (golden/model.py:227-229).
+// The chunks cover positions [s0, s1) of the Tn = T + 1: all of them, or
+// under TP with tp_world > NKV this rank's slice of the group, whose merged
+// (m, l, o) chunk 0 then combines with the other slices' (attn_exchange).
 constexpr int ASB = 16;
-__device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
+template <bool TP>
+__device__ bool attn_exchange(PCtx& c, int p, int hq, int d2, float& M, float& Ls, float& O0, float& O1,
+                              unsigned tag);
+template <bool TP>
+__device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl, int s0, int s1) {
   const PersistArgs& A = *c.A;
   Misc* ms = c.ms;
   const LayerW& L = c.lay[p / 5];
-  const int T = ms->T, pos = ms->pos, Tn = T + 1;
+  const int T = ms->T, pos = ms->pos;
   const int fi = L.full_idx;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int t0 = cc * cl, t1 = min(Tn, t0 + cl);
+  const int t0 = (TP ? s0 : 0) + cc * cl, t1 = min(TP ? s1 : T + 1, t0 + cl);
   const int tc = min(t1, T);                // positions [t0, tc) come from the cache
   float* qn = (float*)(c.sm + OFF_DIG);    // [4][256] normed + roped queries
   float* kn = qn + 4 * HD;                  // [256] new key
@@ -2100,7 +2107,8 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
     return tv_val(w);
   };
   int bad = 0;
-  if (nch == 1) {
+  const bool xsplit = TP && A.tp_world > NKV;   // the group's positions are split across ranks
+  if (nch == 1 && !xsplit) {
     // the whole group in this chunk: o / l * sigmoid(gate)
     if (half == 0) {
 #pragma unroll
@@ -2149,6 +2157,7 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
     }
     if (bad) break;
     const float mq = tv_val(wm), lq = tv_val(wl);
+    if (mq == -INFINITY) continue;   // an empty slice (TP split with Tn < ranks of the group)
     const float Mn = fmaxf(M, mq);
     const float a = M == -INFINITY ? 0.0f : expf(M - Mn), b = expf(mq - Mn);
     Ls = fmaf(lq, b, __fmul_rn(Ls, a));
@@ -2156,12 +2165,74 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl) {
     O1 = fmaf(tv_val(w1), b, __fmul_rn(O1, a));
     M = Mn;
   }
+  if constexpr (TP) {
+    if (xsplit && !bad && !attn_exchange<TP>(c, p, hq, d2, M, Ls, O0, O1, tout)) bad = 1;
+  }
   if (!bad) {
     const float ga = gate(hq, d2, bad), gb = gate(hq, d2 + 1, bad);
     st_tv(A.tv_attn + (4 * g + hq) * HD + d2, __fmul_rn(__fdiv_rn(O0, Ls), sigmoid_f(ga)), tout);
     st_tv(A.tv_attn + (4 * g + hq) * HD + d2 + 1, __fmul_rn(__fdiv_rn(O1, Ls), sigmoid_f(gb)), tout);
   }
   return consumer_and(!bad) != 0;
+}
+
+// The attention sequence split (TP, tp_world > NKV): the ns = tp_world / NKV
+// ranks of a KV group each hold the merged (m, l, o) of their position slice
+// (thread = head hq, dims d2, d2 + 1).  Each stores it as tagged words into
+// slot j = tp_rank % ns of every group rank's exchange buffer (NVLink P2P,
+// system scope), then merges slots 0 .. ns-1 in order, skipping empty slices
+// (m = -inf): the same combine as the chunks' (golden/model.py:219-229), in an
+// order every rank of the group shares, so their outputs are bit-identical.
+// A slot is rewritten four layers later, after the OUT and DOWN exchanges in
+// between have shown that every rank has read it.
+template <bool TP>
+__device__ bool attn_exchange(PCtx& c, int p, int hq, int d2, float& M, float& Ls, float& O0, float& O1,
+                              unsigned tag) {
+  const PersistArgs& A = *c.A;
+  const int ns = A.tp_world / NKV, j = A.tp_rank % ns, r0 = A.tp_rank - j;
+  constexpr size_t SW = 2 + HD;   // words per head
+  const size_t mine = XB_ATT + ((size_t)j * 4 + hq) * SW;
+  for (int q = 0; q < ns; ++q) {
+    unsigned long long* dst = A.xbuf[r0 + q] + mine;
+    st_tv_sys(dst + 2 + d2, O0, tag);
+    st_tv_sys(dst + 3 + d2, O1, tag);
+    if (d2 == 0) {
+      st_tv_sys(dst, M, tag);
+      st_tv_sys(dst + 1, Ls, tag);
+    }
+  }
+  const unsigned long long* xb = A.xbuf[A.tp_rank] + XB_ATT + (size_t)hq * SW;
+  float m2 = -INFINITY, l2 = 0.0f, p0 = 0.0f, p1 = 0.0f;
+  for (int q = 0; q < ns; ++q) {
+    const unsigned long long* src = xb + (size_t)q * 4 * SW;
+    unsigned long long wm, wl, w0, w1;
+    const unsigned long long tw = gtime();
+    int it = 0;
+    for (;;) {
+      wm = ld_tv_sys(src);
+      wl = ld_tv_sys(src + 1);
+      w0 = ld_tv_sys(src + 2 + d2);
+      w1 = ld_tv_sys(src + 3 + d2);
+      if (tag_ok(wm, tag) && tag_ok(wl, tag) && tag_ok(w0, tag) && tag_ok(w1, tag)) break;
+      if (((++it) & 63) == 0) {
+        if (aborted(c)) return false;
+        if (gtime() - tw > WAIT_NS) { raise_abort(c, 23, p | q << 8); return false; }
+      }
+    }
+    const float mq = tv_val(wm);
+    if (mq == -INFINITY) continue;
+    const float Mn = fmaxf(m2, mq);
+    const float a = m2 == -INFINITY ? 0.0f : expf(m2 - Mn), b = expf(mq - Mn);
+    l2 = fmaf(tv_val(wl), b, __fmul_rn(l2, a));
+    p0 = fmaf(tv_val(w0), b, __fmul_rn(p0, a));
+    p1 = fmaf(tv_val(w1), b, __fmul_rn(p1, a));
+    m2 = Mn;
+  }
+  M = m2;
+  Ls = l2;
+  O0 = p0;
+  O1 = p1;
+  return true;
 }
 
 // ---------------------------------------------------------------- the kernel
@@ -2263,12 +2334,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
           // chunks of ASB positions (at most ATT_MAXCH, and one item per CTA)
           const int g0 = TP ? A.kv_g0 : 0, ng = TP ? A.kv_g1 - A.kv_g0 : NKV;   // this rank's KV groups
           const int Tn = ms->T + 1;
-          int nch = (Tn + ASB - 1) / ASB;
+          int s0 = 0, s1 = Tn;   // positions of this rank (TP, tp_world > NKV: its slice of the group)
+          if (TP && A.tp_world > NKV) {
+            const int ns = A.tp_world / NKV, j = A.tp_rank % ns;
+            s0 = j * Tn / ns;
+            s1 = (j + 1) * Tn / ns;
+          }
+          int nch = (s1 - s0 + ASB - 1) / ASB;
           const int cap = min(ATT_MAXCH, (int)gridDim.x / ng);
           nch = nch < 1 ? 1 : (nch > cap ? cap : nch);
-          const int cl = (Tn + nch - 1) / nch;
+          const int cl = (s1 - s0 + nch - 1) / nch;
           for (int it = blockIdx.x; it < ng * nch && ok; it += gridDim.x)
-            ok = attn_item(c, p, g0 + it % ng, it / ng, nch, cl);
+            ok = attn_item<TP>(c, p, g0 + it % ng, it / ng, nch, cl, s0, s1);
         }
         trace_mark(c, p, 3);
         continue;

@@ -55,8 +55,13 @@ cudaError_t repack_head_tiles(const int8_t* emb_q, int8_t* tiles, cudaStream_t s
 // space of every activation; its schedule covers only its shard:
 //   DeltaNet heads [dn_h0, dn_h1) (in_proj_qkv / z / a / b rows, conv, state,
 //     gated norm: column-parallel, no exchange inside the mixer);
-//   attention KV groups [kv_g0, kv_g1) with all four query heads of each (for
-//     tp_world 4 and 8 the ranks sharing a group compute it redundantly);
+//   attention KV groups [kv_g0, kv_g1) with all four query heads of each; for
+//     tp_world 4 and 8 the ns = tp_world / NKV ranks sharing a group split its
+//     cached positions instead: slice j = tp_rank % ns is [j Tn / ns,
+//     (j + 1) Tn / ns) of the Tn = T + 1 positions, and the slices' (m, l, o)
+//     are exchanged and merged in slice order (flash-decoding combine,
+//     golden/model.py:219-229), so the KV bytes each rank reads shrink with
+//     the world (every rank of the group still writes slot T of its copy);
 //   OUT (out_proj / o_proj) row-parallel over input columns [ok0, ok1) (the
 //     rank's heads), DOWN row-parallel over FFN columns [dk0, dk1) (128-column
 //     blocks), gate/up column-parallel over the same FFN rows;
@@ -64,7 +69,8 @@ cudaError_t repack_head_tiles(const int8_t* emb_q, int8_t* tiles, cudaStream_t s
 // An OUT or DOWN phase adds its partial rows across ranks (P2P stores into
 // every rank's exchange buffer, then a fixed-order sum: bit-identical on all
 // ranks); the head exchanges each rank's (max, index); under W8A8 the OUT and
-// DOWN inputs' maxima are exchanged before they are quantised.
+// DOWN inputs' maxima are exchanged before they are quantised; an attention
+// MIX of a split group exchanges the slices' (m, l, o).
 constexpr int TP_MAX = 8;
 struct TpPlan {
   int rank = 0, world = 1;
@@ -79,11 +85,15 @@ bool tp_plan(int rank, int world, TpPlan& out, std::string& err);
 // Exchange buffer of one rank (tagged words): [2 (OUT, DOWN)][TP_MAX source
 // ranks][HID] partial rows, then [TP_MAX source ranks][2] head (max, index)
 // words, then [2 (OUT, DOWN)][TP_MAX source ranks] input maxima (W8A8: the
-// golden quantiser's max over the whole input vector).
+// golden quantiser's max over the whole input vector), then the attention
+// sequence split: [ATT_SPLIT_MAX position slices][4 heads][2 + HD] (m, l, o)
+// of the ranks that share this rank's KV group.
+constexpr int ATT_SPLIT_MAX = TP_MAX / NKV;   // ranks per KV group at the largest world
 constexpr size_t XB_PART = 0;
 constexpr size_t XB_HEAD = 2 * (size_t)TP_MAX * HID;
 constexpr size_t XB_AMAX = XB_HEAD + 2 * TP_MAX;
-constexpr size_t XB_WORDS = XB_AMAX + 2 * TP_MAX;
+constexpr size_t XB_ATT = XB_AMAX + 2 * TP_MAX;
+constexpr size_t XB_WORDS = XB_ATT + (size_t)ATT_SPLIT_MAX * 4 * (2 + HD);
 
 // Everything the persistent kernel reads; tv_* are tagged {value, tag} words.
 struct PersistArgs {

@@ -54,7 +54,7 @@ def _worker(rank, world, port, blob_path, job, q):
                                 world_size=world, timeout=timedelta(seconds=120))
         torch.cuda.set_device(rank)
         from qwen_fpga_b200.tp import TPDecoder
-        d = TPDecoder(blob_path, device=rank, max_ctx=256)
+        d = TPDecoder(blob_path, device=rank, max_ctx=32768 + 16 if job == "config3" else 256)
         fx = fx_load("config0.npz")
         if job == "config0":
             d.reset()
@@ -86,6 +86,24 @@ def _worker(rank, world, port, blob_path, job, q):
                     errs[0] = logits_close(lg, fw, "step0")
             res["agree"], res["errs"] = agree, errs
             res["floor"] = int(fw["self_agreement"].min()) - 2
+        elif job == "config3":
+            # 32768 cached positions: with 4 or 8 ranks the ranks of a KV
+            # group each attend a slice of them and combine (m, l, o)
+            from oracle import golden_port as P
+            from qwen_fpga_b200 import synth
+            f3 = fx_load("config3.npz")
+            st = P.warm_state(synth.model_config(), int(f3["T0"]), seed=3)
+            d.reset()
+            d.import_state(st)
+            del st
+            tok = int(f3["first_token"])
+            ams, errs = [], {}
+            for j in range(len(f3["argmax"])):
+                am, lg = d.decode_step(tok, want_logits=True)
+                ams.append(am)
+                errs[j] = logits_close(lg, f3, f"step{j}")
+                tok = am
+            res["argmax"], res["errs"] = ams, errs
         elif job == "stop":
             # rank world-1 leaves between steps; the others' next step must fail
             # within the device wait bound and report it
@@ -139,6 +157,21 @@ def test_tp_config0_matches_golden(world, blob_path):
     res = _run(world, "config0", blob_path)
     for r in res:
         assert r["ids"] == fx["generated"].tolist(), f"rank {r['rank']}"
+        assert r["argmax"] == [int(v) for v in fx["argmax"]], f"rank {r['rank']}"
+        assert max(r["errs"].values()) < LOGIT_RTOL, r["errs"]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_config3_long_context_matches_golden(world, blob_path):
+    """Config 3 (32768 cached positions) under tensor parallelism: at 4 and
+    8 ranks the positions of each KV group are split across the ranks that
+    share it (flash-decoding combine over NVLink); every step's argmax equals
+    the golden's and the logits are within 1e-4 on every rank."""
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
+    fx = fixture("config3.npz")
+    res = _run(world, "config3", blob_path)
+    for r in res:
         assert r["argmax"] == [int(v) for v in fx["argmax"]], f"rank {r['rank']}"
         assert max(r["errs"].values()) < LOGIT_RTOL, r["errs"]
 
