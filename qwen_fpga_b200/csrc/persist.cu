@@ -2135,6 +2135,7 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl, int s0
     }
   }
   trace_mark(c, p, 2);
+  if (cc != 0) return consumer_and(1) != 0;
   // The merge (the split-KV combine).  Up to AT_SERIAL chunks: chunk 0's CTA,
   // thread = (head hq, dims d2, d2 + 1), chunks in order (online: running
   // max M, sum Ls, output O).  More: the group's first nm chunk CTAs, nm = the
