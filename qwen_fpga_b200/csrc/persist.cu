@@ -1928,8 +1928,6 @@ __device__ __forceinline__ void warp_norm_rope_v(const float* v_in, const float 
 // under TP with tp_world > NKV this rank's slice of the group, whose merged
 // (m, l, o) chunk 0 then combines with the other slices' (attn_exchange).
 constexpr int ASB = 16;
-constexpr int AT_NM = 16;      // CTAs that merge a group's chunks (at most; a power of two)
-constexpr int AT_SERIAL = 8;   // up to this many chunks merge on one CTA in one pass
 template <bool TP>
 __device__ bool attn_exchange(PCtx& c, int p, int hq, int d2, float& M, float& Ls, float& O0, float& O1,
                               unsigned tag);
@@ -2136,134 +2134,41 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl, int s0
   }
   trace_mark(c, p, 2);
   if (cc != 0) return consumer_and(1) != 0;
-  // The merge (the split-KV combine).  Up to AT_SERIAL chunks: chunk 0's CTA,
-  // thread = (head hq, dims d2, d2 + 1), chunks in order (online: running
-  // max M, sum Ls, output O).  More: the group's first nm chunk CTAs, nm = the
-  // largest power of two <= min(AT_NM, nch); CTA cc takes dims [cc D,
-  // cc D + D) of the four heads, D = HD / nm.  Pass 1, thread = (head, chunk):
-  // the chunks' (m, l) into shared memory; warp hq then takes M = max m_c,
-  // the weights w_c = exp(m_c - M) (0 for an empty chunk, m_c = -inf) and
-  // Ls = sum w_c l_c, the same in every merging CTA.  Pass 2: nm threads per
-  // dim pair; thread r sums w_c o_c over chunks r, r + nm, ..., then the nm
-  // sums add up by shuffles.
-  static_assert(ATT_MAXCH <= PT / 4 && 8 * ATT_MAXCH + 8 <= 6 * HD, "merge scratch (qn .. vn)");
-  static_assert(AT_NM <= 32 && (AT_NM & (AT_NM - 1)) == 0, "merging CTAs");
+  // chunk 0's CTA merges the group: thread = (head hq, dims 2 d2, 2 d2 + 1),
+  // chunks in order (online: running max M, sum Ls, output O)
+  const int hq = threadIdx.x >> 7, d2 = 2 * (threadIdx.x & 127);
+  const unsigned long long* pb = A.att_tv + ((size_t)(g * ATT_MAXCH) * 4 + hq) * (2 + HD);
   const size_t stride = 4 * (2 + HD);
-  int hq, d2, r = 0;
   float M = -INFINITY, Ls = 0.0f, O0 = 0.0f, O1 = 0.0f;
-  if (nch <= AT_SERIAL) {
-    if (cc != 0) return consumer_and(1) != 0;
-    hq = threadIdx.x >> 7;
-    d2 = 2 * (threadIdx.x & 127);
-    const unsigned long long* pb = A.att_tv + ((size_t)(g * ATT_MAXCH) * 4 + hq) * (2 + HD);
-    for (int q = 0; q < nch && !bad; ++q) {
-      const unsigned long long* pq_ = pb + q * stride;
-      unsigned long long wm, wl, w0, w1;
-      const unsigned long long tw = gtime();
-      int it = 0;
-      for (;;) {
-        wm = ld_tv(pq_);
-        wl = ld_tv(pq_ + 1);
-        ld_tv2(pq_ + 2 + d2, w0, w1);
-        if (tag_ok(wm, tout) && tag_ok(wl, tout) && tag_ok(w0, tout) && tag_ok(w1, tout)) break;
-        if (((++it) & 63) == 0) {
-          if (aborted(c)) { bad = 1; break; }
-          if (gtime() - tw > WAIT_NS) { raise_abort(c, 22, p); bad = 1; break; }
-        }
-      }
-      if (bad) break;
-      const float mq = tv_val(wm), lq = tv_val(wl);
-      if (mq == -INFINITY) continue;   // an empty slice (TP split with Tn < ranks of the group)
-      const float Mn = fmaxf(M, mq);
-      const float a = M == -INFINITY ? 0.0f : expf(M - Mn), b = expf(mq - Mn);
-      Ls = fmaf(lq, b, __fmul_rn(Ls, a));
-      O0 = fmaf(tv_val(w0), b, __fmul_rn(O0, a));
-      O1 = fmaf(tv_val(w1), b, __fmul_rn(O1, a));
-      M = Mn;
-    }
-  } else {
-    int nm = 1;
-    while (2 * nm <= min(AT_NM, nch)) nm *= 2;
-    if (cc >= nm) return consumer_and(1) != 0;
-    const unsigned long long* pg = A.att_tv + (size_t)g * ATT_MAXCH * stride;   // the group's chunk 0
-    float* cw = qn;                      // [4][ATT_MAXCH] m_c, then w_c (qn .. vn are free now)
-    float* cls = qn + 4 * ATT_MAXCH;     // [4][ATT_MAXCH] l_c
-    float* cml = qn + 8 * ATT_MAXCH;     // [4] M, [4] Ls
-    {
-      const int h1 = threadIdx.x >> 7, q1 = threadIdx.x & 127;
-      if (q1 < nch) {
-        const unsigned long long* src = pg + q1 * stride + h1 * (2 + HD);
-        unsigned long long wm = ld_tv(src), wl = ld_tv(src + 1);
-        const unsigned long long tw = gtime();
-        int it = 0;
-        while (!(tag_ok(wm, tout) && tag_ok(wl, tout))) {
-          if (((++it) & 63) == 0) {
-            if (aborted(c)) { bad = 1; break; }
-            if (gtime() - tw > WAIT_NS) { raise_abort(c, 22, p); bad = 1; break; }
-          }
-          wm = ld_tv(src);
-          wl = ld_tv(src + 1);
-        }
-        cw[h1 * ATT_MAXCH + q1] = tv_val(wm);
-        cls[h1 * ATT_MAXCH + q1] = tv_val(wl);
+  for (int q = 0; q < nch && !bad; ++q) {
+    const unsigned long long* pq_ = pb + q * stride;
+    unsigned long long wm, wl, w0, w1;
+    const unsigned long long tw = gtime();
+    int it = 0;
+    for (;;) {
+      wm = ld_tv(pq_);
+      wl = ld_tv(pq_ + 1);
+      ld_tv2(pq_ + 2 + d2, w0, w1);
+      if (tag_ok(wm, tout) && tag_ok(wl, tout) && tag_ok(w0, tout) && tag_ok(w1, tout)) break;
+      if (((++it) & 63) == 0) {
+        if (aborted(c)) { bad = 1; break; }
+        if (gtime() - tw > WAIT_NS) { raise_abort(c, 22, p); bad = 1; break; }
       }
     }
-    if (!consumer_and(!bad)) return false;
-    if (wid < 4) {
-      float* w = cw + wid * ATT_MAXCH;
-      float mx = -INFINITY;
-      for (int q = lane; q < nch; q += 32) mx = fmaxf(mx, w[q]);
-      mx = warp_max(mx);
-      float ls = 0.0f;
-      for (int q = lane; q < nch; q += 32) {
-        const float mq = w[q];
-        const float wq = mq == -INFINITY ? 0.0f : expf(mq - mx);
-        w[q] = wq;
-        ls = fmaf(cls[wid * ATT_MAXCH + q], wq, ls);
-      }
-      ls = warp_sum(ls);
-      if (lane == 0) {
-        cml[wid] = mx;
-        cml[4 + wid] = ls;
-      }
-    }
-    consumer_sync();
-    const int D = HD / nm;               // dims per head of this CTA
-    const int pi = threadIdx.x / nm;     // dim pair
-    r = threadIdx.x % nm;                // thread within the pair
-    hq = pi / (D / 2);
-    d2 = cc * D + 2 * (pi % (D / 2));
-    const float* wts = cw + hq * ATT_MAXCH;
-    const unsigned long long* ph = pg + hq * (2 + HD) + 2 + d2;
-    for (int q = r; q < nch && !bad; q += nm) {
-      unsigned long long a, b;
-      ld_tv2(ph + q * stride, a, b);
-      if (!(tag_ok(a, tout) && tag_ok(b, tout))) {   // not visible yet: poll this chunk
-        const unsigned long long tw = gtime();
-        int it = 0;
-        do {
-          if (((++it) & 63) == 0) {
-            if (aborted(c)) { bad = 1; break; }
-            if (gtime() - tw > WAIT_NS) { raise_abort(c, 22, p); bad = 1; break; }
-          }
-          ld_tv2(ph + q * stride, a, b);
-        } while (!(tag_ok(a, tout) && tag_ok(b, tout)));
-      }
-      const float wq = wts[q];
-      O0 = fmaf(tv_val(a), wq, O0);
-      O1 = fmaf(tv_val(b), wq, O1);
-    }
-    for (int off = nm >> 1; off > 0; off >>= 1) {   // the lanes of a pair: r = lane % nm
-      O0 = __fadd_rn(O0, __shfl_xor_sync(0xffffffffu, O0, off));
-      O1 = __fadd_rn(O1, __shfl_xor_sync(0xffffffffu, O1, off));
-    }
-    M = cml[hq];
-    Ls = cml[4 + hq];
+    if (bad) break;
+    const float mq = tv_val(wm), lq = tv_val(wl);
+    if (mq == -INFINITY) continue;   // an empty slice (TP split with Tn < ranks of the group)
+    const float Mn = fmaxf(M, mq);
+    const float a = M == -INFINITY ? 0.0f : expf(M - Mn), b = expf(mq - Mn);
+    Ls = fmaf(lq, b, __fmul_rn(Ls, a));
+    O0 = fmaf(tv_val(w0), b, __fmul_rn(O0, a));
+    O1 = fmaf(tv_val(w1), b, __fmul_rn(O1, a));
+    M = Mn;
   }
   if constexpr (TP) {
-    if (xsplit && r == 0 && !bad && !attn_exchange<TP>(c, p, hq, d2, M, Ls, O0, O1, tout)) bad = 1;
+    if (xsplit && !bad && !attn_exchange<TP>(c, p, hq, d2, M, Ls, O0, O1, tout)) bad = 1;
   }
-  if (!bad && r == 0) {
+  if (!bad) {
     const float ga = gate(hq, d2, bad), gb = gate(hq, d2 + 1, bad);
     st_tv(A.tv_attn + (4 * g + hq) * HD + d2, __fmul_rn(__fdiv_rn(O0, Ls), sigmoid_f(ga)), tout);
     st_tv(A.tv_attn + (4 * g + hq) * HD + d2 + 1, __fmul_rn(__fdiv_rn(O1, Ls), sigmoid_f(gb)), tout);
