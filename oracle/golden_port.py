@@ -304,6 +304,47 @@ def delta_rule_chunk(S, q, k, v, g, beta):
     return o, S2
 
 
+def attention_split(q, K, V, n_slices, n_chunks):
+    """The decomposition the decode kernel uses for golden/model.py:219-229
+    (softmax(q K^T / sqrt(hd)) V for one KV group's query heads): the Tn
+    positions cut into n_slices rank slices [j Tn / n, (j + 1) Tn / n), each
+    cut into at most n_chunks chunks of ceil(len / chunks) positions; per chunk
+    (m, l, o) = (max score, sum of exp(s - m), sum of exp(s - m) v); chunks and
+    then slices combined in order, empty ones (m = -inf) skipped.
+    q [H, hd], K / V [Tn, hd]; returns [H, hd]."""
+    q, K, V = (np.asarray(a, np.float64) for a in (q, K, V))
+    Tn, hd = K.shape
+    scale = hd ** -0.5
+
+    def part(t0, t1):
+        if t1 <= t0:
+            return (np.full(q.shape[0], -np.inf), np.zeros(q.shape[0]), np.zeros_like(q))
+        s = (q @ K[t0:t1].T) * scale
+        m = s.max(-1)
+        e = np.exp(s - m[:, None])
+        return m, e.sum(-1), e @ V[t0:t1]
+
+    def merge(parts):
+        M, L, O = np.full(q.shape[0], -np.inf), np.zeros(q.shape[0]), np.zeros_like(q)
+        for m, l, o in parts:
+            if np.all(m == -np.inf):
+                continue
+            Mn = np.maximum(M, m)
+            a = np.where(M == -np.inf, 0.0, np.exp(M - Mn))
+            b = np.exp(m - Mn)
+            L, O, M = L * a + l * b, O * a[:, None] + o * b[:, None], Mn
+        return M, L, O
+
+    slices = []
+    for j in range(n_slices):
+        s0, s1 = j * Tn // n_slices, (j + 1) * Tn // n_slices
+        n = max(1, min(n_chunks, -(-(s1 - s0) // 16)))
+        cl = -(-(s1 - s0) // n)
+        slices.append(merge([part(s0 + c * cl, min(s1, s0 + c * cl + cl)) for c in range(n)]))
+    M, L, O = merge(slices)
+    return O / L[:, None]
+
+
 def gemv_int32(w_i8: np.ndarray, x_i8: np.ndarray) -> np.ndarray:
     """Exact int32 accumulators acc[o] = sum_i w[o,i]*x[i] (scripts/export_gemv_tv.py:49)."""
     return (w_i8.astype(np.int32) @ x_i8.astype(np.int32)).astype(np.int32)

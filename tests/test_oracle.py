@@ -216,3 +216,21 @@ def test_chunked_delta_rule_reproduces_the_golden_trace():
                                    fx["g"][h:h + 1], fx["beta"][h:h + 1])
         np.testing.assert_allclose(o[0], fx["o_core"][h], rtol=0, atol=2e-6)
         np.testing.assert_allclose(S2, fx["S_out"][i], rtol=0, atol=2e-6)
+
+
+@pytest.mark.parametrize("Tn,n_slices,n_chunks", [(1, 2, 64), (1, 4, 64), (3, 4, 64), (17, 2, 64), (80, 4, 5),
+                                                  (1000, 1, 64), (1000, 2, 64), (4097, 4, 64)])
+def test_split_kv_combine_equals_softmax_attention(Tn, n_slices, n_chunks):
+    """The decode kernel's split of a KV group's positions into rank slices and
+    chunks, merged by (m, l, o) in order with empty slices skipped (the case
+    Tn < ranks of the group), is the golden's softmax attention
+    (golden/model.py:219-229) up to rounding."""
+    rng = np.random.default_rng(Tn * 10 + n_slices)
+    q = rng.standard_normal((4, 256)).astype(np.float32)
+    K = rng.standard_normal((Tn, 256)).astype(np.float32)
+    V = rng.standard_normal((Tn, 256)).astype(np.float32)
+    s = (q.astype(np.float64) @ K.T.astype(np.float64)) / 16.0
+    p = np.exp(s - s.max(-1, keepdims=True))
+    ref = (p / p.sum(-1, keepdims=True)) @ V.astype(np.float64)
+    out = P.attention_split(q, K, V, n_slices, n_chunks)
+    assert np.abs(out - ref).max() < 1e-10 * max(1.0, np.abs(ref).max())
