@@ -162,7 +162,10 @@ int qwen_capture_read(qwen_ctx* ctx, float* out, int max_floats);
  * argmax_out (batch ints) are host pointers; logits_out (nullable) may be a
  * host or device pointer of batch x vocab (248320) floats, sequence-major.
  * On a batched context tok may be NULL: every sequence then takes its own
- * previous argmax (greedy continuation). */
+ * previous argmax (greedy continuation).  On a single-GPU batch-1 context,
+ * page-locked host logits (cudaMallocHost, a pinned torch tensor) are written
+ * by the decode kernel itself while the head runs; any other pointer gets a
+ * copy after the kernel.  The values are the same either way. */
 int qwen_decode_step(qwen_ctx* ctx, const int* tok, int batch, float* logits_out,
                      int* argmax_out);
 

@@ -901,9 +901,25 @@ int qwen_decode_step(qwen_ctx* c, const int* tok, int batch, float* logits_out, 
   io[1] = 1;
   io[2] = tok[0];
   if ((rc = push_ctl(c, 1))) return rc;
-  if ((rc = launch_step(c))) return rc;
+  // Page-locked host logits (cudaMallocHost, a pinned torch tensor) are in the
+  // device's address space: the head writes them there itself, over the bus
+  // while it runs, instead of a copy after the kernel.  Any other pointer gets
+  // the copy.  (One GPU only: a TP rank writes its vocab slice.)
+  float* direct = nullptr;
+  if (logits_out && c->tp.world == 1) {
+    cudaPointerAttributes pa;
+    if (cudaPointerGetAttributes(&pa, logits_out) == cudaSuccess) {
+      if (pa.type == cudaMemoryTypeHost && pa.devicePointer) direct = static_cast<float*>(pa.devicePointer);
+    } else {
+      (void)cudaGetLastError();
+    }
+  }
+  if (direct) c->P.logits = direct;
+  rc = launch_step(c);
+  c->P.logits = c->S.logits;
+  if (rc) return rc;
   QCUDA(c, cudaMemcpyAsync(c->h_err, c->S.err, 16 + sizeof(int), cudaMemcpyDeviceToHost, c->st));
-  if (logits_out)
+  if (logits_out && !direct)
     QCUDA(c, cudaMemcpyAsync(logits_out, c->S.logits, (size_t)VOCAB * 4, cudaMemcpyDefault, c->st));
   QCUDA(c, cudaStreamSynchronize(c->st));
   c->seq += 1;

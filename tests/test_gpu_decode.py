@@ -10,6 +10,7 @@ import numpy as np
 import pytest
 
 from golden_util import LOGIT_RTOL, fixture, logits_close
+from qwen_fpga_b200.api import VOCAB
 from oracle import golden_port as P
 
 pytestmark = pytest.mark.gpu
@@ -49,6 +50,27 @@ def test_config0_step_logits_match_golden(dec):
         if want:
             errs[i] = logits_close(lg, fx, f"step{i}")
     assert max(errs.values()) < LOGIT_RTOL, errs
+
+
+def test_pinned_logits_written_by_the_kernel_match_the_copy(dec):
+    """Page-locked host logits are written by the head kernel itself; pageable
+    ones are copied after it.  Both give the same logits bit for bit, every
+    step, and the golden's at step 15."""
+    import torch
+    fx = fixture("config0.npz")
+    pinned = torch.empty(VOCAB, dtype=torch.float32, pin_memory=True).numpy()
+    runs = []
+    for buf in (pinned, np.empty(VOCAB, np.float32)):
+        dec.reset()
+        dec.set_act_int8(False)
+        got = []
+        for t in fx["prompt"].tolist():
+            am, lg = dec.decode_step(t, want_logits=True, out=buf)
+            got.append((am, lg.copy()))
+        runs.append(got)
+    for (a0, l0), (a1, l1) in zip(*runs):
+        assert a0 == a1 and np.array_equal(l0, l1)
+    assert logits_close(runs[0][15][1], fx, "step15") < LOGIT_RTOL
 
 
 def test_generate_and_step_paths_agree(dec):
