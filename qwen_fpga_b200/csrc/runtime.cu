@@ -908,11 +908,11 @@ int qwen_decode_step(qwen_ctx* c, const int* tok, int batch, float* logits_out, 
   float* direct = nullptr;
   if (logits_out && c->tp.world == 1) {
     cudaPointerAttributes pa;
-    if (cudaPointerGetAttributes(&pa, logits_out) == cudaSuccess) {
-      if (pa.type == cudaMemoryTypeHost && pa.devicePointer) direct = static_cast<float*>(pa.devicePointer);
-    } else {
-      (void)cudaGetLastError();
-    }
+    void* dp = nullptr;
+    if (cudaPointerGetAttributes(&pa, logits_out) == cudaSuccess && pa.type == cudaMemoryTypeHost &&
+        cudaHostGetDevicePointer(&dp, logits_out, 0) == cudaSuccess && dp)   // mapped for this device
+      direct = static_cast<float*>(dp);
+    (void)cudaGetLastError();
   }
   if (direct) c->P.logits = direct;
   rc = launch_step(c);
