@@ -53,6 +53,28 @@ def test_tp_plan_partitions_every_dimension(world):
     assert set().union(*(range(*p["kv_groups"]) for p in plans)) == {0, 1}
 
 
+@pytest.mark.parametrize("world", [4, 8])
+def test_kv_sequence_split_groups(world):
+    """At 4 and 8 ranks each KV group is shared by ns = world / 2 ranks that are
+    contiguous in rank order (the decode kernel's exchange addresses them as
+    tp_rank - tp_rank % ns + j) and split its positions: the slices
+    [j Tn / ns, (j + 1) Tn / ns) of those ranks tile [0, Tn) for every Tn,
+    empty slices included when Tn < ns."""
+    ns = world // 2
+    plans = [_plan(r, world) for r in range(world)]
+    for r, p in enumerate(plans):
+        g0, g1 = p["kv_groups"]
+        assert g1 - g0 == 1
+        first = r - r % ns
+        assert all(plans[q]["kv_groups"] == (g0, g1) for q in range(first, first + ns))
+        assert all(plans[q]["kv_groups"] != (g0, g1) for q in range(world) if not first <= q < first + ns)
+    for Tn in list(range(1, 40)) + [4097, 32769]:
+        cover = []
+        for j in range(ns):
+            cover.extend(range(j * Tn // ns, (j + 1) * Tn // ns))
+        assert cover == list(range(Tn))
+
+
 @pytest.mark.parametrize("world,rank", [(3, 0), (16, 0), (2, 2), (2, -1)])
 def test_tp_plan_rejects_bad_shards(world, rank):
     from qwen_fpga_b200 import api
