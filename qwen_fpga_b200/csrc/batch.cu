@@ -1149,7 +1149,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) k_bt_attn(const AttnArgs a) {
             O[h] = fmaf(mw[4 + t], sb, __fmul_rn(O[h], sa));
             M[h] = Mn;
           }
-        if (rnd == 0) bar_compute();   // round 1 rewrites the buffer
+        if (rnd == 0) bar_compute();   // the second merge pass rewrites the buffer
       }
       float* pr = a.part + ((((size_t)it.b * NKV + it.g) * a.maxch + it.cc) * 4) * AT_PROW;
 #pragma unroll

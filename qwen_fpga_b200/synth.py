@@ -14,7 +14,7 @@ model of the exact 0.8B shapes.  The blob is the reference's on-disk contract
 
 Which tensors are int8 follows ``golden/quant.py:22-40`` and the per-row
 symmetric quantiser is ``golden/quant.py:43-49``.  The random draw is the
-survey's pinned generator: ``default_rng(seed)`` walked in read order, each
+pinned generator of the benchmark configs: ``default_rng(seed)`` walked in read order, each
 tensor ``standard_normal(shape, float32) * 0.02``.
 """
 
