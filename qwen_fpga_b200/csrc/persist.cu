@@ -1945,8 +1945,8 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl, int s0
   float* kn = qn + 4 * HD;                  // [256] new key
   float* vn = kn + HD;                      // [256] new value
   float* raw = vn + HD;                     // [6][256] projections as read (q x4, k, v)
-  float* sp = raw;                          // [4][ASB] scores, then probabilities (after raw is consumed)
-  float* st = sp + 4 * ASB;                 // [4] running max, [4] running sum, [4] rescale
+  float* sp = raw;                          // [2][4][ASB] scores, then probabilities, of alternate blocks (after raw is consumed)
+  float* st = sp + 8 * ASB;                 // [4] running max, [4] running sum, [4] rescale
   float* ox = st + 12;                      // [4][256] the second half's o
   const unsigned tin = tag_of(c, p - 1), tout = tag_of(c, p);
   const float* kc = A.kcache + (size_t)fi * A.max_ctx * KVPROJ + g * HD;
@@ -2027,8 +2027,10 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl, int s0
     A.vcache[((size_t)fi * A.max_ctx + T) * KVPROJ + g * HD + threadIdx.x] = vn[threadIdx.x];
   }
   float o[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int s0 = t0; s0 < t1; s0 += ASB) {
+  int par = 0;   // which of the two score buffers this block uses
+  for (int s0 = t0; s0 < t1; s0 += ASB, par ^= 1) {
     const int nb = min(ASB, t1 - s0);
+    float* spc = sp + par * 4 * ASB;
     // scores of the block (256^-0.5, exact): warp = position
     if (wid < nb) {
       const int tp = s0 + wid;
@@ -2042,7 +2044,7 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl, int s0
         float dt = q0.x * kk[0] + q0.y * kk[1] + q0.z * kk[2] + q0.w * kk[3];
         dt += q1.x * kk[4] + q1.y * kk[5] + q1.z * kk[6] + q1.w * kk[7];
         dt = warp_sum(dt);
-        if (lane == 0) sp[hq * ASB + wid] = dt * 0.0625f;
+        if (lane == 0) spc[hq * ASB + wid] = dt * 0.0625f;
       }
     }
     // the block's V stays in registers; the next block's K can be requested now
@@ -2053,12 +2055,12 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl, int s0
     consumer_sync();
     // online softmax: warp hq < 4 updates head hq
     if (wid < 4) {
-      const float sv = lane < nb ? sp[wid * ASB + lane] : -INFINITY;
+      const float sv = lane < nb ? spc[wid * ASB + lane] : -INFINITY;
       const float mold = st[wid];
       const float mnew = fmaxf(mold, warp_max(sv));
       const float pe = lane < nb ? expf(sv - mnew) : 0.0f;
       const float ls = warp_sum(pe);
-      if (lane < ASB) sp[wid * ASB + lane] = pe;
+      if (lane < ASB) spc[wid * ASB + lane] = pe;
       if (lane == 0) {
         const float sc = mold == -INFINITY ? 0.0f : expf(mold - mnew);
         st[8 + wid] = sc;
@@ -2076,10 +2078,11 @@ __device__ bool attn_item(PCtx& c, int p, int g, int cc, int nch, int cl, int s0
       if (tv < t1) {
         const float vv = tv < T ? vb[j] : vn[d];
 #pragma unroll
-        for (int hq = 0; hq < 4; ++hq) o[hq] = fmaf(sp[hq * ASB + 8 * half + j], vv, o[hq]);
+        for (int hq = 0; hq < 4; ++hq) o[hq] = fmaf(spc[hq * ASB + 8 * half + j], vv, o[hq]);
       }
     }
-    consumer_sync();   // sp is rewritten by the next block
+    // no barrier here: the next block's scores go to the other buffer, and
+    // its softmax waits behind a barrier every thread reaches after this P V
   }
   // the two halves' o
   if (half == 1) {
@@ -2403,7 +2406,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) k_decode_persistent(PersistArgs A
   }
 }
 
-static_assert(OFF_DIG + (4 * HD + 2 * HD + 6 * HD) * 4 <= OFF_HS && 4 * ASB + 12 + 4 * HD <= 6 * HD,
+static_assert(OFF_DIG + (4 * HD + 2 * HD + 6 * HD) * 4 <= OFF_HS && 8 * ASB + 12 + 4 * HD <= 6 * HD,
               "attention scratch must fit in the digit/xf region");
 
 }  // namespace
